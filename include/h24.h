@@ -1,0 +1,151 @@
+/*
+ * h24.h -- C ABI of the B200 (sm_100a) H24 codec library (libh24.so).
+ *
+ * Drop-in device implementation of the hot path of alavicka/pollux:
+ * nearest-codeword quantisation onto the 196,561-entry H24 codebook, 18-bit
+ * index pack / unpack, and LUT dequantisation to fp16.  Every entry point
+ * takes plain device pointers and sizes plus a CUDA stream (cudaStream_t
+ * passed as void*; NULL = legacy default stream), launches asynchronously on
+ * that stream and returns a status code.  No entry point synchronises the
+ * device, except where stated.  Buffers are owned by the caller; the library
+ * owns only its per-device codebook tables and stream-ordered scratch.
+ *
+ * Indices are codebook rows: 0 is the origin, 1..196560 the kissing points.
+ */
+#ifndef H24_H_
+#define H24_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define H24_OK 0
+#define H24_ERR_INVALID 1  /* bad argument: size, alignment, null pointer, rule */
+#define H24_ERR_CUDA 2     /* a CUDA runtime call failed (message in h24_last_error) */
+#define H24_ERR_RANGE 3    /* an input index exceeds 196560 */
+#define H24_ERR_TIMEOUT 4  /* a bounded wait inside a kernel ran out */
+#define H24_ERR_STATE 5    /* codebook tables could not be built */
+
+/* ---- nearest-codeword rules -------------------------------------------- */
+/* Training rule: index 0 iff 2 * max_j(x . kp_j) < 3.999999761581421,
+ * else argmax + 1 (castor.py:448-462, 522, 551-557). */
+#define H24_RULE_TRAIN 0
+/* Pack rule: index 0 iff ||x||_2 < 1e-8, else argmax + 1 (pack.py:169-177). */
+#define H24_RULE_PACK 1
+
+/* ---- element types for h24_gather_codewords ---------------------------- */
+#define H24_DTYPE_F32 0
+#define H24_DTYPE_F16 1
+#define H24_DTYPE_BF16 2
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *h24_last_error(void);
+
+/* Library version string. */
+const char *h24_version(void);
+
+/* Build the codebook tables on the host and upload them to `device`
+ * (idempotent; thread-safe).  Replaces the lru-cached table construction of
+ * castor._build_codebook_cpu / get_h24_codebook (castor.py:146-199).  Every
+ * other call initialises the current device on first use. */
+int h24_init(int device);
+
+/* Raw integer coordinates of the 196,560 kissing points, [196560][24] int8 in
+ * the reference's row order (codebook row j+1 = raw row j * 1/sqrt(8)),
+ * written to HOST memory.  Needs no GPU (castor.py:98-190). */
+int h24_codebook_raw(int8_t *out_host);
+
+/* Copy the codebook to device memory as fp32 [196561][24]
+ * (get_h24_codebook(device, torch.float32), castor.py:193-199). */
+int h24_codebook_f32(float *out, void *stream);
+
+/* codebook_fingerprint(): cb[:4,:4] as 16 floats on the host (castor.py:263-266). */
+int h24_fingerprint(float out16[16]);
+
+/* ---- 18-bit pack (castor.pack_indices, castor.py:226-246) ---------------
+ * idx: n indices; each is truncated to 32 bits (as .to(torch.int32) does) and
+ * then to 18 bits by the byte formulas.  out: ((n+3)/4)*9 bytes; missing tail
+ * indices are packed as 0. */
+int h24_pack(const int32_t *idx, int64_t n, uint8_t *out, void *stream);
+int h24_pack_i64(const int64_t *idx, int64_t n, uint8_t *out, void *stream);
+
+/* ---- 18-bit unpack (castor.unpack_indices, castor.py:249-260) -----------
+ * packed: groups*9 bytes.  Writes min(n, 4*groups) indices. */
+int h24_unpack(const uint8_t *packed, int64_t groups, int64_t n, int32_t *out, void *stream);
+int h24_unpack_i64(const uint8_t *packed, int64_t groups, int64_t n, int64_t *out, void *stream);
+
+/* ---- LUT dequant (PackedH24Linear.materialize, pollux.py:485-500) -------
+ * packed: ((rows*in/24+3)/4)*9 bytes, sigma16: rows fp16 bit patterns,
+ * out16: rows*in fp16 bit patterns,
+ *   out = fp16( fp32( fp16(cb16[idx] * sigma16[row]) ) * 0.70710677f ).
+ * in_features must be a positive multiple of 24.  Indices above 196560 are
+ * written as the origin and counted into *bad_count (a device int32; may be
+ * NULL), which the caller reads to raise the reference's IndexError. */
+int h24_dequant(const uint8_t *packed, const uint16_t *sigma16, int64_t rows,
+                int64_t in_features, uint16_t *out16, int32_t *bad_count, void *stream);
+
+/* One layer of h24_dequant_batched. */
+typedef struct h24_dequant_layer {
+  const uint8_t *packed;
+  const uint16_t *sigma16;
+  uint16_t *out16;
+  int64_t rows;
+  int64_t in_features;
+} h24_dequant_layer;
+
+/* Dequantise `count` layers with one launch per 64 layers (the materialize()
+ * loop of PolluxModel.from_packed_checkpoint, pollux.py:748-750).  `layers` is
+ * a host array, read before the call returns. */
+int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad_count,
+                        void *stream);
+
+/* ---- nearest codeword (castor._leech_nn_kernel / castor_quantize_leech,
+ *      castor.py:386-560; pack._quantize_h24_layer search, pack.py:166-177) --
+ * x: n atoms of 24 fp32 values (16-byte aligned), out_idx: n int32 indices.
+ * Exact fp64 argmax of x . kp_j (lowest index on ties) under `rule`.  A
+ * tcgen05 bf16 screening pass keeps every codeword that can still be the
+ * maximum; an fp64 rescore picks the winner. */
+int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *stream);
+
+/* ---- fused pack-rule layer quantiser (pack._quantize_h24_layer, pack.py:139-180)
+ * w: rows x in_features fp32 row-major (16-byte aligned), rows*in_features a
+ * multiple of 24; atoms are consecutive runs of 24 values of the flattened
+ * matrix (pack.py:161).  Writes sigma16_out[rows] =
+ * fp16(clamp_min(sqrt(mean(w^2)+1e-8) * sqrt(12), 1e-8)) and the packed
+ * indices packed_out[((rows*in/24+3)/4)*9] of the pack rule.  Each row's mean
+ * of fp32 squares is summed in fp64 and rounded once to fp32, so sigma16 can
+ * differ from torch's fp32 reduction by one fp16 ulp on a boundary row. */
+int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features,
+                       uint16_t *sigma16_out, uint8_t *packed_out, void *stream);
+
+/* ---- codeword gather (index_select of castor.py:533, 559) ---------------
+ * out[a][0..23] = codebook[idx[a]] converted to `dtype` (H24_DTYPE_*). */
+int h24_gather_codewords(const int32_t *idx, int64_t n, int dtype, void *out, void *stream);
+
+/* ---- instrumentation ----------------------------------------------------
+ * When enabled, every h24_quantize / h24_quantize_layer call records CUDA
+ * events around its tensor-core screening kernel on the caller's stream.
+ * h24_timing_read synchronises on the recorded events and returns the summed
+ * milliseconds and the number of launches since the last read. */
+int h24_timing_enable(int enable);
+int h24_timing_read(double *ms, int64_t *launches);
+
+/* Counters accumulated by the quantize calls on the current device since the
+ * previous read (reading resets them; synchronises `stream`): atoms whose
+ * candidate list overflowed into the exhaustive fp64 scan, and candidate
+ * chunks of 64 codewords rescored in fp64. */
+int h24_quantize_stats(int64_t *overflow_atoms, int64_t *rescored_chunks, void *stream);
+
+/* Synchronise `stream` and report a device-side failure of earlier quantize
+ * calls on the current device: H24_ERR_TIMEOUT if a bounded wait inside the
+ * screening kernel ran out (the word is then cleared), else H24_OK. */
+int h24_check(void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H24_H_ */

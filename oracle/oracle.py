@@ -1,0 +1,280 @@
+"""CPU oracle for the H24 hot path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` may import this module, and only as the checker or as the timed CPU
+baseline.  The product (``pollux_b200``) never calls it and has no CPU fallback.
+
+It wraps ``oracle/h24_oracle.c`` (built by ``oracle/Makefile`` into
+``oracle/_build/libh24_oracle.so``) and adds numpy restatements of the
+reference's three nearest-codeword semantics:
+
+* ``nearest_exact``   -- fp64 argmax of x.kp, lowest index on ties
+                         (the parity judge; C, multithreaded).
+* ``nearest_fp32_pack_rule`` -- fp32 ``atoms @ kp.T``, first max, zero only for
+                         ``||atom|| < 1e-8`` (restates pack.py:139-180).
+* ``nearest_bf16_train_rule`` -- scores of bf16-rounded atoms against the
+                         codebook in fp32, origin snap ``2*max < c_sq_norm``
+                         (restates the Triton kernel castor.py:386-462 and the
+                         autocast fallback castor.py:549-557 up to score
+                         rounding).
+
+Pack / unpack / dequant restate castor.py:226-260 and pollux.py:485-500.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import threading
+from functools import lru_cache
+
+import numpy as np
+
+H24_DIM = 24
+H24_KISSING_COUNT = 196_560
+H24_CODEBOOK_COUNT = 196_561
+C_SQ_NORM = 3.999999761581421          # castor.py:522 (measured on the reference)
+RULE_TRAIN = 0                          # origin iff 2*max < C_SQ_NORM
+RULE_PACK = 1                           # origin iff ||x|| < 1e-8
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libh24_oracle.so")
+_lock = threading.Lock()
+
+
+def build() -> str:
+    """Compile the C oracle (idempotent) and return the library path."""
+    with _lock:
+        src = os.path.join(_HERE, "h24_oracle.c")
+        if (not os.path.exists(_LIB_PATH)
+                or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src)):
+            subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+@lru_cache(maxsize=1)
+def lib() -> ctypes.CDLL:
+    path = build()
+    L = ctypes.CDLL(path)
+    P = ctypes.c_void_p
+    i64 = ctypes.c_int64
+    L.h24o_raw_kissing_points.argtypes = [P]
+    L.h24o_raw_kissing_points.restype = ctypes.c_int
+    L.h24o_codebook_f32.argtypes = [P]
+    L.h24o_codebook_f32.restype = ctypes.c_int
+    L.h24o_nearest.argtypes = [P, P, i64, ctypes.c_int, P, P, ctypes.c_int]
+    L.h24o_nearest.restype = None
+    L.h24o_pack.argtypes = [P, i64, P]
+    L.h24o_pack.restype = None
+    L.h24o_unpack.argtypes = [P, i64, i64, P]
+    L.h24o_unpack.restype = None
+    L.h24o_dequant.argtypes = [P, P, P, i64, i64, P]
+    L.h24o_dequant.restype = i64
+    L.h24o_score.argtypes = [P, P, ctypes.c_int32]
+    L.h24o_score.restype = ctypes.c_double
+    L.h24o_sigma16_from_rms.argtypes = [ctypes.c_float]
+    L.h24o_sigma16_from_rms.restype = ctypes.c_uint16
+    return L
+
+
+def _ptr(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+# ---------------------------------------------------------------------------
+# Codebook (castor.py:98-199)
+# ---------------------------------------------------------------------------
+@lru_cache(maxsize=1)
+def raw_kissing_points() -> np.ndarray:
+    """[196560, 24] int8 raw coordinates, in the reference's sorted order."""
+    out = np.empty((H24_KISSING_COUNT, H24_DIM), dtype=np.int8)
+    rc = lib().h24o_raw_kissing_points(_ptr(out))
+    if rc != 0:
+        raise RuntimeError(f"oracle codebook generation failed (rc={rc})")
+    out.setflags(write=False)
+    return out
+
+
+@lru_cache(maxsize=1)
+def codebook_f32() -> np.ndarray:
+    """[196561, 24] fp32 codebook, origin at row 0 (get_h24_codebook fp32)."""
+    out = np.empty((H24_CODEBOOK_COUNT, H24_DIM), dtype=np.float32)
+    rc = lib().h24o_codebook_f32(_ptr(out))
+    if rc != 0:
+        raise RuntimeError(f"oracle codebook generation failed (rc={rc})")
+    out.setflags(write=False)
+    return out
+
+
+def kissing_points_f32() -> np.ndarray:
+    return codebook_f32()[1:]
+
+
+def fingerprint() -> tuple:
+    """codebook_fingerprint(): cb[:4,:4] as 16 floats (castor.py:263-266)."""
+    return tuple(float(v) for v in codebook_f32()[:4, :4].reshape(-1))
+
+
+# ---------------------------------------------------------------------------
+# Nearest codeword
+# ---------------------------------------------------------------------------
+def nearest_exact(x: np.ndarray, rule: int = RULE_TRAIN, nthreads: int = 0,
+                  return_best: bool = False):
+    """Exact fp64 nearest codeword index for each row of x ([n,24] fp32)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, H24_DIM)
+    n = x.shape[0]
+    idx = np.empty(n, dtype=np.int32)
+    best = np.empty(n, dtype=np.float64)
+    kp = np.ascontiguousarray(kissing_points_f32())
+    if n:
+        lib().h24o_nearest(_ptr(kp), _ptr(x), n, int(rule), _ptr(idx), _ptr(best), int(nthreads))
+    return (idx, best) if return_best else idx
+
+
+def scores_fp64(x: np.ndarray, idx: np.ndarray) -> np.ndarray:
+    """fp64 score x.kp[idx-1] (0 for the origin), same fma order as the GPU."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, H24_DIM)
+    cb = codebook_f32().astype(np.float64)
+    c = cb[np.asarray(idx, dtype=np.int64)]
+    acc = np.zeros(x.shape[0], dtype=np.float64)
+    xd = x.astype(np.float64)
+    for i in range(H24_DIM):
+        acc = acc + xd[:, i] * c[:, i]   # products exact in fp64
+    return acc
+
+
+def dist2_fp64(x: np.ndarray, idx: np.ndarray) -> np.ndarray:
+    """Squared distance ||x - cb[idx]||^2 in fp64."""
+    x = np.asarray(x, dtype=np.float32).reshape(-1, H24_DIM).astype(np.float64)
+    c = codebook_f32().astype(np.float64)[np.asarray(idx, dtype=np.int64)]
+    return ((x - c) ** 2).sum(axis=1)
+
+
+def nearest_fp32_pack_rule(atoms: np.ndarray, chunk: int = 4096) -> np.ndarray:
+    """Restates pack._quantize_h24_layer's search (pack.py:166-177) in numpy:
+    fp32 scores, first maximum, index 0 only when ||atom||_2 < 1e-8."""
+    a = np.ascontiguousarray(atoms, dtype=np.float32).reshape(-1, H24_DIM)
+    kpT = np.ascontiguousarray(kissing_points_f32().T)
+    out = np.zeros(a.shape[0], dtype=np.int64)
+    for i in range(0, a.shape[0], chunk):
+        s = a[i:i + chunk]
+        scores = s @ kpT
+        best = scores.argmax(axis=1) + 1
+        zero = np.linalg.norm(s, axis=1) < np.float32(1e-8)
+        best[zero] = 0
+        out[i:i + chunk] = best
+    return out
+
+
+def to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round fp32 to bf16 (round to nearest even), returned as fp32."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32).reshape(np.shape(x))
+
+
+def nearest_bf16_train_rule(x: np.ndarray, chunk: int = 4096) -> np.ndarray:
+    """bf16(x) . bf16(kp) accumulated in fp32, lowest index among maxima,
+    origin iff 2*max < c_sq_norm (castor.py:436-462)."""
+    a = to_bf16(np.asarray(x, dtype=np.float32).reshape(-1, H24_DIM))
+    kpT = np.ascontiguousarray(to_bf16(kissing_points_f32()).T)
+    out = np.zeros(a.shape[0], dtype=np.int64)
+    for i in range(0, a.shape[0], chunk):
+        scores = a[i:i + chunk] @ kpT
+        best = scores.argmax(axis=1)
+        m = scores[np.arange(scores.shape[0]), best]
+        r = best + 1
+        r[(2.0 * m) < np.float32(C_SQ_NORM)] = 0
+        out[i:i + chunk] = r
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Pack / unpack (castor.py:226-260)
+# ---------------------------------------------------------------------------
+def pack_indices(indices: np.ndarray) -> np.ndarray:
+    """numpy restatement of castor.pack_indices: 4 x 18 bit -> 9 bytes."""
+    v = np.asarray(indices).reshape(-1).astype(np.int64).astype(np.int32)  # .to(int32) wraps
+    rem = v.size % 4
+    if rem:
+        v = np.concatenate([v, np.zeros(4 - rem, dtype=np.int32)])
+    g = v.reshape(-1, 4)
+    i0, i1, i2, i3 = g[:, 0], g[:, 1], g[:, 2], g[:, 3]
+    out = np.empty((g.shape[0], 9), dtype=np.uint8)
+    out[:, 0] = (i0 >> 10) & 0xFF
+    out[:, 1] = (i0 >> 2) & 0xFF
+    out[:, 2] = ((i0 & 0x03) << 6) | ((i1 >> 12) & 0x3F)
+    out[:, 3] = (i1 >> 4) & 0xFF
+    out[:, 4] = ((i1 & 0x0F) << 4) | ((i2 >> 14) & 0x0F)
+    out[:, 5] = (i2 >> 6) & 0xFF
+    out[:, 6] = ((i2 & 0x3F) << 2) | ((i3 >> 16) & 0x03)
+    out[:, 7] = (i3 >> 8) & 0xFF
+    out[:, 8] = i3 & 0xFF
+    return out.reshape(-1)
+
+
+def unpack_indices(packed: np.ndarray, num_indices: int) -> np.ndarray:
+    """numpy restatement of castor.unpack_indices (int64 result)."""
+    c = np.asarray(packed, dtype=np.uint8).reshape(-1, 9).astype(np.int32)
+    i0 = (c[:, 0] << 10) | (c[:, 1] << 2) | (c[:, 2] >> 6)
+    i1 = ((c[:, 2] & 0x3F) << 12) | (c[:, 3] << 4) | (c[:, 4] >> 4)
+    i2 = ((c[:, 4] & 0x0F) << 14) | (c[:, 5] << 6) | (c[:, 6] >> 2)
+    i3 = ((c[:, 6] & 0x03) << 16) | (c[:, 7] << 8) | c[:, 8]
+    return np.stack([i0, i1, i2, i3], axis=1).reshape(-1)[:num_indices].astype(np.int64)
+
+
+def pack_indices_c(indices: np.ndarray) -> np.ndarray:
+    v = np.ascontiguousarray(np.asarray(indices).reshape(-1).astype(np.int64).astype(np.int32))
+    out = np.empty(((v.size + 3) // 4) * 9, dtype=np.uint8)
+    if v.size:
+        lib().h24o_pack(_ptr(v), v.size, _ptr(out))
+    return out
+
+
+def unpack_indices_c(packed: np.ndarray, num_indices: int) -> np.ndarray:
+    p = np.ascontiguousarray(packed, dtype=np.uint8).reshape(-1)
+    groups = p.size // 9
+    n = min(int(num_indices), 4 * groups)
+    out = np.empty(max(n, 0), dtype=np.int32)
+    if n > 0:
+        lib().h24o_unpack(_ptr(p), groups, n, _ptr(out))
+    return out.astype(np.int64)
+
+
+# ---------------------------------------------------------------------------
+# Dequant (pollux.py:485-500) and the pack-rule row scale (pack.py:164)
+# ---------------------------------------------------------------------------
+def dequant(packed: np.ndarray, sigma16: np.ndarray, rows: int, in_features: int) -> np.ndarray:
+    """fp16 [rows, in_features] weight rebuilt like PackedH24Linear.materialize."""
+    p = np.ascontiguousarray(packed, dtype=np.uint8).reshape(-1)
+    s = np.ascontiguousarray(sigma16, dtype=np.float16).reshape(-1)
+    out = np.empty((rows, in_features), dtype=np.float16)
+    cb = np.ascontiguousarray(codebook_f32())
+    bad = lib().h24o_dequant(_ptr(cb), _ptr(p), _ptr(s.view(np.uint16)), rows, in_features,
+                             _ptr(out.view(np.uint16)))
+    if bad:
+        raise ValueError(f"{bad} packed indices exceed the codebook")
+    return out
+
+
+def dequant_numpy(packed: np.ndarray, sigma16: np.ndarray, rows: int, in_features: int) -> np.ndarray:
+    """Same as ``dequant`` with numpy's fp16 arithmetic (two roundings)."""
+    atoms = rows * in_features // H24_DIM
+    idx = unpack_indices(packed, atoms)
+    cb16 = codebook_f32().astype(np.float16)[idx].reshape(rows, in_features // H24_DIM, H24_DIM)
+    s16 = np.asarray(sigma16, dtype=np.float16).reshape(-1, 1, 1)
+    t = (cb16.astype(np.float32) * s16.astype(np.float32)).astype(np.float16)
+    w = (t.astype(np.float32) * np.float32(0.7071067811865476)).astype(np.float16)
+    return w.reshape(rows, in_features)
+
+
+def sigma16_pack_rule(weight: np.ndarray) -> np.ndarray:
+    """fp16 row scale of pack.py:164: fp32 squares summed in fp64, the mean
+    rounded once to fp32 (the reference reduces in fp32 in torch's order)."""
+    w = np.asarray(weight, dtype=np.float32)
+    ms = (w * w).astype(np.float64).mean(axis=1)
+    rms = np.sqrt((ms.astype(np.float32) + np.float32(1e-8)).astype(np.float32)).astype(np.float32)
+    s = (rms * np.float32(np.sqrt(12.0))).astype(np.float32)
+    s = np.maximum(s, np.float32(1e-8))
+    return s.astype(np.float16)

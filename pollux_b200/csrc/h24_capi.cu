@@ -1,0 +1,391 @@
+// h24_capi.cu -- extern "C" entry points of libh24 (declared in include/h24.h),
+// per-device codebook tables, error reporting and instrumentation, plus the
+// pack-rule row-scale kernel.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "h24_internal.cuh"
+
+namespace h24 {
+
+// ---------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------
+namespace {
+thread_local std::string t_last_error;
+}
+
+const char *last_error_cstr() { return t_last_error.c_str(); }
+
+void set_error(const std::string &msg) { t_last_error = msg; }
+
+int fail(int code, const std::string &msg) {
+  t_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  t_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return H24_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// codebook tables
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_tables_mu;
+Tables g_tables[kMaxDevices];
+bool g_tables_ok[kMaxDevices] = {};
+
+struct HostTables {
+  std::vector<int8_t> raw;        // [kKissing][24]
+  std::vector<uint16_t> tiled;    // [kKissingPad][32] bf16 bits, tiled
+  std::vector<uint32_t> nib;      // [kCount][3]
+  float fingerprint[16];
+  bool ok = false;
+  std::string err;
+};
+
+uint16_t bf16_bits_of_int(int v) {
+  // Small integers are exact in bf16: the top half of their fp32 pattern.
+  const float f = static_cast<float>(v);
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+const HostTables &host_tables() {
+  static HostTables H;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    H.raw.resize(static_cast<size_t>(kKissing) * kDim);
+    if (!build_raw_kissing_points(H.raw.data(), &H.err)) return;
+    H.tiled.assign(static_cast<size_t>(kKissingPad) * kKPad, 0);
+    for (int j = 0; j < kKissing; ++j) {
+      const int t = j / kTileN, rr = j % kTileN, g = rr / 8, r = rr % 8;
+      for (int k = 0; k < kDim; ++k) {
+        const size_t byte = static_cast<size_t>(t) * kTileN * kRowBytes + g * 512 + (k / 8) * 128 +
+                            r * 16 + (k % 8) * 2;
+        H.tiled[byte / 2] = bf16_bits_of_int(H.raw[static_cast<size_t>(j) * kDim + k]);
+      }
+    }
+    H.nib.assign(static_cast<size_t>(kCount) * 3, 0);
+    for (int row = 0; row < kCount; ++row)
+      for (int k = 0; k < kDim; ++k) {
+        const int raw = row == 0 ? 0 : H.raw[static_cast<size_t>(row - 1) * kDim + k];
+        H.nib[static_cast<size_t>(row) * 3 + k / 8] |= static_cast<uint32_t>(raw + 4)
+                                                       << (4 * (k % 8));
+      }
+    for (int r = 0; r < 4; ++r)
+      for (int c = 0; c < 4; ++c)
+        H.fingerprint[r * 4 + c] =
+            r == 0 ? 0.f
+                   : static_cast<float>(H.raw[static_cast<size_t>(r - 1) * kDim + c]) * kLeechScaleF;
+    H.ok = true;
+  });
+  return H;
+}
+
+int build_device_tables(int dev, Tables *T) {
+  const HostTables &H = host_tables();
+  if (!H.ok) return fail(H24_ERR_STATE, "codebook construction failed: " + H.err);
+  void *p = nullptr;
+  H24_CUDA_TRY(cudaMalloc(&p, H.tiled.size() * sizeof(uint16_t)));
+  H24_CUDA_TRY(cudaMemcpy(p, H.tiled.data(), H.tiled.size() * sizeof(uint16_t),
+                          cudaMemcpyHostToDevice));
+  T->cb_tiled = static_cast<const __nv_bfloat16 *>(p);
+  H24_CUDA_TRY(cudaMalloc(&p, H.raw.size()));
+  H24_CUDA_TRY(cudaMemcpy(p, H.raw.data(), H.raw.size(), cudaMemcpyHostToDevice));
+  T->cb_raw = static_cast<const int8_t *>(p);
+  H24_CUDA_TRY(cudaMalloc(&p, H.nib.size() * sizeof(uint32_t)));
+  H24_CUDA_TRY(
+      cudaMemcpy(p, H.nib.data(), H.nib.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
+  T->cb_nib = static_cast<const uint32_t *>(p);
+  H24_CUDA_TRY(cudaMalloc(&p, 2 * sizeof(int64_t) + 16));
+  H24_CUDA_TRY(cudaMemset(p, 0, 2 * sizeof(int64_t) + 16));
+  T->stats = static_cast<int64_t *>(p);
+  T->err = reinterpret_cast<int *>(static_cast<char *>(p) + 2 * sizeof(int64_t));
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.handleTypes = cudaMemHandleTypeNone;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = dev;
+  H24_CUDA_TRY(cudaMemPoolCreate(&T->pool, &props));
+  uint64_t keep = ~uint64_t(0);
+  H24_CUDA_TRY(cudaMemPoolSetAttribute(T->pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  std::memcpy(T->fingerprint, H.fingerprint, sizeof(T->fingerprint));
+  T->device = dev;
+  return H24_OK;
+}
+
+}  // namespace
+
+const Tables *tables_for_current_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cuda_fail(e, "cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("device ordinal out of range");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_tables_mu);
+  if (!g_tables_ok[dev]) {
+    if (build_device_tables(dev, &g_tables[dev]) != H24_OK) return nullptr;
+    g_tables_ok[dev] = true;
+  }
+  return &g_tables[dev];
+}
+
+// ---------------------------------------------------------------------------
+// instrumentation
+// ---------------------------------------------------------------------------
+namespace {
+std::mutex g_timing_mu;
+bool g_timing = false;
+std::vector<std::pair<cudaEvent_t, cudaEvent_t>> g_events;
+}  // namespace
+
+bool timing_enabled() {
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  return g_timing;
+}
+
+void timing_record(cudaEvent_t start, cudaEvent_t stop) {
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  g_events.emplace_back(start, stop);
+}
+
+// ---------------------------------------------------------------------------
+// pack-rule row scale: sigma16 = fp16(clamp_min(sqrt(mean(w^2)+1e-8)*sqrt(12), 1e-8))
+// (pack.py:164, castor.py:309-313).  The fp32 squares are summed in fp64 and
+// the mean rounded once to fp32; torch's own fp32 reduction order differs, so
+// sigma16 can differ by one fp16 ulp on rows whose value sits on a rounding
+// boundary.
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void sigma16_kernel(const float *__restrict__ w, int64_t rows, int64_t in_f,
+                               uint16_t *__restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (row >= rows) return;
+  const float *p = w + row * in_f;
+  double acc = 0.0;
+  for (int64_t i = lane; i < in_f; i += 32) {
+    const float v = __ldg(p + i);
+    acc += static_cast<double>(__fmul_rn(v, v));  // weight.pow(2) rounds to fp32
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const float mean = static_cast<float>(acc / static_cast<double>(in_f));
+    const float rms = sqrtf(mean + 1e-8f);
+    float s = rms * 3.4641016151377544f;
+    s = fmaxf(s, 1e-8f);
+    out[row] = __half_as_ushort(__float2half_rn(s));
+  }
+}
+}  // namespace
+
+int launch_sigma16(const float *w, int64_t rows, int64_t in_f, uint16_t *sigma16, cudaStream_t s) {
+  if (rows <= 0) return H24_OK;
+  const int64_t threads = rows * 32;
+  sigma16_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(w, rows, in_f,
+                                                                             sigma16);
+  H24_CUDA_TRY(cudaGetLastError());
+  return H24_OK;
+}
+
+}  // namespace h24
+
+// ===========================================================================
+// extern "C" API
+// ===========================================================================
+using namespace h24;
+
+#define H24_TABLES_OR_FAIL(T)                       \
+  const Tables *T = tables_for_current_device();    \
+  if (!T) return H24_ERR_STATE
+
+static cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
+
+extern "C" {
+
+const char *h24_last_error(void) { return last_error_cstr(); }
+
+const char *h24_version(void) { return "h24-b200 0.1 (sm_100a, tcgen05)"; }
+
+int h24_init(int device) {
+  int prev = 0;
+  H24_CUDA_TRY(cudaGetDevice(&prev));
+  H24_CUDA_TRY(cudaSetDevice(device));
+  const Tables *t = tables_for_current_device();
+  cudaSetDevice(prev);
+  return t ? H24_OK : H24_ERR_STATE;
+}
+
+int h24_codebook_raw(int8_t *out_host) {
+  if (!out_host) return fail(H24_ERR_INVALID, "codebook_raw: null pointer");
+  const HostTables &H = host_tables();
+  if (!H.ok) return fail(H24_ERR_STATE, "codebook construction failed: " + H.err);
+  std::memcpy(out_host, H.raw.data(), H.raw.size());
+  return H24_OK;
+}
+
+int h24_codebook_f32(float *out, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (!out) return fail(H24_ERR_INVALID, "codebook_f32: null pointer");
+  // Row 0 is the origin; rows 1.. are the kissing points.
+  H24_CUDA_TRY(cudaMemsetAsync(out, 0, kDim * sizeof(float), as_stream(stream)));
+  return launch_codebook_f32(T, out + kDim, as_stream(stream));
+}
+
+int h24_fingerprint(float out16[16]) {
+  H24_TABLES_OR_FAIL(T);
+  if (!out16) return fail(H24_ERR_INVALID, "fingerprint: null pointer");
+  std::memcpy(out16, T->fingerprint, 16 * sizeof(float));
+  return H24_OK;
+}
+
+int h24_pack(const int32_t *idx, int64_t n, uint8_t *out, void *stream) {
+  if (n < 0) return fail(H24_ERR_INVALID, "pack: negative length");
+  if (n > 0 && (!idx || !out)) return fail(H24_ERR_INVALID, "pack: null pointer");
+  return launch_pack_i32(idx, n, out, as_stream(stream));
+}
+
+int h24_pack_i64(const int64_t *idx, int64_t n, uint8_t *out, void *stream) {
+  if (n < 0) return fail(H24_ERR_INVALID, "pack: negative length");
+  if (n > 0 && (!idx || !out)) return fail(H24_ERR_INVALID, "pack: null pointer");
+  return launch_pack_i64(idx, n, out, as_stream(stream));
+}
+
+int h24_unpack(const uint8_t *packed, int64_t groups, int64_t n, int32_t *out, void *stream) {
+  if (n < 0 || groups < 0) return fail(H24_ERR_INVALID, "unpack: negative size");
+  if (n > 0 && groups > 0 && (!packed || !out)) return fail(H24_ERR_INVALID, "unpack: null pointer");
+  return launch_unpack_i32(packed, groups, n, out, as_stream(stream));
+}
+
+int h24_unpack_i64(const uint8_t *packed, int64_t groups, int64_t n, int64_t *out, void *stream) {
+  if (n < 0 || groups < 0) return fail(H24_ERR_INVALID, "unpack: negative size");
+  if (n > 0 && groups > 0 && (!packed || !out)) return fail(H24_ERR_INVALID, "unpack: null pointer");
+  return launch_unpack_i64(packed, groups, n, out, as_stream(stream));
+}
+
+int h24_dequant(const uint8_t *packed, const uint16_t *sigma16, int64_t rows, int64_t in_features,
+                uint16_t *out16, int32_t *bad_count, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  h24_dequant_layer L{packed, sigma16, out16, rows, in_features};
+  return launch_dequant(T, nullptr, &L, 1, bad_count, as_stream(stream));
+}
+
+int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad_count,
+                        void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (count < 0 || (count > 0 && !layers)) return fail(H24_ERR_INVALID, "dequant_batched: bad layer list");
+  return launch_dequant(T, nullptr, layers, count, bad_count, as_stream(stream));
+}
+
+int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (n < 0) return fail(H24_ERR_INVALID, "quantize: negative atom count");
+  if (rule != H24_RULE_TRAIN && rule != H24_RULE_PACK)
+    return fail(H24_ERR_INVALID, "quantize: unknown rule");
+  if (n == 0) return H24_OK;
+  if (!x || !out_idx) return fail(H24_ERR_INVALID, "quantize: null pointer");
+  if (!aligned16(x)) return fail(H24_ERR_INVALID, "quantize: x must be 16-byte aligned");
+  return quantize(T, x, n, rule, out_idx, as_stream(stream));
+}
+
+int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16_t *sigma16_out,
+                       uint8_t *packed_out, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (rows < 0 || in_features <= 0 || (rows * in_features) % kDim != 0)
+    return fail(H24_ERR_INVALID, "quantize_layer: rows*in_features must be a multiple of 24");
+  if (rows == 0) return H24_OK;
+  if (!w || !sigma16_out || !packed_out) return fail(H24_ERR_INVALID, "quantize_layer: null pointer");
+  if (!aligned16(w)) return fail(H24_ERR_INVALID, "quantize_layer: w must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  int rc = launch_sigma16(w, rows, in_features, sigma16_out, s);
+  if (rc != H24_OK) return rc;
+  const int64_t atoms = rows * in_features / kDim;
+  int32_t *idx = nullptr;
+  H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&idx),
+                                       static_cast<size_t>(atoms) * sizeof(int32_t), T->pool, s));
+  rc = quantize(T, w, atoms, H24_RULE_PACK, idx, s);
+  if (rc == H24_OK) rc = launch_pack_i32(idx, atoms, packed_out, s);
+  cudaError_t e = cudaFreeAsync(idx, s);
+  if (rc == H24_OK && e != cudaSuccess) rc = cuda_fail(e, "cudaFreeAsync");
+  return rc;
+}
+
+int h24_gather_codewords(const int32_t *idx, int64_t n, int dtype, void *out, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (n < 0) return fail(H24_ERR_INVALID, "gather: negative length");
+  if (n > 0 && (!idx || !out)) return fail(H24_ERR_INVALID, "gather: null pointer");
+  return launch_gather(T, idx, n, dtype, out, as_stream(stream));
+}
+
+int h24_timing_enable(int enable) {
+  std::lock_guard<std::mutex> lk(g_timing_mu);
+  g_timing = enable != 0;
+  return H24_OK;
+}
+
+int h24_timing_read(double *ms, int64_t *launches) {
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+  {
+    std::lock_guard<std::mutex> lk(g_timing_mu);
+    ev.swap(g_events);
+  }
+  double total = 0.0;
+  int rc = H24_OK;
+  for (auto &p : ev) {
+    cudaError_t e = cudaEventSynchronize(p.second);
+    float t = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&t, p.first, p.second);
+    if (e != cudaSuccess && rc == H24_OK) rc = cuda_fail(e, "timing");
+    total += t;
+    cudaEventDestroy(p.first);
+    cudaEventDestroy(p.second);
+  }
+  if (ms) *ms = total;
+  if (launches) *launches = static_cast<int64_t>(ev.size());
+  return rc;
+}
+
+int h24_quantize_stats(int64_t *overflow_atoms, int64_t *rescored_chunks, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  int64_t h[2] = {0, 0};
+  cudaStream_t s = as_stream(stream);
+  H24_CUDA_TRY(cudaMemcpyAsync(h, T->stats, sizeof(h), cudaMemcpyDeviceToHost, s));
+  H24_CUDA_TRY(cudaStreamSynchronize(s));
+  H24_CUDA_TRY(cudaMemsetAsync(T->stats, 0, sizeof(h), s));
+  if (overflow_atoms) *overflow_atoms = h[0];
+  if (rescored_chunks) *rescored_chunks = h[1];
+  return H24_OK;
+}
+
+int h24_check(void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  cudaStream_t s = as_stream(stream);
+  int err = 0;
+  H24_CUDA_TRY(cudaMemcpyAsync(&err, T->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  H24_CUDA_TRY(cudaStreamSynchronize(s));
+  if (err != 0) {
+    H24_CUDA_TRY(cudaMemsetAsync(T->err, 0, sizeof(int), s));
+    return fail(H24_ERR_TIMEOUT, "a bounded wait in the screening kernel ran out");
+  }
+  return H24_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,98 @@
+// h24_internal.cuh -- shared definitions of the libh24 CUDA sources.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/h24.h"
+
+namespace h24 {
+
+constexpr int kDim = 24;
+constexpr int kKissing = 196560;
+constexpr int kCount = 196561;
+
+// Screening tiles: the codebook is streamed in tiles of kTileN codewords, the
+// last one padded with zero rows up to kKissingPad.
+constexpr int kTileN = 128;
+constexpr int kNumTiles = (kKissing + kTileN - 1) / kTileN;  // 1536
+constexpr int kKissingPad = kNumTiles * kTileN;              // 196608
+constexpr int kChunk = 64;                                   // candidate granularity
+constexpr int kNumChunks = kKissingPad / kChunk;             // 3072
+constexpr int kKPad = 32;                                    // K padded 24 -> 32 (bf16)
+constexpr int kRowBytes = kKPad * 2;                         // 64 bytes per operand row
+
+// fp32 value of LEECH_SCALE = 1/sqrt(8) and of s_lattice = 1/sqrt(2) as torch
+// rounds the Python floats (castor.py:49, 68).
+constexpr float kLeechScaleF = 0.35355339059327373f;
+constexpr float kSLatticeF = 0.7071067811865476f;
+// float(kissing_points[0].pow(2).sum()) of castor.py:522.
+constexpr double kCSqNorm = 3.999999761581421;
+
+// Per-device tables (all device pointers).
+struct Tables {
+  int device = -1;
+  // bf16 raw coordinates [kKissingPad][32], core-matrix tiled for the MMA B
+  // operand: tile t (128 rows) at t*8192 B; inside it 8-row group g at g*512,
+  // 16-byte K chunk c at c*128, row r at r*16.
+  const __nv_bfloat16 *cb_tiled = nullptr;
+  // raw int8 coordinates [kKissing][24] (kissing point j = codebook row j+1).
+  const int8_t *cb_raw = nullptr;
+  // 4-bit codes (raw + 4) [kCount][3] u32 words, element 8p+e in bits 4e..4e+3
+  // of word p; row 0 is the origin.
+  const uint32_t *cb_nib = nullptr;
+  float fingerprint[16];
+  // Device counters: [0] atoms sent to the exhaustive scan, [1] candidate
+  // chunks rescored; and the error word set by a timed-out wait.
+  int64_t *stats = nullptr;
+  int *err = nullptr;
+  // Stream-ordered pool for per-call scratch (kept warm between calls).
+  cudaMemPool_t pool = nullptr;
+};
+
+// Returns the tables of the current device, building them on first use.
+// nullptr on failure (message set).
+const Tables *tables_for_current_device();
+
+// Error helpers (thread-local message).
+const char *last_error_cstr();
+void set_error(const std::string &msg);
+int fail(int code, const std::string &msg);
+int cuda_fail(cudaError_t e, const char *what);
+
+#define H24_CUDA_TRY(expr)                                   \
+  do {                                                       \
+    cudaError_t _e = (expr);                                 \
+    if (_e != cudaSuccess) return ::h24::cuda_fail(_e, #expr); \
+  } while (0)
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Host-side raw codebook generation (h24_codebook.cpp).  out: [kKissing][24].
+bool build_raw_kissing_points(int8_t *out, std::string *err);
+
+// Kernel launchers (stream-ordered; return H24_OK or an error code).
+int launch_pack_i32(const int32_t *idx, int64_t n, uint8_t *out, cudaStream_t s);
+int launch_pack_i64(const int64_t *idx, int64_t n, uint8_t *out, cudaStream_t s);
+int launch_unpack_i32(const uint8_t *p, int64_t groups, int64_t n, int32_t *out, cudaStream_t s);
+int launch_unpack_i64(const uint8_t *p, int64_t groups, int64_t n, int64_t *out, cudaStream_t s);
+int launch_dequant(const Tables *t, const h24_dequant_layer *layers_dev,
+                   const h24_dequant_layer *layers_host, int count, int32_t *bad,
+                   cudaStream_t s);
+int launch_codebook_f32(const Tables *t, float *out_kissing, cudaStream_t s);
+int launch_gather(const Tables *t, const int32_t *idx, int64_t n, int dtype, void *out,
+                  cudaStream_t s);
+int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
+             cudaStream_t s);
+int launch_sigma16(const float *w, int64_t rows, int64_t in_f, uint16_t *sigma16,
+                   cudaStream_t s);
+
+// Instrumentation of the screening kernel.
+bool timing_enabled();
+void timing_record(cudaEvent_t start, cudaEvent_t stop);
+
+}  // namespace h24

@@ -1,0 +1,791 @@
+// h24_search.cu -- nearest-codeword search over the 196,560 H24 kissing points
+// (castor._leech_nn_kernel, castor.py:386-462; castor_quantize_leech,
+// castor.py:487-560; the search of pack._quantize_h24_layer, pack.py:166-177).
+//
+// Result semantics: index = argmax_j fp64(x . kp_j) + 1 with the lowest j on
+// ties, where fp64(x . kp_j) accumulates fma(x_i, kp_ji) for i = 0..23 in
+// order, kp_ji = fp32(raw_ji * fp32(1/sqrt(8))) as stored by the reference,
+// followed by the caller's origin rule (H24_RULE_TRAIN / H24_RULE_PACK).
+//
+// Pipeline per batch of atoms (one CUDA stream, no host synchronisation):
+//   1. prep_kernel      x -> bf16 "hi" operand (core-matrix tiled for UMMA) and
+//                       a per-atom bound 2E on |screening score - exact score|.
+//   2. screen_kernel    persistent tcgen05 kernel, one CTA per SM.  Each CTA
+//                       owns 256 atoms (two M=128 tiles) at a time and streams
+//                       the bf16 codebook (raw integers, exact in bf16, K
+//                       padded 24 -> 32) through shared memory with bulk
+//                       copies, 128 codewords per stage.  Scores accumulate in
+//                       TMEM (fp32), double-buffered; 8 epilogue warps read
+//                       them with tcgen05.ld, one thread per atom, and keep
+//                       the 64-codeword chunks whose maximum is within 2E of
+//                       the running best.
+//   3. rescore_kernel   one warp per atom rescans the surviving chunks in fp64
+//                       and applies the origin rule.
+//   4. exhaustive_kernel  fp64 scan of all codewords for the rare atoms whose
+//                       candidate list overflowed (exact ties over many chunks).
+//
+// Why the bound is sufficient: with S~ the screening score and R the exact
+// score (in raw-integer units), |S~_j - R_j| <= E for every j.  If j* is the
+// exact winner and B~ the screening maximum, S~_j* >= R_j* - E >= R_jhat - E
+// >= B~ - 2E.  Every chunk whose screening maximum is >= B~ - 2E is kept.
+#include <cstdio>
+#include <mutex>
+
+#include "h24_internal.cuh"
+
+namespace h24 {
+namespace {
+
+constexpr int kBlockAtoms = 256;                    // atoms per CTA work item
+constexpr int kStages = 10;                         // codebook ring depth
+constexpr int kBTileBytes = kTileN * kRowBytes;     // 8192
+constexpr int kATileBytes = kBlockAtoms * kRowBytes;  // 16384
+constexpr int kCap = 8;                             // candidate chunks per atom
+constexpr int kEpiWarps = 8;
+constexpr int kScreenThreads = 32 * (2 + kEpiWarps);  // 320
+constexpr uint32_t kTmemCols = 512;
+constexpr uint8_t kOverflow = 0xFF;
+constexpr int64_t kBatchAtoms = int64_t(1) << 22;    // atoms per pipeline batch
+constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s
+
+struct __align__(1024) ScreenSmem {
+  uint8_t a[2][kATileBytes];
+  uint8_t b[kStages][kBTileBytes];
+  float cand_score[kCap][kBlockAtoms];
+  uint16_t cand_chunk[kCap][kBlockAtoms];
+  uint64_t bar_b_full[kStages];
+  uint64_t bar_b_empty[kStages];
+  uint64_t bar_a_full[2];
+  uint64_t bar_a_empty[2];
+  uint64_t bar_acc_full[2];
+  uint64_t bar_acc_empty[2];
+  uint64_t bar_final;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// ---------------------------------------------------------------------------
+// PTX helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase of `bar` with the given parity.  Gives up after
+// kWaitLimitNs or when another role of the CTA has aborted; on a timeout it
+// raises the CTA abort flag and the device error word.
+__device__ __noinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          int *err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicExch(err, H24_ERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand without swizzle
+// (core matrices of 8 rows x 16 bytes): LBO = distance between the two
+// K-adjacent core matrices of one MMA (128 B), SBO = distance between 8-row
+// groups (512 B), version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128 >> 4) << 16) |
+         (static_cast<uint64_t>(512 >> 4) << 32) | (uint64_t(1) << 46);
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major,
+// M = 128, N = kTileN.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                            (static_cast<uint32_t>(kTileN >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+#define H24_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), \
+                  "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
+
+// 32 lanes x 64 consecutive 32-bit TMEM columns.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t *r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24), H24_R8(32), H24_R8(40), H24_R8(48),
+        H24_R8(56)
+      : "r"(taddr));
+}
+#undef H24_R8
+
+#define H24_T8(b) "+r"(r[b + 0]), "+r"(r[b + 1]), "+r"(r[b + 2]), "+r"(r[b + 3]), \
+                  "+r"(r[b + 4]), "+r"(r[b + 5]), "+r"(r[b + 6]), "+r"(r[b + 7])
+// Waits for this thread's outstanding tcgen05.ld and ties the loaded registers
+// to the wait so that no use of them is scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t *r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : H24_T8(0), H24_T8(8), H24_T8(16), H24_T8(24), H24_T8(32), H24_T8(40),
+                 H24_T8(48), H24_T8(56)
+               :
+               : "memory");
+}
+// Orders a second block of loaded registers after the preceding wait.
+__device__ __forceinline__ void tmem_tie(uint32_t *r) {
+  asm volatile(""
+               : H24_T8(0), H24_T8(8), H24_T8(16), H24_T8(24), H24_T8(32), H24_T8(40),
+                 H24_T8(48), H24_T8(56)
+               :
+               : "memory");
+}
+#undef H24_T8
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Maximum of 64 fp32 values held as raw bits (balanced tree of 3-input max).
+__device__ __forceinline__ float max64(const uint32_t *r) {
+  float m[22];
+#pragma unroll
+  for (int k = 0; k < 21; ++k)
+    m[k] = fmax3(__uint_as_float(r[3 * k]), __uint_as_float(r[3 * k + 1]),
+                 __uint_as_float(r[3 * k + 2]));
+  m[21] = __uint_as_float(r[63]);
+  float n[8];
+#pragma unroll
+  for (int k = 0; k < 7; ++k) n[k] = fmax3(m[3 * k], m[3 * k + 1], m[3 * k + 2]);
+  n[7] = m[21];
+  const float p0 = fmax3(n[0], n[1], n[2]);
+  const float p1 = fmax3(n[3], n[4], n[5]);
+  return fmax3(p0, p1, fmaxf(n[6], n[7]));
+}
+
+// ---------------------------------------------------------------------------
+// 1. prep
+// ---------------------------------------------------------------------------
+// Byte offset of (atom, 16-byte K chunk c) in the tiled bf16 operand.
+__device__ __forceinline__ int64_t tiled_offset(int64_t atom, int c) {
+  const int64_t blk = atom / kBlockAtoms;
+  const int l = static_cast<int>(atom - blk * kBlockAtoms);
+  const int h = l >> 7, r128 = l & 127;
+  return blk * kATileBytes + h * (128 * kRowBytes) + (r128 >> 3) * 512 + c * 128 + (r128 & 7) * 16;
+}
+
+__global__ void __launch_bounds__(256) prep_kernel(const float *__restrict__ x, int64_t n,
+                                                   int64_t n_pad, uint8_t *__restrict__ a_tiled,
+                                                   float *__restrict__ two_e) {
+  const int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (a >= n_pad) return;
+  float v[kDim];
+  if (a < n) {
+    const float4 *src = reinterpret_cast<const float4 *>(x + a * kDim);
+#pragma unroll
+    for (int q = 0; q < 6; ++q) {
+      const float4 f = __ldcs(src + q);
+      v[4 * q + 0] = f.x;
+      v[4 * q + 1] = f.y;
+      v[4 * q + 2] = f.z;
+      v[4 * q + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kDim; ++i) v[i] = 0.f;
+  }
+  float sum_d = 0.f, sum_d2 = 0.f, sum_x = 0.f;
+  bool finite = true;
+  uint32_t hi_bits[12];
+#pragma unroll
+  for (int i = 0; i < kDim; i += 2) {
+    const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[i], v[i + 1]);
+    const float h0 = __low2float(h2), h1 = __high2float(h2);
+    const float d0 = fabsf(v[i] - h0), d1 = fabsf(v[i + 1] - h1);
+    sum_d += d0 + d1;
+    sum_d2 = fmaf(d0, d0, fmaf(d1, d1, sum_d2));
+    sum_x += fabsf(v[i]) + fabsf(v[i + 1]);
+    finite = finite && isfinite(v[i]) && isfinite(v[i + 1]);
+    hi_bits[i / 2] = *reinterpret_cast<const uint32_t *>(&h2);
+  }
+  // |sum_i raw_ji d_i| <= min(4 sum|d|, sqrt(32) ||d||); tensor-core
+  // accumulation, the fp32 rounding of 3*LEECH_SCALE and the fp64 rescore add
+  // at most 2^-12 * sum|x| (raw units).  The factor 1.001 absorbs the fp32
+  // rounding of these sums.
+  const float e_hi = fminf(4.f * sum_d, 5.656854249f * sqrtf(sum_d2));
+  const float e = (e_hi + 2.44140625e-4f * sum_x) * 1.001f;
+  if (a < n) two_e[a] = finite ? 2.f * e : -1.f;
+  uint4 *dst = reinterpret_cast<uint4 *>(a_tiled);
+#pragma unroll
+  for (int c = 0; c < 3; ++c)
+    dst[tiled_offset(a, c) / 16] =
+        make_uint4(hi_bits[4 * c], hi_bits[4 * c + 1], hi_bits[4 * c + 2], hi_bits[4 * c + 3]);
+  dst[tiled_offset(a, 3) / 16] = make_uint4(0, 0, 0, 0);
+}
+
+// ---------------------------------------------------------------------------
+// 2. tcgen05 screening
+// ---------------------------------------------------------------------------
+struct ScreenArgs {
+  const uint8_t *a_tiled;
+  const float *two_e;
+  const uint8_t *cb_tiled;
+  uint16_t *cand;     // [n_pad][kCap]
+  uint8_t *cand_n;    // [n_pad]
+  float *best;        // [n_pad]
+  int64_t n;
+  int64_t nblocks;
+  int *err;
+};
+
+__device__ __forceinline__ void epilogue_insert(ScreenSmem &S, int local, float m, uint16_t chunk,
+                                                float thr, int &cnt, bool &ovf) {
+  if (!(m >= thr)) return;
+  if (cnt == kCap) {
+    int k = 0;
+    for (int i = 0; i < kCap; ++i) {
+      const float s = S.cand_score[i][local];
+      if (s >= thr) {
+        S.cand_score[k][local] = s;
+        S.cand_chunk[k][local] = S.cand_chunk[i][local];
+        ++k;
+      }
+    }
+    cnt = k;
+  }
+  if (cnt < kCap) {
+    S.cand_score[cnt][local] = m;
+    S.cand_chunk[cnt][local] = chunk;
+    ++cnt;
+  } else {
+    ovf = true;
+  }
+}
+
+__global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  ScreenSmem &S = *reinterpret_cast<ScreenSmem *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int *abort_flag = &S.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&S.bar_b_full[s], 1);
+      mbar_init(&S.bar_b_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&S.bar_a_full[s], 1);
+      mbar_init(&S.bar_a_empty[s], 1);
+      mbar_init(&S.bar_acc_full[s], 1);
+      mbar_init(&S.bar_acc_empty[s], kEpiWarps);
+    }
+    mbar_init(&S.bar_final, 1);
+    S.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&S.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = S.tmem_base;
+
+  if (warp == 0) {
+    // ---------------- producer: bulk copies of A tiles and codebook tiles --
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
+      const uint64_t stream_once = policy_evict_first();
+      int bs = 0, ab = 0;
+      uint32_t bph = 0, aph = 0;
+      int last_b[kStages];
+      int last_a[2] = {-1, -1};
+      for (int s = 0; s < kStages; ++s) last_b[s] = -1;
+      bool ok = true;
+      for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
+        if (!wait_bounded(&S.bar_a_empty[ab], aph ^ 1, abort_flag, args.err)) { ok = false; break; }
+        mbar_arrive_expect_tx(&S.bar_a_full[ab], kATileBytes);
+        bulk_g2s(S.a[ab], args.a_tiled + blk * kATileBytes, kATileBytes, &S.bar_a_full[ab],
+                 stream_once);
+        last_a[ab] = static_cast<int>(aph);
+        if (++ab == 2) { ab = 0; aph ^= 1; }
+        for (int t = 0; t < kNumTiles; ++t) {
+          if (!wait_bounded(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&S.bar_b_full[bs], kBTileBytes);
+          bulk_g2s(S.b[bs], args.cb_tiled + static_cast<int64_t>(t) * kBTileBytes, kBTileBytes,
+                   &S.bar_b_full[bs], keep);
+          last_b[bs] = static_cast<int>(bph);
+          if (++bs == kStages) { bs = 0; bph ^= 1; }
+        }
+      }
+      if (!ok) {
+        // Let every copy already issued land before the CTA leaves.
+        for (int s = 0; s < kStages; ++s)
+          if (last_b[s] >= 0) {
+            const unsigned long long t0 = global_ns();
+            while (!mbar_try_wait(&S.bar_b_full[s], static_cast<uint32_t>(last_b[s])) &&
+                   global_ns() - t0 < kWaitLimitNs) {
+            }
+          }
+        for (int s = 0; s < 2; ++s)
+          if (last_a[s] >= 0) {
+            const unsigned long long t0 = global_ns();
+            while (!mbar_try_wait(&S.bar_a_full[s], static_cast<uint32_t>(last_a[s])) &&
+                   global_ns() - t0 < kWaitLimitNs) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ------------------------------------------
+    if (lane == 0) {
+      int bs = 0, ab = 0, as = 0;
+      uint32_t bph = 0, aph = 0, cph = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
+        if (!wait_bounded(&S.bar_a_full[ab], aph, abort_flag, args.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(S.a[ab]);
+        for (int t = 0; t < kNumTiles; ++t) {
+          if (!wait_bounded(&S.bar_b_full[bs], bph, abort_flag, args.err)) { ok = false; break; }
+          if (!wait_bounded(&S.bar_acc_empty[as], cph ^ 1, abort_flag, args.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t b_addr = smem_u32(S.b[bs]);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t d = tmem_base + static_cast<uint32_t>(as * 2 * kTileN + h * kTileN);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk)
+              mma_bf16(d, smem_desc(a_addr + h * (128 * kRowBytes) + kk * 256),
+                       smem_desc(b_addr + kk * 256), kk);
+          }
+          issued = true;
+          mma_commit(&S.bar_b_empty[bs]);
+          mma_commit(&S.bar_acc_full[as]);
+          if (++bs == kStages) { bs = 0; bph ^= 1; }
+          if (++as == 2) { as = 0; cph ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&S.bar_a_empty[ab]);
+        if (++ab == 2) { ab = 0; aph ^= 1; }
+      }
+      if (issued) {
+        // All MMAs of this CTA complete before TMEM is released.
+        mma_commit(&S.bar_final);
+        const unsigned long long t0 = global_ns();
+        while (!mbar_try_wait(&S.bar_final, 0) && global_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: one thread per atom -------------------------
+    const int ew = warp - 2;
+    const int h = ew >> 2;               // which M=128 tile
+    const int q = warp & 3;              // TMEM lane quarter this warp may access
+    const int local = h * 128 + q * 32 + lane;
+    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(h * kTileN);
+    int as = 0;
+    uint32_t cph = 0;
+    bool ok = true;
+    for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
+      const int64_t atom = blk * kBlockAtoms + local;
+      const float te = atom < args.n ? args.two_e[atom] : -1.f;
+      const bool track = te >= 0.f;
+      float best = -INFINITY;
+      float thr = track ? -INFINITY : INFINITY;
+      int cnt = 0;
+      bool ovf = false;
+      for (int t = 0; t < kNumTiles; ++t) {
+        // Every lane waits; the warp proceeds only if all of them saw the
+        // phase complete, so the .sync.aligned TMEM loads stay convergent.
+        const bool got = wait_bounded(&S.bar_acc_full[as], cph, abort_flag, args.err);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t r0[64], r1[64];
+        const uint32_t taddr = t_lane + static_cast<uint32_t>(as * 2 * kTileN);
+        tmem_ld64(taddr, r0);
+        tmem_ld64(taddr + 64, r1);
+        tmem_wait_ld(r0);
+        tmem_tie(r1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.bar_acc_empty[as]);
+        if (++as == 2) { as = 0; cph ^= 1; }
+        if (t == kNumTiles - 1) {
+          // Codewords past 196559 are zero padding rows.
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (t * kTileN + 64 + c >= kKissing) r1[c] = __float_as_uint(-INFINITY);
+        }
+        const float m0 = max64(r0);
+        const float m1 = max64(r1);
+        const float mt = fmaxf(m0, m1);
+        if (mt >= thr) {
+          if (mt > best) {
+            best = mt;
+            thr = best - te;
+          }
+          epilogue_insert(S, local, m0, static_cast<uint16_t>(2 * t), thr, cnt, ovf);
+          epilogue_insert(S, local, m1, static_cast<uint16_t>(2 * t + 1), thr, cnt, ovf);
+          if (ovf) thr = INFINITY;
+        }
+        best = fmaxf(best, mt);
+      }
+      if (!ok) break;
+      if (atom < args.n) {
+        uint8_t n_out = kOverflow;
+        if (track && !ovf) {
+          int k = 0;
+          for (int i = 0; i < cnt; ++i)
+            if (S.cand_score[i][local] >= thr) args.cand[atom * kCap + k++] = S.cand_chunk[i][local];
+          n_out = static_cast<uint8_t>(k);
+        }
+        args.cand_n[atom] = n_out;
+        args.best[atom] = best;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 3. rescore (one warp per atom) and 4. exhaustive fallback
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ double score64(const float (&x)[kDim], const int8_t *__restrict__ row) {
+  const int2 w0 = __ldg(reinterpret_cast<const int2 *>(row));
+  const int2 w1 = __ldg(reinterpret_cast<const int2 *>(row + 8));
+  const int2 w2 = __ldg(reinterpret_cast<const int2 *>(row + 16));
+  const uint32_t words[6] = {static_cast<uint32_t>(w0.x), static_cast<uint32_t>(w0.y),
+                             static_cast<uint32_t>(w1.x), static_cast<uint32_t>(w1.y),
+                             static_cast<uint32_t>(w2.x), static_cast<uint32_t>(w2.y)};
+  double acc = 0.0;
+#pragma unroll
+  for (int i = 0; i < kDim; ++i) {
+    const int raw = static_cast<int8_t>((words[i >> 2] >> (8 * (i & 3))) & 0xFF);
+    const float kp = static_cast<float>(raw) * kLeechScaleF;
+    acc = __fma_rn(static_cast<double>(x[i]), static_cast<double>(kp), acc);
+  }
+  return acc;
+}
+
+__device__ __forceinline__ void better(double &bs, int &bj, double s, int j) {
+  if (s > bs || (s == bs && j < bj)) {
+    bs = s;
+    bj = j;
+  }
+}
+
+__device__ __forceinline__ void load_atom(const float *__restrict__ x, int64_t a, float (&v)[kDim]) {
+  const float4 *src = reinterpret_cast<const float4 *>(x + a * kDim);
+#pragma unroll
+  for (int q = 0; q < 6; ++q) {
+    const float4 f = __ldg(src + q);
+    v[4 * q] = f.x;
+    v[4 * q + 1] = f.y;
+    v[4 * q + 2] = f.z;
+    v[4 * q + 3] = f.w;
+  }
+}
+
+// Index for atoms that need no search: non-finite input (training rule: the
+// origin, as the Triton kernel's never-improving running max snaps; pack rule:
+// row 1, torch.max's first NaN), or the pack rule's ||x|| < 1e-8.
+// Returns -1 when a search is needed.
+__device__ __forceinline__ int trivial_index(const float (&v)[kDim], int rule) {
+  bool finite = true;
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < kDim; ++i) {
+    finite = finite && isfinite(v[i]);
+    ss = __fma_rn(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+  }
+  if (!finite) return rule == H24_RULE_TRAIN ? 0 : 1;
+  if (rule == H24_RULE_PACK && sqrt(ss) < 1e-8) return 0;
+  return -1;
+}
+
+__device__ __forceinline__ int32_t apply_rule(double best, int bj, int rule) {
+  if (rule == H24_RULE_TRAIN && 2.0 * best < kCSqNorm) return 0;
+  return bj + 1;
+}
+
+__global__ void __launch_bounds__(256) rescore_kernel(
+    const float *__restrict__ x, int64_t n, int rule, const uint16_t *__restrict__ cand,
+    const uint8_t *__restrict__ cand_n, const float *__restrict__ best_approx,
+    const float *__restrict__ two_e, const int8_t *__restrict__ cb_raw, int32_t *__restrict__ out,
+    int32_t *__restrict__ ovf_list, int32_t *__restrict__ ovf_count, int64_t *__restrict__ stats) {
+  __shared__ int block_ovf, block_chunks;
+  if (threadIdx.x == 0) {
+    block_ovf = 0;
+    block_chunks = 0;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t a = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (a < n) {
+    float v[kDim];
+    load_atom(x, a, v);
+    const int triv = trivial_index(v, rule);
+    const int cn = cand_n[a];
+    if (triv >= 0) {
+      if (lane == 0) out[a] = triv;
+    } else if (cn == kOverflow) {
+      // Certain origin under the training rule: even best + E stays below the
+      // snap threshold (1e-6 covers the fp32 codebook's rounding).
+      const double ub = static_cast<double>(kLeechScaleF) *
+                        (static_cast<double>(best_approx[a]) + 0.5 * two_e[a]) * (1.0 + 1e-6);
+      if (lane == 0) {
+        if (rule == H24_RULE_TRAIN && 2.0 * ub < kCSqNorm) {
+          out[a] = 0;
+        } else {
+          out[a] = 0;
+          ovf_list[atomicAdd(ovf_count, 1)] = static_cast<int32_t>(a);
+          atomicAdd(&block_ovf, 1);
+        }
+      }
+    } else {
+      double bs = -INFINITY;
+      int bj = 0x7FFFFFFF;
+      for (int k = 0; k < cn; ++k) {
+        const int c = cand[a * kCap + k];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int j = c * kChunk + half * 32 + lane;
+          if (j < kKissing) better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const double os = __shfl_xor_sync(0xffffffffu, bs, off);
+        const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+        better(bs, bj, os, oj);
+      }
+      if (lane == 0) {
+        out[a] = cn > 0 ? apply_rule(bs, bj, rule) : 0;
+        atomicAdd(&block_chunks, cn);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && (block_ovf || block_chunks)) {
+    atomicAdd(reinterpret_cast<unsigned long long *>(&stats[0]),
+              static_cast<unsigned long long>(block_ovf));
+    atomicAdd(reinterpret_cast<unsigned long long *>(&stats[1]),
+              static_cast<unsigned long long>(block_chunks));
+  }
+}
+
+__global__ void __launch_bounds__(256) exhaustive_kernel(const float *__restrict__ x, int rule,
+                                                         const int32_t *__restrict__ ovf_list,
+                                                         const int32_t *__restrict__ ovf_count,
+                                                         const int8_t *__restrict__ cb_raw,
+                                                         int32_t *__restrict__ out) {
+  __shared__ double ws[8];
+  __shared__ int wj[8];
+  const int count = *ovf_count;
+  for (int e = blockIdx.x; e < count; e += gridDim.x) {
+    const int64_t a = ovf_list[e];
+    float v[kDim];
+    load_atom(x, a, v);
+    double bs = -INFINITY;
+    int bj = 0x7FFFFFFF;
+    for (int j = threadIdx.x; j < kKissing; j += blockDim.x)
+      better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const double os = __shfl_xor_sync(0xffffffffu, bs, off);
+      const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+      better(bs, bj, os, oj);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      ws[threadIdx.x >> 5] = bs;
+      wj[threadIdx.x >> 5] = bj;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < 8; ++w) better(bs, bj, ws[w], wj[w]);
+      out[a] = apply_rule(bs, bj, rule);
+    }
+    __syncthreads();
+  }
+}
+
+std::mutex g_mu;
+int g_sms[64] = {};
+
+}  // namespace
+
+int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
+             cudaStream_t s) {
+  if (n <= 0) return H24_OK;
+  int sms = 0;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int dev = t->device;
+    if (g_sms[dev] == 0) {
+      int count = 0;
+      H24_CUDA_TRY(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
+      H24_CUDA_TRY(cudaFuncSetAttribute(screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(sizeof(ScreenSmem) + 1024)));
+      g_sms[dev] = count;
+    }
+    sms = g_sms[dev];
+  }
+  int64_t *stats = t->stats;
+  int *err = t->err;
+
+  const int64_t batch = n < kBatchAtoms ? n : kBatchAtoms;
+  const int64_t nb_max = (batch + kBlockAtoms - 1) / kBlockAtoms;
+  const int64_t pad_max = nb_max * kBlockAtoms;
+  auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
+  const size_t off_two_e = up(static_cast<size_t>(nb_max) * kATileBytes);
+  const size_t off_cand = off_two_e + up(pad_max * sizeof(float));
+  const size_t off_cand_n = off_cand + up(pad_max * kCap * sizeof(uint16_t));
+  const size_t off_best = off_cand_n + up(pad_max);
+  const size_t off_ovf = off_best + up(pad_max * sizeof(float));
+  const size_t off_cnt = off_ovf + up(batch * sizeof(int32_t));
+  const size_t bytes = off_cnt + 256;
+  uint8_t *scratch = nullptr;
+  H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&scratch), bytes, t->pool, s));
+  int rc = H24_OK;
+  for (int64_t base = 0; base < n && rc == H24_OK; base += batch) {
+    const int64_t nbatch = (n - base) < batch ? (n - base) : batch;
+    const int64_t nb = (nbatch + kBlockAtoms - 1) / kBlockAtoms;
+    const int64_t npad = nb * kBlockAtoms;
+    const float *xb = x + base * kDim;
+    int32_t *ob = out_idx + base;
+    uint8_t *a_tiled = scratch;
+    float *two_e = reinterpret_cast<float *>(scratch + off_two_e);
+    uint16_t *cand = reinterpret_cast<uint16_t *>(scratch + off_cand);
+    uint8_t *cand_n = scratch + off_cand_n;
+    float *best = reinterpret_cast<float *>(scratch + off_best);
+    int32_t *ovf_list = reinterpret_cast<int32_t *>(scratch + off_ovf);
+    int32_t *ovf_count = reinterpret_cast<int32_t *>(scratch + off_cnt);
+    cudaError_t e = cudaMemsetAsync(ovf_count, 0, sizeof(int32_t), s);
+    if (e != cudaSuccess) { rc = cuda_fail(e, "memset"); break; }
+    prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(xb, nbatch, npad, a_tiled,
+                                                                        two_e);
+    ScreenArgs sa{a_tiled, two_e, reinterpret_cast<const uint8_t *>(t->cb_tiled), cand, cand_n,
+                  best, nbatch, nb, err};
+    const int grid = static_cast<int>(nb < sms ? nb : sms);
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    if (timing_enabled()) {
+      cudaEventCreate(&ev0);
+      cudaEventCreate(&ev1);
+      cudaEventRecord(ev0, s);
+    }
+    screen_kernel<<<grid, kScreenThreads, sizeof(ScreenSmem) + 1024, s>>>(sa);
+    if (ev1) {
+      cudaEventRecord(ev1, s);
+      timing_record(ev0, ev1);
+    }
+    const int64_t rthreads = nbatch * 32;
+    rescore_kernel<<<static_cast<unsigned>((rthreads + 255) / 256), 256, 0, s>>>(
+        xb, nbatch, rule, cand, cand_n, best, two_e, t->cb_raw, ob, ovf_list, ovf_count, stats);
+    exhaustive_kernel<<<2 * sms, 256, 0, s>>>(xb, rule, ovf_list, ovf_count, t->cb_raw, ob);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) rc = cuda_fail(e, "quantize launch");
+  }
+  cudaError_t e = cudaFreeAsync(scratch, s);
+  if (rc == H24_OK && e != cudaSuccess) rc = cuda_fail(e, "cudaFreeAsync");
+  return rc;
+}
+
+}  // namespace h24

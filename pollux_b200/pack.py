@@ -1,0 +1,56 @@
+"""Drop-in mirror of the reference's ``pack._quantize_h24_layer``
+(pack.py:139-180), the checkpoint -> .plx quantiser, on libh24.
+
+``_quantize_h24_layer(weight, codebook) -> (packed_u8_cpu, sigma_f16_cpu)``:
+  * sigma_rows = fp16(clamp_min(sqrt(mean(w^2)+1e-8) * sqrt(12), 1e-8)) per row
+    (pack.py:164);
+  * atoms = w.reshape(-1, 24); index = argmax(atom . kp) + 1, 0 only when
+    ||atom||_2 < 1e-8 (pack.py:166-177) -- computed as the exact fp64 argmax
+    with the lowest index on ties;
+  * packed with the 18-bit format (pack.py:179, castor.py:226-246).
+Quantisation, scale and packing run in one pass on the GPU
+(h24_quantize_layer); only the results are copied back to the host, as the
+reference returns them.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+from .castor import (BYTES_PER_CHUNK, H24_DIM, _aligned, _call, _check_codebook, _stream,
+                     _work_device)
+
+
+def _quantize_h24_layer(weight: torch.Tensor, codebook: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Map an H24 weight matrix to packed 18-bit indices + per-row FP16 sigma."""
+    w = weight.detach()
+    if w.dim() != 2:
+        raise ValueError(f"row_rms_from_matrix expects a 2D weight matrix, got {w.dim()}D.")
+    if w.numel() % H24_DIM != 0:
+        raise RuntimeError(f"shape '[-1, {H24_DIM}]' is invalid for input of size {w.numel()}")
+    _check_codebook(codebook)
+    rows, in_f = w.shape
+    atoms = w.numel() // H24_DIM
+    dev = _work_device(w)
+    wd = _aligned(w.to(device=dev, dtype=torch.float32))
+    packed = torch.empty(((atoms + 3) // 4) * BYTES_PER_CHUNK, dtype=torch.uint8, device=dev)
+    sigma = torch.empty(rows, dtype=torch.float16, device=dev)
+    if rows:
+        _call(dev, "h24_quantize_layer", wd.data_ptr(), rows, in_f, sigma.data_ptr(),
+              packed.data_ptr(), _stream(dev))
+    return packed.cpu(), sigma.cpu()
+
+
+def quantize_layer_device(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Device-resident variant: (packed u8, sigma16) left on the weight's CUDA device."""
+    w = weight.detach()
+    rows, in_f = w.shape
+    atoms = w.numel() // H24_DIM
+    dev = _work_device(w)
+    wd = _aligned(w.to(device=dev, dtype=torch.float32))
+    packed = torch.empty(((atoms + 3) // 4) * BYTES_PER_CHUNK, dtype=torch.uint8, device=dev)
+    sigma = torch.empty(rows, dtype=torch.float16, device=dev)
+    if rows:
+        _call(dev, "h24_quantize_layer", wd.data_ptr(), rows, in_f, sigma.data_ptr(),
+              packed.data_ptr(), _stream(dev))
+    return packed, sigma

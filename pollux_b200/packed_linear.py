@@ -1,0 +1,129 @@
+"""Drop-in mirror of ``PackedH24Linear`` and its ``materialize`` (pollux.py:461-507),
+the inference-time LUT dequantisation, on libh24.
+
+``materialize`` rebuilds the dense fp16 weight from the packed 18-bit indices
+and the per-row fp16 scales,
+    weight = fp16( fp32( fp16(cb16[idx] * sigma16[row]) ) * fp32(s_lattice) ),
+bit-identical to the reference's two torch multiplications (pollux.py:497-499),
+then drops the packed buffers exactly as the reference does (pollux.py:500-504).
+``materialize_all`` dequantises every packed layer of a model with one launch
+per 64 layers (the loop of from_packed_checkpoint, pollux.py:748-750).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import _native as N
+from .castor import (BYTES_PER_CHUNK, H24_DIM, _aligned, _call, _stream, _work_device,
+                     assert_row_aligned_in_features, h24_linear_atom_count,
+                     h24_linear_scale_row_count)
+
+
+def _raise_bad(bad: torch.Tensor) -> None:
+    n = int(bad.item())
+    if n:
+        raise IndexError(f"index out of range in self ({n} packed indices exceed 196560)")
+
+
+def dequant(packed: torch.Tensor, sigma_rows: torch.Tensor, out_features: int,
+            in_features: int) -> torch.Tensor:
+    """fp16 [out_features, in_features] weight from packed indices and fp16 row scales."""
+    if sigma_rows.dtype != torch.float16:
+        raise TypeError(f"sigma_rows must be float16, got {sigma_rows.dtype}")
+    atoms = h24_linear_atom_count(out_features, in_features)
+    if in_features % H24_DIM != 0:
+        raise ValueError(f"in_features must be a multiple of {H24_DIM}, got {in_features}")
+    need = ((atoms + 3) // 4) * BYTES_PER_CHUNK
+    flat = packed.reshape(-1)
+    if flat.dtype != torch.uint8 or flat.numel() < need:
+        raise ValueError(f"packed_weights must be uint8 with at least {need} bytes")
+    if sigma_rows.numel() < out_features:
+        raise ValueError(f"sigma_rows must hold {out_features} scales")
+    dev = _work_device(flat)
+    p = flat.to(dev).contiguous()
+    s = sigma_rows.reshape(-1).to(dev).contiguous()
+    out = torch.empty(out_features, in_features, dtype=torch.float16, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    _call(dev, "h24_dequant", p.data_ptr(), s.data_ptr(), out_features, in_features,
+          out.data_ptr(), bad.data_ptr(), _stream(dev))
+    _raise_bad(bad)
+    return out
+
+
+def materialize(self) -> None:
+    """PackedH24Linear.materialize (pollux.py:485-504) on libh24."""
+    if self._materialized:
+        return
+    weight = dequant(self.packed_weights, self.sigma_rows, self.out_features, self.in_features)
+    self.weight = nn.Parameter(weight.to(self.packed_weights.device), requires_grad=False)
+    del self.packed_weights
+    del self.sigma_rows
+    self._materialized = True
+
+
+class PackedH24Linear(nn.Module):
+    """H24 linear layer with packed uint8 indices + fp16 per-row sigma
+    (same buffers, shapes and forward as pollux.py:461-507)."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False) -> None:
+        super().__init__()
+        assert_row_aligned_in_features(in_features)
+        self.in_features = int(in_features)
+        self.out_features = int(out_features)
+        self.num_atoms = h24_linear_atom_count(self.out_features, self.in_features)
+        self.num_sigma_rows = h24_linear_scale_row_count(self.out_features)
+        packed_len = ((self.num_atoms + 3) // 4) * BYTES_PER_CHUNK
+        self.register_buffer("packed_weights", torch.zeros(packed_len, dtype=torch.uint8))
+        self.register_buffer("sigma_rows", torch.ones(self.num_sigma_rows, dtype=torch.float16))
+        self._materialized = False
+        if bias:
+            self.bias = nn.Parameter(torch.zeros(self.out_features))
+        else:
+            self.register_parameter("bias", None)
+
+    materialize = materialize
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.linear(x, self.weight.to(dtype=x.dtype), self.bias)
+
+
+def materialize_all(model: nn.Module) -> int:
+    """Materialise every not-yet-materialised packed H24 layer of ``model`` with
+    batched launches; returns the number of layers.  Layers must already be on
+    one CUDA device (as after model.to(device))."""
+    mods = [m for m in model.modules()
+            if hasattr(m, "packed_weights") and hasattr(m, "sigma_rows")
+            and not getattr(m, "_materialized", False)]
+    if not mods:
+        return 0
+    dev = mods[0].packed_weights.device
+    if dev.type != "cuda":
+        for m in mods:
+            materialize(m)
+        return len(mods)
+    layers = (N.DequantLayer * len(mods))()
+    outs, keep = [], []
+    for i, m in enumerate(mods):
+        if m.sigma_rows.dtype != torch.float16:
+            raise TypeError(f"sigma_rows must be float16, got {m.sigma_rows.dtype}")
+        p = m.packed_weights.contiguous()
+        s = m.sigma_rows.contiguous()
+        o = torch.empty(m.out_features, m.in_features, dtype=torch.float16, device=dev)
+        keep += [p, s]
+        outs.append(o)
+        layers[i] = N.DequantLayer(p.data_ptr(), s.data_ptr(), o.data_ptr(),
+                                   m.out_features, m.in_features)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    _call(dev, "h24_dequant_batched", ctypes.cast(layers, ctypes.c_void_p), len(mods),
+          bad.data_ptr(), _stream(dev))
+    _raise_bad(bad)
+    for m, o in zip(mods, outs):
+        m.weight = nn.Parameter(o, requires_grad=False)
+        del m.packed_weights
+        del m.sigma_rows
+        m._materialized = True
+    return len(mods)

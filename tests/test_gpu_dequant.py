@@ -1,0 +1,73 @@
+"""LUT dequant on the GPU (PackedH24Linear.materialize, pollux.py:485-504):
+bit-exact against the reference's golden outputs and the oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def PL(lib):
+    from pollux_b200 import packed_linear
+    return packed_linear
+
+
+def test_golden_materialize(PL, golden):
+    m = golden("materialize.npz")
+    for t in "abcd":
+        rows, in_f = (int(v) for v in m[t + "_shape"])
+        w = PL.dequant(torch.from_numpy(m[t + "_packed"]).cuda(),
+                       torch.from_numpy(m[t + "_sigma16"]).cuda(), rows, in_f)
+        assert np.array_equal(w.cpu().numpy().view(np.uint16), m[t + "_weight16"].view(np.uint16)), t
+
+
+def test_module_materialize(PL, golden):
+    m = golden("materialize.npz")
+    layer = PL.PackedH24Linear(192, 48).cuda()
+    layer.packed_weights.copy_(torch.from_numpy(m["a_packed"]))
+    layer.sigma_rows.copy_(torch.from_numpy(m["a_sigma16"]))
+    layer.materialize()
+    assert not hasattr(layer, "packed_weights") and layer._materialized
+    assert layer.weight.dtype == torch.float16 and not layer.weight.requires_grad
+    assert np.array_equal(layer.weight.detach().cpu().numpy().view(np.uint16),
+                          m["a_weight16"].view(np.uint16))
+    y = layer(torch.randn(3, 192, device="cuda", dtype=torch.float16))
+    assert y.shape == (3, 48)
+
+
+def test_config5_layer_against_oracle(PL, oracle):
+    from pollux_b200 import synth, castor
+    idx, sigma = synth.config5_layer(seed=5, device="cuda")
+    packed = castor.pack_indices(idx)
+    w = PL.dequant(packed, sigma, 7680, 1920)
+    ref = oracle.dequant(packed.cpu().numpy(), sigma.cpu().numpy(), 7680, 1920)
+    assert np.array_equal(w.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+def test_batched_equals_single(PL):
+    from pollux_b200 import castor
+    torch.manual_seed(0)
+    shapes = [(3, 24), (17, 72), (128, 1920), (5, 4608)]
+    mods, singles = [], []
+    for (o, i) in shapes:
+        n = o * i // 24
+        idx = torch.randint(0, 196561, (n,), device="cuda")
+        sig = (torch.rand(o, device="cuda") * 0.1 + 0.001).half()
+        m = PL.PackedH24Linear(i, o).cuda()
+        m.packed_weights.copy_(castor.pack_indices(idx))
+        m.sigma_rows.copy_(sig)
+        singles.append(PL.dequant(m.packed_weights, m.sigma_rows, o, i))
+        mods.append(m)
+    model = torch.nn.ModuleList(mods)
+    assert PL.materialize_all(model) == len(shapes)
+    for m, w in zip(mods, singles):
+        assert torch.equal(m.weight.data, w)
+
+
+def test_out_of_range_index_raises(PL, oracle):
+    packed = torch.from_numpy(oracle.pack_indices(np.array([5, 196561, 7, 9]))).cuda()
+    with pytest.raises(IndexError):
+        PL.dequant(packed, torch.ones(1, dtype=torch.float16, device="cuda"), 1, 96)
