@@ -1,0 +1,356 @@
+#!/usr/bin/env python3
+"""Benchmark of the H24 hot path on B200 (one JSON line on rank 0).
+
+Workload (config 2 of the benchmark plan): a synthetic Pollux-1152 backbone,
+12 layers x {QKV [3456,1152], O [1152,1152], up [4608,1152], down [1152,4608]}
+fp32 N(0, 0.02^2) from seed 1: 48 matrices, 7,962,624 atoms of 24 values.
+One step = the whole path over the backbone:
+  1. pack-rule quantisation of every matrix: per-row fp16 sigma, nearest
+     codeword (tcgen05 screening + fp64 rescore), 18-bit pack
+     (pack._quantize_h24_layer, pack.py:139-180), one shared pipeline;
+  2. LUT dequant of every packed matrix back to fp16 (materialize,
+     pollux.py:485-504), one launch.
+value = atoms quantised per second (whole job; N ranks each run their own
+backbone -- weak scaling, no collective on the path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's algorithm on the host cores: the CPU
+port in oracle/ of pack._quantize_h24_layer's fp32 matmul + argmax search, row
+scale and 18-bit pack, on a bounded sample of the same atoms.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+FLOP_PER_ATOM = 2 * 24 * 196_560          # algorithmic FLOPs of one exhaustive search
+METRIC = "G atoms/s quantized (config-2 backbone: quantize + sigma + 18-bit pack, then LUT dequant)"
+WORKLOAD = ("config2: synthetic Pollux-1152 backbone, 12 layers x [3456x1152, 1152x1152, "
+            "4608x1152, 1152x4608] fp32 N(0,0.02^2) seed 1 (rank r: seed 1+r); step = pack-rule "
+            "quantize + sigma16 + 18-bit pack of all 48 matrices, then unpack + LUT dequant to fp16")
+
+
+def _env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons, power = [], None, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's pack-rule algorithm restated in oracle/
+# ---------------------------------------------------------------------------
+def cpu_baseline(seconds: float = 12.0, chunk: int = 2048) -> dict:
+    import torch
+    from oracle import oracle as O
+    from pollux_b200 import synth
+    nthreads = os.cpu_count() or 1
+    w = synth.backbone_weights(2, device="cpu", seed=1, shapes=[(3456, 1152)])[0]
+    atoms = w.numpy().reshape(-1, 24)
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and done + chunk <= atoms.shape[0]:
+        a = atoms[done:done + chunk]
+        idx = O.nearest_fp32_pack_rule(a)
+        O.sigma16_pack_rule(w.numpy()[done // 48: done // 48 + chunk // 48])
+        O.pack_indices(idx)
+        done += chunk
+    dt = time.perf_counter() - t0
+    return {"value": done / dt / 1e9, "unit": "G atoms/s", "cores": nthreads, "kind": "port",
+            "sample": f"{done} atoms of config-2 layer 0 (QKV 3456x1152), fp32 matmul + argmax "
+                      f"+ sigma16 + pack with numpy/BLAS on {nthreads} host threads ({dt:.1f} s); "
+                      f"torch threads {torch.get_num_threads()}"}
+
+
+def run_reference(args) -> None:
+    rank = _env_int("RANK", 0)
+    if rank != 0:
+        return
+    per_step, total_atoms = [], 0
+    from oracle import oracle as O
+    O.build()
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(seconds=max(2.0, 60.0 / max(1, args.steps + args.warmup)))
+        if i >= args.warmup:
+            per_step.append(r)
+    value = statistics.median(r["value"] for r in per_step)
+    out = {"metric": METRIC, "value": value, "unit": "G atoms/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup,
+           "ms_per_step": 7_962_624 / (value * 1e9) * 1e3, "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "impl": "reference",
+           "config": {"workload": WORKLOAD, "atoms_per_step": 7_962_624},
+           "cpu_baseline": {**per_step[-1], "value": value},
+           "e2e": {"value": value, "unit": "G atoms/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local = _env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from pollux_b200 import castor, pack, packed_linear, synth
+    from pollux_b200 import _native as N
+    import ctypes
+
+    shapes = synth.backbone_shapes(2)
+    weights = synth.backbone_weights(2, device=dev, seed=1 + rank)
+    atoms_per_step = sum(o * i // 24 for o, i in shapes)
+    packed_bytes = sum(((o * i // 24 + 3) // 4) * 9 for o, i in shapes)
+    fp16_bytes = sum(o * i * 2 for o, i in shapes)
+
+    outs16 = [torch.empty(o, i, dtype=torch.float16, device=dev) for o, i in shapes]
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        res = pack.quantize_layers(weights)
+        layers = (N.DequantLayer * len(res))()
+        for k, ((p, s), o) in enumerate(zip(res, outs16)):
+            layers[k] = N.DequantLayer(p.data_ptr(), s.data_ptr(), o.data_ptr(), o.shape[0], o.shape[1])
+        castor._call(dev, "h24_dequant_batched", ctypes.cast(layers, ctypes.c_void_p), len(res),
+                     bad.data_ptr(), stream.cuda_stream)
+        return res
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        res = step()
+    torch.cuda.synchronize()
+    castor.device_check(dev)
+
+    # Round-trip check outside the timed region: unpack(packed) re-packs to the
+    # same bytes and dequant found no out-of-range index.
+    p0, _s0 = res[0]
+    n0 = shapes[0][0] * shapes[0][1] // 24
+    idx0 = castor.unpack_indices(p0, n0)
+    assert torch.equal(castor.pack_indices(idx0), p0), "pack/unpack round trip failed"
+    assert int(bad.item()) == 0, "dequant saw out-of-range indices"
+    assert int(idx0.max()) <= 196560
+
+    N.load().h24_timing_enable(1)
+    N.load().h24_timing_read(None, None)
+    castor.quantize_stats(dev)
+    launches0 = castor.launch_count()
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(args.steps):
+        step()
+    t_stop.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    launches = castor.launch_count() - launches0
+    ms = ctypes.c_double(0)
+    nlaunch = ctypes.c_int64(0)
+    N.load().h24_timing_read(ctypes.byref(ms), ctypes.byref(nlaunch))
+    N.load().h24_timing_enable(0)
+    exhaustive, bitmap, chunks = castor.quantize_stats(dev)
+    elapsed_ms = t_start.elapsed_time(t_stop)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = world * atoms_per_step * args.steps / (elapsed_ms / 1e3) / 1e9
+
+    # Roofline of the dominant kernel (tensor-core screening): algorithmic
+    # FLOPs per launch over its mean CUDA-event duration.
+    screen_launches = max(1, int(nlaunch.value))
+    screen_ms = ms.value / screen_launches
+    flops_per_launch = FLOP_PER_ATOM * atoms_per_step * args.steps / screen_launches
+    achieved_tflops = flops_per_launch / (screen_ms / 1e3) / 1e12
+    peaks = {}
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("bf16_tflops_sustained")
+    peak_src = "measured sustained bf16 (MEASURED_PEAKS.json)"
+    if peak is None:
+        peak, peak_src = 1400.0, "fallback sustained bf16 1.4 PFLOP/s"
+
+    # End-to-end through the public drop-in API with host buffers.
+    e2e = None
+    if rank == 0 and not args.skip_e2e:
+        e2e = run_e2e(args, weights, shapes, dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline()
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "G atoms/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "atoms_per_step": atoms_per_step,
+                       "matrices": len(shapes), "packed_bytes_per_step": packed_bytes,
+                       "fp16_bytes_per_step": fp16_bytes,
+                       "l2": "inputs larger than L2: 764 MB of fp32 weights read per step",
+                       "compute": "bf16 x bf16 -> fp32 tcgen05 screening, fp64 rescore"},
+            "roofline": {"bound": "tensor", "kernel": "screen_kernel",
+                         "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved_tflops / peak, "peak_source": peak_src,
+                         "flop_per_atom": FLOP_PER_ATOM,
+                         "launch_ms_mean": screen_ms, "launches": screen_launches,
+                         "traffic": None},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "search_stats": {"exhaustive_atoms": exhaustive, "bitmap_atoms": bitmap,
+                             "chunks_rescored": chunks},
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(args, weights, shapes, dev) -> dict:
+    """Same step through the public API with host (pinned) buffers: the
+    drop-in pack._quantize_h24_layer per matrix (returns packed bytes and
+    sigma on the host, as the reference does), then materialize of every layer
+    from those host tensors; the H2D/D2H copies are inside the timed region."""
+    import torch
+    from pollux_b200 import pack, packed_linear, castor
+    cb = castor.get_h24_codebook(dev, torch.float32)
+    host_w = [w.cpu().pin_memory() for w in weights]
+    torch.cuda.synchronize()
+
+    def e2e_step():
+        res = [pack._quantize_h24_layer(w, cb) for w in host_w]
+        mods = []
+        for (o, i), (p, s) in zip(shapes, res):
+            m = packed_linear.PackedH24Linear(i, o)
+            m.packed_weights = p.to(dev, non_blocking=True)
+            m.sigma_rows = s.to(dev, non_blocking=True)
+            mods.append(m)
+        n = packed_linear.materialize_all(torch.nn.ModuleList(mods))
+        check = torch.stack([m.weight[0, 0] for m in mods]).float().sum().item()
+        return n, check, res
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        e2e_step()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        _, _, res = e2e_step()
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / steps
+    atoms = sum(o * i // 24 for o, i in shapes)
+    h2d = sum(w.numel() * 4 for w in host_w) + sum(p.numel() + s.numel() * 2 for p, s in res)
+    d2h = sum(p.numel() + s.numel() * 2 for p, s in res) + 4
+    return {"value": atoms / dt / 1e9, "unit": "G atoms/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": dt * 1e3, "steps": steps,
+            "api": "pollux_b200.pack._quantize_h24_layer + packed_linear.materialize_all"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

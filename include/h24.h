@@ -110,6 +110,16 @@ int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad
  * maximum; an fp64 rescore picks the winner. */
 int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *stream);
 
+/* ---- nearest codeword over several inputs in one pipeline ---------------
+ * Segment i holds counts[i] atoms of 24 fp32 values at xs[i] (device
+ * pointers, 16-byte aligned; `xs` and `counts` are host arrays read before the
+ * call returns).  out_idx receives the indices of all segments back to back.
+ * One screening launch covers up to 4M atoms of up to 64 segments, so many
+ * small matrices fill the GPU like one large one (the per-parameter loop of
+ * pollux_step, pollux.py:828-884). */
+int h24_quantize_segments(const float *const *xs, const int64_t *counts, int nseg, int rule,
+                          int32_t *out_idx, void *stream);
+
 /* ---- fused pack-rule layer quantiser (pack._quantize_h24_layer, pack.py:139-180)
  * w: rows x in_features fp32 row-major (16-byte aligned), rows*in_features a
  * multiple of 24; atoms are consecutive runs of 24 values of the flattened
@@ -120,6 +130,20 @@ int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *st
  * differ from torch's fp32 reduction by one fp16 ulp on a boundary row. */
 int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features,
                        uint16_t *sigma16_out, uint8_t *packed_out, void *stream);
+
+/* One layer of h24_quantize_layers. */
+typedef struct h24_layer {
+  const float *w;
+  int64_t rows;
+  int64_t in_features;
+  uint16_t *sigma16_out;
+  uint8_t *packed_out;
+} h24_layer;
+
+/* h24_quantize_layer for `count` layers with one shared search pipeline (the
+ * H24 branch of pack_checkpoint's loop, pack.py:268-283).  `layers` is a host
+ * array read before the call returns. */
+int h24_quantize_layers(const h24_layer *layers, int count, void *stream);
 
 /* ---- codeword gather (index_select of castor.py:533, 559) ---------------
  * out[a][0..23] = codebook[idx[a]] converted to `dtype` (H24_DTYPE_*). */
@@ -134,10 +158,14 @@ int h24_timing_enable(int enable);
 int h24_timing_read(double *ms, int64_t *launches);
 
 /* Counters accumulated by the quantize calls on the current device since the
- * previous read (reading resets them; synchronises `stream`): atoms whose
- * candidate list overflowed into the exhaustive fp64 scan, and candidate
- * chunks of 64 codewords rescored in fp64. */
-int h24_quantize_stats(int64_t *overflow_atoms, int64_t *rescored_chunks, void *stream);
+ * previous read (reading resets them; synchronises `stream`): atoms resolved
+ * by the exhaustive fp64 scan, atoms whose candidate chunks overflowed the
+ * per-atom list into a bitmap, and 64-codeword chunks rescored in fp64. */
+int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *bitmap_atoms, int64_t *rescored_chunks,
+                       void *stream);
+
+/* Number of CUDA kernels this library has launched in this process. */
+int64_t h24_launch_count(void);
 
 /* Synchronise `stream` and report a device-side failure of earlier quantize
  * calls on the current device: H24_ERR_TIMEOUT if a bounded wait inside the

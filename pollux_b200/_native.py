@@ -42,10 +42,13 @@ SIGNATURES = {
     "h24_dequant_batched": (_I, [_P, _I, _P, _P]),
     "h24_quantize": (_I, [_P, _I64, _I, _P, _P]),
     "h24_quantize_layer": (_I, [_P, _I64, _I64, _P, _P, _P]),
+    "h24_quantize_segments": (_I, [_P, _P, _I, _I, _P, _P]),
+    "h24_quantize_layers": (_I, [_P, _I, _P]),
+    "h24_launch_count": (ctypes.c_int64, []),
     "h24_gather_codewords": (_I, [_P, _I64, _I, _P, _P]),
     "h24_timing_enable": (_I, [_I]),
     "h24_timing_read": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
-    "h24_quantize_stats": (_I, [ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), _P]),
+    "h24_quantize_stats": (_I, [ctypes.POINTER(ctypes.c_int64)] * 3 + [_P]),
     "h24_check": (_I, [_P]),
 }
 
@@ -54,6 +57,12 @@ class DequantLayer(ctypes.Structure):
     """Mirror of h24_dequant_layer."""
     _fields_ = [("packed", _P), ("sigma16", _P), ("out16", _P),
                 ("rows", ctypes.c_int64), ("in_features", ctypes.c_int64)]
+
+
+class Layer(ctypes.Structure):
+    """Mirror of h24_layer."""
+    _fields_ = [("w", _P), ("rows", ctypes.c_int64), ("in_features", ctypes.c_int64),
+                ("sigma16_out", _P), ("packed_out", _P)]
 
 
 class H24Error(RuntimeError):

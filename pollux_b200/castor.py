@@ -244,6 +244,22 @@ def quantize_indices(x: torch.Tensor, rule: int = N.RULE_TRAIN) -> torch.Tensor:
     return out
 
 
+def quantize_indices_many(xs: list[torch.Tensor], rule: int = N.RULE_TRAIN) -> list[torch.Tensor]:
+    """quantize_indices for several tensors with one shared search pipeline
+    (all on one CUDA device); returns one int32 index tensor per input."""
+    if not xs:
+        return []
+    dev = _work_device(xs[0])
+    flats = [_aligned(x.reshape(-1, H24_DIM).to(device=dev, dtype=torch.float32)) for x in xs]
+    counts = [f.shape[0] for f in flats]
+    out = torch.empty(sum(counts), dtype=torch.int32, device=dev)
+    ptrs = (ctypes.c_void_p * len(flats))(*[f.data_ptr() for f in flats])
+    cnts = (ctypes.c_int64 * len(flats))(*counts)
+    _call(dev, "h24_quantize_segments", ctypes.cast(ptrs, ctypes.c_void_p),
+          ctypes.cast(cnts, ctypes.c_void_p), len(flats), int(rule), out.data_ptr(), _stream(dev))
+    return list(torch.split(out, counts))
+
+
 _GATHER_DTYPES = {torch.float32: N.DTYPE_F32, torch.float16: N.DTYPE_F16, torch.bfloat16: N.DTYPE_BF16}
 
 
@@ -311,9 +327,15 @@ def device_check(device=None) -> None:
     _call(dev, "h24_check", _stream(dev))
 
 
-def quantize_stats(device=None) -> tuple[int, int]:
-    """(atoms sent to the exhaustive scan, 64-codeword chunks rescored) since the last read."""
+def quantize_stats(device=None) -> tuple[int, int, int]:
+    """(atoms resolved by the exhaustive scan, atoms rescored from a bitmap,
+    64-codeword chunks rescored) since the last read."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    a, b = ctypes.c_int64(0), ctypes.c_int64(0)
-    _call(dev, "h24_quantize_stats", ctypes.byref(a), ctypes.byref(b), _stream(dev))
-    return int(a.value), int(b.value)
+    a, b, c = ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int64(0)
+    _call(dev, "h24_quantize_stats", ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), _stream(dev))
+    return int(a.value), int(b.value), int(c.value)
+
+
+def launch_count() -> int:
+    """Kernels libh24 has launched in this process."""
+    return int(N.load().h24_launch_count())

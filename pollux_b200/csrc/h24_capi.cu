@@ -5,6 +5,7 @@
 
 #include <cmath>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <utility>
@@ -109,10 +110,10 @@ int build_device_tables(int dev, Tables *T) {
   H24_CUDA_TRY(
       cudaMemcpy(p, H.nib.data(), H.nib.size() * sizeof(uint32_t), cudaMemcpyHostToDevice));
   T->cb_nib = static_cast<const uint32_t *>(p);
-  H24_CUDA_TRY(cudaMalloc(&p, 2 * sizeof(int64_t) + 16));
-  H24_CUDA_TRY(cudaMemset(p, 0, 2 * sizeof(int64_t) + 16));
+  H24_CUDA_TRY(cudaMalloc(&p, 3 * sizeof(int64_t) + 16));
+  H24_CUDA_TRY(cudaMemset(p, 0, 3 * sizeof(int64_t) + 16));
   T->stats = static_cast<int64_t *>(p);
-  T->err = reinterpret_cast<int *>(static_cast<char *>(p) + 2 * sizeof(int64_t));
+  T->err = reinterpret_cast<int *>(static_cast<char *>(p) + 3 * sizeof(int64_t));
   cudaMemPoolProps props = {};
   props.allocType = cudaMemAllocationTypePinned;
   props.handleTypes = cudaMemHandleTypeNone;
@@ -155,6 +156,12 @@ std::mutex g_timing_mu;
 bool g_timing = false;
 std::vector<std::pair<cudaEvent_t, cudaEvent_t>> g_events;
 }  // namespace
+
+namespace {
+std::atomic<int64_t> g_launches{0};
+}
+
+void count_launches(int64_t k) { g_launches.fetch_add(k, std::memory_order_relaxed); }
 
 bool timing_enabled() {
   std::lock_guard<std::mutex> lk(g_timing_mu);
@@ -203,6 +210,7 @@ int launch_sigma16(const float *w, int64_t rows, int64_t in_f, uint16_t *sigma16
   sigma16_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(w, rows, in_f,
                                                                              sigma16);
   H24_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
   return H24_OK;
 }
 
@@ -247,6 +255,7 @@ int h24_codebook_f32(float *out, void *stream) {
   if (!out) return fail(H24_ERR_INVALID, "codebook_f32: null pointer");
   // Row 0 is the origin; rows 1.. are the kissing points.
   H24_CUDA_TRY(cudaMemsetAsync(out, 0, kDim * sizeof(float), as_stream(stream)));
+  count_launches(0);
   return launch_codebook_f32(T, out + kDim, as_stream(stream));
 }
 
@@ -306,26 +315,68 @@ int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *st
   return quantize(T, x, n, rule, out_idx, as_stream(stream));
 }
 
-int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16_t *sigma16_out,
-                       uint8_t *packed_out, void *stream) {
+int h24_quantize_segments(const float *const *xs, const int64_t *counts, int nseg, int rule,
+                          int32_t *out_idx, void *stream) {
   H24_TABLES_OR_FAIL(T);
-  if (rows < 0 || in_features <= 0 || (rows * in_features) % kDim != 0)
+  if (nseg < 0 || (nseg > 0 && (!xs || !counts)))
+    return fail(H24_ERR_INVALID, "quantize_segments: bad segment list");
+  if (rule != H24_RULE_TRAIN && rule != H24_RULE_PACK)
+    return fail(H24_ERR_INVALID, "quantize_segments: unknown rule");
+  int64_t total = 0;
+  for (int i = 0; i < nseg; ++i) total += counts[i] > 0 ? counts[i] : 0;
+  if (total > 0 && !out_idx) return fail(H24_ERR_INVALID, "quantize_segments: null output");
+  return quantize_segments(T, xs, counts, nseg, rule, out_idx, as_stream(stream));
+}
+
+static int validate_layer(const h24_layer &L) {
+  if (L.rows < 0 || L.in_features <= 0 || (L.rows * L.in_features) % kDim != 0)
     return fail(H24_ERR_INVALID, "quantize_layer: rows*in_features must be a multiple of 24");
-  if (rows == 0) return H24_OK;
-  if (!w || !sigma16_out || !packed_out) return fail(H24_ERR_INVALID, "quantize_layer: null pointer");
-  if (!aligned16(w)) return fail(H24_ERR_INVALID, "quantize_layer: w must be 16-byte aligned");
+  if (L.rows > 0 && (!L.w || !L.sigma16_out || !L.packed_out))
+    return fail(H24_ERR_INVALID, "quantize_layer: null pointer");
+  if (L.rows > 0 && !aligned16(L.w))
+    return fail(H24_ERR_INVALID, "quantize_layer: w must be 16-byte aligned");
+  return H24_OK;
+}
+
+int h24_quantize_layers(const h24_layer *layers, int count, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (count < 0 || (count > 0 && !layers)) return fail(H24_ERR_INVALID, "quantize_layers: bad list");
   cudaStream_t s = as_stream(stream);
-  int rc = launch_sigma16(w, rows, in_features, sigma16_out, s);
-  if (rc != H24_OK) return rc;
-  const int64_t atoms = rows * in_features / kDim;
+  std::vector<const float *> xs;
+  std::vector<int64_t> counts;
+  int64_t total = 0;
+  for (int i = 0; i < count; ++i) {
+    int rc = validate_layer(layers[i]);
+    if (rc != H24_OK) return rc;
+    const int64_t atoms = layers[i].rows * layers[i].in_features / kDim;
+    xs.push_back(layers[i].w);
+    counts.push_back(atoms);
+    total += atoms;
+  }
+  if (total == 0) return H24_OK;
+  for (int i = 0; i < count; ++i) {
+    int rc = launch_sigma16(layers[i].w, layers[i].rows, layers[i].in_features,
+                            layers[i].sigma16_out, s);
+    if (rc != H24_OK) return rc;
+  }
   int32_t *idx = nullptr;
   H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&idx),
-                                       static_cast<size_t>(atoms) * sizeof(int32_t), T->pool, s));
-  rc = quantize(T, w, atoms, H24_RULE_PACK, idx, s);
-  if (rc == H24_OK) rc = launch_pack_i32(idx, atoms, packed_out, s);
+                                       static_cast<size_t>(total) * sizeof(int32_t), T->pool, s));
+  int rc = quantize_segments(T, xs.data(), counts.data(), count, H24_RULE_PACK, idx, s);
+  int64_t off = 0;
+  for (int i = 0; i < count && rc == H24_OK; ++i) {
+    rc = launch_pack_i32(idx + off, counts[i], layers[i].packed_out, s);
+    off += counts[i];
+  }
   cudaError_t e = cudaFreeAsync(idx, s);
   if (rc == H24_OK && e != cudaSuccess) rc = cuda_fail(e, "cudaFreeAsync");
   return rc;
+}
+
+int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16_t *sigma16_out,
+                       uint8_t *packed_out, void *stream) {
+  h24_layer L{w, rows, in_features, sigma16_out, packed_out};
+  return h24_quantize_layers(&L, 1, stream);
 }
 
 int h24_gather_codewords(const int32_t *idx, int64_t n, int dtype, void *out, void *stream) {
@@ -363,17 +414,21 @@ int h24_timing_read(double *ms, int64_t *launches) {
   return rc;
 }
 
-int h24_quantize_stats(int64_t *overflow_atoms, int64_t *rescored_chunks, void *stream) {
+int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *bitmap_atoms, int64_t *rescored_chunks,
+                       void *stream) {
   H24_TABLES_OR_FAIL(T);
-  int64_t h[2] = {0, 0};
+  int64_t h[3] = {0, 0, 0};
   cudaStream_t s = as_stream(stream);
   H24_CUDA_TRY(cudaMemcpyAsync(h, T->stats, sizeof(h), cudaMemcpyDeviceToHost, s));
   H24_CUDA_TRY(cudaStreamSynchronize(s));
   H24_CUDA_TRY(cudaMemsetAsync(T->stats, 0, sizeof(h), s));
-  if (overflow_atoms) *overflow_atoms = h[0];
+  if (exhaustive_atoms) *exhaustive_atoms = h[0];
+  if (bitmap_atoms) *bitmap_atoms = h[2];
   if (rescored_chunks) *rescored_chunks = h[1];
   return H24_OK;
 }
+
+int64_t h24_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int h24_check(void *stream) {
   H24_TABLES_OR_FAIL(T);

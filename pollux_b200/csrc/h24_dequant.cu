@@ -181,6 +181,7 @@ int launch_dequant(const Tables *t, const h24_dequant_layer * /*layers_dev*/,
     const int grid = static_cast<int>(tiles < cap ? tiles : cap);
     dequant_kernel<<<grid, kThreads, 0, s>>>(b, t->cb_nib, bad);
     H24_CUDA_TRY(cudaGetLastError());
+    count_launches(1);
   }
   return H24_OK;
 }
@@ -188,6 +189,7 @@ int launch_dequant(const Tables *t, const h24_dequant_layer * /*layers_dev*/,
 int launch_codebook_f32(const Tables *t, float *out_kissing, cudaStream_t s) {
   codebook_f32_kernel<<<sm_count() * 4, 256, 0, s>>>(t->cb_raw, out_kissing);
   H24_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
   return H24_OK;
 }
 
@@ -214,6 +216,7 @@ int launch_gather(const Tables *t, const int32_t *idx, int64_t n, int dtype, voi
       return fail(H24_ERR_INVALID, "gather: unknown dtype");
   }
   H24_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
   return H24_OK;
 }
 

@@ -47,7 +47,8 @@ struct Tables {
   const uint32_t *cb_nib = nullptr;
   float fingerprint[16];
   // Device counters: [0] atoms sent to the exhaustive scan, [1] candidate
-  // chunks rescored; and the error word set by a timed-out wait.
+  // chunks rescored, [2] atoms rescored from a bitmap; and the error word set
+  // by a timed-out wait.
   int64_t *stats = nullptr;
   int *err = nullptr;
   // Stream-ordered pool for per-call scratch (kept warm between calls).
@@ -88,8 +89,13 @@ int launch_gather(const Tables *t, const int32_t *idx, int64_t n, int dtype, voi
                   cudaStream_t s);
 int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
              cudaStream_t s);
+int quantize_segments(const Tables *t, const float *const *xs, const int64_t *counts, int nseg,
+                      int rule, int32_t *out_idx, cudaStream_t s);
 int launch_sigma16(const float *w, int64_t rows, int64_t in_f, uint16_t *sigma16,
                    cudaStream_t s);
+
+// Number of kernels this library has launched (all devices, all threads).
+void count_launches(int64_t k);
 
 // Instrumentation of the screening kernel.
 bool timing_enabled();

@@ -195,6 +195,7 @@ int launch_pack_i32(const int32_t *idx, int64_t n, uint8_t *out, cudaStream_t s)
   pack_kernel<int32_t><<<grid_for(tiles), kThreads, 0, s>>>(idx, n, out, aligned16(idx),
                                                             aligned16(out));
   H24_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
   return H24_OK;
 }
 
@@ -204,6 +205,7 @@ int launch_pack_i64(const int64_t *idx, int64_t n, uint8_t *out, cudaStream_t s)
   pack_kernel<int64_t><<<grid_for(tiles), kThreads, 0, s>>>(idx, n, out, aligned16(idx),
                                                             aligned16(out));
   H24_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
   return H24_OK;
 }
 
@@ -214,6 +216,7 @@ int launch_unpack_i32(const uint8_t *p, int64_t groups, int64_t n, int32_t *out,
   unpack_kernel<int32_t><<<grid_for(tiles), kThreads, 0, s>>>(p, groups, n, out, aligned16(p),
                                                               aligned16(out));
   H24_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
   return H24_OK;
 }
 
@@ -224,6 +227,7 @@ int launch_unpack_i64(const uint8_t *p, int64_t groups, int64_t n, int64_t *out,
   unpack_kernel<int64_t><<<grid_for(tiles), kThreads, 0, s>>>(p, groups, n, out, aligned16(p),
                                                               aligned16(out));
   H24_CUDA_TRY(cudaGetLastError());
+  count_launches(1);
   return H24_OK;
 }
 

@@ -40,11 +40,14 @@ constexpr int kBlockAtoms = 256;                    // atoms per CTA work item
 constexpr int kStages = 10;                         // codebook ring depth
 constexpr int kBTileBytes = kTileN * kRowBytes;     // 8192
 constexpr int kATileBytes = kBlockAtoms * kRowBytes;  // 16384
-constexpr int kCap = 8;                             // candidate chunks per atom
+constexpr int kCap = 16;                            // candidate chunks per atom (list mode)
+constexpr int kBitmapWords = kNumChunks / 32;       // 96 words: one bit per chunk
+constexpr int kMaxSegs = 64;                        // input segments per pipeline batch
 constexpr int kEpiWarps = 8;
 constexpr int kScreenThreads = 32 * (2 + kEpiWarps);  // 320
 constexpr uint32_t kTmemCols = 512;
-constexpr uint8_t kOverflow = 0xFF;
+constexpr uint8_t kOverflow = 0xFF;   // exhaustive fp64 scan
+constexpr uint8_t kBitmapMode = 0xFE; // candidate chunks in a global bitmap slot
 constexpr int64_t kBatchAtoms = int64_t(1) << 22;    // atoms per pipeline batch
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s
 
@@ -254,14 +257,31 @@ __device__ __forceinline__ int64_t tiled_offset(int64_t atom, int c) {
   return blk * kATileBytes + h * (128 * kRowBytes) + (r128 >> 3) * 512 + c * 128 + (r128 & 7) * 16;
 }
 
-__global__ void __launch_bounds__(256) prep_kernel(const float *__restrict__ x, int64_t n,
+// Input atoms of one pipeline batch: segment i holds atoms [start[i],
+// start[i+1]) of the batch, stored contiguously at x[i] (24 fp32 per atom).
+struct Segs {
+  const float *x[kMaxSegs];
+  int64_t start[kMaxSegs + 1];
+  int count;
+};
+
+__device__ __forceinline__ const float *atom_ptr(const Segs &sg, int64_t a) {
+  int lo = 0, hi = sg.count - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (sg.start[mid] <= a) lo = mid; else hi = mid - 1;
+  }
+  return sg.x[lo] + (a - sg.start[lo]) * kDim;
+}
+
+__global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
                                                    int64_t n_pad, uint8_t *__restrict__ a_tiled,
                                                    float *__restrict__ two_e) {
   const int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (a >= n_pad) return;
   float v[kDim];
   if (a < n) {
-    const float4 *src = reinterpret_cast<const float4 *>(x + a * kDim);
+    const float4 *src = reinterpret_cast<const float4 *>(atom_ptr(sg, a));
 #pragma unroll
     for (int q = 0; q < 6; ++q) {
       const float4 f = __ldcs(src + q);
@@ -313,33 +333,73 @@ struct ScreenArgs {
   uint16_t *cand;     // [n_pad][kCap]
   uint8_t *cand_n;    // [n_pad]
   float *best;        // [n_pad]
+  uint32_t *bitmaps;  // [pool_slots][kBitmapWords]
+  int32_t *slot_count;
+  int32_t pool_slots;
   int64_t n;
   int64_t nblocks;
   int *err;
 };
 
-__device__ __forceinline__ void epilogue_insert(ScreenSmem &S, int local, float m, uint16_t chunk,
-                                                float thr, int &cnt, bool &ovf) {
+// Per-atom candidate state of one epilogue thread.
+struct Cands {
+  int cnt = 0;          // list entries in shared memory
+  bool ovf = false;     // give up: exhaustive fp64 scan
+  int slot = -1;        // bitmap slot once the list has overflowed
+  int bm_idx = -1;      // bitmap word being accumulated in bm_word
+  uint32_t bm_word = 0;
+};
+
+// Bitmap mode: chunks arrive in increasing order, so each 32-chunk word is
+// accumulated in a register and stored once.
+__device__ __forceinline__ void bitmap_set(const ScreenArgs &args, Cands &c, int chunk) {
+  const int w = chunk >> 5;
+  if (w != c.bm_idx) {
+    if (c.bm_idx >= 0) args.bitmaps[static_cast<int64_t>(c.slot) * kBitmapWords + c.bm_idx] = c.bm_word;
+    c.bm_idx = w;
+    c.bm_word = 0;
+  }
+  c.bm_word |= 1u << (chunk & 31);
+}
+
+__device__ __forceinline__ void epilogue_insert(ScreenSmem &S, const ScreenArgs &args, int local,
+                                                float m, int chunk, float thr, Cands &c) {
   if (!(m >= thr)) return;
-  if (cnt == kCap) {
+  if (c.slot >= 0) {
+    bitmap_set(args, c, chunk);
+    return;
+  }
+  if (c.cnt == kCap) {
     int k = 0;
     for (int i = 0; i < kCap; ++i) {
-      const float s = S.cand_score[i][local];
-      if (s >= thr) {
-        S.cand_score[k][local] = s;
+      const float sc = S.cand_score[i][local];
+      if (sc >= thr) {
+        S.cand_score[k][local] = sc;
         S.cand_chunk[k][local] = S.cand_chunk[i][local];
         ++k;
       }
     }
-    cnt = k;
+    c.cnt = k;
   }
-  if (cnt < kCap) {
-    S.cand_score[cnt][local] = m;
-    S.cand_chunk[cnt][local] = chunk;
-    ++cnt;
-  } else {
-    ovf = true;
+  if (c.cnt < kCap) {
+    S.cand_score[c.cnt][local] = m;
+    S.cand_chunk[c.cnt][local] = static_cast<uint16_t>(chunk);
+    ++c.cnt;
+    return;
   }
+  // The list holds kCap chunks within 2E of the running best: exact ties over
+  // many chunks.  Move to a bitmap slot (zeroed here by its owner).
+  const int slot = atomicAdd(args.slot_count, 1);
+  if (slot >= args.pool_slots) {
+    c.ovf = true;
+    return;
+  }
+  c.slot = slot;
+  uint32_t *bm = args.bitmaps + static_cast<int64_t>(slot) * kBitmapWords;
+  for (int w = 0; w < kBitmapWords; ++w) bm[w] = 0u;
+  for (int i = 0; i < c.cnt; ++i)
+    if (S.cand_score[i][local] >= thr) bitmap_set(args, c, S.cand_chunk[i][local]);
+  bitmap_set(args, c, chunk);
 }
 
 __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenArgs args) {
@@ -482,8 +542,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       const bool track = te >= 0.f;
       float best = -INFINITY;
       float thr = track ? -INFINITY : INFINITY;
-      int cnt = 0;
-      bool ovf = false;
+      Cands cs;
       for (int t = 0; t < kNumTiles; ++t) {
         // Every lane waits; the warp proceeds only if all of them saw the
         // phase complete, so the .sync.aligned TMEM loads stay convergent.
@@ -514,20 +573,27 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
             best = mt;
             thr = best - te;
           }
-          epilogue_insert(S, local, m0, static_cast<uint16_t>(2 * t), thr, cnt, ovf);
-          epilogue_insert(S, local, m1, static_cast<uint16_t>(2 * t + 1), thr, cnt, ovf);
-          if (ovf) thr = INFINITY;
+          epilogue_insert(S, args, local, m0, 2 * t, thr, cs);
+          epilogue_insert(S, args, local, m1, 2 * t + 1, thr, cs);
+          if (cs.ovf) thr = INFINITY;
         }
         best = fmaxf(best, mt);
       }
       if (!ok) break;
       if (atom < args.n) {
         uint8_t n_out = kOverflow;
-        if (track && !ovf) {
-          int k = 0;
-          for (int i = 0; i < cnt; ++i)
-            if (S.cand_score[i][local] >= thr) args.cand[atom * kCap + k++] = S.cand_chunk[i][local];
-          n_out = static_cast<uint8_t>(k);
+        if (track && !cs.ovf) {
+          if (cs.slot >= 0) {
+            args.bitmaps[static_cast<int64_t>(cs.slot) * kBitmapWords + cs.bm_idx] = cs.bm_word;
+            args.cand[atom * kCap] = static_cast<uint16_t>(cs.slot & 0xFFFF);
+            args.cand[atom * kCap + 1] = static_cast<uint16_t>(cs.slot >> 16);
+            n_out = kBitmapMode;
+          } else {
+            int k = 0;
+            for (int i = 0; i < cs.cnt; ++i)
+              if (S.cand_score[i][local] >= thr) args.cand[atom * kCap + k++] = S.cand_chunk[i][local];
+            n_out = static_cast<uint8_t>(k);
+          }
         }
         args.cand_n[atom] = n_out;
         args.best[atom] = best;
@@ -572,8 +638,8 @@ __device__ __forceinline__ void better(double &bs, int &bj, double s, int j) {
   }
 }
 
-__device__ __forceinline__ void load_atom(const float *__restrict__ x, int64_t a, float (&v)[kDim]) {
-  const float4 *src = reinterpret_cast<const float4 *>(x + a * kDim);
+__device__ __forceinline__ void load_atom(const float *__restrict__ p, float (&v)[kDim]) {
+  const float4 *src = reinterpret_cast<const float4 *>(p);
 #pragma unroll
   for (int q = 0; q < 6; ++q) {
     const float4 f = __ldg(src + q);
@@ -606,50 +672,80 @@ __device__ __forceinline__ int32_t apply_rule(double best, int bj, int rule) {
   return bj + 1;
 }
 
-__global__ void __launch_bounds__(256) rescore_kernel(
-    const float *__restrict__ x, int64_t n, int rule, const uint16_t *__restrict__ cand,
-    const uint8_t *__restrict__ cand_n, const float *__restrict__ best_approx,
-    const float *__restrict__ two_e, const int8_t *__restrict__ cb_raw, int32_t *__restrict__ out,
-    int32_t *__restrict__ ovf_list, int32_t *__restrict__ ovf_count, int64_t *__restrict__ stats) {
-  __shared__ int block_ovf, block_chunks;
+// fp64 rescore of one 64-codeword chunk by a warp (two codewords per lane).
+__device__ __forceinline__ void rescore_chunk(const float (&v)[kDim], const int8_t *__restrict__ cb_raw,
+                                              int c, int lane, double &bs, int &bj) {
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int j = c * kChunk + half * 32 + lane;
+    if (j < kKissing) better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
+  }
+}
+
+struct RescoreArgs {
+  const uint16_t *cand;
+  const uint8_t *cand_n;
+  const float *best_approx;
+  const float *two_e;
+  const uint32_t *bitmaps;
+  const int8_t *cb_raw;
+  int32_t *out;
+  int32_t *ovf_list;
+  int32_t *ovf_count;
+  int64_t *stats;  // [0] exhaustive atoms, [1] rescored chunks, [2] bitmap atoms
+  int64_t n;
+  int rule;
+};
+
+__global__ void __launch_bounds__(256) rescore_kernel(const __grid_constant__ Segs sg,
+                                                      const RescoreArgs r) {
+  __shared__ int block_ovf, block_chunks, block_bitmap;
   if (threadIdx.x == 0) {
     block_ovf = 0;
     block_chunks = 0;
+    block_bitmap = 0;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t a = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-  if (a < n) {
+  if (a < r.n) {
     float v[kDim];
-    load_atom(x, a, v);
-    const int triv = trivial_index(v, rule);
-    const int cn = cand_n[a];
+    load_atom(atom_ptr(sg, a), v);
+    const int triv = trivial_index(v, r.rule);
+    const int cn = r.cand_n[a];
     if (triv >= 0) {
-      if (lane == 0) out[a] = triv;
+      if (lane == 0) r.out[a] = triv;
     } else if (cn == kOverflow) {
       // Certain origin under the training rule: even best + E stays below the
       // snap threshold (1e-6 covers the fp32 codebook's rounding).
       const double ub = static_cast<double>(kLeechScaleF) *
-                        (static_cast<double>(best_approx[a]) + 0.5 * two_e[a]) * (1.0 + 1e-6);
+                        (static_cast<double>(r.best_approx[a]) + 0.5 * r.two_e[a]) * (1.0 + 1e-6);
       if (lane == 0) {
-        if (rule == H24_RULE_TRAIN && 2.0 * ub < kCSqNorm) {
-          out[a] = 0;
-        } else {
-          out[a] = 0;
-          ovf_list[atomicAdd(ovf_count, 1)] = static_cast<int32_t>(a);
+        r.out[a] = 0;
+        if (!(r.rule == H24_RULE_TRAIN && 2.0 * ub < kCSqNorm)) {
+          r.ovf_list[atomicAdd(r.ovf_count, 1)] = static_cast<int32_t>(a);
           atomicAdd(&block_ovf, 1);
         }
       }
     } else {
       double bs = -INFINITY;
       int bj = 0x7FFFFFFF;
-      for (int k = 0; k < cn; ++k) {
-        const int c = cand[a * kCap + k];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int j = c * kChunk + half * 32 + lane;
-          if (j < kKissing) better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
+      int chunks = 0;
+      if (cn == kBitmapMode) {
+        const int slot = static_cast<int>(r.cand[a * kCap]) | (static_cast<int>(r.cand[a * kCap + 1]) << 16);
+        const uint32_t *bm = r.bitmaps + static_cast<int64_t>(slot) * kBitmapWords;
+        for (int w = 0; w < kBitmapWords; ++w) {
+          uint32_t word = __ldg(bm + w);
+          while (word) {
+            const int b = __ffs(word) - 1;
+            word &= word - 1;
+            rescore_chunk(v, r.cb_raw, w * 32 + b, lane, bs, bj);
+            ++chunks;
+          }
         }
+      } else {
+        for (int k = 0; k < cn; ++k) rescore_chunk(v, r.cb_raw, r.cand[a * kCap + k], lane, bs, bj);
+        chunks = cn;
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
@@ -658,21 +754,24 @@ __global__ void __launch_bounds__(256) rescore_kernel(
         better(bs, bj, os, oj);
       }
       if (lane == 0) {
-        out[a] = cn > 0 ? apply_rule(bs, bj, rule) : 0;
-        atomicAdd(&block_chunks, cn);
+        r.out[a] = chunks > 0 ? apply_rule(bs, bj, r.rule) : 0;
+        atomicAdd(&block_chunks, chunks);
+        if (cn == kBitmapMode) atomicAdd(&block_bitmap, 1);
       }
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0 && (block_ovf || block_chunks)) {
-    atomicAdd(reinterpret_cast<unsigned long long *>(&stats[0]),
+  if (threadIdx.x == 0 && (block_ovf || block_chunks || block_bitmap)) {
+    atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[0]),
               static_cast<unsigned long long>(block_ovf));
-    atomicAdd(reinterpret_cast<unsigned long long *>(&stats[1]),
+    atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[1]),
               static_cast<unsigned long long>(block_chunks));
+    atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[2]),
+              static_cast<unsigned long long>(block_bitmap));
   }
 }
 
-__global__ void __launch_bounds__(256) exhaustive_kernel(const float *__restrict__ x, int rule,
+__global__ void __launch_bounds__(256) exhaustive_kernel(const __grid_constant__ Segs sg, int rule,
                                                          const int32_t *__restrict__ ovf_list,
                                                          const int32_t *__restrict__ ovf_count,
                                                          const int8_t *__restrict__ cb_raw,
@@ -683,7 +782,7 @@ __global__ void __launch_bounds__(256) exhaustive_kernel(const float *__restrict
   for (int e = blockIdx.x; e < count; e += gridDim.x) {
     const int64_t a = ovf_list[e];
     float v[kDim];
-    load_atom(x, a, v);
+    load_atom(atom_ptr(sg, a), v);
     double bs = -INFINITY;
     int bj = 0x7FFFFFFF;
     for (int j = threadIdx.x; j < kKissing; j += blockDim.x)
@@ -712,9 +811,16 @@ int g_sms[64] = {};
 
 }  // namespace
 
-int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
-             cudaStream_t s) {
-  if (n <= 0) return H24_OK;
+int quantize_segments(const Tables *t, const float *const *xs, const int64_t *counts, int nseg,
+                      int rule, int32_t *out_idx, cudaStream_t s) {
+  int64_t total = 0;
+  for (int i = 0; i < nseg; ++i) {
+    if (counts[i] < 0) return fail(H24_ERR_INVALID, "quantize: negative segment length");
+    if (counts[i] > 0 && (!xs[i] || !aligned16(xs[i])))
+      return fail(H24_ERR_INVALID, "quantize: segment pointers must be non-null and 16-byte aligned");
+    total += counts[i];
+  }
+  if (total == 0) return H24_OK;
   int sms = 0;
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -728,42 +834,60 @@ int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_
     }
     sms = g_sms[dev];
   }
-  int64_t *stats = t->stats;
-  int *err = t->err;
 
-  const int64_t batch = n < kBatchAtoms ? n : kBatchAtoms;
+  const int64_t batch = total < kBatchAtoms ? total : kBatchAtoms;
   const int64_t nb_max = (batch + kBlockAtoms - 1) / kBlockAtoms;
   const int64_t pad_max = nb_max * kBlockAtoms;
+  const int64_t pool_slots = batch / 4 > 4096 ? batch / 4 : 4096;
   auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
   const size_t off_two_e = up(static_cast<size_t>(nb_max) * kATileBytes);
   const size_t off_cand = off_two_e + up(pad_max * sizeof(float));
   const size_t off_cand_n = off_cand + up(pad_max * kCap * sizeof(uint16_t));
   const size_t off_best = off_cand_n + up(pad_max);
   const size_t off_ovf = off_best + up(pad_max * sizeof(float));
-  const size_t off_cnt = off_ovf + up(batch * sizeof(int32_t));
+  const size_t off_bm = off_ovf + up(batch * sizeof(int32_t));
+  const size_t off_cnt = off_bm + up(static_cast<size_t>(pool_slots) * kBitmapWords * 4);
   const size_t bytes = off_cnt + 256;
   uint8_t *scratch = nullptr;
   H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&scratch), bytes, t->pool, s));
   int rc = H24_OK;
-  for (int64_t base = 0; base < n && rc == H24_OK; base += batch) {
-    const int64_t nbatch = (n - base) < batch ? (n - base) : batch;
+  int seg = 0;
+  int64_t seg_off = 0;  // atoms of segment `seg` already consumed
+  int64_t done = 0;
+  while (done < total && rc == H24_OK) {
+    // Collect up to kMaxSegs (pieces of) segments, at most `batch` atoms.
+    Segs sg;
+    sg.count = 0;
+    sg.start[0] = 0;
+    int64_t nbatch = 0;
+    while (seg < nseg && sg.count < kMaxSegs && nbatch < batch) {
+      const int64_t avail = counts[seg] - seg_off;
+      if (avail <= 0) { ++seg; seg_off = 0; continue; }
+      const int64_t take = avail < batch - nbatch ? avail : batch - nbatch;
+      sg.x[sg.count] = xs[seg] + seg_off * kDim;
+      nbatch += take;
+      sg.start[++sg.count] = nbatch;
+      seg_off += take;
+      if (seg_off == counts[seg]) { ++seg; seg_off = 0; }
+    }
     const int64_t nb = (nbatch + kBlockAtoms - 1) / kBlockAtoms;
     const int64_t npad = nb * kBlockAtoms;
-    const float *xb = x + base * kDim;
-    int32_t *ob = out_idx + base;
+    int32_t *ob = out_idx + done;
     uint8_t *a_tiled = scratch;
     float *two_e = reinterpret_cast<float *>(scratch + off_two_e);
     uint16_t *cand = reinterpret_cast<uint16_t *>(scratch + off_cand);
     uint8_t *cand_n = scratch + off_cand_n;
     float *best = reinterpret_cast<float *>(scratch + off_best);
     int32_t *ovf_list = reinterpret_cast<int32_t *>(scratch + off_ovf);
+    uint32_t *bitmaps = reinterpret_cast<uint32_t *>(scratch + off_bm);
     int32_t *ovf_count = reinterpret_cast<int32_t *>(scratch + off_cnt);
-    cudaError_t e = cudaMemsetAsync(ovf_count, 0, sizeof(int32_t), s);
+    int32_t *slot_count = ovf_count + 1;
+    cudaError_t e = cudaMemsetAsync(ovf_count, 0, 2 * sizeof(int32_t), s);
     if (e != cudaSuccess) { rc = cuda_fail(e, "memset"); break; }
-    prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(xb, nbatch, npad, a_tiled,
+    prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(sg, nbatch, npad, a_tiled,
                                                                         two_e);
     ScreenArgs sa{a_tiled, two_e, reinterpret_cast<const uint8_t *>(t->cb_tiled), cand, cand_n,
-                  best, nbatch, nb, err};
+                  best, bitmaps, slot_count, static_cast<int32_t>(pool_slots), nbatch, nb, t->err};
     const int grid = static_cast<int>(nb < sms ? nb : sms);
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     if (timing_enabled()) {
@@ -776,16 +900,24 @@ int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_
       cudaEventRecord(ev1, s);
       timing_record(ev0, ev1);
     }
+    RescoreArgs ra{cand, cand_n, best, two_e, bitmaps, t->cb_raw, ob, ovf_list, ovf_count,
+                   t->stats, nbatch, rule};
     const int64_t rthreads = nbatch * 32;
-    rescore_kernel<<<static_cast<unsigned>((rthreads + 255) / 256), 256, 0, s>>>(
-        xb, nbatch, rule, cand, cand_n, best, two_e, t->cb_raw, ob, ovf_list, ovf_count, stats);
-    exhaustive_kernel<<<2 * sms, 256, 0, s>>>(xb, rule, ovf_list, ovf_count, t->cb_raw, ob);
+    rescore_kernel<<<static_cast<unsigned>((rthreads + 255) / 256), 256, 0, s>>>(sg, ra);
+    exhaustive_kernel<<<2 * sms, 256, 0, s>>>(sg, rule, ovf_list, ovf_count, t->cb_raw, ob);
+    count_launches(4);
     e = cudaGetLastError();
     if (e != cudaSuccess) rc = cuda_fail(e, "quantize launch");
+    done += nbatch;
   }
   cudaError_t e = cudaFreeAsync(scratch, s);
   if (rc == H24_OK && e != cudaSuccess) rc = cuda_fail(e, "cudaFreeAsync");
   return rc;
+}
+
+int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
+             cudaStream_t s) {
+  return quantize_segments(t, &x, &n, 1, rule, out_idx, s);
 }
 
 }  // namespace h24

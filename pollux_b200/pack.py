@@ -14,6 +14,8 @@ reference returns them.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _native as N
@@ -54,3 +56,27 @@ def quantize_layer_device(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Ten
         _call(dev, "h24_quantize_layer", wd.data_ptr(), rows, in_f, sigma.data_ptr(),
               packed.data_ptr(), _stream(dev))
     return packed, sigma
+
+
+def quantize_layers(weights: list[torch.Tensor]) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """Pack-rule quantisation of many 2-D weights (on one CUDA device) with one
+    shared search pipeline; returns device-resident (packed u8, sigma16) pairs."""
+    if not weights:
+        return []
+    dev = _work_device(weights[0])
+    ws = []
+    for w in weights:
+        if w.dim() != 2 or w.numel() % H24_DIM != 0:
+            raise ValueError(f"weights must be 2-D with a multiple of {H24_DIM} elements, got {tuple(w.shape)}")
+        ws.append(_aligned(w.detach().to(device=dev, dtype=torch.float32)))
+    outs = []
+    layers = (N.Layer * len(ws))()
+    for i, w in enumerate(ws):
+        rows, in_f = w.shape
+        atoms = w.numel() // H24_DIM
+        packed = torch.empty(((atoms + 3) // 4) * BYTES_PER_CHUNK, dtype=torch.uint8, device=dev)
+        sigma = torch.empty(rows, dtype=torch.float16, device=dev)
+        layers[i] = N.Layer(w.data_ptr(), rows, in_f, sigma.data_ptr(), packed.data_ptr())
+        outs.append((packed, sigma))
+    _call(dev, "h24_quantize_layers", ctypes.cast(layers, ctypes.c_void_p), len(ws), _stream(dev))
+    return outs
