@@ -337,6 +337,33 @@ def run_e2e(args, weights, shapes, dev) -> dict:
             "api": "pollux_b200.pack._quantize_h24_layer + packed_linear.materialize_all"}
 
 
+def run_search_only(args) -> None:
+    """Search kernel alone on ``--search-atoms`` seeded N(0, 2) atoms (the
+    scale of normalised weights); for profiling the screening kernel on a
+    small case."""
+    import torch
+    from pollux_b200 import castor
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(args.search_atoms, 24, generator=g, device=dev) * 1.4142135
+    for _ in range(args.warmup):
+        castor.quantize_indices(x, 1)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        castor.quantize_indices(x, 1)
+    t1.record()
+    torch.cuda.synchronize()
+    castor.device_check(dev)
+    ms = t0.elapsed_time(t1) / args.steps
+    atoms_s = args.search_atoms / (ms / 1e3)
+    print(json.dumps({"search_atoms": args.search_atoms, "ms_per_call": ms,
+                      "G_atoms_per_s": atoms_s / 1e9,
+                      "algorithmic_TFLOPs": atoms_s * FLOP_PER_ATOM / 1e12}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -345,8 +372,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--search-atoms", type=int, default=0,
+                    help="profile mode: time only the search on this many atoms")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.search_atoms:
+        run_search_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

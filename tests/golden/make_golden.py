@@ -20,6 +20,8 @@ Fixtures written (all small):
   stress.npz             4096 config-4 atoms (seed 3) with the reference's
                          pack-rule and training-rule indices
   materialize.npz        PackedH24Linear.materialize outputs (pollux.py:485-504)
+  tiny.plx, plx_state.npz  (with --plx) a .plx written by pack._write_plx and
+                         the tensors that went into it
 """
 from __future__ import annotations
 
@@ -51,7 +53,10 @@ def vectors_to_indices(vec: torch.Tensor, raw_table: np.ndarray) -> np.ndarray:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--plx", action="store_true", help="only write the .plx fixture")
     args = ap.parse_args()
+    if args.plx:
+        return
     sys.path.insert(0, args.reference)
     sys.path.insert(0, REPO)
     import castor  # noqa: E402  (reference)
@@ -169,3 +174,33 @@ def main() -> None:
 
 if __name__ == "__main__":
     main()
+
+
+def make_plx(reference: str) -> None:
+    """tiny.plx written by the reference's own pack._write_plx (pack.py:187-247)
+    plus the tensors that went in (plx_state.npz)."""
+    sys.path.insert(0, reference)
+    sys.path.insert(0, REPO)
+    import castor  # noqa: E402
+    import pack as ref_pack  # noqa: E402
+    g = torch.Generator().manual_seed(21)
+    idx = torch.randint(0, 196561, (96 * 4,), generator=g)
+    state = {
+        "blocks.0.attn.q.packed_weights": castor.pack_indices(idx),
+        "blocks.0.attn.q.sigma_rows": (torch.rand(96, generator=g) * 0.1).to(torch.float16),
+        "tok_emb.weight_int8": torch.randint(-128, 128, (7, 24), generator=g, dtype=torch.int8),
+        "ln_f.weight": torch.randn(24, generator=g),
+        "head.mu_rows": (torch.rand(7, generator=g) + 0.5).to(torch.float16),
+    }
+    cfg = {"n_embd": 24, "n_layers": 1, "scales_per_row": 1, "note": "tiny fixture"}
+    path = os.path.join(HERE, "tiny.plx")
+    ref_pack._write_plx(path, cfg, state)
+    np.savez_compressed(os.path.join(HERE, "plx_state.npz"),
+                        **{k.replace(".", "__"): (v.float().numpy() if v.dtype == torch.bfloat16
+                                                  else v.numpy()) for k, v in state.items()},
+                        config=np.array(json.dumps(cfg)))
+    print("tiny.plx written")
+
+
+if __name__ == "__main__" and "--plx" in sys.argv:
+    make_plx(sys.argv[sys.argv.index("--reference") + 1])

@@ -117,7 +117,7 @@ def test_config4_scale_sample(C, oracle):
     exhaustive, bitmap, chunks = C.quantize_stats()
     assert exhaustive < 100
     assert bitmap < 0.2 * (1 << 20)
-    assert chunks < 8 * (1 << 20)
+    assert chunks < 16 * (1 << 20)
     sel = torch.randperm(1 << 20, generator=torch.Generator().manual_seed(0))[:3000]
     xs = x[sel.cuda()].cpu().numpy()
     assert np.array_equal(ours[sel.cuda()].cpu().numpy(), oracle.nearest_exact(xs, 1))
