@@ -11,7 +11,8 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_lib", "libh24.so")
+# H24_LIBRARY selects another build of the same library (e.g. a tuning variant).
+LIB_PATH = os.environ.get("H24_LIBRARY") or os.path.join(_HERE, "_lib", "libh24.so")
 
 H24_OK = 0
 H24_ERR_INVALID = 1

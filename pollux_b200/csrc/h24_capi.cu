@@ -48,7 +48,7 @@ bool g_tables_ok[kMaxDevices] = {};
 
 struct HostTables {
   std::vector<int8_t> raw;        // [kKissing][24]
-  std::vector<uint16_t> tiled;    // [kKissingPad][32] bf16 bits, tiled
+  std::vector<uint16_t> tiled;    // [kKissing][32] bf16 bits, tiled
   std::vector<uint32_t> nib;      // [kCount][3]
   float fingerprint[16];
   bool ok = false;
@@ -69,7 +69,7 @@ const HostTables &host_tables() {
   std::call_once(once, [] {
     H.raw.resize(static_cast<size_t>(kKissing) * kDim);
     if (!build_raw_kissing_points(H.raw.data(), &H.err)) return;
-    H.tiled.assign(static_cast<size_t>(kKissingPad) * kKPad, 0);
+    H.tiled.assign(static_cast<size_t>(kKissing) * kKPad, 0);
     for (int j = 0; j < kKissing; ++j) {
       const int t = j / kTileN, rr = j % kTileN, g = rr / 8, r = rr % 8;
       for (int k = 0; k < kDim; ++k) {

@@ -16,15 +16,16 @@ constexpr int kDim = 24;
 constexpr int kKissing = 196560;
 constexpr int kCount = 196561;
 
-// Screening tiles: the codebook is streamed in tiles of kTileN codewords, the
-// last one padded with zero rows up to kKissingPad.
-constexpr int kTileN = 128;
-constexpr int kNumTiles = (kKissing + kTileN - 1) / kTileN;  // 1536
-constexpr int kKissingPad = kNumTiles * kTileN;              // 196608
-constexpr int kChunk = 64;                                   // candidate granularity
-constexpr int kNumChunks = kKissingPad / kChunk;             // 3072
+// Screening tiles: the codebook is streamed in tiles of kTileN codewords;
+// 196,560 = 1638 x 120, so no tile is padded.  Candidates are tracked per
+// chunk of kChunk codewords (two chunks per tile).
+constexpr int kTileN = 120;
+constexpr int kNumTiles = kKissing / kTileN;                 // 1638
+constexpr int kChunk = kTileN / 2;                           // 60
+constexpr int kNumChunks = kKissing / kChunk;                // 3276
 constexpr int kKPad = 32;                                    // K padded 24 -> 32 (bf16)
 constexpr int kRowBytes = kKPad * 2;                         // 64 bytes per operand row
+static_assert(kNumTiles * kTileN == kKissing, "tiles cover the codebook exactly");
 
 // fp32 value of LEECH_SCALE = 1/sqrt(8) and of s_lattice = 1/sqrt(2) as torch
 // rounds the Python floats (castor.py:49, 68).
@@ -36,9 +37,9 @@ constexpr double kCSqNorm = 3.999999761581421;
 // Per-device tables (all device pointers).
 struct Tables {
   int device = -1;
-  // bf16 raw coordinates [kKissingPad][32], core-matrix tiled for the MMA B
-  // operand: tile t (128 rows) at t*8192 B; inside it 8-row group g at g*512,
-  // 16-byte K chunk c at c*128, row r at r*16.
+  // bf16 raw coordinates [kKissing][32], core-matrix tiled for the MMA B
+  // operand: tile t (kTileN rows) at t*kTileN*64 B; inside it 8-row group g
+  // at g*512, 16-byte K chunk c at c*128, row r at r*16.
   const __nv_bfloat16 *cb_tiled = nullptr;
   // raw int8 coordinates [kKissing][24] (kissing point j = codebook row j+1).
   const int8_t *cb_raw = nullptr;

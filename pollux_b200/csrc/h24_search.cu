@@ -8,21 +8,24 @@
 // followed by the caller's origin rule (H24_RULE_TRAIN / H24_RULE_PACK).
 //
 // Pipeline per batch of atoms (one CUDA stream, no host synchronisation):
-//   1. prep_kernel      x -> bf16 "hi" operand (core-matrix tiled for UMMA) and
-//                       a per-atom bound 2E on |screening score - exact score|.
+//   1. prep_kernel      x -> bf16 "hi" rows (24 values + 8 zeros) and a
+//                       per-atom bound 2E on |screening score - exact score|.
 //   2. screen_kernel    persistent tcgen05 kernel, one CTA per SM.  Each CTA
-//                       owns 256 atoms (two M=128 tiles) at a time and streams
-//                       the bf16 codebook (raw integers, exact in bf16, K
-//                       padded 24 -> 32) through shared memory with bulk
-//                       copies, 128 codewords per stage.  Scores accumulate in
-//                       TMEM (fp32), double-buffered; 8 epilogue warps read
-//                       them with tcgen05.ld, one thread per atom, and keep
-//                       the 64-codeword chunks whose maximum is within 2E of
-//                       the running best.
+//                       owns 256 atoms (two M=128 tiles) at a time; their bf16
+//                       rows live in tensor memory (A operand), written by the
+//                       epilogue warps with tcgen05.st.  The bf16 codebook (raw
+//                       integers, exact in bf16, K padded 24 -> 32) streams
+//                       through a shared-memory ring by bulk copies, 112
+//                       codewords per stage, so the MMAs read only B from shared
+//                       memory.  Scores accumulate in TMEM (fp32), double
+//                       buffered; 16 epilogue warps read them with tcgen05.ld,
+//                       one thread per (atom, 56-codeword chunk parity), and
+//                       keep the chunks whose maximum is within 2E of the
+//                       running best.
 //   3. rescore_kernel   one warp per atom rescans the surviving chunks in fp64
 //                       and applies the origin rule.
 //   4. exhaustive_kernel  fp64 scan of all codewords for the rare atoms whose
-//                       candidate list overflowed (exact ties over many chunks).
+//                       candidate bookkeeping overflowed.
 //
 // Why the bound is sufficient: with S~ the screening score and R the exact
 // score (in raw-integer units), |S~_j - R_j| <= E for every j.  If j* is the
@@ -37,32 +40,39 @@ namespace h24 {
 namespace {
 
 constexpr int kBlockAtoms = 256;                    // atoms per CTA work item
-constexpr int kStages = 10;                         // codebook ring depth
-constexpr int kBTileBytes = kTileN * kRowBytes;     // 8192
-constexpr int kATileBytes = kBlockAtoms * kRowBytes;  // 16384
-constexpr int kCap = 16;                            // candidate chunks per atom (list mode)
-constexpr int kBitmapWords = kNumChunks / 32;       // 96 words: one bit per chunk
+constexpr int kStages = 16;                         // codebook ring depth
+constexpr int kAccStages = 2;                       // TMEM accumulator stages
+constexpr int kBTileBytes = kTileN * kRowBytes;     // 7680
+constexpr int kHiBytes = kRowBytes;                 // bf16 row of one atom in global memory
+constexpr int kCap = 12;                            // candidate chunks per (atom, half) list
+constexpr int kBitmapWords = (kNumChunks + 31) / 32;  // 103 words: one bit per chunk
 constexpr int kMaxSegs = 64;                        // input segments per pipeline batch
-constexpr int kEpiWarps = 8;
-constexpr int kScreenThreads = 32 * (2 + kEpiWarps);  // 320
+constexpr int kEpiWarps = 16;                        // 2 M-tiles x 4 lane quarters x 2 halves
+constexpr int kLists = 2 * kBlockAtoms;               // one list per (atom, column half)
+constexpr int kTileWarps = 8;                        // epilogue warps reading one M-tile
+constexpr int kFirstEpiWarp = 3;                      // warp 0 producer, warps 1-2 MMA issuers
+constexpr int kScreenThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 608
 constexpr uint32_t kTmemCols = 512;
+// TMEM columns: accumulator stage s, M-tile h at s*2*kTileN + h*kTileN; the
+// A operand of M-tile h at kAColBase + h*kACols.
+constexpr uint32_t kACols = kKPad / 2;                // 16 columns: 32 bf16 per lane
+constexpr uint32_t kAColBase = kAccStages * 2 * kTileN;  // 480
+static_assert(kAColBase + 2 * kACols == kTmemCols, "accumulators + A operand fill TMEM");
 constexpr uint8_t kOverflow = 0xFF;   // exhaustive fp64 scan
 constexpr uint8_t kBitmapMode = 0xFE; // candidate chunks in a global bitmap slot
 constexpr int64_t kBatchAtoms = int64_t(1) << 22;    // atoms per pipeline batch
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s
 
 struct __align__(1024) ScreenSmem {
-  uint8_t a[2][kATileBytes];
   uint8_t b[kStages][kBTileBytes];
-  float cand_score[kCap][kBlockAtoms];
-  uint16_t cand_chunk[kCap][kBlockAtoms];
+  float cand_score[kCap][kLists];
+  uint16_t cand_chunk[kCap][kLists];
   uint64_t bar_b_full[kStages];
   uint64_t bar_b_empty[kStages];
-  uint64_t bar_a_full[2];
-  uint64_t bar_a_empty[2];
-  uint64_t bar_acc_full[2];
-  uint64_t bar_acc_empty[2];
-  uint64_t bar_final;
+  uint64_t bar_a_full[2][2];              // [A buffer][M-tile]
+  uint64_t bar_acc_full[kAccStages][2];   // [stage][M-tile]
+  uint64_t bar_acc_empty[kAccStages][2];
+  uint64_t bar_final[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -88,8 +98,24 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                : "memory");
 }
 
+// Suspend-time hint (ns) of the mbarrier waits: a waiting thread sleeps until
+// the phase completes or the hint expires instead of spinning.  0 = no hint.
+#ifndef H24_WAIT_HINT_NS
+#define H24_WAIT_HINT_NS 1000000
+#endif
+
+// One potentially blocking test of the phase.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
+#if H24_WAIT_HINT_NS > 0
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(static_cast<uint32_t>(H24_WAIT_HINT_NS))
+      : "memory");
+#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -97,6 +123,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
+#endif
   return ok != 0;
 }
 
@@ -106,24 +133,41 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Waits for the phase of `bar` with the given parity.  Gives up after
-// kWaitLimitNs or when another role of the CTA has aborted; on a timeout it
-// raises the CTA abort flag and the device error word.
-__device__ __noinline__ bool wait_bounded(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          int *err) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Non-blocking test of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Slow path of wait_bar.  Gives up after kWaitLimitNs or when another role of
+// the CTA has aborted; on a timeout it raises the CTA abort flag and the
+// device error word.
+__device__ __noinline__ bool wait_slow(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                       int *err) {
   const unsigned long long t0 = global_ns();
-  for (uint32_t it = 1;; ++it) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        atomicExch(err, H24_ERR_TIMEOUT);
-        return false;
-      }
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicExch(err, H24_ERR_TIMEOUT);
+      return false;
     }
   }
+}
+
+// Waits for the phase of `bar` with the given parity (inline fast path).
+__device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                         int *err) {
+  if (mbar_test(bar, parity)) return true;
+  return wait_slow(bar, parity, abort_flag, err);
 }
 
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
@@ -141,11 +185,6 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
-__device__ __forceinline__ uint64_t policy_evict_first() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
 
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -168,14 +207,31 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
                             (static_cast<uint32_t>(kTileN >> 3) << 17) | ((128u >> 4) << 24);
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t accumulate) {
+// D (TMEM) += A (TMEM) x B (shared memory descriptor); accumulate == 0
+// overwrites D.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
       : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit TMEM columns from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -213,14 +269,6 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t *r) {
                :
                : "memory");
 }
-// Orders a second block of loaded registers after the preceding wait.
-__device__ __forceinline__ void tmem_tie(uint32_t *r) {
-  asm volatile(""
-               : H24_T8(0), H24_T8(8), H24_T8(16), H24_T8(24), H24_T8(32), H24_T8(40),
-                 H24_T8(48), H24_T8(56)
-               :
-               : "memory");
-}
 #undef H24_T8
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -229,34 +277,23 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Maximum of 64 fp32 values held as raw bits (balanced tree of 3-input max).
-__device__ __forceinline__ float max64(const uint32_t *r) {
-  float m[22];
+// Maximum of 60 fp32 values held as raw bits (tree of 3-input max).
+__device__ __forceinline__ float max60(const uint32_t *r) {
+  float m[20];
 #pragma unroll
-  for (int k = 0; k < 21; ++k)
+  for (int k = 0; k < 20; ++k)
     m[k] = fmax3(__uint_as_float(r[3 * k]), __uint_as_float(r[3 * k + 1]),
                  __uint_as_float(r[3 * k + 2]));
-  m[21] = __uint_as_float(r[63]);
-  float n[8];
+  float n[7];
 #pragma unroll
-  for (int k = 0; k < 7; ++k) n[k] = fmax3(m[3 * k], m[3 * k + 1], m[3 * k + 2]);
-  n[7] = m[21];
-  const float p0 = fmax3(n[0], n[1], n[2]);
-  const float p1 = fmax3(n[3], n[4], n[5]);
-  return fmax3(p0, p1, fmaxf(n[6], n[7]));
+  for (int k = 0; k < 6; ++k) n[k] = fmax3(m[3 * k], m[3 * k + 1], m[3 * k + 2]);
+  n[6] = fmaxf(m[18], m[19]);
+  return fmax3(fmax3(n[0], n[1], n[2]), fmax3(n[3], n[4], n[5]), n[6]);
 }
 
 // ---------------------------------------------------------------------------
 // 1. prep
 // ---------------------------------------------------------------------------
-// Byte offset of (atom, 16-byte K chunk c) in the tiled bf16 operand.
-__device__ __forceinline__ int64_t tiled_offset(int64_t atom, int c) {
-  const int64_t blk = atom / kBlockAtoms;
-  const int l = static_cast<int>(atom - blk * kBlockAtoms);
-  const int h = l >> 7, r128 = l & 127;
-  return blk * kATileBytes + h * (128 * kRowBytes) + (r128 >> 3) * 512 + c * 128 + (r128 & 7) * 16;
-}
-
 // Input atoms of one pipeline batch: segment i holds atoms [start[i],
 // start[i+1]) of the batch, stored contiguously at x[i] (24 fp32 per atom).
 struct Segs {
@@ -275,7 +312,7 @@ __device__ __forceinline__ const float *atom_ptr(const Segs &sg, int64_t a) {
 }
 
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
-                                                   int64_t n_pad, uint8_t *__restrict__ a_tiled,
+                                                   int64_t n_pad, uint8_t *__restrict__ a_hi,
                                                    float *__restrict__ two_e) {
   const int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (a >= n_pad) return;
@@ -315,24 +352,28 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   const float e_hi = fminf(4.f * sum_d, 5.656854249f * sqrtf(sum_d2));
   const float e = (e_hi + 2.44140625e-4f * sum_x) * 1.001f;
   if (a < n) two_e[a] = finite ? 2.f * e : -1.f;
-  uint4 *dst = reinterpret_cast<uint4 *>(a_tiled);
+  // Row of 32 bf16 (24 values, 8 zeros): the atom's lane of the A operand.
+  uint4 *dst = reinterpret_cast<uint4 *>(a_hi + a * kHiBytes);
 #pragma unroll
   for (int c = 0; c < 3; ++c)
-    dst[tiled_offset(a, c) / 16] =
-        make_uint4(hi_bits[4 * c], hi_bits[4 * c + 1], hi_bits[4 * c + 2], hi_bits[4 * c + 3]);
-  dst[tiled_offset(a, 3) / 16] = make_uint4(0, 0, 0, 0);
+    dst[c] = make_uint4(hi_bits[4 * c], hi_bits[4 * c + 1], hi_bits[4 * c + 2], hi_bits[4 * c + 3]);
+  dst[3] = make_uint4(0, 0, 0, 0);
 }
 
 // ---------------------------------------------------------------------------
 // 2. tcgen05 screening
 // ---------------------------------------------------------------------------
+// Per atom and column half h (chunks 2t+h): cand_n[2a+h] entries (or the
+// bitmap / overflow codes), chunk ids cand[(2a+h)*kCap + k] with their
+// screening maxima cand_sc[...], and the half's screening maximum best[2a+h].
 struct ScreenArgs {
-  const uint8_t *a_tiled;
+  const uint8_t *a_hi;        // [n_pad][32] bf16 rows
   const float *two_e;
   const uint8_t *cb_tiled;
-  uint16_t *cand;     // [n_pad][kCap]
-  uint8_t *cand_n;    // [n_pad]
-  float *best;        // [n_pad]
+  uint16_t *cand;     // [n_pad*2][kCap]
+  float *cand_sc;     // [n_pad*2][kCap]
+  uint8_t *cand_n;    // [n_pad*2]
+  float *best;        // [n_pad*2]
   uint32_t *bitmaps;  // [pool_slots][kBitmapWords]
   int32_t *slot_count;
   int32_t pool_slots;
@@ -362,8 +403,9 @@ __device__ __forceinline__ void bitmap_set(const ScreenArgs &args, Cands &c, int
   c.bm_word |= 1u << (chunk & 31);
 }
 
-__device__ __forceinline__ void epilogue_insert(ScreenSmem &S, const ScreenArgs &args, int local,
+__device__ __forceinline__ void epilogue_insert(ScreenSmem &S, const ScreenArgs &args, int list,
                                                 float m, int chunk, float thr, Cands &c) {
+  const int local = list;
   if (!(m >= thr)) return;
   if (c.slot >= 0) {
     bitmap_set(args, c, chunk);
@@ -413,15 +455,16 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.bar_b_full[s], 1);
-      mbar_init(&S.bar_b_empty[s], 1);
+      mbar_init(&S.bar_b_empty[s], 2);       // one commit per MMA issuer
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&S.bar_a_full[s], 1);
-      mbar_init(&S.bar_a_empty[s], 1);
-      mbar_init(&S.bar_acc_full[s], 1);
-      mbar_init(&S.bar_acc_empty[s], kEpiWarps);
+    for (int h = 0; h < 2; ++h) {
+      for (int s = 0; s < 2; ++s) mbar_init(&S.bar_a_full[s][h], kTileWarps / 2);
+      for (int s = 0; s < kAccStages; ++s) {
+        mbar_init(&S.bar_acc_full[s][h], 1);
+        mbar_init(&S.bar_acc_empty[s][h], kTileWarps);
+      }
+      mbar_init(&S.bar_final[h], 1);
     }
-    mbar_init(&S.bar_final, 1);
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -439,25 +482,17 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
   const uint32_t tmem_base = S.tmem_base;
 
   if (warp == 0) {
-    // ---------------- producer: bulk copies of A tiles and codebook tiles --
+    // ---------------- producer: bulk copies of codebook tiles ----------------
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
-      const uint64_t stream_once = policy_evict_first();
-      int bs = 0, ab = 0;
-      uint32_t bph = 0, aph = 0;
+      int bs = 0;
+      uint32_t bph = 0;
       int last_b[kStages];
-      int last_a[2] = {-1, -1};
       for (int s = 0; s < kStages; ++s) last_b[s] = -1;
       bool ok = true;
       for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
-        if (!wait_bounded(&S.bar_a_empty[ab], aph ^ 1, abort_flag, args.err)) { ok = false; break; }
-        mbar_arrive_expect_tx(&S.bar_a_full[ab], kATileBytes);
-        bulk_g2s(S.a[ab], args.a_tiled + blk * kATileBytes, kATileBytes, &S.bar_a_full[ab],
-                 stream_once);
-        last_a[ab] = static_cast<int>(aph);
-        if (++ab == 2) { ab = 0; aph ^= 1; }
         for (int t = 0; t < kNumTiles; ++t) {
-          if (!wait_bounded(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err)) { ok = false; break; }
+          if (!wait_bar(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err)) { ok = false; break; }
           mbar_arrive_expect_tx(&S.bar_b_full[bs], kBTileBytes);
           bulk_g2s(S.b[bs], args.cb_tiled + static_cast<int64_t>(t) * kBTileBytes, kBTileBytes,
                    &S.bar_b_full[bs], keep);
@@ -474,129 +509,155 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
                    global_ns() - t0 < kWaitLimitNs) {
             }
           }
-        for (int s = 0; s < 2; ++s)
-          if (last_a[s] >= 0) {
-            const unsigned long long t0 = global_ns();
-            while (!mbar_try_wait(&S.bar_a_full[s], static_cast<uint32_t>(last_a[s])) &&
-                   global_ns() - t0 < kWaitLimitNs) {
-            }
-          }
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ------------------------------------------
+  } else if (warp <= 2) {
+    // ---------------- MMA issuers: warp 1 -> M-tile 0, warp 2 -> M-tile 1 ---
+    // MMA issue blocks until the tensor core accepts the instruction, so two
+    // issuers let one wait on its barriers while the other's MMAs run.
+    const int h = warp - 1;
     if (lane == 0) {
+      const uint64_t bd0 = smem_desc(smem_u32(S.b[0]));
+      constexpr uint64_t kBStep = kBTileBytes >> 4;           // descriptor units
+      constexpr uint64_t kKStep = 256 >> 4;                   // next 16 K in shared memory
+      constexpr uint32_t kAKStep = 8;                         // next 16 K in TMEM (columns)
       int bs = 0, ab = 0, as = 0;
       uint32_t bph = 0, aph = 0, cph = 0;
       bool ok = true;
       bool issued = false;
       for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
-        if (!wait_bounded(&S.bar_a_full[ab], aph, abort_flag, args.err)) { ok = false; break; }
+        if (!wait_bar(&S.bar_a_full[ab][h], aph, abort_flag, args.err)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(S.a[ab]);
+        const uint32_t a = tmem_base + kAColBase + static_cast<uint32_t>(h) * kACols;
         for (int t = 0; t < kNumTiles; ++t) {
-          if (!wait_bounded(&S.bar_b_full[bs], bph, abort_flag, args.err)) { ok = false; break; }
-          if (!wait_bounded(&S.bar_acc_empty[as], cph ^ 1, abort_flag, args.err)) { ok = false; break; }
+          if (!wait_bar(&S.bar_b_full[bs], bph, abort_flag, args.err)) { ok = false; break; }
+          if (!wait_bar(&S.bar_acc_empty[as][h], cph ^ 1, abort_flag, args.err)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t b_addr = smem_u32(S.b[bs]);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t d = tmem_base + static_cast<uint32_t>(as * 2 * kTileN + h * kTileN);
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-              mma_bf16(d, smem_desc(a_addr + h * (128 * kRowBytes) + kk * 256),
-                       smem_desc(b_addr + kk * 256), kk);
-          }
-          issued = true;
+          const uint64_t bd = bd0 + static_cast<uint64_t>(bs) * kBStep;
+          const uint32_t d = tmem_base + static_cast<uint32_t>(as * 2 * kTileN + h * kTileN);
+          mma_bf16_ts(d, a, bd, 0);
+          mma_bf16_ts(d, a + kAKStep, bd + kKStep, 1);
+          mma_commit(&S.bar_acc_full[as][h]);
           mma_commit(&S.bar_b_empty[bs]);
-          mma_commit(&S.bar_acc_full[as]);
+          issued = true;
           if (++bs == kStages) { bs = 0; bph ^= 1; }
-          if (++as == 2) { as = 0; cph ^= 1; }
+          as ^= 1;
+          cph ^= (as == 0);
         }
-        if (!ok) break;
-        mma_commit(&S.bar_a_empty[ab]);
         if (++ab == 2) { ab = 0; aph ^= 1; }
       }
       if (issued) {
-        // All MMAs of this CTA complete before TMEM is released.
-        mma_commit(&S.bar_final);
+        // All MMAs of this issuer complete before TMEM is released.
+        mma_commit(&S.bar_final[h]);
         const unsigned long long t0 = global_ns();
-        while (!mbar_try_wait(&S.bar_final, 0) && global_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(&S.bar_final[h], 0) && global_ns() - t0 < kWaitLimitNs) {
         }
       }
     }
   } else {
-    // ---------------- epilogue: one thread per atom -------------------------
-    const int ew = warp - 2;
-    const int h = ew >> 2;               // which M=128 tile
-    const int q = warp & 3;              // TMEM lane quarter this warp may access
+    // ---------------- epilogue: one thread per (atom, column half) --------
+    // Warp w may only access TMEM lanes 32*(w%4)..+31.  The 16 warps cover two
+    // M=128 tiles x four lane quarters x two column halves of each tile;
+    // every half is one 60-codeword candidate chunk (chunk 2t + half).
+    const int ew = warp - kFirstEpiWarp;
+    const int h = ew >> 3;               // which M=128 tile
+    const int q = warp & 3;              // TMEM lane quarter
+    const int half = (ew >> 2) & 1;      // column half = chunk parity
     const int local = h * 128 + q * 32 + lane;
-    const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                            static_cast<uint32_t>(h * kTileN);
-    int as = 0;
-    uint32_t cph = 0;
+    const int list = half * kBlockAtoms + local;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    // A 64-column load that covers the chunk: half 0 reads columns 0..63
+    // (values r[0..59]), half 1 reads 56..119 (values r[4..63]).
+    const uint32_t t_lane = tmem_base + lane_off + static_cast<uint32_t>(h * kTileN + half * 56);
     bool ok = true;
+    int ab = 0;
+    int acc_stage_ = 0;
+    uint32_t acc_phase_ = 0;
     for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
       const int64_t atom = blk * kBlockAtoms + local;
+      if (half == 0) {
+        // Write this atom's bf16 row into the A operand.  It was last read by
+        // the MMAs of block blk-1, all complete: this warp has already consumed
+        // every accumulator of that block.  The barrier `ab` alternates per
+        // block so that its phase parity identifies the block.
+        uint32_t v[16];
+        const uint4 *src = reinterpret_cast<const uint4 *>(args.a_hi + atom * kHiBytes);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 u = __ldcs(src + k);
+          v[4 * k] = u.x;
+          v[4 * k + 1] = u.y;
+          v[4 * k + 2] = u.z;
+          v[4 * k + 3] = u.w;
+        }
+        tmem_st16(tmem_base + lane_off + kAColBase + static_cast<uint32_t>(h) * kACols, v);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.bar_a_full[ab][h]);
+      }
+      ab ^= 1;
       const float te = atom < args.n ? args.two_e[atom] : -1.f;
       const bool track = te >= 0.f;
       float best = -INFINITY;
       float thr = track ? -INFINITY : INFINITY;
       Cands cs;
+      // Tiles alternate between the two accumulator stages; a stage's phase
+      // parity flips every second tile.  kNumTiles is odd, so the stage and
+      // parity sequence continues across blocks.
       for (int t = 0; t < kNumTiles; ++t) {
-        // Every lane waits; the warp proceeds only if all of them saw the
-        // phase complete, so the .sync.aligned TMEM loads stay convergent.
-        const bool got = wait_bounded(&S.bar_acc_full[as], cph, abort_flag, args.err);
-        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        // Lane 0 waits on the barrier; the warp then synchronises and fences
+        // so that the .sync.aligned TMEM load is ordered after the MMAs.
+        bool got = true;
+        if (lane == 0) got = wait_bar(&S.bar_acc_full[acc_stage_][h], acc_phase_, abort_flag, args.err);
+        if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
         tc_fence_after();
-        uint32_t r0[64], r1[64];
-        const uint32_t taddr = t_lane + static_cast<uint32_t>(as * 2 * kTileN);
-        tmem_ld64(taddr, r0);
-        tmem_ld64(taddr + 64, r1);
-        tmem_wait_ld(r0);
-        tmem_tie(r1);
+        uint32_t r[64];
+        tmem_ld64(t_lane + static_cast<uint32_t>(acc_stage_ * 2 * kTileN), r);
+        tmem_wait_ld(r);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.bar_acc_empty[as]);
-        if (++as == 2) { as = 0; cph ^= 1; }
-        if (t == kNumTiles - 1) {
-          // Codewords past 196559 are zero padding rows.
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (t * kTileN + 64 + c >= kKissing) r1[c] = __float_as_uint(-INFINITY);
-        }
-        const float m0 = max64(r0);
-        const float m1 = max64(r1);
-        const float mt = fmaxf(m0, m1);
-        if (mt >= thr) {
-          if (mt > best) {
-            best = mt;
+        if (lane == 0) mbar_arrive(&S.bar_acc_empty[acc_stage_][h]);
+        acc_stage_ ^= 1;
+        acc_phase_ ^= (acc_stage_ == 0);
+        float m = -INFINITY;
+        if (half == 0) m = max60(r);
+        else m = max60(r + 4);
+        if (m >= thr) {
+          if (m > best) {
+            best = m;
             thr = best - te;
           }
-          epilogue_insert(S, args, local, m0, 2 * t, thr, cs);
-          epilogue_insert(S, args, local, m1, 2 * t + 1, thr, cs);
+          epilogue_insert(S, args, list, m, 2 * t + half, thr, cs);
           if (cs.ovf) thr = INFINITY;
         }
-        best = fmaxf(best, mt);
+        best = fmaxf(best, m);
       }
       if (!ok) break;
       if (atom < args.n) {
+        const int64_t li = atom * 2 + half;
         uint8_t n_out = kOverflow;
         if (track && !cs.ovf) {
           if (cs.slot >= 0) {
             args.bitmaps[static_cast<int64_t>(cs.slot) * kBitmapWords + cs.bm_idx] = cs.bm_word;
-            args.cand[atom * kCap] = static_cast<uint16_t>(cs.slot & 0xFFFF);
-            args.cand[atom * kCap + 1] = static_cast<uint16_t>(cs.slot >> 16);
+            args.cand[li * kCap] = static_cast<uint16_t>(cs.slot & 0xFFFF);
+            args.cand[li * kCap + 1] = static_cast<uint16_t>(cs.slot >> 16);
             n_out = kBitmapMode;
           } else {
             int k = 0;
-            for (int i = 0; i < cs.cnt; ++i)
-              if (S.cand_score[i][local] >= thr) args.cand[atom * kCap + k++] = S.cand_chunk[i][local];
+            for (int i = 0; i < cs.cnt; ++i) {
+              const float sc = S.cand_score[i][list];
+              if (sc >= thr) {
+                args.cand[li * kCap + k] = S.cand_chunk[i][list];
+                args.cand_sc[li * kCap + k] = sc;
+                ++k;
+              }
+            }
             n_out = static_cast<uint8_t>(k);
           }
         }
-        args.cand_n[atom] = n_out;
-        args.best[atom] = best;
+        args.cand_n[li] = n_out;
+        args.best[li] = best;
       }
     }
   }
@@ -672,18 +733,22 @@ __device__ __forceinline__ int32_t apply_rule(double best, int bj, int rule) {
   return bj + 1;
 }
 
-// fp64 rescore of one 64-codeword chunk by a warp (two codewords per lane).
+// fp64 rescore of one 60-codeword chunk by a warp (up to two codewords per lane).
 __device__ __forceinline__ void rescore_chunk(const float (&v)[kDim], const int8_t *__restrict__ cb_raw,
                                               int c, int lane, double &bs, int &bj) {
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    const int j = c * kChunk + half * 32 + lane;
-    if (j < kKissing) better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
+    const int o = half * 32 + lane;
+    if (o < kChunk) {
+      const int j = c * kChunk + o;
+      better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
+    }
   }
 }
 
 struct RescoreArgs {
   const uint16_t *cand;
+  const float *cand_sc;
   const uint8_t *cand_n;
   const float *best_approx;
   const float *two_e;
@@ -712,14 +777,17 @@ __global__ void __launch_bounds__(256) rescore_kernel(const __grid_constant__ Se
     float v[kDim];
     load_atom(atom_ptr(sg, a), v);
     const int triv = trivial_index(v, r.rule);
-    const int cn = r.cand_n[a];
+    const int cn0 = r.cand_n[2 * a], cn1 = r.cand_n[2 * a + 1];
+    // The screening maximum over both halves sets the candidate threshold.
+    const float gbest = fmaxf(r.best_approx[2 * a], r.best_approx[2 * a + 1]);
+    const float te = r.two_e[a];
     if (triv >= 0) {
       if (lane == 0) r.out[a] = triv;
-    } else if (cn == kOverflow) {
+    } else if (cn0 == kOverflow || cn1 == kOverflow) {
       // Certain origin under the training rule: even best + E stays below the
       // snap threshold (1e-6 covers the fp32 codebook's rounding).
       const double ub = static_cast<double>(kLeechScaleF) *
-                        (static_cast<double>(r.best_approx[a]) + 0.5 * r.two_e[a]) * (1.0 + 1e-6);
+                        (static_cast<double>(gbest) + 0.5 * te) * (1.0 + 1e-6);
       if (lane == 0) {
         r.out[a] = 0;
         if (!(r.rule == H24_RULE_TRAIN && 2.0 * ub < kCSqNorm)) {
@@ -728,24 +796,36 @@ __global__ void __launch_bounds__(256) rescore_kernel(const __grid_constant__ Se
         }
       }
     } else {
+      const float thr = gbest - te;
       double bs = -INFINITY;
       int bj = 0x7FFFFFFF;
       int chunks = 0;
-      if (cn == kBitmapMode) {
-        const int slot = static_cast<int>(r.cand[a * kCap]) | (static_cast<int>(r.cand[a * kCap + 1]) << 16);
-        const uint32_t *bm = r.bitmaps + static_cast<int64_t>(slot) * kBitmapWords;
-        for (int w = 0; w < kBitmapWords; ++w) {
-          uint32_t word = __ldg(bm + w);
-          while (word) {
-            const int b = __ffs(word) - 1;
-            word &= word - 1;
-            rescore_chunk(v, r.cb_raw, w * 32 + b, lane, bs, bj);
+      bool used_bitmap = false;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int cn = hf ? cn1 : cn0;
+        const int64_t li = 2 * a + hf;
+        if (cn == kBitmapMode) {
+          used_bitmap = true;
+          const int slot = static_cast<int>(r.cand[li * kCap]) |
+                           (static_cast<int>(r.cand[li * kCap + 1]) << 16);
+          const uint32_t *bm = r.bitmaps + static_cast<int64_t>(slot) * kBitmapWords;
+          for (int w = 0; w < kBitmapWords; ++w) {
+            uint32_t word = __ldg(bm + w);
+            while (word) {
+              const int b = __ffs(word) - 1;
+              word &= word - 1;
+              rescore_chunk(v, r.cb_raw, w * 32 + b, lane, bs, bj);
+              ++chunks;
+            }
+          }
+        } else {
+          for (int k = 0; k < cn; ++k) {
+            if (!(r.cand_sc[li * kCap + k] >= thr)) continue;
+            rescore_chunk(v, r.cb_raw, r.cand[li * kCap + k], lane, bs, bj);
             ++chunks;
           }
         }
-      } else {
-        for (int k = 0; k < cn; ++k) rescore_chunk(v, r.cb_raw, r.cand[a * kCap + k], lane, bs, bj);
-        chunks = cn;
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
@@ -756,7 +836,7 @@ __global__ void __launch_bounds__(256) rescore_kernel(const __grid_constant__ Se
       if (lane == 0) {
         r.out[a] = chunks > 0 ? apply_rule(bs, bj, r.rule) : 0;
         atomicAdd(&block_chunks, chunks);
-        if (cn == kBitmapMode) atomicAdd(&block_bitmap, 1);
+        if (used_bitmap) atomicAdd(&block_bitmap, 1);
       }
     }
   }
@@ -840,11 +920,12 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
   const int64_t pad_max = nb_max * kBlockAtoms;
   const int64_t pool_slots = batch / 4 > 4096 ? batch / 4 : 4096;
   auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
-  const size_t off_two_e = up(static_cast<size_t>(nb_max) * kATileBytes);
+  const size_t off_two_e = up(static_cast<size_t>(pad_max) * kHiBytes);
   const size_t off_cand = off_two_e + up(pad_max * sizeof(float));
-  const size_t off_cand_n = off_cand + up(pad_max * kCap * sizeof(uint16_t));
-  const size_t off_best = off_cand_n + up(pad_max);
-  const size_t off_ovf = off_best + up(pad_max * sizeof(float));
+  const size_t off_cand_sc = off_cand + up(pad_max * 2 * kCap * sizeof(uint16_t));
+  const size_t off_cand_n = off_cand_sc + up(pad_max * 2 * kCap * sizeof(float));
+  const size_t off_best = off_cand_n + up(pad_max * 2);
+  const size_t off_ovf = off_best + up(pad_max * 2 * sizeof(float));
   const size_t off_bm = off_ovf + up(batch * sizeof(int32_t));
   const size_t off_cnt = off_bm + up(static_cast<size_t>(pool_slots) * kBitmapWords * 4);
   const size_t bytes = off_cnt + 256;
@@ -873,9 +954,10 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
     const int64_t nb = (nbatch + kBlockAtoms - 1) / kBlockAtoms;
     const int64_t npad = nb * kBlockAtoms;
     int32_t *ob = out_idx + done;
-    uint8_t *a_tiled = scratch;
+    uint8_t *a_hi = scratch;
     float *two_e = reinterpret_cast<float *>(scratch + off_two_e);
     uint16_t *cand = reinterpret_cast<uint16_t *>(scratch + off_cand);
+    float *cand_sc = reinterpret_cast<float *>(scratch + off_cand_sc);
     uint8_t *cand_n = scratch + off_cand_n;
     float *best = reinterpret_cast<float *>(scratch + off_best);
     int32_t *ovf_list = reinterpret_cast<int32_t *>(scratch + off_ovf);
@@ -884,10 +966,11 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
     int32_t *slot_count = ovf_count + 1;
     cudaError_t e = cudaMemsetAsync(ovf_count, 0, 2 * sizeof(int32_t), s);
     if (e != cudaSuccess) { rc = cuda_fail(e, "memset"); break; }
-    prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(sg, nbatch, npad, a_tiled,
+    prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(sg, nbatch, npad, a_hi,
                                                                         two_e);
-    ScreenArgs sa{a_tiled, two_e, reinterpret_cast<const uint8_t *>(t->cb_tiled), cand, cand_n,
-                  best, bitmaps, slot_count, static_cast<int32_t>(pool_slots), nbatch, nb, t->err};
+    ScreenArgs sa{a_hi, two_e, reinterpret_cast<const uint8_t *>(t->cb_tiled), cand, cand_sc,
+                  cand_n, best, bitmaps, slot_count, static_cast<int32_t>(pool_slots), nbatch, nb,
+                  t->err};
     const int grid = static_cast<int>(nb < sms ? nb : sms);
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     if (timing_enabled()) {
@@ -900,7 +983,7 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
       cudaEventRecord(ev1, s);
       timing_record(ev0, ev1);
     }
-    RescoreArgs ra{cand, cand_n, best, two_e, bitmaps, t->cb_raw, ob, ovf_list, ovf_count,
+    RescoreArgs ra{cand, cand_sc, cand_n, best, two_e, bitmaps, t->cb_raw, ob, ovf_list, ovf_count,
                    t->stats, nbatch, rule};
     const int64_t rthreads = nbatch * 32;
     rescore_kernel<<<static_cast<unsigned>((rthreads + 255) / 256), 256, 0, s>>>(sg, ra);
