@@ -267,6 +267,9 @@ def run_ours(args) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_baseline()
+    comps = None
+    if rank == 0 and world == 1 and not args.skip_components:
+        comps = run_components(args)
 
     if rank == 0:
         out = {
@@ -291,6 +294,7 @@ def run_ours(args) -> None:
                              "chunks_rescored": chunks},
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "hbm_kernels": comps,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -364,6 +368,91 @@ def run_search_only(args) -> None:
                       "algorithmic_TFLOPs": atoms_s * FLOP_PER_ATOM / 1e12}), flush=True)
 
 
+def run_components(args) -> dict:
+    """HBM-bound kernels on config 5: the packed indices of 18 [7680,1920]
+    layers (11,059,200 indices, uniform in [0,196560]) -- 18-bit pack of the
+    int32 indices, unpack back to int32, and LUT dequant of all 18 layers to
+    fp16 in one batched launch.  Each call is timed alone with CUDA events on
+    the current stream after an L2 flush (a 512 MB write)."""
+    import ctypes
+    import torch
+    from pollux_b200 import castor, synth
+    from pollux_b200 import _native as N
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layers = 18
+    rows, in_f = synth.CONFIG5_SHAPE
+    per = rows * in_f // 24
+    idx_l, sig_l = [], []
+    for l in range(layers):
+        i, sg = synth.config5_layer(seed=5 + l, device=dev)
+        idx_l.append(i)
+        sig_l.append(sg)
+    idx = torch.cat(idx_l)
+    n = idx.numel()
+    packed = torch.empty(((n + 3) // 4) * 9, dtype=torch.uint8, device=dev)
+    back = torch.empty(n, dtype=torch.int32, device=dev)
+    outs = [torch.empty(rows, in_f, dtype=torch.float16, device=dev) for _ in range(layers)]
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    lib = N.load()
+    per_layer_bytes = per // 4 * 9
+
+    def pack():
+        N.check(lib.h24_pack(idx.data_ptr(), n, packed.data_ptr(), stream), "pack")
+
+    def unpack():
+        N.check(lib.h24_unpack(packed.data_ptr(), packed.numel() // 9, n, back.data_ptr(), stream),
+                "unpack")
+
+    def dequant():
+        L = (N.DequantLayer * layers)()
+        for l in range(layers):
+            L[l] = N.DequantLayer(packed.data_ptr() + l * per_layer_bytes, sig_l[l].data_ptr(),
+                                  outs[l].data_ptr(), rows, in_f)
+        N.check(lib.h24_dequant_batched(ctypes.cast(L, ctypes.c_void_p), layers, bad.data_ptr(),
+                                        stream), "dequant")
+
+    def timed(fn, reps):
+        ts = []
+        for i in range(reps + 3):
+            flush.fill_(i & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            if i >= 3:
+                ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    reps = max(5, args.steps)
+    t_pack = timed(pack, reps)
+    t_unpack = timed(unpack, reps)
+    t_deq = timed(dequant, reps)
+    torch.cuda.synchronize()
+    assert torch.equal(back, idx), "pack/unpack round trip failed"
+    assert int(bad.item()) == 0
+    peak = 6557.1
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["hbm_gbs"])
+    except (OSError, ValueError, KeyError):
+        pass
+    pack_bytes = n * 4 + packed.numel()
+    deq_bytes = packed.numel() + layers * rows * 2 + layers * rows * in_f * 2
+    res = {}
+    for name, t, b in (("pack", t_pack, pack_bytes), ("unpack", t_unpack, pack_bytes),
+                       ("dequant", t_deq, deq_bytes)):
+        gbs = b / (t / 1e3) / 1e9
+        res[name] = {"ms": t, "algorithmic_bytes": b, "GB_per_s": gbs, "frac_of_measured_hbm": gbs / peak}
+    res["workload"] = ("config5: 18 layers x [7680,1920], 11,059,200 uniform indices; pack int32->18-bit, "
+                       "unpack 18-bit->int32, batched LUT dequant to fp16; L2 flushed before each call")
+    res["hbm_peak_gbs"] = peak
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -374,9 +463,14 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--search-atoms", type=int, default=0,
                     help="profile mode: time only the search on this many atoms")
+    ap.add_argument("--components", action="store_true",
+                    help="time the HBM-bound kernels (pack/unpack/dequant) on config 5 only")
+    ap.add_argument("--skip-components", action="store_true")
     args = ap.parse_args()
     if args.search_atoms:
         run_search_only(args)
+    elif args.components:
+        print(json.dumps(run_components(args)), flush=True)
     elif args.impl == "reference":
         run_reference(args)
     else:

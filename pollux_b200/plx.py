@@ -74,7 +74,15 @@ def read_plx(path: str, device: torch.device | str | None = None) -> dict[str, A
     with open(path, "rb") as fh:
         mm = mmap.mmap(fh.fileno(), 0, access=mmap.ACCESS_READ)
     try:
-        buf = memoryview(mm)
+        return _parse(path, mm, device)
+    finally:
+        mm.close()
+
+
+def _parse(path: str, mm: mmap.mmap, device) -> dict[str, Any]:
+    # Every view of the mapping lives in this frame, so all of them are gone
+    # (also after an exception) before the caller closes the mapping.
+    with memoryview(mm) as buf:
         if bytes(buf[:8]) != PLX_MAGIC:
             raise ValueError(f"{path!r} is not a .plx file (bad magic {bytes(buf[:8])!r}).")
         (version,) = struct.unpack_from("B7x", buf, 8)
@@ -104,13 +112,12 @@ def read_plx(path: str, device: torch.device | str | None = None) -> dict[str, A
             if pos + nbytes > len(buf):
                 raise ValueError(f"{path!r} is truncated inside tensor {name!r}")
             np_dtype = _ID_TO_NUMPY.get(dtype_id, np.dtype("float32"))
-            arr = np.frombuffer(buf[pos:pos + nbytes], dtype=np_dtype).reshape(shape)
+            with buf[pos:pos + nbytes] as view:
+                arr = np.frombuffer(view, dtype=np_dtype).reshape(shape)
+                state[name] = (torch.from_numpy(arr.copy()) if device is None
+                               else _to_device(arr, device))
+                del arr
             pos += nbytes
-            t = torch.from_numpy(arr.copy()) if device is None else _to_device(arr, device)
-            state[name] = t
-        del buf
-    finally:
-        mm.close()
     return {"format": "pollux_packed_v4", "config": config,
             "codebook_fingerprint": fingerprint, "state_dict": state}
 
