@@ -110,6 +110,19 @@ int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad
  * maximum; an fp64 rescore picks the winner. */
 int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *stream);
 
+/* ---- allocation-free nearest codeword (no counterpart in the reference) --
+ * Same result as h24_quantize for callers that must not allocate device
+ * memory at call time (code under an external memory manager that owns every
+ * device allocation, or latency-critical loops).  All per-call scratch lives
+ * in one fixed device array of about 10.5 MB inside the library, so the call
+ * makes no cudaMalloc, cudaMallocAsync or cudaFree.  Limits: at most 32768
+ * atoms per call (more is H24_ERR_INVALID); the codebook tables must already
+ * be resident (call h24_init(device) once at set-up, else H24_ERR_STATE); the
+ * first call on a device resolves the array's address (make it before any
+ * stream capture); the array is shared by every call on the device and keeps
+ * the last call's contents, so calls that overlap on the GPU race. */
+int h24_quantize_noalloc(const float *x, int64_t n, int rule, int32_t *out_idx, void *stream);
+
 /* ---- nearest codeword over several inputs in one pipeline ---------------
  * Segment i holds counts[i] atoms of 24 fp32 values at xs[i] (device
  * pointers, 16-byte aligned; `xs` and `counts` are host arrays read before the

@@ -148,6 +148,15 @@ const Tables *tables_for_current_device() {
   return &g_tables[dev];
 }
 
+// Tables of the current device if they are already built, else nullptr; never
+// allocates (used by the allocation-free entry point).
+const Tables *tables_if_ready() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_tables_mu);
+  return g_tables_ok[dev] ? &g_tables[dev] : nullptr;
+}
+
 // ---------------------------------------------------------------------------
 // instrumentation
 // ---------------------------------------------------------------------------

@@ -59,6 +59,8 @@ struct Tables {
 // Returns the tables of the current device, building them on first use.
 // nullptr on failure (message set).
 const Tables *tables_for_current_device();
+// Tables of the current device only if already built (never allocates).
+const Tables *tables_if_ready();
 
 // Error helpers (thread-local message).
 const char *last_error_cstr();

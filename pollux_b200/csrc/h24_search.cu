@@ -1003,4 +1003,136 @@ int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_
   return quantize_segments(t, &x, &n, 1, rule, out_idx, s);
 }
 
+
+
+// ===========================================================================
+// Allocation-free variant of the nearest-codeword pipeline.
+//
+// Some callers must not allocate device memory at call time: code running
+// under an external memory manager that owns every device allocation (a
+// framework's caching allocator or a serving runtime with a fixed memory
+// budget), or latency-critical loops where an allocation call would stall or
+// fragment memory.  For them h24_quantize_noalloc runs the same kernels with
+// all per-call scratch in one file-scope device array of fixed size, so it
+// calls no cudaMalloc, cudaMallocAsync, cudaFree or other allocating routine.
+//
+// Limits and rules:
+//   * at most kNoAllocMaxAtoms atoms per call (larger calls are rejected);
+//   * the codebook tables must already be resident: call h24_init(device)
+//     (or any other h24 entry point) once at set-up, because building them
+//     allocates; this entry point returns H24_ERR_STATE otherwise;
+//   * the first call on a device resolves the array's device address with
+//     cudaGetSymbolAddress (set-up work, no allocation); make that first call
+//     before any stream capture;
+//   * every call on a device shares the one array and it keeps the previous
+//     call's contents: the counters that must start at zero are cleared at
+//     the start of each call, everything else is written before it is read.
+//     Calls whose executions overlap on the GPU (other streams or host
+//     threads without ordering) race on the array.
+// ===========================================================================
+namespace {
+
+constexpr int64_t kNoAllocMaxAtoms = 32768;
+constexpr int64_t kNoAllocPad = kNoAllocMaxAtoms;  // a multiple of kBlockAtoms
+constexpr int64_t kNoAllocSlots = kNoAllocMaxAtoms / 4;
+constexpr size_t na_up(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+constexpr size_t kNaTwoE = na_up(kNoAllocPad * kHiBytes);
+constexpr size_t kNaCand = kNaTwoE + na_up(kNoAllocPad * sizeof(float));
+constexpr size_t kNaCandSc = kNaCand + na_up(kNoAllocPad * 2 * kCap * sizeof(uint16_t));
+constexpr size_t kNaCandN = kNaCandSc + na_up(kNoAllocPad * 2 * kCap * sizeof(float));
+constexpr size_t kNaBest = kNaCandN + na_up(kNoAllocPad * 2);
+constexpr size_t kNaOvf = kNaBest + na_up(kNoAllocPad * 2 * sizeof(float));
+constexpr size_t kNaBm = kNaOvf + na_up(kNoAllocMaxAtoms * sizeof(int32_t));
+constexpr size_t kNaCnt = kNaBm + na_up(static_cast<size_t>(kNoAllocSlots) * kBitmapWords * 4);
+constexpr size_t kNoAllocBytes = kNaCnt + 256;  // about 10.5 MB
+static_assert(kNoAllocMaxAtoms % kBlockAtoms == 0, "whole CTA work items");
+static_assert(kNoAllocBytes < (size_t(16) << 20), "modest fixed footprint");
+
+// The scratch array.  In host code this name is a host-side stand-in, not a
+// device address: host code must use the address from cudaGetSymbolAddress.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_ptr[64] = {};
+
+// Per-device set-up: resolve the array's device address (once, with the device
+// current) and allow the screening kernel its dynamic shared memory.
+int noalloc_setup(int dev, uint8_t **out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+    e = cudaFuncSetAttribute(screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sizeof(ScreenSmem) + 1024));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    g_noalloc_ptr[dev] = static_cast<uint8_t *>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return H24_OK;
+}
+
+int quantize_noalloc(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
+                     cudaStream_t s) {
+  uint8_t *scratch = nullptr;
+  int rc = noalloc_setup(t->device, &scratch);
+  if (rc != H24_OK) return rc;
+  int sms = 0;
+  H24_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, t->device));
+  Segs sg;
+  sg.count = 1;
+  sg.x[0] = x;
+  sg.start[0] = 0;
+  sg.start[1] = n;
+  const int64_t nb = (n + kBlockAtoms - 1) / kBlockAtoms;
+  const int64_t npad = nb * kBlockAtoms;
+  uint8_t *a_hi = scratch;
+  float *two_e = reinterpret_cast<float *>(scratch + kNaTwoE);
+  uint16_t *cand = reinterpret_cast<uint16_t *>(scratch + kNaCand);
+  float *cand_sc = reinterpret_cast<float *>(scratch + kNaCandSc);
+  uint8_t *cand_n = scratch + kNaCandN;
+  float *best = reinterpret_cast<float *>(scratch + kNaBest);
+  int32_t *ovf_list = reinterpret_cast<int32_t *>(scratch + kNaOvf);
+  uint32_t *bitmaps = reinterpret_cast<uint32_t *>(scratch + kNaBm);
+  int32_t *ovf_count = reinterpret_cast<int32_t *>(scratch + kNaCnt);
+  int32_t *slot_count = ovf_count + 1;
+  // The array keeps the previous call's contents: clear the two counters.
+  H24_CUDA_TRY(cudaMemsetAsync(ovf_count, 0, 2 * sizeof(int32_t), s));
+  prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(sg, n, npad, a_hi, two_e);
+  ScreenArgs sa{a_hi, two_e, reinterpret_cast<const uint8_t *>(t->cb_tiled), cand, cand_sc,
+                cand_n, best, bitmaps, slot_count, static_cast<int32_t>(kNoAllocSlots), n, nb,
+                t->err};
+  screen_kernel<<<static_cast<int>(nb < sms ? nb : sms), kScreenThreads, sizeof(ScreenSmem) + 1024,
+                  s>>>(sa);
+  RescoreArgs ra{cand, cand_sc, cand_n, best, two_e, bitmaps, t->cb_raw, out_idx, ovf_list,
+                 ovf_count, t->stats, n, rule};
+  rescore_kernel<<<static_cast<unsigned>((n * 32 + 255) / 256), 256, 0, s>>>(sg, ra);
+  exhaustive_kernel<<<2 * sms, 256, 0, s>>>(sg, rule, ovf_list, ovf_count, t->cb_raw, out_idx);
+  count_launches(4);
+  H24_CUDA_TRY(cudaGetLastError());
+  return H24_OK;
+}
+
+}  // namespace
 }  // namespace h24
+
+extern "C" int h24_quantize_noalloc(const float *x, int64_t n, int rule, int32_t *out_idx,
+                                    void *stream) {
+  using namespace h24;
+  if (n < 0) return fail(H24_ERR_INVALID, "quantize_noalloc: negative atom count");
+  if (n > kNoAllocMaxAtoms)
+    return fail(H24_ERR_INVALID, "quantize_noalloc: " + std::to_string(n) +
+                                     " atoms exceed the allocation-free limit of " +
+                                     std::to_string(kNoAllocMaxAtoms) + " atoms per call");
+  if (rule != H24_RULE_TRAIN && rule != H24_RULE_PACK)
+    return fail(H24_ERR_INVALID, "quantize_noalloc: unknown rule");
+  if (n == 0) return H24_OK;
+  if (!x || !out_idx) return fail(H24_ERR_INVALID, "quantize_noalloc: null pointer");
+  if (!aligned16(x)) return fail(H24_ERR_INVALID, "quantize_noalloc: x must be 16-byte aligned");
+  const Tables *t = tables_if_ready();
+  if (!t)
+    return fail(H24_ERR_STATE,
+                "quantize_noalloc: codebook tables are not resident on this device; call "
+                "h24_init(device) once at set-up (it allocates them)");
+  return quantize_noalloc(t, x, n, rule, out_idx, static_cast<cudaStream_t>(stream));
+}
