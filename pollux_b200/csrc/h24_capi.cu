@@ -3,7 +3,9 @@
 // pack-rule row-scale kernel.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -49,7 +51,7 @@ bool g_tables_ok[kMaxDevices] = {};
 struct HostTables {
   std::vector<int8_t> raw;        // [kKissing][24]
   std::vector<uint16_t> tiled;    // [kKissing][32] bf16 bits, tiled
-  std::vector<uint32_t> nib;      // [kCount][3]
+  std::vector<uint32_t> nib;      // [kCount][4] dequant codes
   float fingerprint[16];
   bool ok = false;
   std::string err;
@@ -78,13 +80,37 @@ const HostTables &host_tables() {
         H.tiled[byte / 2] = bf16_bits_of_int(H.raw[static_cast<size_t>(j) * kDim + k]);
       }
     }
-    H.nib.assign(static_cast<size_t>(kCount) * 3, 0);
-    for (int row = 0; row < kCount; ++row)
+    // Dequant codes, 16 bytes per codeword (word k = elements 8k..8k+7, one
+    // nibble each; word 3 is zero).  A codeword takes at most four distinct
+    // values, fixed by its type: {+1,-1,+3,-3} (one 3, 23 ones), {0,+2,-2}
+    // (eight twos; also the origin) or {0,+4,-4} (two fours).  Nibble bits
+    // 0-1 index the type's value list (dequant_value_lists in h24_dequant.cu
+    // holds the same orders), bit 2 of nibbles 0 and 1 of every word holds
+    // the list selector (0, 1, 2), bit 3 stays zero.
+    H.nib.assign(static_cast<size_t>(kCount) * 4, 0);
+    for (int row = 0; row < kCount && H.err.empty(); ++row) {
+      const int8_t *cw = row == 0 ? nullptr : &H.raw[static_cast<size_t>(row - 1) * kDim];
+      int maxabs = 0;
+      for (int k = 0; k < kDim; ++k) maxabs = std::max(maxabs, cw ? std::abs(int(cw[k])) : 0);
+      const int list = maxabs == 4 ? 2 : (maxabs == 3 ? 0 : 1);
       for (int k = 0; k < kDim; ++k) {
-        const int raw = row == 0 ? 0 : H.raw[static_cast<size_t>(row - 1) * kDim + k];
-        H.nib[static_cast<size_t>(row) * 3 + k / 8] |= static_cast<uint32_t>(raw + 4)
-                                                       << (4 * (k % 8));
+        const int raw = cw ? cw[k] : 0;
+        int code = -1;
+        if (list == 0) code = raw == 1 ? 0 : raw == -1 ? 1 : raw == 3 ? 2 : raw == -3 ? 3 : -1;
+        if (list == 1) code = raw == 0 ? 0 : raw == 2 ? 1 : raw == -2 ? 2 : -1;
+        if (list == 2) code = raw == 0 ? 3 : raw == 4 ? 1 : raw == -4 ? 2 : -1;
+        if (code < 0) {
+          H.err = "codeword " + std::to_string(row) + " mixes value types";
+          break;
+        }
+        const int e = k % 8;
+        uint32_t nib = static_cast<uint32_t>(code);
+        if (e == 0) nib |= static_cast<uint32_t>(list & 1) << 2;
+        if (e == 1) nib |= static_cast<uint32_t>(list >> 1) << 2;
+        H.nib[static_cast<size_t>(row) * 4 + k / 8] |= nib << (4 * e);
       }
+    }
+    if (!H.err.empty()) return;
     for (int r = 0; r < 4; ++r)
       for (int c = 0; c < 4; ++c)
         H.fingerprint[r * 4 + c] =

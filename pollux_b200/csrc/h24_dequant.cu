@@ -6,24 +6,45 @@
 // where v is the raw Leech coordinate (-4..4) of the element's codeword and
 // cb16[v] = fp16(v * fp32(1/sqrt(8))).  Both roundings of the reference are
 // reproduced, so the result is bit-identical given the same indices and
-// scales.  The codebook is read as 4-bit codes (12 bytes per codeword, 2.4 MB,
-// L2-resident); the per-row values live in a shared-memory LUT built once per
-// tile.  The kernel is bound by the 48-byte fp16 output per atom: each warp
-// writes its 32 atoms (1536 bytes) as three fully coalesced 512-byte stores.
+// scales.
+//
+// The kernel is bound by the 48-byte fp16 output per atom.  A codeword holds
+// at most four distinct coordinates, fixed by its type, so the codebook is
+// stored as 2-bit positions in a per-type value list (16 bytes per codeword,
+// one 32-byte sector, 3.1 MB, L2-resident) and two output values come from
+// one byte permute (prmt) of the row's values for that list: per 8 elements,
+// one 4-byte gather, six prmt and one 16-byte store.  Each warp owns an equal
+// contiguous range of atoms (one resident wave, no block barriers) and walks
+// it in sub-tiles of up to 128 atoms; the per-row value lists live in an
+// 8-row shared-memory ring.
+#include <cstddef>
+
 #include "h24_internal.cuh"
 
 namespace h24 {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kTileAtoms = kThreads;  // one atom per thread and tile
-constexpr int kMaxBatch = 64;  // keeps the kernel parameter block under 4 KB
+constexpr int kWarpsPerBlock = kThreads / 32;
+constexpr int kSub = 128;        // atoms per sub-tile
+constexpr int kSlots = 8;        // rows in the per-warp value-list ring
+constexpr int kMaxBatch = 64;    // keeps the kernel parameter block under 4 KB
 
 struct DequantBatch {
   h24_dequant_layer layer[kMaxBatch];
-  int64_t tile_start[kMaxBatch + 1];
+  int64_t atom_start[kMaxBatch + 1];  // atoms before each layer
   int count;
 };
+
+// Per-warp shared memory: the sub-tile's packed bytes, the decoded
+// (index, ring slot) of its atoms and the value lists of up to 8 rows.
+struct WarpSmem {
+  alignas(16) uint32_t lists[kSlots][8];  // [slot][2*list .. 2*list+1] = a prmt source pair
+  uint32_t info[kSub];
+  uint8_t packed[9 * 33 + 3];
+};
+static_assert(offsetof(WarpSmem, lists) % 8 == 0 && sizeof(WarpSmem) % 16 == 0,
+              "value lists are read as 8-byte pairs");
 
 __device__ __forceinline__ uint16_t dequant_value(int raw, uint16_t sigma_bits) {
   const __half cb = __float2half_rn(static_cast<float>(raw) * kLeechScaleF);
@@ -33,77 +54,150 @@ __device__ __forceinline__ uint16_t dequant_value(int raw, uint16_t sigma_bits) 
   return __half_as_ushort(w);
 }
 
-__global__ void __launch_bounds__(kThreads) dequant_kernel(const __grid_constant__ DequantBatch b,
-                                                           const uint32_t *__restrict__ cb_nib,
-                                                           int32_t *__restrict__ bad) {
-  __shared__ uint16_t lut[kTileAtoms][16];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int64_t total = b.tile_start[b.count];
-  for (int64_t tile = blockIdx.x; tile < total; tile += gridDim.x) {
-    int li = 0;
-    while (li + 1 < b.count && b.tile_start[li + 1] <= tile) ++li;
-    const h24_dequant_layer L = b.layer[li];
-    const int64_t apr = L.in_features / kDim;
-    const int64_t atoms = L.rows * apr;
-    const int64_t a0 = (tile - b.tile_start[li]) * kTileAtoms;
-    const int64_t a_last = (a0 + kTileAtoms < atoms ? a0 + kTileAtoms : atoms) - 1;
-    const int64_t r_first = a0 / apr;
-    const int nrows = static_cast<int>(a_last / apr - r_first + 1);
-
-    // Per-row LUT: lut[row - r_first][raw + 4].
-    for (int e = threadIdx.x; e < nrows * 9; e += kThreads) {
-      const int rl = e / 9, code = e - rl * 9;
-      lut[rl][code] = dequant_value(code - 4, L.sigma16[r_first + rl]);
+// Value lists of rows r_lo..r_hi (at most kSlots) into their ring slots, the
+// code orders of h24_capi.cu's table:
+//   list 0 {+1,-1,+3,-3}, list 1 {0,+2,-2,+4}, list 2 {-2,+4,-4,0},
+// stored as six words of two fp16 values (one prmt source pair per list).
+// Lane 8j+k computes word k of row r_lo+j, so 4 rows take one pass.
+__device__ __forceinline__ void build_lists(uint32_t (*lists)[8], const uint16_t *sigma16,
+                                            int64_t r_lo, int64_t r_hi, int lane) {
+  const int k = lane & 7;
+  // (lo, hi) raw coordinates of word k, packed as nibbles lo+4 | (hi+4) << 4.
+  constexpr uint32_t kPairs = 0x82641735u;  // words 0-3: (1,-1) (3,-3) (0,2) (-2,4)
+  const uint32_t pair = k < 4 ? (kPairs >> (8 * k)) & 0xFFu : (k == 4 ? 0x82u : 0x40u);  // (-2,4) (-4,0)
+  for (int64_t r = r_lo + (lane >> 3); r <= r_hi; r += 4) {
+    if (k < 6) {
+      const uint16_t sg = __ldg(sigma16 + r);
+      const uint32_t lo = dequant_value(static_cast<int>(pair & 15u) - 4, sg);
+      const uint32_t hi = dequant_value(static_cast<int>(pair >> 4) - 4, sg);
+      lists[r & (kSlots - 1)][k] = lo | (hi << 16);
     }
-    __syncthreads();
-
-    // Each lane decodes the index of its own atom.
-    const int64_t wa0 = a0 + warp * 32;
-    const int64_t atom = wa0 + lane;
-    uint32_t info = 0;
-    bool bad_idx = false;
-    if (atom < atoms) {
-      const int64_t g = atom >> 2;
-      const int k = static_cast<int>(atom & 3);
-      const uint8_t *p = L.packed + 9 * g + 2 * k;
-      const uint32_t v24 = (static_cast<uint32_t>(__ldg(p)) << 16) |
-                           (static_cast<uint32_t>(__ldg(p + 1)) << 8) | __ldg(p + 2);
-      uint32_t idx = (v24 >> (6 - 2 * k)) & 0x3FFFFu;
-      if (idx > static_cast<uint32_t>(kKissing)) {
-        bad_idx = true;
-        idx = 0;
-      }
-      const uint32_t rl = static_cast<uint32_t>(atom / apr - r_first);
-      info = idx | (rl << 18);
-    }
-    const unsigned nbad = __popc(__ballot_sync(0xffffffffu, bad_idx));
-    if (lane == 0 && nbad && bad) atomicAdd(bad, static_cast<int32_t>(nbad));
-
-    // 32 atoms x 48 bytes = 96 uint4 per warp; lane writes uint4 lane+32j.
-#pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      const int v = lane + 32 * j;
-      const int src = v / 3;
-      const int part = v - 3 * src;
-      const uint32_t inf = __shfl_sync(0xffffffffu, info, src);
-      if (wa0 + src < atoms) {
-        const uint32_t idx = inf & 0x3FFFFu;
-        const uint16_t *row = lut[inf >> 18];
-        const uint32_t word = __ldg(cb_nib + 3 * idx + part);
-        uint32_t o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t lo = row[(word >> (8 * e)) & 0xF];
-          const uint32_t hi = row[(word >> (8 * e + 4)) & 0xF];
-          o[e] = lo | (hi << 16);
-        }
-        uint4 *dst = reinterpret_cast<uint4 *>(L.out16 + (wa0 + src) * kDim + part * 8);
-        __stcs(dst, make_uint4(o[0], o[1], o[2], o[3]));
-      }
-    }
-    __syncthreads();
   }
+}
+
+// 8 fp16 outputs from one code word: nibble e -> element e.
+__device__ __forceinline__ uint4 expand8(uint32_t w, const uint32_t *lists) {
+  // Code c -> the prmt selector pair (2c, 2c+1) of fp16 value c; the list bit
+  // (bit 2) only selects the identical upper copy of the table.
+  constexpr uint32_t kSel = 0x76543210u;
+  const uint32_t list = ((w >> 2) & 1u) | ((w >> 5) & 2u);
+  const uint2 src = reinterpret_cast<const uint2 *>(lists)[list];
+  const uint32_t s_lo = __byte_perm(kSel, kSel, w);
+  const uint32_t s_hi = __byte_perm(kSel, kSel, w >> 16);
+  uint4 o;
+  o.x = __byte_perm(src.x, src.y, s_lo);
+  o.y = __byte_perm(src.x, src.y, s_lo >> 16);
+  o.z = __byte_perm(src.x, src.y, s_hi);
+  o.w = __byte_perm(src.x, src.y, s_hi >> 16);
+  return o;
+}
+
+__global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_constant__ DequantBatch b,
+                                                           const uint32_t *__restrict__ codes,
+                                                           int32_t *__restrict__ bad) {
+  __shared__ WarpSmem smem[kWarpsPerBlock];
+  const int lane = threadIdx.x & 31;
+  WarpSmem &W = smem[threadIdx.x >> 5];
+  const int64_t total = b.atom_start[b.count];
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
+  const int64_t wid = blockIdx.x * static_cast<int64_t>(kWarpsPerBlock) + (threadIdx.x >> 5);
+  const int64_t per = (total + nwarps - 1) / nwarps;
+  const int64_t g_end = (wid + 1) * per < total ? (wid + 1) * per : total;
+  // Output mapping: 10 atoms x 3 parts per round, lanes 30-31 idle, so the
+  // three gathers of one atom share one request.
+  const int my_atom = lane / 3, my_part = lane - 3 * (lane / 3);
+  int li = -1;
+  int64_t row = 0;     // row of the next atom
+  int32_t off = 0;     // its position in the row
+  int32_t apr = 1;     // atoms per row of layer li
+  int64_t built_hi = -1;
+  unsigned nbad = 0;
+  for (int64_t g = wid * per; g < g_end;) {
+    if (li < 0 || b.atom_start[li + 1] <= g) {  // entering a layer
+      while (b.atom_start[li + 1] <= g) ++li;
+      apr = static_cast<int32_t>(b.layer[li].in_features / kDim);
+      const int64_t la = g - b.atom_start[li];
+      row = la / apr;
+      off = static_cast<int32_t>(la - row * apr);
+      built_hi = row - 1;
+    }
+    const h24_dequant_layer &L = b.layer[li];
+    const int64_t la0 = g - b.atom_start[li];
+    int64_t lim = b.atom_start[li + 1] - g;
+    if (g_end - g < lim) lim = g_end - g;
+    if (7 * static_cast<int64_t>(apr) < lim) lim = 7 * static_cast<int64_t>(apr);  // <= kSlots rows
+    const int na = static_cast<int>(lim < kSub ? lim : kSub);
+    const int64_t r1 = row + static_cast<uint32_t>(off + na - 1) / static_cast<uint32_t>(apr);
+
+    // 1. Packed bytes of the groups the sub-tile touches.
+    const int q0 = static_cast<int>(la0 & 3);
+    const int nbytes = 9 * ((q0 + na - 1) / 4 + 1);
+    const uint8_t *src = L.packed + 9 * (la0 >> 2);
+    {
+      constexpr int kLoads = (sizeof(W.packed) + 31) / 32;
+      uint8_t v[kLoads];
+#pragma unroll
+      for (int i = 0; i < kLoads; ++i)
+        if (lane + 32 * i < nbytes) v[i] = __ldcs(src + lane + 32 * i);
+#pragma unroll
+      for (int i = 0; i < kLoads; ++i)
+        if (lane + 32 * i < nbytes) W.packed[lane + 32 * i] = v[i];
+    }
+    // 2. Value lists of rows not yet in the ring.
+    if (r1 > built_hi) {
+      build_lists(W.lists, L.sigma16, built_hi + 1 > row ? built_hi + 1 : row, r1, lane);
+      built_hi = r1;
+    }
+    __syncwarp();
+    // 3. 18-bit index and ring slot of each atom.
+#pragma unroll
+    for (int k = 0; k < kSub / 32; ++k) {
+      const int a = lane + 32 * k;
+      if (a < na) {
+        const int sa = q0 + a, q = sa & 3;
+        const uint8_t *p = W.packed + 9 * (sa >> 2) + 2 * q;
+        const uint32_t v24 = (static_cast<uint32_t>(p[0]) << 16) | (static_cast<uint32_t>(p[1]) << 8) | p[2];
+        uint32_t idx = (v24 >> (6 - 2 * q)) & 0x3FFFFu;
+        if (idx > static_cast<uint32_t>(kKissing)) {
+          ++nbad;
+          idx = 0;
+        }
+        const uint32_t rl = static_cast<uint32_t>(off + a) / static_cast<uint32_t>(apr);
+        W.info[a] = idx | (static_cast<uint32_t>((row + rl) & (kSlots - 1)) << 18);
+      }
+    }
+    __syncwarp();
+    // 4. Gather all code words of the sub-tile, then expand and store.
+    constexpr int kRounds = (kSub + 9) / 10;
+    uint32_t word[kRounds], slot[kRounds];
+#pragma unroll
+    for (int m = 0; m < kRounds; ++m) {
+      const int a = 10 * m + my_atom;
+      word[m] = 0;
+      slot[m] = 0;
+      if (lane < 30 && a < na) {
+        const uint32_t inf = W.info[a];
+        slot[m] = inf >> 18;
+        word[m] = __ldg(codes + 4 * (inf & 0x3FFFFu) + my_part);
+      }
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(L.out16 + la0 * kDim);
+#pragma unroll
+    for (int m = 0; m < kRounds; ++m) {
+      const int a = 10 * m + my_atom;
+      if (lane < 30 && a < na) __stcs(dst + 3 * a + my_part, expand8(word[m], W.lists[slot[m]]));
+    }
+    __syncwarp();
+    g += na;
+    off += na;
+    if (off >= apr) {
+      const int32_t dr = static_cast<int32_t>(static_cast<uint32_t>(off) / static_cast<uint32_t>(apr));
+      row += dr;
+      off -= dr * apr;
+    }
+  }
+  const unsigned total_bad = __reduce_add_sync(0xffffffffu, nbad);
+  if (lane == 0 && total_bad && bad) atomicAdd(bad, static_cast<int32_t>(total_bad));
 }
 
 template <typename T>
@@ -153,6 +247,18 @@ int sm_count() {
   return sms;
 }
 
+// Blocks of dequant_kernel resident per SM (same on every device of a run).
+int resident_blocks() {
+  static const int n = [] {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, dequant_kernel, kThreads, 0) != cudaSuccess ||
+        v < 1)
+      v = 4;
+    return v;
+  }();
+  return n;
+}
+
 }  // namespace
 
 int launch_dequant(const Tables *t, const h24_dequant_layer * /*layers_dev*/,
@@ -160,7 +266,7 @@ int launch_dequant(const Tables *t, const h24_dequant_layer * /*layers_dev*/,
   for (int base = 0; base < count; base += kMaxBatch) {
     DequantBatch b;
     b.count = 0;
-    b.tile_start[0] = 0;
+    b.atom_start[0] = 0;
     for (int i = base; i < count && b.count < kMaxBatch; ++i) {
       const h24_dequant_layer &L = layers[i];
       if (L.rows < 0 || L.in_features <= 0 || L.in_features % kDim != 0)
@@ -170,15 +276,16 @@ int launch_dequant(const Tables *t, const h24_dequant_layer * /*layers_dev*/,
         return fail(H24_ERR_INVALID, "dequant: null pointer");
       if (!aligned16(L.out16))
         return fail(H24_ERR_INVALID, "dequant: out16 must be 16-byte aligned");
-      const int64_t atoms = L.rows * (L.in_features / kDim);
       b.layer[b.count] = L;
-      b.tile_start[b.count + 1] = b.tile_start[b.count] + (atoms + kTileAtoms - 1) / kTileAtoms;
+      b.atom_start[b.count + 1] = b.atom_start[b.count] + L.rows * (L.in_features / kDim);
       ++b.count;
     }
     if (b.count == 0) continue;
-    const int64_t tiles = b.tile_start[b.count];
-    const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
-    const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+    // One resident wave; every warp gets at least one full sub-tile.
+    const int64_t atoms = b.atom_start[b.count];
+    const int64_t want = (atoms + kSub * kWarpsPerBlock - 1) / (kSub * kWarpsPerBlock);
+    const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks();
+    const int grid = static_cast<int>(want < cap ? want : cap);
     dequant_kernel<<<grid, kThreads, 0, s>>>(b, t->cb_nib, bad);
     H24_CUDA_TRY(cudaGetLastError());
     count_launches(1);

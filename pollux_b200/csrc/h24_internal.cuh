@@ -43,8 +43,9 @@ struct Tables {
   const __nv_bfloat16 *cb_tiled = nullptr;
   // raw int8 coordinates [kKissing][24] (kissing point j = codebook row j+1).
   const int8_t *cb_raw = nullptr;
-  // 4-bit codes (raw + 4) [kCount][3] u32 words, element 8p+e in bits 4e..4e+3
-  // of word p; row 0 is the origin.
+  // Dequant codes [kCount][4] u32 words (16 bytes per codeword, row 0 is the
+  // origin): element 8p+e in nibble e of word p, bits 0-1 = position in the
+  // codeword's value list, bit 2 of nibbles 0-1 = the list (see h24_capi.cu).
   const uint32_t *cb_nib = nullptr;
   float fingerprint[16];
   // Device counters: [0] atoms sent to the exhaustive scan, [1] candidate

@@ -71,3 +71,18 @@ def test_out_of_range_index_raises(PL, oracle):
     packed = torch.from_numpy(oracle.pack_indices(np.array([5, 196561, 7, 9]))).cuda()
     with pytest.raises(IndexError):
         PL.dequant(packed, torch.ones(1, dtype=torch.float16, device="cuda"), 1, 96)
+
+
+@pytest.mark.parametrize("in_f", [24, 48, 72, 96, 120, 4608])
+def test_rows_per_tile_regimes(PL, oracle, in_f):
+    # 128-atom warp tiles span >34 rows for in_features < 96 (values computed
+    # per element) and at most 33 rows otherwise (per-warp row table).
+    from pollux_b200 import castor
+    rows = 517
+    gen = torch.Generator(device="cuda").manual_seed(in_f)
+    idx = torch.randint(0, 196561, (rows * in_f // 24,), generator=gen, device="cuda")
+    sig = (torch.rand(rows, generator=gen, device="cuda") * 0.2 + 1e-4).half()
+    packed = castor.pack_indices(idx)
+    w = PL.dequant(packed, sig, rows, in_f)
+    ref = oracle.dequant(packed.cpu().numpy(), sig.cpu().numpy(), rows, in_f)
+    assert np.array_equal(w.cpu().numpy().view(np.uint16), ref.view(np.uint16))

@@ -78,3 +78,24 @@ def test_unpack_errors(C):
     # Negative num_indices follows Python slicing like indices[:num_indices].
     p = C.pack_indices(torch.arange(8, device="cuda"))
     assert C.unpack_indices(p, -3).tolist() == [0, 1, 2, 3, 4]
+
+
+@pytest.mark.parametrize("n", [511, 512, 513, 2048 + 5, 3 * 4096 + 1])
+@pytest.mark.parametrize("dtype", [torch.int32, torch.int64])
+def test_warp_tile_boundaries(C, oracle, n, dtype):
+    gen = torch.Generator(device="cuda").manual_seed(n)
+    idx = torch.randint(0, 196561, (n,), generator=gen, device="cuda").to(dtype)
+    p = C.pack_indices(idx)
+    assert np.array_equal(p.cpu().numpy(), oracle.pack_indices(idx.cpu().numpy().astype(np.int64)))
+    back = C.unpack_indices(p, n)
+    assert torch.equal(back, idx.to(torch.int64))
+
+
+def test_unpack_capacity_below_count(C, oracle):
+    # num_indices beyond the packed capacity: only the decodable prefix comes back.
+    idx = torch.randint(0, 196561, (4 * 1000,), device="cuda")
+    p = C.pack_indices(idx)
+    for n in (4 * 1000 + 600, 4 * 1000 + 1, 8000):
+        u = C.unpack_indices(p, n)
+        ref = oracle.unpack_indices(p.cpu().numpy(), n)
+        assert np.array_equal(u.cpu().numpy(), ref)
