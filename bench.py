@@ -233,7 +233,7 @@ def run_ours(args) -> None:
     nlaunch = ctypes.c_int64(0)
     N.load().h24_timing_read(ctypes.byref(ms), ctypes.byref(nlaunch))
     N.load().h24_timing_enable(0)
-    exhaustive, bitmap, chunks = castor.quantize_stats(dev)
+    exhaustive, exact_scores, chunks = castor.quantize_stats(dev)
     elapsed_ms = t_start.elapsed_time(t_stop)
     if world > 1:
         t = torch.tensor([elapsed_ms], device=dev)
@@ -290,8 +290,8 @@ def run_ours(args) -> None:
                          "traffic": None},
             "gpu_launches": launches,
             "clocks": clk,
-            "search_stats": {"exhaustive_atoms": exhaustive, "bitmap_atoms": bitmap,
-                             "chunks_rescored": chunks},
+            "search_stats": {"exhaustive_atoms": exhaustive, "exact_scores": exact_scores,
+                             "flagged_chunks": chunks},
             "e2e": e2e,
             "cpu_baseline": cpu,
             "hbm_kernels": comps,
@@ -351,9 +351,14 @@ def run_search_only(args) -> None:
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(7)
     x = torch.randn(args.search_atoms, 24, generator=g, device=dev) * 1.4142135
+    import ctypes
+    from pollux_b200 import _native as N
     for _ in range(args.warmup):
         castor.quantize_indices(x, 1)
     torch.cuda.synchronize()
+    castor.quantize_stats(dev)
+    N.load().h24_timing_enable(1)
+    N.load().h24_timing_read(None, None)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
@@ -361,11 +366,18 @@ def run_search_only(args) -> None:
     t1.record()
     torch.cuda.synchronize()
     castor.device_check(dev)
+    screen_ms, nscreen = ctypes.c_double(0), ctypes.c_int64(0)
+    N.load().h24_timing_read(ctypes.byref(screen_ms), ctypes.byref(nscreen))
+    N.load().h24_timing_enable(0)
+    exhaustive, exact_scores, chunks = castor.quantize_stats(dev)
     ms = t0.elapsed_time(t1) / args.steps
     atoms_s = args.search_atoms / (ms / 1e3)
+    n = args.search_atoms * args.steps
     print(json.dumps({"search_atoms": args.search_atoms, "ms_per_call": ms,
                       "G_atoms_per_s": atoms_s / 1e9,
-                      "algorithmic_TFLOPs": atoms_s * FLOP_PER_ATOM / 1e12}), flush=True)
+                      "screen_ms_per_call": screen_ms.value / args.steps,
+                      "exhaustive_per_atom": exhaustive / n, "exact_scores_per_atom": exact_scores / n,
+                      "flagged_chunks_per_atom": chunks / n}), flush=True)
 
 
 def run_components(args) -> dict:

@@ -172,9 +172,9 @@ int h24_timing_read(double *ms, int64_t *launches);
 
 /* Counters accumulated by the quantize calls on the current device since the
  * previous read (reading resets them; synchronises `stream`): atoms resolved
- * by the exhaustive fp64 scan, atoms whose candidate chunks overflowed the
- * per-atom list into a bitmap, and 64-codeword chunks rescored in fp64. */
-int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *bitmap_atoms, int64_t *rescored_chunks,
+ * by the exhaustive fp64 scan, codewords scored exactly in fp64 by the
+ * rescore, and 128-codeword candidate chunks flagged by the screen. */
+int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *exact_scores, int64_t *flagged_chunks,
                        void *stream);
 
 /* Number of CUDA kernels this library has launched in this process. */

@@ -328,8 +328,8 @@ def device_check(device=None) -> None:
 
 
 def quantize_stats(device=None) -> tuple[int, int, int]:
-    """(atoms resolved by the exhaustive scan, atoms rescored from a bitmap,
-    64-codeword chunks rescored) since the last read."""
+    """(atoms resolved by the exhaustive scan, codewords scored exactly in
+    fp64, candidate chunks flagged by the screen) since the last read."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     a, b, c = ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int64(0)
     _call(dev, "h24_quantize_stats", ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), _stream(dev))

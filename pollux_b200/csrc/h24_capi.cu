@@ -9,6 +9,7 @@
 #include <cstring>
 #include <atomic>
 #include <mutex>
+#include <unordered_map>
 #include <string>
 #include <utility>
 #include <vector>
@@ -49,9 +50,11 @@ Tables g_tables[kMaxDevices];
 bool g_tables_ok[kMaxDevices] = {};
 
 struct HostTables {
-  std::vector<int8_t> raw;        // [kKissing][24]
-  std::vector<uint16_t> tiled;    // [kKissing][32] bf16 bits, tiled
-  std::vector<uint32_t> nib;      // [kCount][4] dequant codes
+  std::vector<int8_t> raw;         // [kKissing][24]
+  std::vector<uint16_t> golay;     // [kGolay][32] bf16 bits, tiled (Tables::golay_tiled)
+  std::vector<uint32_t> golay_mask;  // [kGolay]
+  std::vector<int32_t> idx3, idx2, idx1;
+  std::vector<uint32_t> nib;       // [kCount][4] dequant codes
   float fingerprint[16];
   bool ok = false;
   std::string err;
@@ -65,21 +68,118 @@ uint16_t bf16_bits_of_int(int v) {
   return static_cast<uint16_t>(u >> 16);
 }
 
+// Decomposes the kissing points into the three types (see h24_internal.cuh)
+// and fills the Golay operand and the index maps.  Fails, with a message,
+// if the codebook does not have that structure.
+bool build_structure(HostTables &H) {
+  // Type 3: the sign word w (bit i = coordinate i negative) and the position
+  // p of the -3.  The Golay codeword is w or w ^ (1 << p); it is the one of
+  // the two that occurs for all 24 positions.
+  std::unordered_map<uint32_t, int> seen;
+  std::vector<std::pair<uint32_t, int>> t3;  // (w, p) per type-3 point, with j
+  std::vector<int> t3j;
+  for (int j = 0; j < kKissing; ++j) {
+    const int8_t *r = &H.raw[static_cast<size_t>(j) * kDim];
+    int p = -1, maxabs = 0;
+    uint32_t w = 0;
+    for (int i = 0; i < kDim; ++i) {
+      maxabs = std::max(maxabs, std::abs(int(r[i])));
+      if (r[i] < 0) w |= 1u << i;
+      if (r[i] == -3) p = i;
+    }
+    if (maxabs == 3) {
+      if (p < 0) { H.err = "type-3 point without a -3"; return false; }
+      t3.emplace_back(w, p);
+      t3j.push_back(j);
+      ++seen[w];
+      ++seen[w ^ (1u << p)];
+    }
+  }
+  std::vector<uint32_t> golay;
+  for (const auto &kv : seen)
+    if (kv.second == kDim) golay.push_back(kv.first);
+  if (golay.size() != static_cast<size_t>(kGolay) || t3.size() != static_cast<size_t>(kGolay) * kDim) {
+    H.err = "type-3 points do not form Golay codeword x position pairs";
+    return false;
+  }
+  std::sort(golay.begin(), golay.end(), [](uint32_t a, uint32_t b) {
+    const int wa = __builtin_popcount(a), wb = __builtin_popcount(b);
+    return wa != wb ? wa < wb : a < b;
+  });
+  std::unordered_map<uint32_t, int> col;
+  for (int c = 0; c < kGolay; ++c) col[golay[c]] = c;
+  if (__builtin_popcount(golay[kW16First]) != 16 || __builtin_popcount(golay[kW16First - 1]) != 12 ||
+      __builtin_popcount(golay[kGolay - 1]) != 24 || __builtin_popcount(golay[kW16First + kOctads - 1]) != 16) {
+    H.err = "unexpected Golay weight distribution";
+    return false;
+  }
+  H.golay_mask = golay;
+  H.idx3.assign(static_cast<size_t>(kGolay) * kDim, -1);
+  for (size_t k = 0; k < t3.size(); ++k) {
+    const uint32_t w = t3[k].first;
+    const int p = t3[k].second;
+    auto it = col.find(w);
+    if (it == col.end()) it = col.find(w ^ (1u << p));
+    if (it == col.end()) { H.err = "type-3 point outside the Golay code"; return false; }
+    H.idx3[static_cast<size_t>(it->second) * kDim + p] = t3j[k];
+  }
+  // Types 1 and 2.
+  H.idx2.assign(static_cast<size_t>(kOctads) * 128, -1);
+  H.idx1.assign(static_cast<size_t>(kDim) * kDim * 4, -1);
+  for (int j = 0; j < kKissing; ++j) {
+    const int8_t *r = &H.raw[static_cast<size_t>(j) * kDim];
+    int maxabs = 0;
+    uint32_t nz = 0;
+    for (int i = 0; i < kDim; ++i) {
+      maxabs = std::max(maxabs, std::abs(int(r[i])));
+      if (r[i] != 0) nz |= 1u << i;
+    }
+    if (maxabs == 2) {
+      const auto it = col.find(~nz & 0xFFFFFFu);
+      const int o = it == col.end() ? -1 : it->second - kW16First;
+      if (o < 0 || o >= kOctads || __builtin_popcount(nz) != 8) { H.err = "type-2 support is not an octad"; return false; }
+      int s = 0, k = 0, minus = 0;
+      for (int i = 0; i < kDim; ++i)
+        if (nz >> i & 1) {
+          if (r[i] < 0) { ++minus; if (k < 7) s |= 1 << k; }
+          ++k;
+        }
+      if (minus & 1) { H.err = "type-2 point with an odd number of minus signs"; return false; }
+      H.idx2[static_cast<size_t>(o) * 128 + s] = j;
+    } else if (maxabs == 4) {
+      int a = -1, b = -1;
+      for (int i = 0; i < kDim; ++i)
+        if (r[i] != 0) (a < 0 ? a : b) = i;
+      if (b < 0 || __builtin_popcount(nz) != 2) { H.err = "type-1 point without two nonzeros"; return false; }
+      const int s = (r[a] < 0) | ((r[b] < 0) << 1);
+      H.idx1[(static_cast<size_t>(a) * kDim + b) * 4 + s] = j;
+    }
+  }
+  for (const int32_t v : H.idx3) if (v < 0) { H.err = "missing type-3 point"; return false; }
+  for (const int32_t v : H.idx2) if (v < 0) { H.err = "missing type-2 point"; return false; }
+  int t1 = 0;
+  for (const int32_t v : H.idx1) t1 += v >= 0;
+  if (t1 != 276 * 4) { H.err = "missing type-1 point"; return false; }
+  // B operand: column c = (-1)^c_k, canonical tiled layout.
+  H.golay.assign(static_cast<size_t>(kGolay) * kKPad, 0);
+  for (int c = 0; c < kGolay; ++c) {
+    const int t = c / kGolayTileN, cc = c % kGolayTileN, g = cc / 8, rr = cc % 8;
+    for (int k = 0; k < kDim; ++k) {
+      const size_t byte = static_cast<size_t>(t) * kGolayTileN * kRowBytes + g * 512 + (k / 8) * 128 +
+                          rr * 16 + (k % 8) * 2;
+      H.golay[byte / 2] = bf16_bits_of_int((golay[c] >> k & 1) ? -1 : 1);
+    }
+  }
+  return true;
+}
+
 const HostTables &host_tables() {
   static HostTables H;
   static std::once_flag once;
   std::call_once(once, [] {
     H.raw.resize(static_cast<size_t>(kKissing) * kDim);
     if (!build_raw_kissing_points(H.raw.data(), &H.err)) return;
-    H.tiled.assign(static_cast<size_t>(kKissing) * kKPad, 0);
-    for (int j = 0; j < kKissing; ++j) {
-      const int t = j / kTileN, rr = j % kTileN, g = rr / 8, r = rr % 8;
-      for (int k = 0; k < kDim; ++k) {
-        const size_t byte = static_cast<size_t>(t) * kTileN * kRowBytes + g * 512 + (k / 8) * 128 +
-                            r * 16 + (k % 8) * 2;
-        H.tiled[byte / 2] = bf16_bits_of_int(H.raw[static_cast<size_t>(j) * kDim + k]);
-      }
-    }
+    if (!build_structure(H)) return;
     // Dequant codes, 16 bytes per codeword (word k = elements 8k..8k+7, one
     // nibble each; word 3 is zero).  A codeword takes at most four distinct
     // values, fixed by its type: {+1,-1,+3,-3} (one 3, 23 ones), {0,+2,-2}
@@ -125,10 +225,22 @@ int build_device_tables(int dev, Tables *T) {
   const HostTables &H = host_tables();
   if (!H.ok) return fail(H24_ERR_STATE, "codebook construction failed: " + H.err);
   void *p = nullptr;
-  H24_CUDA_TRY(cudaMalloc(&p, H.tiled.size() * sizeof(uint16_t)));
-  H24_CUDA_TRY(cudaMemcpy(p, H.tiled.data(), H.tiled.size() * sizeof(uint16_t),
-                          cudaMemcpyHostToDevice));
-  T->cb_tiled = static_cast<const __nv_bfloat16 *>(p);
+  const auto upload = [&p](const void *src, size_t bytes) -> int {
+    H24_CUDA_TRY(cudaMalloc(&p, bytes));
+    H24_CUDA_TRY(cudaMemcpy(p, src, bytes, cudaMemcpyHostToDevice));
+    return H24_OK;
+  };
+  int rc = upload(H.golay.data(), H.golay.size() * sizeof(uint16_t));
+  if (rc != H24_OK) return rc;
+  T->golay_tiled = static_cast<const __nv_bfloat16 *>(p);
+  if ((rc = upload(H.golay_mask.data(), H.golay_mask.size() * 4)) != H24_OK) return rc;
+  T->golay_mask = static_cast<const uint32_t *>(p);
+  if ((rc = upload(H.idx3.data(), H.idx3.size() * 4)) != H24_OK) return rc;
+  T->idx3 = static_cast<const int32_t *>(p);
+  if ((rc = upload(H.idx2.data(), H.idx2.size() * 4)) != H24_OK) return rc;
+  T->idx2 = static_cast<const int32_t *>(p);
+  if ((rc = upload(H.idx1.data(), H.idx1.size() * 4)) != H24_OK) return rc;
+  T->idx1 = static_cast<const int32_t *>(p);
   H24_CUDA_TRY(cudaMalloc(&p, H.raw.size()));
   H24_CUDA_TRY(cudaMemcpy(p, H.raw.data(), H.raw.size(), cudaMemcpyHostToDevice));
   T->cb_raw = static_cast<const int8_t *>(p);
@@ -449,7 +561,7 @@ int h24_timing_read(double *ms, int64_t *launches) {
   return rc;
 }
 
-int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *bitmap_atoms, int64_t *rescored_chunks,
+int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *exact_scores, int64_t *flagged_chunks,
                        void *stream) {
   H24_TABLES_OR_FAIL(T);
   int64_t h[3] = {0, 0, 0};
@@ -458,8 +570,8 @@ int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *bitmap_atoms, int64_t
   H24_CUDA_TRY(cudaStreamSynchronize(s));
   H24_CUDA_TRY(cudaMemsetAsync(T->stats, 0, sizeof(h), s));
   if (exhaustive_atoms) *exhaustive_atoms = h[0];
-  if (bitmap_atoms) *bitmap_atoms = h[2];
-  if (rescored_chunks) *rescored_chunks = h[1];
+  if (exact_scores) *exact_scores = h[1];
+  if (flagged_chunks) *flagged_chunks = h[2];
   return H24_OK;
 }
 

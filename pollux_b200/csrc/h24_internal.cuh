@@ -16,16 +16,23 @@ constexpr int kDim = 24;
 constexpr int kKissing = 196560;
 constexpr int kCount = 196561;
 
-// Screening tiles: the codebook is streamed in tiles of kTileN codewords;
-// 196,560 = 1638 x 120, so no tile is padded.  Candidates are tracked per
-// chunk of kChunk codewords (two chunks per tile).
-constexpr int kTileN = 120;
-constexpr int kNumTiles = kKissing / kTileN;                 // 1638
-constexpr int kChunk = kTileN / 2;                           // 60
-constexpr int kNumChunks = kKissing / kChunk;                // 3276
-constexpr int kKPad = 32;                                    // K padded 24 -> 32 (bf16)
-constexpr int kRowBytes = kKPad * 2;                         // 64 bytes per operand row
-static_assert(kNumTiles * kTileN == kKissing, "tiles cover the codebook exactly");
+// Structure of the 196,560 kissing points (verified when the tables are
+// built): every one is of exactly one type,
+//   type 1  (+-4, +-4, 0^22): 276 position pairs x 4 sign pairs;
+//   type 2  (+-2^8, 0^16): 759 octads x the 128 sign patterns with an even
+//           number of minus signs;
+//   type 3  (-3, +-1^23): one of the 4096 Golay codewords c and a position p;
+//           coordinate i != p is (-1)^c_i and coordinate p is -3.
+// The Golay codewords are kept in order of (weight, bit pattern): column 0 is
+// the zero word, 1-759 the octads, 760-3335 the dodecads, 3336-4094 the
+// weight-16 words (complements of the octads), 4095 the all-ones word.
+constexpr int kGolay = 4096;
+constexpr int kOctads = 759;
+constexpr int kW16First = 3336;               // first weight-16 Golay column
+constexpr int kGolayTileN = 128;              // Golay columns per MMA tile
+constexpr int kGolayTiles = kGolay / kGolayTileN;  // 32
+constexpr int kKPad = 32;                     // K padded 24 -> 32 (bf16)
+constexpr int kRowBytes = kKPad * 2;          // 64 bytes per operand row
 
 // fp32 value of LEECH_SCALE = 1/sqrt(8) and of s_lattice = 1/sqrt(2) as torch
 // rounds the Python floats (castor.py:49, 68).
@@ -37,10 +44,21 @@ constexpr double kCSqNorm = 3.999999761581421;
 // Per-device tables (all device pointers).
 struct Tables {
   int device = -1;
-  // bf16 raw coordinates [kKissing][32], core-matrix tiled for the MMA B
-  // operand: tile t (kTileN rows) at t*kTileN*64 B; inside it 8-row group g
-  // at g*512, 16-byte K chunk c at c*128, row r at r*16.
-  const __nv_bfloat16 *cb_tiled = nullptr;
+  // bf16 Golay sign matrix, the B operand of the screening MMAs: column c
+  // holds (-1)^c_k for k < 24 and zeros for k = 24..31, in tiles of 128
+  // columns in the UMMA canonical K-major layout without swizzle (tile t at
+  // t*8192 B; 8-column group g at g*512, 16-byte K chunk q at q*128, column r
+  // of the group at r*16).
+  const __nv_bfloat16 *golay_tiled = nullptr;
+  const uint32_t *golay_mask = nullptr;  // [kGolay] bit i = c_i
+  // Kissing-point index (codebook row - 1) of each structured codeword:
+  // idx3[c*24 + p] type 3; idx2[o*128 + s] type 2, octad o = complement of
+  // Golay column kW16First + o, s = minus signs of its first 7 positions
+  // (bit k for the k-th lowest position); idx1[(a*24 + b)*4 + s] type 1,
+  // positions a < b, s = (x_a < 0) | (x_b < 0) << 1.
+  const int32_t *idx3 = nullptr;
+  const int32_t *idx2 = nullptr;
+  const int32_t *idx1 = nullptr;
   // raw int8 coordinates [kKissing][24] (kissing point j = codebook row j+1).
   const int8_t *cb_raw = nullptr;
   // Dequant codes [kCount][4] u32 words (16 bytes per codeword, row 0 is the
@@ -48,9 +66,9 @@ struct Tables {
   // codeword's value list, bit 2 of nibbles 0-1 = the list (see h24_capi.cu).
   const uint32_t *cb_nib = nullptr;
   float fingerprint[16];
-  // Device counters: [0] atoms sent to the exhaustive scan, [1] candidate
-  // chunks rescored, [2] atoms rescored from a bitmap; and the error word set
-  // by a timed-out wait.
+  // Device counters: [0] atoms sent to the exhaustive scan, [1] exact fp64
+  // codeword scores of the rescore, [2] candidate chunks flagged by the
+  // screen; and the error word set by a timed-out wait.
   int64_t *stats = nullptr;
   int *err = nullptr;
   // Stream-ordered pool for per-call scratch (kept warm between calls).

@@ -7,30 +7,59 @@
 // order, kp_ji = fp32(raw_ji * fp32(1/sqrt(8))) as stored by the reference,
 // followed by the caller's origin rule (H24_RULE_TRAIN / H24_RULE_PACK).
 //
-// Pipeline per batch of atoms (one CUDA stream, no host synchronisation):
-//   1. prep_kernel      x -> bf16 "hi" rows (24 values + 8 zeros) and a
-//                       per-atom bound 2E on |screening score - exact score|.
-//   2. screen_kernel    persistent tcgen05 kernel, one CTA per SM.  Each CTA
-//                       owns 256 atoms (two M=128 tiles) at a time; their bf16
-//                       rows live in tensor memory (A operand), written by the
-//                       epilogue warps with tcgen05.st.  The bf16 codebook (raw
-//                       integers, exact in bf16, K padded 24 -> 32) streams
-//                       through a shared-memory ring by bulk copies, 112
-//                       codewords per stage, so the MMAs read only B from shared
-//                       memory.  Scores accumulate in TMEM (fp32), double
-//                       buffered; 16 epilogue warps read them with tcgen05.ld,
-//                       one thread per (atom, 56-codeword chunk parity), and
-//                       keep the chunks whose maximum is within 2E of the
-//                       running best.
-//   3. rescore_kernel   one warp per atom rescans the surviving chunks in fp64
-//                       and applies the origin rule.
-//   4. exhaustive_kernel  fp64 scan of all codewords for the rare atoms whose
-//                       candidate bookkeeping overflowed.
+// The search uses the structure of the codebook (h24_internal.cuh) instead of
+// scoring all 196,560 codewords.  In raw units (coordinates x 1/sqrt(8)
+// removed), with B(c) = sum_i (-1)^c_i x_i for a Golay codeword c:
+//   type 3 (c, p):  S = B(c) - x_p (3 + (-1)^c_p)
+//                     = sum_{i != p} (-1)^c_i x_i - 3 x_p;
+//   type 2 (octad O, signs s):  S = 2 sum_{i in O} s_i x_i
+//                     <= 2 T(O),  T(O) = sum_{i in O} |x_i|;
+//   type 1 (a, b, signs):  S = 4 (s_a x_a + s_b x_b) <= 4 (|x_a| + |x_b|).
+// Per atom four rows go through one GEMM against the 4096 Golay sign columns
+// ((-1)^c_k, bf16): "slice" rows x with x_p1 or x_p2 zeroed (p1, p2, p3 =
+// the positions of the three smallest coordinates), which give the exact
+// type-3 scores of the codewords (c, p1) and (c, p2) up to the constant
+// -3 x_p; the plain row, which gives B(c); and the row |x|, whose value at the
+// weight-16 column c is 2 T(O) - sum|x| for the octad O = complement of c.
 //
-// Why the bound is sufficient: with S~ the screening score and R the exact
-// score (in raw-integer units), |S~_j - R_j| <= E for every j.  If j* is the
-// exact winner and B~ the screening maximum, S~_j* >= R_j* - E >= R_jhat - E
-// >= B~ - 2E.  Every chunk whose screening maximum is >= B~ - 2E is kept.
+// Pipeline per batch of atoms (one CUDA stream, no host synchronisation):
+//   1. prep_kernel      per atom: the four bf16 rows, written straight into
+//                       the UMMA shared-memory layout of the screening A
+//                       operand, and the per-atom constants (AtomInfo).
+//   2. screen_kernel    persistent tcgen05 kernel, one CTA per SM, 128 atoms
+//                       (four M=128 tiles of 32 atoms x 4 rows) per work item;
+//                       the Golay operand streams through a shared-memory ring
+//                       in tiles of 128 columns; M128 N128 K32 MMAs into four
+//                       TMEM accumulator stages.  16 epilogue warps keep, per
+//                       row, the maximum of each 128-column chunk; at the end
+//                       of a work item they form the atom's best achievable
+//                       screening score and flag every chunk that may hold a
+//                       codeword within 2E of it (one 32-bit mask per row).
+//   3. rescore_kernel   one warp per atom: fp32 scores (from per-atom
+//                       partial-sum tables) of the codewords behind the
+//                       flagged chunks, then fp64 scores in the reference's
+//                       order for those within 2E of the best, lowest index on
+//                       ties, and the origin rule.
+//   4. exhaustive_kernel  fp64 scan of all codewords for atoms with more than
+//                       kHeavyChunks flagged chunks (exact ties over many
+//                       codewords).
+//
+// Why the flags are sufficient: let S~_j be a screening score with
+// |S~_j - sqrt(8) R_j| <= E for every codeword j (R_j the exact score; E from
+// the bf16 rounding of x, see prep_kernel).  The atom's `best` is S~ of an
+// achievable codeword or a lower bound of the best score among a set of
+// codewords computed the same way, so sqrt(8) R_j* >= best - E for the winner
+// j*, and S~_j* >= best - 2E = thr.  A chunk is flagged if an upper bound of
+// S~ over the codewords it stands for reaches thr:
+//   slice rows     the chunk maximum + (-3 x_p);
+//   plain row      the chunk maximum + max(4 y3, 2 y3), y3 = -x_p3: every
+//                  type-3 codeword (c, p) with p outside {p1, p2} has
+//                  y_p <= y3 (y = -x);
+//   |x| row        the chunk maximum + sum|hi| = max 2 T~(O) over its octads;
+// type-1 codewords are bounded by 4 (|x|_(1) + |x|_(2)) and checked in the
+// rescore.  The type-2 contribution to `best` is max_O 2 T~(O) - 4 |x|_(8),
+// |x|_(8) the 8th largest |x_i|: flipping the sign of the smallest |x_i| of
+// O, which is at most |x|_(8), repairs the parity of any octad.
 #include <cstdio>
 #include <mutex>
 
@@ -39,40 +68,52 @@
 namespace h24 {
 namespace {
 
-constexpr int kBlockAtoms = 256;                    // atoms per CTA work item
-constexpr int kStages = 16;                         // codebook ring depth
-constexpr int kAccStages = 2;                       // TMEM accumulator stages
-constexpr int kBTileBytes = kTileN * kRowBytes;     // 7680
-constexpr int kHiBytes = kRowBytes;                 // bf16 row of one atom in global memory
-constexpr int kCap = 12;                            // candidate chunks per (atom, half) list
-constexpr int kBitmapWords = (kNumChunks + 31) / 32;  // 103 words: one bit per chunk
-constexpr int kMaxSegs = 64;                        // input segments per pipeline batch
-constexpr int kEpiWarps = 16;                        // 2 M-tiles x 4 lane quarters x 2 halves
-constexpr int kLists = 2 * kBlockAtoms;               // one list per (atom, column half)
-constexpr int kTileWarps = 8;                        // epilogue warps reading one M-tile
-constexpr int kFirstEpiWarp = 3;                      // warp 0 producer, warps 1-2 MMA issuers
-constexpr int kScreenThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 608
-constexpr uint32_t kTmemCols = 512;
-// TMEM columns: accumulator stage s, M-tile h at s*2*kTileN + h*kTileN; the
-// A operand of M-tile h at kAColBase + h*kACols.
-constexpr uint32_t kACols = kKPad / 2;                // 16 columns: 32 bf16 per lane
-constexpr uint32_t kAColBase = kAccStages * 2 * kTileN;  // 480
-static_assert(kAColBase + 2 * kACols == kTmemCols, "accumulators + A operand fill TMEM");
-constexpr uint8_t kOverflow = 0xFF;   // exhaustive fp64 scan
-constexpr uint8_t kBitmapMode = 0xFE; // candidate chunks in a global bitmap slot
-constexpr int64_t kBatchAtoms = int64_t(1) << 22;    // atoms per pipeline batch
+constexpr int kWorkAtoms = 128;                    // atoms per CTA work item
+constexpr int kRowsPerAtom = 4;                    // slice p1, slice p2, plain, |x|
+constexpr int kMTiles = kWorkAtoms * kRowsPerAtom / 128;  // 4
+constexpr int kATileBytes = 128 * kRowBytes;       // 8192
+constexpr int kAItemBytes = kMTiles * kATileBytes; // 32768
+constexpr int kBTileBytes = kGolayTileN * kRowBytes;  // 8192
+constexpr int kStages = 8;                         // Golay tile ring depth
+constexpr int kW16Chunk = kW16First / kGolayTileN; // 26: first chunk with weight-16 columns
+constexpr int kW16Skip = kW16First - kW16Chunk * kGolayTileN;  // 8 dodecads lead chunk 26
+constexpr int kEpiWarps = 16;                      // 4 M-tiles x 4 TMEM lane quarters
+constexpr int kFirstEpiWarp = 2;                   // warp 0 producer, warp 1 MMA issuer
+constexpr int kScreenThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 576
+constexpr uint32_t kTmemCols = kMTiles * kGolayTileN;  // 512: one accumulator stage per M-tile
+constexpr int kHeavyChunks = 96;                   // flagged chunks (of 102) beyond which the exhaustive scan runs
+constexpr int kMaxSegs = 64;                       // input segments per pipeline batch
+constexpr int64_t kBatchAtoms = int64_t(1) << 20;  // atoms per pipeline batch
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s
+static_assert(kW16Chunk == 26 && kW16Skip == 8, "weight-16 block starts 8 columns into chunk 26");
+static_assert(kW16First + kOctads == kGolay - 1, "the all-ones word closes the weight-16 block");
+
+// Per-atom constants of the search (prep_kernel -> screen and rescore).
+struct __align__(16) AtomInfo {
+  float off[2];  // -3 x_p1, -3 x_p2: added to the slice rows
+  float u;       // max(4 y3, 2 y3): bound for type-3 positions outside {p1, p2}
+  float shi;     // sum |hi_i|: added to the |x| row at weight-16 columns
+  float t1;      // 4 (|x|_(1) + |x|_(2)): best type-1 score
+  float l2s;     // 4 |x|_(8): type-2 parity allowance
+  float two_e;   // 2E, or -1 for an atom with a non-finite coordinate
+  uint8_t p[3];  // p1, p2, p3
+  uint8_t pad;
+};
+static_assert(sizeof(AtomInfo) == 32, "AtomInfo is two 16-byte loads");
 
 struct __align__(1024) ScreenSmem {
-  uint8_t b[kStages][kBTileBytes];
-  float cand_score[kCap][kLists];
-  uint16_t cand_chunk[kCap][kLists];
+  uint8_t a[2][kAItemBytes];          // A operand of two work items
+  uint8_t b[kStages][kBTileBytes];    // Golay tile ring
+  float rowval[2][kWorkAtoms][kRowsPerAtom];  // per-row bests, by work-item parity
+  float cmax[kGolayTiles][kEpiWarps * 32];    // chunk maxima of each epilogue thread
+  uint64_t bar_a_full[2];
+  uint64_t bar_a_empty[2];
   uint64_t bar_b_full[kStages];
   uint64_t bar_b_empty[kStages];
-  uint64_t bar_a_full[2][2];              // [A buffer][M-tile]
-  uint64_t bar_acc_full[kAccStages][2];   // [stage][M-tile]
-  uint64_t bar_acc_empty[kAccStages][2];
-  uint64_t bar_final[2];
+  uint64_t bar_acc_full[kMTiles];
+  uint64_t bar_acc_empty[kMTiles];
+  uint64_t bar_rows[2];
+  uint64_t bar_final;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -170,6 +211,23 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
   return wait_slow(bar, parity, abort_flag, err);
 }
 
+// Fully inlined form of wait_bar for loops that keep many values in
+// registers (no call, so nothing is saved around it).
+__device__ __forceinline__ bool wait_bar_inl(uint64_t *bar, uint32_t parity,
+                                             volatile int *abort_flag, int *err) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicExch(err, H24_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
                                          uint64_t policy) {
   asm volatile(
@@ -177,6 +235,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 
 __device__ __forceinline__ uint64_t policy_evict_last() {
@@ -203,35 +267,20 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
 }
 
 // Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major,
-// M = 128, N = kTileN.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
-                            (static_cast<uint32_t>(kTileN >> 3) << 17) | ((128u >> 4) << 24);
+// M = 128, N = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) |
+                            ((128u >> 4) << 24);
 
-// D (TMEM) += A (TMEM) x B (shared memory descriptor); accumulate == 0
+// D (TMEM) += A x B, both from shared-memory descriptors; accumulate == 0
 // overwrites D.
-__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                             uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
       : "memory");
-}
-
-// 32 lanes x 16 consecutive 32-bit TMEM columns from registers.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-      "r"(v[15])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -244,32 +293,19 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 #define H24_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), \
                   "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
 
-// 32 lanes x 64 consecutive 32-bit TMEM columns.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t *r) {
+// 32 lanes x 32 consecutive 32-bit TMEM columns, waited for in the same
+// statement (so no use of r can be scheduled before the wait).
+__device__ __forceinline__ void tmem_ld32_wait(uint32_t taddr, uint32_t *r) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
-      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24), H24_R8(32), H24_R8(40), H24_R8(48),
-        H24_R8(56)
-      : "r"(taddr));
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24)
+      : "r"(taddr)
+      : "memory");
 }
 #undef H24_R8
-
-#define H24_T8(b) "+r"(r[b + 0]), "+r"(r[b + 1]), "+r"(r[b + 2]), "+r"(r[b + 3]), \
-                  "+r"(r[b + 4]), "+r"(r[b + 5]), "+r"(r[b + 6]), "+r"(r[b + 7])
-// Waits for this thread's outstanding tcgen05.ld and ties the loaded registers
-// to the wait so that no use of them is scheduled before it.
-__device__ __forceinline__ void tmem_wait_ld(uint32_t *r) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : H24_T8(0), H24_T8(8), H24_T8(16), H24_T8(24), H24_T8(32), H24_T8(40),
-                 H24_T8(48), H24_T8(56)
-               :
-               : "memory");
-}
-#undef H24_T8
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
@@ -277,18 +313,17 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Maximum of 60 fp32 values held as raw bits (tree of 3-input max).
-__device__ __forceinline__ float max60(const uint32_t *r) {
-  float m[20];
+// max(m, the 32 fp32 values held as raw bits): a tree of 3-input max.
+__device__ __forceinline__ float max32(float m, const uint32_t *r) {
+  float t[11];
 #pragma unroll
-  for (int k = 0; k < 20; ++k)
-    m[k] = fmax3(__uint_as_float(r[3 * k]), __uint_as_float(r[3 * k + 1]),
+  for (int k = 0; k < 10; ++k)
+    t[k] = fmax3(__uint_as_float(r[3 * k]), __uint_as_float(r[3 * k + 1]),
                  __uint_as_float(r[3 * k + 2]));
-  float n[7];
-#pragma unroll
-  for (int k = 0; k < 6; ++k) n[k] = fmax3(m[3 * k], m[3 * k + 1], m[3 * k + 2]);
-  n[6] = fmaxf(m[18], m[19]);
-  return fmax3(fmax3(n[0], n[1], n[2]), fmax3(n[3], n[4], n[5]), n[6]);
+  t[10] = fmax3(__uint_as_float(r[30]), __uint_as_float(r[31]), m);
+  const float u0 = fmax3(t[0], t[1], t[2]), u1 = fmax3(t[3], t[4], t[5]);
+  const float u2 = fmax3(t[6], t[7], t[8]);
+  return fmax3(fmax3(u0, u1, u2), t[9], t[10]);
 }
 
 // ---------------------------------------------------------------------------
@@ -311,9 +346,20 @@ __device__ __forceinline__ const float *atom_ptr(const Segs &sg, int64_t a) {
   return sg.x[lo] + (a - sg.start[lo]) * kDim;
 }
 
+// Byte offset of M-tile lane L, 16-byte K chunk q in an A tile (UMMA
+// canonical K-major layout without swizzle: 8-row groups at 512 B, K chunks
+// at 128 B, rows at 16 B).
+__device__ __forceinline__ uint32_t a_offset(int L, int q) {
+  return static_cast<uint32_t>((L >> 3) * 512 + q * 128 + (L & 7) * 16);
+}
+
+// Atom a of work item w = a / 128 sits in M-tile g = (a / 32) % 4 at lane
+// 32 * ((r - g) mod 4) + a % 32 for row type r (0 slice p1, 1 slice p2,
+// 2 plain, 3 |x|), so that each TMEM lane quarter holds every row type once
+// over the four M-tiles and the epilogue's work spreads evenly over the SM.
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
-                                                   int64_t n_pad, uint8_t *__restrict__ a_hi,
-                                                   float *__restrict__ two_e) {
+                                                   int64_t n_pad, uint8_t *__restrict__ a_tiles,
+                                                   AtomInfo *__restrict__ info) {
   const int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (a >= n_pad) return;
   float v[kDim];
@@ -331,120 +377,107 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
 #pragma unroll
     for (int i = 0; i < kDim; ++i) v[i] = 0.f;
   }
-  float sum_d = 0.f, sum_d2 = 0.f, sum_x = 0.f;
+  float sum_d = 0.f, sum_d2 = 0.f, sum_x = 0.f, shi = 0.f;
   bool finite = true;
-  uint32_t hi_bits[12];
+  uint16_t hb[kDim];
+  // Three smallest coordinates (lowest position first on ties) and the two
+  // largest and eighth largest |x_i|.
+  float s0 = INFINITY, s1 = INFINITY, s2 = INFINITY;
+  int q0 = 0, q1 = 1, q2 = 2;
+  float top[8];
 #pragma unroll
-  for (int i = 0; i < kDim; i += 2) {
-    const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[i], v[i + 1]);
-    const float h0 = __low2float(h2), h1 = __high2float(h2);
-    const float d0 = fabsf(v[i] - h0), d1 = fabsf(v[i + 1] - h1);
-    sum_d += d0 + d1;
-    sum_d2 = fmaf(d0, d0, fmaf(d1, d1, sum_d2));
-    sum_x += fabsf(v[i]) + fabsf(v[i + 1]);
-    finite = finite && isfinite(v[i]) && isfinite(v[i + 1]);
-    hi_bits[i / 2] = *reinterpret_cast<const uint32_t *>(&h2);
+  for (int k = 0; k < 8; ++k) top[k] = 0.f;
+#pragma unroll
+  for (int i = 0; i < kDim; ++i) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
+    const float hf = __bfloat162float(h);
+    hb[i] = __bfloat16_as_ushort(h);
+    const float d = fabsf(v[i] - hf);
+    sum_d += d;
+    sum_d2 = fmaf(d, d, sum_d2);
+    sum_x += fabsf(v[i]);
+    shi += fabsf(hf);
+    finite = finite && isfinite(v[i]);
+    const float x = v[i];
+    if (x < s2) {
+      if (x < s1) {
+        s2 = s1; q2 = q1;
+        if (x < s0) { s1 = s0; q1 = q0; s0 = x; q0 = i; }
+        else { s1 = x; q1 = i; }
+      } else { s2 = x; q2 = i; }
+    }
+    float t = fabsf(x);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float hi_k = fmaxf(top[k], t);
+      t = fminf(top[k], t);
+      top[k] = hi_k;
+    }
   }
-  // |sum_i raw_ji d_i| <= min(4 sum|d|, sqrt(32) ||d||); tensor-core
-  // accumulation, the fp32 rounding of 3*LEECH_SCALE and the fp64 rescore add
-  // at most 2^-12 * sum|x| (raw units).  The factor 1.001 absorbs the fp32
-  // rounding of these sums.
+  // |sum_i coef_i d_i| <= min(4 sum|d|, sqrt(32) ||d||) for every codeword
+  // (|coef| <= 4, sum coef^2 = 32); tensor-core accumulation, the fp32
+  // rounding of 3*LEECH_SCALE, the fp32 terms of the screen and rescore and
+  // the fp64 rescore add at most 2^-12 * sum|x| (raw units).  The factor
+  // 1.001 absorbs the fp32 rounding of these sums.
   const float e_hi = fminf(4.f * sum_d, 5.656854249f * sqrtf(sum_d2));
   const float e = (e_hi + 2.44140625e-4f * sum_x) * 1.001f;
-  if (a < n) two_e[a] = finite ? 2.f * e : -1.f;
-  // Row of 32 bf16 (24 values, 8 zeros): the atom's lane of the A operand.
-  uint4 *dst = reinterpret_cast<uint4 *>(a_hi + a * kHiBytes);
+  AtomInfo inf;
+  inf.off[0] = -3.f * s0;
+  inf.off[1] = -3.f * s1;
+  const float y3 = -s2;
+  inf.u = fmaxf(4.f * y3, 2.f * y3);
+  inf.shi = shi;
+  inf.t1 = 4.f * (top[0] + top[1]);
+  inf.l2s = 4.f * top[7];
+  inf.two_e = finite ? 2.f * e : -1.f;
+  inf.p[0] = static_cast<uint8_t>(q0);
+  inf.p[1] = static_cast<uint8_t>(q1);
+  inf.p[2] = static_cast<uint8_t>(q2);
+  inf.pad = 0;
+  info[a] = inf;
+
+  uint8_t *item = a_tiles + (a >> 7) * kAItemBytes;
+  const int g = static_cast<int>((a >> 5) & 3), l = static_cast<int>(a & 31);
 #pragma unroll
-  for (int c = 0; c < 3; ++c)
-    dst[c] = make_uint4(hi_bits[4 * c], hi_bits[4 * c + 1], hi_bits[4 * c + 2], hi_bits[4 * c + 3]);
-  dst[3] = make_uint4(0, 0, 0, 0);
+  for (int r = 0; r < kRowsPerAtom; ++r) {
+    uint32_t w[16];
+#pragma unroll
+    for (int k = 0; k < 12; ++k) {
+      uint32_t lo = hb[2 * k], hi = hb[2 * k + 1];
+      if (r == 3) { lo &= 0x7FFFu; hi &= 0x7FFFu; }
+      if (r < 2) {
+        const int p = r == 0 ? q0 : q1;
+        if (p == 2 * k) lo = 0;
+        if (p == 2 * k + 1) hi = 0;
+      }
+      w[k] = lo | (hi << 16);
+    }
+#pragma unroll
+    for (int k = 12; k < 16; ++k) w[k] = 0;
+    uint8_t *tile = item + g * kATileBytes;
+    const int L = 32 * ((r - g) & 3) + l;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4 *>(tile + a_offset(L, q)) =
+          make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  }
 }
 
 // ---------------------------------------------------------------------------
 // 2. tcgen05 screening
 // ---------------------------------------------------------------------------
-// Per atom and column half h (chunks 2t+h): cand_n[2a+h] entries (or the
-// bitmap / overflow codes), chunk ids cand[(2a+h)*kCap + k] with their
-// screening maxima cand_sc[...], and the half's screening maximum best[2a+h].
 struct ScreenArgs {
-  const uint8_t *a_hi;        // [n_pad][32] bf16 rows
-  const float *two_e;
-  const uint8_t *cb_tiled;
-  uint16_t *cand;     // [n_pad*2][kCap]
-  float *cand_sc;     // [n_pad*2][kCap]
-  uint8_t *cand_n;    // [n_pad*2]
-  float *best;        // [n_pad*2]
-  uint32_t *bitmaps;  // [pool_slots][kBitmapWords]
-  int32_t *slot_count;
-  int32_t pool_slots;
+  const uint8_t *a_tiles;   // [items][kAItemBytes]
+  const AtomInfo *info;     // [n_pad]
+  const uint8_t *golay;     // [kGolayTiles][kBTileBytes]
+  uint32_t *masks;          // [n][4] flagged chunks per row type
+  float *thr;               // [n] best - 2E
   int64_t n;
-  int64_t nblocks;
+  int64_t items;
   int *err;
 };
 
-// Per-atom candidate state of one epilogue thread.
-struct Cands {
-  int cnt = 0;          // list entries in shared memory
-  bool ovf = false;     // give up: exhaustive fp64 scan
-  int slot = -1;        // bitmap slot once the list has overflowed
-  int bm_idx = -1;      // bitmap word being accumulated in bm_word
-  uint32_t bm_word = 0;
-};
-
-// Bitmap mode: chunks arrive in increasing order, so each 32-chunk word is
-// accumulated in a register and stored once.
-__device__ __forceinline__ void bitmap_set(const ScreenArgs &args, Cands &c, int chunk) {
-  const int w = chunk >> 5;
-  if (w != c.bm_idx) {
-    if (c.bm_idx >= 0) args.bitmaps[static_cast<int64_t>(c.slot) * kBitmapWords + c.bm_idx] = c.bm_word;
-    c.bm_idx = w;
-    c.bm_word = 0;
-  }
-  c.bm_word |= 1u << (chunk & 31);
-}
-
-__device__ __forceinline__ void epilogue_insert(ScreenSmem &S, const ScreenArgs &args, int list,
-                                                float m, int chunk, float thr, Cands &c) {
-  const int local = list;
-  if (!(m >= thr)) return;
-  if (c.slot >= 0) {
-    bitmap_set(args, c, chunk);
-    return;
-  }
-  if (c.cnt == kCap) {
-    int k = 0;
-    for (int i = 0; i < kCap; ++i) {
-      const float sc = S.cand_score[i][local];
-      if (sc >= thr) {
-        S.cand_score[k][local] = sc;
-        S.cand_chunk[k][local] = S.cand_chunk[i][local];
-        ++k;
-      }
-    }
-    c.cnt = k;
-  }
-  if (c.cnt < kCap) {
-    S.cand_score[c.cnt][local] = m;
-    S.cand_chunk[c.cnt][local] = static_cast<uint16_t>(chunk);
-    ++c.cnt;
-    return;
-  }
-  // The list holds kCap chunks within 2E of the running best: exact ties over
-  // many chunks.  Move to a bitmap slot (zeroed here by its owner).
-  const int slot = atomicAdd(args.slot_count, 1);
-  if (slot >= args.pool_slots) {
-    c.ovf = true;
-    return;
-  }
-  c.slot = slot;
-  uint32_t *bm = args.bitmaps + static_cast<int64_t>(slot) * kBitmapWords;
-  for (int w = 0; w < kBitmapWords; ++w) bm[w] = 0u;
-  for (int i = 0; i < c.cnt; ++i)
-    if (S.cand_score[i][local] >= thr) bitmap_set(args, c, S.cand_chunk[i][local]);
-  bitmap_set(args, c, chunk);
-}
-
-__global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenArgs args) {
+__global__ void __maxnreg__(112) screen_kernel(const ScreenArgs args) {
   extern __shared__ uint8_t smem_raw[];
   ScreenSmem &S = *reinterpret_cast<ScreenSmem *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -453,18 +486,20 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
   volatile int *abort_flag = &S.abort_flag;
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.bar_a_full[i], 1);
+      mbar_init(&S.bar_a_empty[i], 1);
+      mbar_init(&S.bar_rows[i], kEpiWarps);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.bar_b_full[s], 1);
-      mbar_init(&S.bar_b_empty[s], 2);       // one commit per MMA issuer
+      mbar_init(&S.bar_b_empty[s], 1);
     }
-    for (int h = 0; h < 2; ++h) {
-      for (int s = 0; s < 2; ++s) mbar_init(&S.bar_a_full[s][h], kTileWarps / 2);
-      for (int s = 0; s < kAccStages; ++s) {
-        mbar_init(&S.bar_acc_full[s][h], 1);
-        mbar_init(&S.bar_acc_empty[s][h], kTileWarps);
-      }
-      mbar_init(&S.bar_final[h], 1);
+    for (int g = 0; g < kMTiles; ++g) {
+      mbar_init(&S.bar_acc_full[g], 1);
+      mbar_init(&S.bar_acc_empty[g], 4);  // the four warps of M-tile g
     }
+    mbar_init(&S.bar_final, 1);
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -482,183 +517,167 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
   const uint32_t tmem_base = S.tmem_base;
 
   if (warp == 0) {
-    // ---------------- producer: bulk copies of codebook tiles ----------------
+    // ---------------- producer: A of each work item, Golay tiles ----------
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
-      int bs = 0;
-      uint32_t bph = 0;
-      int last_b[kStages];
+      const uint64_t once = policy_evict_first();
+      int bs = 0, ab = 0;
+      uint32_t bph = 0, aph = 0;
+      int last_b[kStages], last_a[2] = {-1, -1};
       for (int s = 0; s < kStages; ++s) last_b[s] = -1;
       bool ok = true;
-      for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
-        for (int t = 0; t < kNumTiles; ++t) {
+      for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
+        if (!wait_bar(&S.bar_a_empty[ab], aph ^ 1, abort_flag, args.err)) { ok = false; break; }
+        mbar_arrive_expect_tx(&S.bar_a_full[ab], kAItemBytes);
+        bulk_g2s(S.a[ab], args.a_tiles + it * kAItemBytes, kAItemBytes, &S.bar_a_full[ab], once);
+        last_a[ab] = static_cast<int>(aph);
+        if (++ab == 2) { ab = 0; aph ^= 1; }
+        for (int t = 0; t < kGolayTiles; ++t) {
           if (!wait_bar(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err)) { ok = false; break; }
           mbar_arrive_expect_tx(&S.bar_b_full[bs], kBTileBytes);
-          bulk_g2s(S.b[bs], args.cb_tiled + static_cast<int64_t>(t) * kBTileBytes, kBTileBytes,
-                   &S.bar_b_full[bs], keep);
+          bulk_g2s(S.b[bs], args.golay + t * kBTileBytes, kBTileBytes, &S.bar_b_full[bs], keep);
           last_b[bs] = static_cast<int>(bph);
           if (++bs == kStages) { bs = 0; bph ^= 1; }
         }
       }
       if (!ok) {
         // Let every copy already issued land before the CTA leaves.
+        const unsigned long long t0 = global_ns();
         for (int s = 0; s < kStages; ++s)
-          if (last_b[s] >= 0) {
-            const unsigned long long t0 = global_ns();
+          if (last_b[s] >= 0)
             while (!mbar_try_wait(&S.bar_b_full[s], static_cast<uint32_t>(last_b[s])) &&
                    global_ns() - t0 < kWaitLimitNs) {
             }
-          }
+        for (int i = 0; i < 2; ++i)
+          if (last_a[i] >= 0)
+            while (!mbar_try_wait(&S.bar_a_full[i], static_cast<uint32_t>(last_a[i])) &&
+                   global_ns() - t0 < kWaitLimitNs) {
+            }
       }
     }
-  } else if (warp <= 2) {
-    // ---------------- MMA issuers: warp 1 -> M-tile 0, warp 2 -> M-tile 1 ---
-    // MMA issue blocks until the tensor core accepts the instruction, so two
-    // issuers let one wait on its barriers while the other's MMAs run.
-    const int h = warp - 1;
+  } else if (warp == 1) {
+    // ---------------- MMA issuer --------------------------------------------
+    // Per Golay tile, one M128 N128 K32 product (two K=16 MMAs) for each of
+    // the four M-tiles into TMEM stage g (columns 128 g).
     if (lane == 0) {
-      const uint64_t bd0 = smem_desc(smem_u32(S.b[0]));
-      constexpr uint64_t kBStep = kBTileBytes >> 4;           // descriptor units
-      constexpr uint64_t kKStep = 256 >> 4;                   // next 16 K in shared memory
-      constexpr uint32_t kAKStep = 8;                         // next 16 K in TMEM (columns)
-      int bs = 0, ab = 0, as = 0;
-      uint32_t bph = 0, aph = 0, cph = 0;
-      bool ok = true;
-      bool issued = false;
-      for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
-        if (!wait_bar(&S.bar_a_full[ab][h], aph, abort_flag, args.err)) { ok = false; break; }
+      const uint32_t a0 = smem_u32(S.a[0]), b0 = smem_u32(S.b[0]);
+      constexpr uint64_t kKStep = 256 >> 4;  // next 16 K: two 16-byte chunks, descriptor units
+      int bs = 0, ab = 0;
+      uint32_t bph = 0, aph = 0;
+      bool ok = true, issued = false;
+      for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
+        if (!wait_bar(&S.bar_a_full[ab], aph, abort_flag, args.err)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t a = tmem_base + kAColBase + static_cast<uint32_t>(h) * kACols;
-        for (int t = 0; t < kNumTiles; ++t) {
+        for (int t = 0; ok && t < kGolayTiles; ++t) {
           if (!wait_bar(&S.bar_b_full[bs], bph, abort_flag, args.err)) { ok = false; break; }
-          if (!wait_bar(&S.bar_acc_empty[as][h], cph ^ 1, abort_flag, args.err)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t bd = bd0 + static_cast<uint64_t>(bs) * kBStep;
-          const uint32_t d = tmem_base + static_cast<uint32_t>(as * 2 * kTileN + h * kTileN);
-          mma_bf16_ts(d, a, bd, 0);
-          mma_bf16_ts(d, a + kAKStep, bd + kKStep, 1);
-          mma_commit(&S.bar_acc_full[as][h]);
+          const uint64_t bd = smem_desc(b0 + static_cast<uint32_t>(bs) * kBTileBytes);
+          for (int g = 0; g < kMTiles; ++g) {
+            // Use t of stage g (32 per work item, so parity t & 1) waits for
+            // the release of use t - 1.
+            if (!wait_bar(&S.bar_acc_empty[g], (t & 1) ^ 1, abort_flag, args.err)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t ad = smem_desc(a0 + static_cast<uint32_t>(ab * kAItemBytes + g * kATileBytes));
+            const uint32_t d = tmem_base + static_cast<uint32_t>(g * kGolayTileN);
+            mma_bf16_ss(d, ad, bd, 0);
+            mma_bf16_ss(d, ad + kKStep, bd + kKStep, 1);
+            mma_commit(&S.bar_acc_full[g]);
+            issued = true;
+          }
+          if (!ok) break;
           mma_commit(&S.bar_b_empty[bs]);
-          issued = true;
           if (++bs == kStages) { bs = 0; bph ^= 1; }
-          as ^= 1;
-          cph ^= (as == 0);
         }
+        if (!ok) break;
+        mma_commit(&S.bar_a_empty[ab]);
         if (++ab == 2) { ab = 0; aph ^= 1; }
       }
       if (issued) {
-        // All MMAs of this issuer complete before TMEM is released.
-        mma_commit(&S.bar_final[h]);
+        // All MMAs of this CTA complete before TMEM is released.
+        mma_commit(&S.bar_final);
         const unsigned long long t0 = global_ns();
-        while (!mbar_try_wait(&S.bar_final[h], 0) && global_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(&S.bar_final, 0) && global_ns() - t0 < kWaitLimitNs) {
         }
       }
     }
   } else {
-    // ---------------- epilogue: one thread per (atom, column half) --------
-    // Warp w may only access TMEM lanes 32*(w%4)..+31.  The 16 warps cover two
-    // M=128 tiles x four lane quarters x two column halves of each tile;
-    // every half is one 60-codeword candidate chunk (chunk 2t + half).
-    const int ew = warp - kFirstEpiWarp;
-    const int h = ew >> 3;               // which M=128 tile
-    const int q = warp & 3;              // TMEM lane quarter
-    const int half = (ew >> 2) & 1;      // column half = chunk parity
-    const int local = h * 128 + q * 32 + lane;
-    const int list = half * kBlockAtoms + local;
-    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    // A 64-column load that covers the chunk: half 0 reads columns 0..63
-    // (values r[0..59]), half 1 reads 56..119 (values r[4..63]).
-    const uint32_t t_lane = tmem_base + lane_off + static_cast<uint32_t>(h * kTileN + half * 56);
+    // ---------------- epilogue: one thread per (atom, row type) -------------
+    // Warp w may only access TMEM lanes 32*(w%4)..+31: warps of M-tile g
+    // (e / 4) cover its four lane quarters, quarter q holding row type
+    // (q + g) mod 4 of atoms 32 g .. 32 g + 31 of the work item.
+    const int e = warp - kFirstEpiWarp;
+    const int g = e >> 2;
+    const int q = warp & 3;
+    const int r = (q + g) & 3;
+    const int local = 32 * g + lane;
+    const uint32_t t_row =
+        tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(g * kGolayTileN);
     bool ok = true;
-    int ab = 0;
-    int acc_stage_ = 0;
-    uint32_t acc_phase_ = 0;
-    for (int64_t blk = blockIdx.x; ok && blk < args.nblocks; blk += gridDim.x) {
-      const int64_t atom = blk * kBlockAtoms + local;
-      if (half == 0) {
-        // Write this atom's bf16 row into the A operand.  It was last read by
-        // the MMAs of block blk-1, all complete: this warp has already consumed
-        // every accumulator of that block.  The barrier `ab` alternates per
-        // block so that its phase parity identifies the block.
-        uint32_t v[16];
-        const uint4 *src = reinterpret_cast<const uint4 *>(args.a_hi + atom * kHiBytes);
+    int ip = 0;
+    uint32_t rph = 0;  // bit i: parity of the next phase of bar_rows[i]
+    for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
+      const int64_t atom = it * kWorkAtoms + local;
+      const AtomInfo inf = args.info[atom];
+      float *cm = &S.cmax[0][e * 32 + lane];  // chunk t at cm[t * kEpiWarps * 32]
+      float rowmax = -INFINITY;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint4 u = __ldcs(src + k);
-          v[4 * k] = u.x;
-          v[4 * k + 1] = u.y;
-          v[4 * k + 2] = u.z;
-          v[4 * k + 3] = u.w;
-        }
-        tmem_st16(tmem_base + lane_off + kAColBase + static_cast<uint32_t>(h) * kACols, v);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.bar_a_full[ab][h]);
-      }
-      ab ^= 1;
-      const float te = atom < args.n ? args.two_e[atom] : -1.f;
-      const bool track = te >= 0.f;
-      float best = -INFINITY;
-      float thr = track ? -INFINITY : INFINITY;
-      Cands cs;
-      // Tiles alternate between the two accumulator stages; a stage's phase
-      // parity flips every second tile.  kNumTiles is odd, so the stage and
-      // parity sequence continues across blocks.
-      for (int t = 0; t < kNumTiles; ++t) {
-        // Lane 0 waits on the barrier; the warp then synchronises and fences
-        // so that the .sync.aligned TMEM load is ordered after the MMAs.
+      for (int t = 0; t < kGolayTiles; ++t) {
         bool got = true;
-        if (lane == 0) got = wait_bar(&S.bar_acc_full[acc_stage_][h], acc_phase_, abort_flag, args.err);
+        if (lane == 0) got = wait_bar_inl(&S.bar_acc_full[g], t & 1, abort_flag, args.err);
         if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
         tc_fence_after();
-        uint32_t r[64];
-        tmem_ld64(t_lane + static_cast<uint32_t>(acc_stage_ * 2 * kTileN), r);
-        tmem_wait_ld(r);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.bar_acc_empty[acc_stage_][h]);
-        acc_stage_ ^= 1;
-        acc_phase_ ^= (acc_stage_ == 0);
         float m = -INFINITY;
-        if (half == 0) m = max60(r);
-        else m = max60(r + 4);
-        if (m >= thr) {
-          if (m > best) {
-            best = m;
-            thr = best - te;
+        if (r != 3 || t >= kW16Chunk) {
+          uint32_t x[32];
+          // Rolled: an unrolled loop lets the compiler keep several blocks of
+          // loaded values live at once (register spills).
+#pragma unroll 1
+          for (int k = 0; k < 4; ++k) {
+            tmem_ld32_wait(t_row + static_cast<uint32_t>(32 * k), x);
+            if (k == 3) {
+              // All four loads done: hand the stage back to the MMA issuer.
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&S.bar_acc_empty[g]);
+            }
+            if (r == 3 && t == kW16Chunk && k == 0) {
+#pragma unroll
+              for (int i = 0; i < kW16Skip; ++i) x[i] = 0xFF800000u;  // dodecad columns
+            }
+            if (r == 3 && t == kGolayTiles - 1 && k == 3) x[31] = 0xFF800000u;  // all-ones word
+            m = max32(m, x);
           }
-          epilogue_insert(S, args, list, m, 2 * t + half, thr, cs);
-          if (cs.ovf) thr = INFINITY;
+        } else {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.bar_acc_empty[g]);
         }
-        best = fmaxf(best, m);
+        cm[t * kEpiWarps * 32] = m;
+        rowmax = fmaxf(rowmax, m);
       }
       if (!ok) break;
+      // Per-row best, exchanged through shared memory.
+      const float add = r < 2 ? inf.off[r] : (r == 2 ? inf.u : inf.shi);
+      S.rowval[ip][local][r] = r < 2 ? rowmax + add : (r == 3 ? rowmax + inf.shi - inf.l2s : -INFINITY);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.bar_rows[ip]);
+      bool got = true;
+      if (lane == 0) got = wait_bar_inl(&S.bar_rows[ip], (rph >> ip) & 1u, abort_flag, args.err);
+      if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
+      __syncwarp();
+      rph ^= 1u << ip;
+      const float *rv = S.rowval[ip][local];
+      const float best = fmaxf(fmaxf(rv[0], rv[1]), fmaxf(rv[3], inf.t1));
+      const float thr = best - inf.two_e;
+      uint32_t mask = 0;
+#pragma unroll
+      for (int t = 0; t < kGolayTiles; ++t) mask |= (cm[t * kEpiWarps * 32] + add >= thr ? 1u : 0u) << t;
+      if (!(inf.two_e >= 0.f)) mask = 0;
       if (atom < args.n) {
-        const int64_t li = atom * 2 + half;
-        uint8_t n_out = kOverflow;
-        if (track && !cs.ovf) {
-          if (cs.slot >= 0) {
-            args.bitmaps[static_cast<int64_t>(cs.slot) * kBitmapWords + cs.bm_idx] = cs.bm_word;
-            args.cand[li * kCap] = static_cast<uint16_t>(cs.slot & 0xFFFF);
-            args.cand[li * kCap + 1] = static_cast<uint16_t>(cs.slot >> 16);
-            n_out = kBitmapMode;
-          } else {
-            int k = 0;
-            for (int i = 0; i < cs.cnt; ++i) {
-              const float sc = S.cand_score[i][list];
-              if (sc >= thr) {
-                args.cand[li * kCap + k] = S.cand_chunk[i][list];
-                args.cand_sc[li * kCap + k] = sc;
-                ++k;
-              }
-            }
-            n_out = static_cast<uint8_t>(k);
-          }
-        }
-        args.cand_n[li] = n_out;
-        args.best[li] = best;
+        args.masks[atom * kRowsPerAtom + r] = mask;
+        if (r == 0) args.thr[atom] = thr;
       }
+      ip ^= 1;
     }
   }
 
@@ -717,14 +736,15 @@ __device__ __forceinline__ void load_atom(const float *__restrict__ p, float (&v
 // Returns -1 when a search is needed.
 __device__ __forceinline__ int trivial_index(const float (&v)[kDim], int rule) {
   bool finite = true;
-  double ss = 0.0;
 #pragma unroll
-  for (int i = 0; i < kDim; ++i) {
-    finite = finite && isfinite(v[i]);
-    ss = __fma_rn(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
-  }
+  for (int i = 0; i < kDim; ++i) finite = finite && isfinite(v[i]);
   if (!finite) return rule == H24_RULE_TRAIN ? 0 : 1;
-  if (rule == H24_RULE_PACK && sqrt(ss) < 1e-8) return 0;
+  if (rule == H24_RULE_PACK) {
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < kDim; ++i) ss = __fma_rn(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+    if (sqrt(ss) < 1e-8) return 0;
+  }
   return -1;
 }
 
@@ -733,121 +753,240 @@ __device__ __forceinline__ int32_t apply_rule(double best, int bj, int rule) {
   return bj + 1;
 }
 
-// fp64 rescore of one 60-codeword chunk by a warp (up to two codewords per lane).
-__device__ __forceinline__ void rescore_chunk(const float (&v)[kDim], const int8_t *__restrict__ cb_raw,
-                                              int c, int lane, double &bs, int &bj) {
-#pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    const int o = half * 32 + lane;
-    if (o < kChunk) {
-      const int j = c * kChunk + o;
-      better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
-    }
-  }
-}
-
 struct RescoreArgs {
-  const uint16_t *cand;
-  const float *cand_sc;
-  const uint8_t *cand_n;
-  const float *best_approx;
-  const float *two_e;
-  const uint32_t *bitmaps;
+  const uint4 *masks;        // [n] flagged chunks per row type
+  const float *thr;          // [n]
+  const AtomInfo *info;      // [n]
+  const uint32_t *gmask;     // Golay masks
+  const int32_t *idx3, *idx2, *idx1;
   const int8_t *cb_raw;
   int32_t *out;
   int32_t *ovf_list;
   int32_t *ovf_count;
-  int64_t *stats;  // [0] exhaustive atoms, [1] rescored chunks, [2] bitmap atoms
+  int64_t *stats;            // [0] exhaustive atoms, [1] exact scores, [2] flagged chunks
   int64_t n;
   int rule;
 };
 
-__global__ void __launch_bounds__(256) rescore_kernel(const __grid_constant__ Segs sg,
-                                                      const RescoreArgs r) {
-  __shared__ int block_ovf, block_chunks, block_bitmap;
-  if (threadIdx.x == 0) {
-    block_ovf = 0;
-    block_chunks = 0;
-    block_bitmap = 0;
-  }
-  __syncthreads();
+__device__ __forceinline__ float pick(const float (&v)[kDim], int p) {
+  float r = 0.f;
+#pragma unroll
+  for (int i = 0; i < kDim; ++i) r = i == p ? v[i] : r;
+  return r;
+}
+
+// Exact score of kissing point j into the lane's running best: one copy of
+// the fp64 loop for all call sites; it reloads the atom (an L1 hit) so that
+// the caller's copy stays in registers.
+__device__ __noinline__ void exact(const float *__restrict__ xg, const int8_t *__restrict__ cb_raw,
+                                   int j, double &bs, int &bj, int &nex) {
+  float v[kDim];
+  load_atom(xg, v);
+  better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
+  ++nex;
+}
+
+constexpr int kRescoreWarps = 8;
+constexpr int kRescoreBlocksPerSm = 2;
+
+// Persistent: each warp takes atoms a = warp, warp + warps, ...; no block
+// barrier inside the loop, so a slow atom holds up only its own warp.
+// Screening scores of single codewords are recomputed in fp32 from the exact
+// coordinates (error far below E): sum_{i in c} x_i is three lookups in
+// per-atom tables of the partial sums over each byte of the position mask.
+__global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
+    rescore_kernel(const __grid_constant__ Segs sg, const RescoreArgs r) {
+  __shared__ float tab[kRescoreWarps][3][256];
   const int lane = threadIdx.x & 31;
-  const int64_t a = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-  if (a < r.n) {
+  float(*T)[256] = tab[threadIdx.x >> 5];
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
+  unsigned long long st_exh = 0, st_exact = 0, st_chunks = 0;
+  for (int64_t a = blockIdx.x * static_cast<int64_t>(kRescoreWarps) + (threadIdx.x >> 5); a < r.n;
+       a += nwarps) {
+    const float *xg = atom_ptr(sg, a);
     float v[kDim];
-    load_atom(atom_ptr(sg, a), v);
+    load_atom(xg, v);
     const int triv = trivial_index(v, r.rule);
-    const int cn0 = r.cand_n[2 * a], cn1 = r.cand_n[2 * a + 1];
-    // The screening maximum over both halves sets the candidate threshold.
-    const float gbest = fmaxf(r.best_approx[2 * a], r.best_approx[2 * a + 1]);
-    const float te = r.two_e[a];
+    const uint4 mk = r.masks[a];
+    const int nch = __popc(mk.x) + __popc(mk.y) + __popc(mk.z) + __popc(mk.w);
     if (triv >= 0) {
       if (lane == 0) r.out[a] = triv;
-    } else if (cn0 == kOverflow || cn1 == kOverflow) {
-      // Certain origin under the training rule: even best + E stays below the
-      // snap threshold (1e-6 covers the fp32 codebook's rounding).
-      const double ub = static_cast<double>(kLeechScaleF) *
-                        (static_cast<double>(gbest) + 0.5 * te) * (1.0 + 1e-6);
+      continue;
+    }
+    st_chunks += nch;
+    if (nch > kHeavyChunks) {
       if (lane == 0) {
+        // Certain origin under the training rule: every score is at most
+        // 2 ||x|| (Cauchy-Schwarz, ||kp|| = 2).
+        double ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < kDim; ++i)
+          ss = __fma_rn(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
         r.out[a] = 0;
-        if (!(r.rule == H24_RULE_TRAIN && 2.0 * ub < kCSqNorm)) {
+        if (!(r.rule == H24_RULE_TRAIN && 4.0 * sqrt(ss) * (1.0 + 1e-6) < kCSqNorm)) {
           r.ovf_list[atomicAdd(r.ovf_count, 1)] = static_cast<int32_t>(a);
-          atomicAdd(&block_ovf, 1);
+          ++st_exh;
         }
       }
-    } else {
-      const float thr = gbest - te;
-      double bs = -INFINITY;
-      int bj = 0x7FFFFFFF;
-      int chunks = 0;
-      bool used_bitmap = false;
+      continue;
+    }
+    const float thr = r.thr[a];
+    const AtomInfo inf = r.info[a];
+    // Partial-sum tables: T[k][s] = sum of x_{8k+i} over the bits i of s.
+    __syncwarp();  // the previous atom's lookups are done
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int cn = hf ? cn1 : cn0;
-        const int64_t li = 2 * a + hf;
-        if (cn == kBitmapMode) {
-          used_bitmap = true;
-          const int slot = static_cast<int>(r.cand[li * kCap]) |
-                           (static_cast<int>(r.cand[li * kCap + 1]) << 16);
-          const uint32_t *bm = r.bitmaps + static_cast<int64_t>(slot) * kBitmapWords;
-          for (int w = 0; w < kBitmapWords; ++w) {
-            uint32_t word = __ldg(bm + w);
-            while (word) {
-              const int b = __ffs(word) - 1;
-              word &= word - 1;
-              rescore_chunk(v, r.cb_raw, w * 32 + b, lane, bs, bj);
-              ++chunks;
+    for (int k = 0; k < 3; ++k) {
+      float lo5 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 5; ++i)
+        if (lane >> i & 1) lo5 += v[8 * k + i];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        float hi3 = lo5;
+        if (m & 1) hi3 += v[8 * k + 5];
+        if (m & 2) hi3 += v[8 * k + 6];
+        if (m & 4) hi3 += v[8 * k + 7];
+        T[k][lane + 32 * m] = hi3;
+      }
+    }
+    __syncwarp();
+    float sumx = 0.f, sumabs = 0.f;
+    uint32_t negm = 0;
+#pragma unroll
+    for (int i = 0; i < kDim; ++i) {
+      sumx += v[i];
+      sumabs += fabsf(v[i]);
+      negm |= (v[i] < 0.f ? 1u : 0u) << i;
+    }
+    const auto tsum = [&](uint32_t m) { return T[0][m & 255] + T[1][(m >> 8) & 255] + T[2][m >> 16]; };
+    double bs = -INFINITY;
+    int bj = 0x7FFFFFFF;
+    int nex = 0;
+    const int p1 = inf.p[0], p2 = inf.p[1];
+    // Type 3 at the slice positions p1, p2.
+#pragma unroll 1
+    for (int s = 0; s < 2; ++s) {
+      uint32_t m = s ? mk.y : mk.x;
+      const int p = s ? p2 : p1;
+      const float xp = pick(v, p);
+      while (m) {
+        const int b = __ffs(m) - 1;
+        m &= m - 1;
+#pragma unroll 1
+        for (int k = 0; k < 4; ++k) {
+          const int c = b * kGolayTileN + 32 * k + lane;
+          const uint32_t gm = __ldg(r.gmask + c);
+          const float bc = sumx - 2.f * tsum(gm);
+          if (bc - xp * ((gm >> p & 1u) ? 2.f : 4.f) >= thr)
+            exact(xg, r.cb_raw, __ldg(r.idx3 + c * kDim + p), bs, bj, nex);
+        }
+      }
+    }
+    // Type 3 at the other positions, behind flagged chunks of the plain row.
+    {
+      uint32_t m = mk.z;
+      while (m) {
+        const int b = __ffs(m) - 1;
+        m &= m - 1;
+#pragma unroll 1
+        for (int k = 0; k < 4; ++k) {
+          const int c = b * kGolayTileN + 32 * k + lane;
+          const uint32_t gm = __ldg(r.gmask + c);
+          const float bc = sumx - 2.f * tsum(gm);
+          if (bc + inf.u >= thr) {
+            uint32_t hit = 0;
+#pragma unroll
+            for (int p = 0; p < kDim; ++p)
+              hit |= (bc - v[p] * ((gm >> p & 1u) ? 2.f : 4.f) >= thr ? 1u : 0u) << p;
+            hit &= ~((1u << p1) | (1u << p2));
+            while (hit) {
+              const int p = __ffs(hit) - 1;
+              hit &= hit - 1;
+              exact(xg, r.cb_raw, __ldg(r.idx3 + c * kDim + p), bs, bj, nex);
             }
           }
-        } else {
-          for (int k = 0; k < cn; ++k) {
-            if (!(r.cand_sc[li * kCap + k] >= thr)) continue;
-            rescore_chunk(v, r.cb_raw, r.cand[li * kCap + k], lane, bs, bj);
-            ++chunks;
+        }
+      }
+    }
+    // Type 2, behind flagged chunks of the |x| row: octads first, then the
+    // 128 sign patterns of each surviving octad across the warp.
+    {
+      uint32_t m = mk.w;
+      while (m) {
+        const int b = __ffs(m) - 1;
+        m &= m - 1;
+#pragma unroll 1
+        for (int k = 0; k < 4; ++k) {
+          const int c = b * kGolayTileN + 32 * k + lane;
+          const int o = c - kW16First;
+          uint32_t om = 0;
+          bool cand = false;
+          if (o >= 0 && o < kOctads) {
+            const uint32_t gm = __ldg(r.gmask + c);
+            om = ~gm & 0xFFFFFFu;
+            const float in_c = tsum(gm & ~negm) - tsum(gm & negm);  // sum_{i in c} |x_i|
+            cand = 2.f * (sumabs - in_c) >= thr;
+          }
+          uint32_t bal = __ballot_sync(0xffffffffu, cand);
+          while (bal) {
+            const int src = __ffs(bal) - 1;
+            bal &= bal - 1;
+            const int oc = __shfl_sync(0xffffffffu, o, src);
+            const uint32_t omc = __shfl_sync(0xffffffffu, om, src);
+            // The octad's 8 coordinates, lowest position first, to every lane.
+            float ov = 0.f;
+            if (lane < 8) ov = pick(v, static_cast<int>(__fns(omc, 0, lane + 1)));
+            float o8[8];
+#pragma unroll
+            for (int k2 = 0; k2 < 8; ++k2) o8[k2] = __shfl_sync(0xffffffffu, ov, k2);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int pid = lane + 32 * t;
+              float sc = (__popc(pid) & 1) ? -o8[7] : o8[7];
+#pragma unroll
+              for (int k2 = 0; k2 < 7; ++k2) sc += (pid >> k2 & 1) ? -o8[k2] : o8[k2];
+              if (2.f * sc >= thr) exact(xg, r.cb_raw, __ldg(r.idx2 + oc * 128 + pid), bs, bj, nex);
+            }
           }
         }
       }
+    }
+    // Type 1: every score is at most t1.
+    if (inf.t1 >= thr && lane < kDim) {
+      const float xa = pick(v, lane);
+#pragma unroll 1
+      for (int b2 = lane + 1; b2 < kDim; ++b2) {
+        const float xb = pick(v, b2);
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const double os = __shfl_xor_sync(0xffffffffu, bs, off);
-        const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
-        better(bs, bj, os, oj);
+        for (int s = 0; s < 4; ++s) {
+          const float sc = 4.f * ((s & 1 ? -xa : xa) + (s & 2 ? -xb : xb));
+          if (sc >= thr) exact(xg, r.cb_raw, __ldg(r.idx1 + (lane * kDim + b2) * 4 + s), bs, bj, nex);
+        }
       }
-      if (lane == 0) {
-        r.out[a] = chunks > 0 ? apply_rule(bs, bj, r.rule) : 0;
-        atomicAdd(&block_chunks, chunks);
-        if (used_bitmap) atomicAdd(&block_bitmap, 1);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const double os = __shfl_xor_sync(0xffffffffu, bs, off);
+      const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+      better(bs, bj, os, oj);
+      nex += __shfl_xor_sync(0xffffffffu, nex, off);
+    }
+    st_exact += nex;
+    if (lane == 0) {
+      if (bj == 0x7FFFFFFF) {
+        // No codeword passed (cannot happen when the bound holds): scan all.
+        r.out[a] = 0;
+        r.ovf_list[atomicAdd(r.ovf_count, 1)] = static_cast<int32_t>(a);
+        ++st_exh;
+      } else {
+        r.out[a] = apply_rule(bs, bj, r.rule);
       }
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0 && (block_ovf || block_chunks || block_bitmap)) {
-    atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[0]),
-              static_cast<unsigned long long>(block_ovf));
-    atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[1]),
-              static_cast<unsigned long long>(block_chunks));
-    atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[2]),
-              static_cast<unsigned long long>(block_bitmap));
+  if (lane == 0) {
+    if (st_exh) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[0]), st_exh);
+    if (st_exact) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[1]), st_exact);
+    if (st_chunks) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[2]), st_chunks);
   }
 }
 
@@ -889,6 +1028,86 @@ __global__ void __launch_bounds__(256) exhaustive_kernel(const __grid_constant__
 std::mutex g_mu;
 int g_sms[64] = {};
 
+// Per-atom scratch of one pipeline batch of up to `pad` atoms.
+struct Scratch {
+  uint8_t *a_tiles;
+  AtomInfo *info;
+  uint32_t *masks;
+  float *thr;
+  int32_t *ovf_list;
+  int32_t *ovf_count;
+};
+constexpr size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+constexpr size_t scratch_bytes(int64_t pad) {
+  return up256(static_cast<size_t>(pad) / kWorkAtoms * kAItemBytes) +
+         up256(static_cast<size_t>(pad) * sizeof(AtomInfo)) +
+         up256(static_cast<size_t>(pad) * kRowsPerAtom * 4) + up256(static_cast<size_t>(pad) * 4) +
+         up256(static_cast<size_t>(pad) * 4) + 256;
+}
+Scratch carve(uint8_t *base, int64_t pad) {
+  Scratch sc;
+  size_t o = 0;
+  sc.a_tiles = base + o;
+  o += up256(static_cast<size_t>(pad) / kWorkAtoms * kAItemBytes);
+  sc.info = reinterpret_cast<AtomInfo *>(base + o);
+  o += up256(static_cast<size_t>(pad) * sizeof(AtomInfo));
+  sc.masks = reinterpret_cast<uint32_t *>(base + o);
+  o += up256(static_cast<size_t>(pad) * kRowsPerAtom * 4);
+  sc.thr = reinterpret_cast<float *>(base + o);
+  o += up256(static_cast<size_t>(pad) * 4);
+  sc.ovf_list = reinterpret_cast<int32_t *>(base + o);
+  o += up256(static_cast<size_t>(pad) * 4);
+  sc.ovf_count = reinterpret_cast<int32_t *>(base + o);
+  return sc;
+}
+
+// The four kernels of one batch (the overflow counter must be zero).
+int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int32_t *ob,
+                 const Scratch &sc, int sms, cudaStream_t s) {
+  const int64_t items = (nbatch + kWorkAtoms - 1) / kWorkAtoms;
+  const int64_t npad = items * kWorkAtoms;
+  prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(sg, nbatch, npad,
+                                                                      sc.a_tiles, sc.info);
+  ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
+                sc.thr, nbatch, items, t->err};
+  const int grid = static_cast<int>(items < sms ? items : sms);
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  if (timing_enabled()) {
+    cudaEventCreate(&ev0);
+    cudaEventCreate(&ev1);
+    cudaEventRecord(ev0, s);
+  }
+  screen_kernel<<<grid, kScreenThreads, sizeof(ScreenSmem) + 1024, s>>>(sa);
+  if (ev1) {
+    cudaEventRecord(ev1, s);
+    timing_record(ev0, ev1);
+  }
+  RescoreArgs ra{reinterpret_cast<const uint4 *>(sc.masks), sc.thr, sc.info, t->golay_mask, t->idx3,
+                 t->idx2, t->idx1, t->cb_raw, ob, sc.ovf_list, sc.ovf_count, t->stats, nbatch,
+                 rule};
+  const int64_t rblocks = (nbatch + kRescoreWarps - 1) / kRescoreWarps;
+  const int64_t rcap = static_cast<int64_t>(sms) * kRescoreBlocksPerSm;
+  rescore_kernel<<<static_cast<unsigned>(rblocks < rcap ? rblocks : rcap), 32 * kRescoreWarps, 0,
+                   s>>>(sg, ra);
+  exhaustive_kernel<<<2 * sms, 256, 0, s>>>(sg, rule, sc.ovf_list, sc.ovf_count, t->cb_raw, ob);
+  count_launches(4);
+  H24_CUDA_TRY(cudaGetLastError());
+  return H24_OK;
+}
+
+int screen_setup(int dev, int *sms) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_sms[dev] == 0) {
+    int count = 0;
+    H24_CUDA_TRY(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
+    H24_CUDA_TRY(cudaFuncSetAttribute(screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(sizeof(ScreenSmem) + 1024)));
+    g_sms[dev] = count;
+  }
+  *sms = g_sms[dev];
+  return H24_OK;
+}
+
 }  // namespace
 
 int quantize_segments(const Tables *t, const float *const *xs, const int64_t *counts, int nseg,
@@ -902,36 +1121,15 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
   }
   if (total == 0) return H24_OK;
   int sms = 0;
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    const int dev = t->device;
-    if (g_sms[dev] == 0) {
-      int count = 0;
-      H24_CUDA_TRY(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
-      H24_CUDA_TRY(cudaFuncSetAttribute(screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(sizeof(ScreenSmem) + 1024)));
-      g_sms[dev] = count;
-    }
-    sms = g_sms[dev];
-  }
+  int rc = screen_setup(t->device, &sms);
+  if (rc != H24_OK) return rc;
 
   const int64_t batch = total < kBatchAtoms ? total : kBatchAtoms;
-  const int64_t nb_max = (batch + kBlockAtoms - 1) / kBlockAtoms;
-  const int64_t pad_max = nb_max * kBlockAtoms;
-  const int64_t pool_slots = batch / 4 > 4096 ? batch / 4 : 4096;
-  auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
-  const size_t off_two_e = up(static_cast<size_t>(pad_max) * kHiBytes);
-  const size_t off_cand = off_two_e + up(pad_max * sizeof(float));
-  const size_t off_cand_sc = off_cand + up(pad_max * 2 * kCap * sizeof(uint16_t));
-  const size_t off_cand_n = off_cand_sc + up(pad_max * 2 * kCap * sizeof(float));
-  const size_t off_best = off_cand_n + up(pad_max * 2);
-  const size_t off_ovf = off_best + up(pad_max * 2 * sizeof(float));
-  const size_t off_bm = off_ovf + up(batch * sizeof(int32_t));
-  const size_t off_cnt = off_bm + up(static_cast<size_t>(pool_slots) * kBitmapWords * 4);
-  const size_t bytes = off_cnt + 256;
+  const int64_t pad_max = (batch + kWorkAtoms - 1) / kWorkAtoms * kWorkAtoms;
   uint8_t *scratch = nullptr;
-  H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&scratch), bytes, t->pool, s));
-  int rc = H24_OK;
+  H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&scratch), scratch_bytes(pad_max),
+                                       t->pool, s));
+  const Scratch sc = carve(scratch, pad_max);
   int seg = 0;
   int64_t seg_off = 0;  // atoms of segment `seg` already consumed
   int64_t done = 0;
@@ -951,46 +1149,9 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
       seg_off += take;
       if (seg_off == counts[seg]) { ++seg; seg_off = 0; }
     }
-    const int64_t nb = (nbatch + kBlockAtoms - 1) / kBlockAtoms;
-    const int64_t npad = nb * kBlockAtoms;
-    int32_t *ob = out_idx + done;
-    uint8_t *a_hi = scratch;
-    float *two_e = reinterpret_cast<float *>(scratch + off_two_e);
-    uint16_t *cand = reinterpret_cast<uint16_t *>(scratch + off_cand);
-    float *cand_sc = reinterpret_cast<float *>(scratch + off_cand_sc);
-    uint8_t *cand_n = scratch + off_cand_n;
-    float *best = reinterpret_cast<float *>(scratch + off_best);
-    int32_t *ovf_list = reinterpret_cast<int32_t *>(scratch + off_ovf);
-    uint32_t *bitmaps = reinterpret_cast<uint32_t *>(scratch + off_bm);
-    int32_t *ovf_count = reinterpret_cast<int32_t *>(scratch + off_cnt);
-    int32_t *slot_count = ovf_count + 1;
-    cudaError_t e = cudaMemsetAsync(ovf_count, 0, 2 * sizeof(int32_t), s);
+    cudaError_t e = cudaMemsetAsync(sc.ovf_count, 0, sizeof(int32_t), s);
     if (e != cudaSuccess) { rc = cuda_fail(e, "memset"); break; }
-    prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(sg, nbatch, npad, a_hi,
-                                                                        two_e);
-    ScreenArgs sa{a_hi, two_e, reinterpret_cast<const uint8_t *>(t->cb_tiled), cand, cand_sc,
-                  cand_n, best, bitmaps, slot_count, static_cast<int32_t>(pool_slots), nbatch, nb,
-                  t->err};
-    const int grid = static_cast<int>(nb < sms ? nb : sms);
-    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-    if (timing_enabled()) {
-      cudaEventCreate(&ev0);
-      cudaEventCreate(&ev1);
-      cudaEventRecord(ev0, s);
-    }
-    screen_kernel<<<grid, kScreenThreads, sizeof(ScreenSmem) + 1024, s>>>(sa);
-    if (ev1) {
-      cudaEventRecord(ev1, s);
-      timing_record(ev0, ev1);
-    }
-    RescoreArgs ra{cand, cand_sc, cand_n, best, two_e, bitmaps, t->cb_raw, ob, ovf_list, ovf_count,
-                   t->stats, nbatch, rule};
-    const int64_t rthreads = nbatch * 32;
-    rescore_kernel<<<static_cast<unsigned>((rthreads + 255) / 256), 256, 0, s>>>(sg, ra);
-    exhaustive_kernel<<<2 * sms, 256, 0, s>>>(sg, rule, ovf_list, ovf_count, t->cb_raw, ob);
-    count_launches(4);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) rc = cuda_fail(e, "quantize launch");
+    rc = launch_batch(t, sg, nbatch, rule, out_idx + done, sc, sms, s);
     done += nbatch;
   }
   cudaError_t e = cudaFreeAsync(scratch, s);
@@ -1002,8 +1163,6 @@ int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_
              cudaStream_t s) {
   return quantize_segments(t, &x, &n, 1, rule, out_idx, s);
 }
-
-
 
 // ===========================================================================
 // Allocation-free variant of the nearest-codeword pipeline.
@@ -1025,7 +1184,7 @@ int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_
 //     cudaGetSymbolAddress (set-up work, no allocation); make that first call
 //     before any stream capture;
 //   * every call on a device shares the one array and it keeps the previous
-//     call's contents: the counters that must start at zero are cleared at
+//     call's contents: the counter that must start at zero is cleared at
 //     the start of each call, everything else is written before it is read.
 //     Calls whose executions overlap on the GPU (other streams or host
 //     threads without ordering) race on the array.
@@ -1033,19 +1192,8 @@ int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_
 namespace {
 
 constexpr int64_t kNoAllocMaxAtoms = 32768;
-constexpr int64_t kNoAllocPad = kNoAllocMaxAtoms;  // a multiple of kBlockAtoms
-constexpr int64_t kNoAllocSlots = kNoAllocMaxAtoms / 4;
-constexpr size_t na_up(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
-constexpr size_t kNaTwoE = na_up(kNoAllocPad * kHiBytes);
-constexpr size_t kNaCand = kNaTwoE + na_up(kNoAllocPad * sizeof(float));
-constexpr size_t kNaCandSc = kNaCand + na_up(kNoAllocPad * 2 * kCap * sizeof(uint16_t));
-constexpr size_t kNaCandN = kNaCandSc + na_up(kNoAllocPad * 2 * kCap * sizeof(float));
-constexpr size_t kNaBest = kNaCandN + na_up(kNoAllocPad * 2);
-constexpr size_t kNaOvf = kNaBest + na_up(kNoAllocPad * 2 * sizeof(float));
-constexpr size_t kNaBm = kNaOvf + na_up(kNoAllocMaxAtoms * sizeof(int32_t));
-constexpr size_t kNaCnt = kNaBm + na_up(static_cast<size_t>(kNoAllocSlots) * kBitmapWords * 4);
-constexpr size_t kNoAllocBytes = kNaCnt + 256;  // about 10.5 MB
-static_assert(kNoAllocMaxAtoms % kBlockAtoms == 0, "whole CTA work items");
+constexpr size_t kNoAllocBytes = scratch_bytes(kNoAllocMaxAtoms);  // about 9.8 MB
+static_assert(kNoAllocMaxAtoms % kWorkAtoms == 0, "whole CTA work items");
 static_assert(kNoAllocBytes < (size_t(16) << 20), "modest fixed footprint");
 
 // The scratch array.  In host code this name is a host-side stand-in, not a
@@ -1057,15 +1205,14 @@ uint8_t *g_noalloc_ptr[64] = {};
 
 // Per-device set-up: resolve the array's device address (once, with the device
 // current) and allow the screening kernel its dynamic shared memory.
-int noalloc_setup(int dev, uint8_t **out) {
+int noalloc_setup(int dev, uint8_t **out, int *sms) {
+  int rc = screen_setup(dev, sms);
+  if (rc != H24_OK) return rc;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void *ptr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
-    e = cudaFuncSetAttribute(screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(sizeof(ScreenSmem) + 1024));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     g_noalloc_ptr[dev] = static_cast<uint8_t *>(ptr);
   }
   *out = g_noalloc_ptr[dev];
@@ -1075,42 +1222,18 @@ int noalloc_setup(int dev, uint8_t **out) {
 int quantize_noalloc(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
                      cudaStream_t s) {
   uint8_t *scratch = nullptr;
-  int rc = noalloc_setup(t->device, &scratch);
-  if (rc != H24_OK) return rc;
   int sms = 0;
-  H24_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, t->device));
+  int rc = noalloc_setup(t->device, &scratch, &sms);
+  if (rc != H24_OK) return rc;
   Segs sg;
   sg.count = 1;
   sg.x[0] = x;
   sg.start[0] = 0;
   sg.start[1] = n;
-  const int64_t nb = (n + kBlockAtoms - 1) / kBlockAtoms;
-  const int64_t npad = nb * kBlockAtoms;
-  uint8_t *a_hi = scratch;
-  float *two_e = reinterpret_cast<float *>(scratch + kNaTwoE);
-  uint16_t *cand = reinterpret_cast<uint16_t *>(scratch + kNaCand);
-  float *cand_sc = reinterpret_cast<float *>(scratch + kNaCandSc);
-  uint8_t *cand_n = scratch + kNaCandN;
-  float *best = reinterpret_cast<float *>(scratch + kNaBest);
-  int32_t *ovf_list = reinterpret_cast<int32_t *>(scratch + kNaOvf);
-  uint32_t *bitmaps = reinterpret_cast<uint32_t *>(scratch + kNaBm);
-  int32_t *ovf_count = reinterpret_cast<int32_t *>(scratch + kNaCnt);
-  int32_t *slot_count = ovf_count + 1;
-  // The array keeps the previous call's contents: clear the two counters.
-  H24_CUDA_TRY(cudaMemsetAsync(ovf_count, 0, 2 * sizeof(int32_t), s));
-  prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(sg, n, npad, a_hi, two_e);
-  ScreenArgs sa{a_hi, two_e, reinterpret_cast<const uint8_t *>(t->cb_tiled), cand, cand_sc,
-                cand_n, best, bitmaps, slot_count, static_cast<int32_t>(kNoAllocSlots), n, nb,
-                t->err};
-  screen_kernel<<<static_cast<int>(nb < sms ? nb : sms), kScreenThreads, sizeof(ScreenSmem) + 1024,
-                  s>>>(sa);
-  RescoreArgs ra{cand, cand_sc, cand_n, best, two_e, bitmaps, t->cb_raw, out_idx, ovf_list,
-                 ovf_count, t->stats, n, rule};
-  rescore_kernel<<<static_cast<unsigned>((n * 32 + 255) / 256), 256, 0, s>>>(sg, ra);
-  exhaustive_kernel<<<2 * sms, 256, 0, s>>>(sg, rule, ovf_list, ovf_count, t->cb_raw, out_idx);
-  count_launches(4);
-  H24_CUDA_TRY(cudaGetLastError());
-  return H24_OK;
+  const Scratch sc = carve(scratch, kNoAllocMaxAtoms);
+  // The array keeps the previous call's contents: clear the overflow counter.
+  H24_CUDA_TRY(cudaMemsetAsync(sc.ovf_count, 0, sizeof(int32_t), s));
+  return launch_batch(t, sg, n, rule, out_idx, sc, sms, s);
 }
 
 }  // namespace

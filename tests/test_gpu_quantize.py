@@ -107,17 +107,18 @@ def test_ragged_sizes(C, oracle, n):
 
 def test_config4_scale_sample(C, oracle):
     """2^20 stress atoms in one call: a seeded sample is bit-exact against the
-    oracle, and the overflow path stays rare."""
+    oracle, and the exhaustive path and the exact rescoring stay rare."""
     from pollux_b200 import synth
     cb = C.get_h24_codebook("cuda", torch.float32)
     x = synth.stress_atoms(1 << 20, cb, seed=3, device="cuda")
     C.quantize_stats()
     ours = C.quantize_indices(x, 1)
     C.device_check()
-    exhaustive, bitmap, chunks = C.quantize_stats()
-    assert exhaustive < 100
-    assert bitmap < 0.2 * (1 << 20)
-    assert chunks < 16 * (1 << 20)
+    stats = C.quantize_stats()
+    exhaustive, exact_scores, chunks = stats
+    assert exhaustive < 0.01 * (1 << 20), stats
+    assert exact_scores < 64 * (1 << 20), stats
+    assert chunks < 24 * (1 << 20), stats
     sel = torch.randperm(1 << 20, generator=torch.Generator().manual_seed(0))[:3000]
     xs = x[sel.cuda()].cpu().numpy()
     assert np.array_equal(ours[sel.cuda()].cpu().numpy(), oracle.nearest_exact(xs, 1))

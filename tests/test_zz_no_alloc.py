@@ -44,8 +44,8 @@ def test_matches_h24_quantize_on_two_calls_in_a_row(h24):
     from pollux_b200 import synth, castor
     gen = torch.Generator(device="cuda").manual_seed(101)
     first = torch.randn(20000, 24, generator=gen, device="cuda") * 1.4
-    # The second call is larger and full of exact ties (bitmap path), so any
-    # state left by the first call would show.
+    # The second call is larger and full of exact ties (many flagged chunks and
+    # exhaustive scans), so any state left by the first call would show.
     second = synth.stress_atoms(32768, castor.get_h24_codebook("cuda", torch.float32), seed=9,
                                 device="cuda")
     for x, rule in ((first, 0), (second, 1)):
