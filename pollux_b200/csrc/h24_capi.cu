@@ -54,6 +54,7 @@ struct HostTables {
   std::vector<uint16_t> golay;     // [kGolay][32] bf16 bits, tiled (Tables::golay_tiled)
   std::vector<uint32_t> golay_mask;  // [kGolay]
   std::vector<int32_t> idx3, idx2, idx1;
+  std::vector<uint16_t> oct_by_triple;  // [kTriples][kTripleRow]
   std::vector<uint32_t> nib;       // [kCount][4] dequant codes
   float fingerprint[16];
   bool ok = false;
@@ -160,6 +161,26 @@ bool build_structure(HostTables &H) {
   int t1 = 0;
   for (const int32_t v : H.idx1) t1 += v >= 0;
   if (t1 != 276 * 4) { H.err = "missing type-1 point"; return false; }
+  // The 21 octads through each position triple (Steiner system S(5,8,24)).
+  H.oct_by_triple.assign(static_cast<size_t>(kTriples) * kTripleRow, 0);
+  {
+    std::vector<int> fill(kTriples, 0);
+    const auto c3 = [](int k) { return k * (k - 1) * (k - 2) / 6; };
+    const auto c2 = [](int j) { return j * (j - 1) / 2; };
+    for (int o = 0; o < kOctads; ++o) {
+      const uint32_t om = ~golay[kW16First + o] & 0xFFFFFFu;
+      for (int k = 2; k < kDim; ++k)
+        for (int j = 1; j < k; ++j)
+          for (int i = 0; i < j; ++i)
+            if ((om >> i & 1) && (om >> j & 1) && (om >> k & 1)) {
+              const int t = c3(k) + c2(j) + i;
+              if (fill[t] >= 21) { H.err = "more than 21 octads through a triple"; return false; }
+              H.oct_by_triple[static_cast<size_t>(t) * kTripleRow + fill[t]++] = static_cast<uint16_t>(o);
+            }
+    }
+    for (int t = 0; t < kTriples; ++t)
+      if (fill[t] != 21) { H.err = "a position triple is not in 21 octads"; return false; }
+  }
   // B operand: column c = (-1)^c_k, canonical tiled layout.
   H.golay.assign(static_cast<size_t>(kGolay) * kKPad, 0);
   for (int c = 0; c < kGolay; ++c) {
@@ -241,6 +262,8 @@ int build_device_tables(int dev, Tables *T) {
   T->idx2 = static_cast<const int32_t *>(p);
   if ((rc = upload(H.idx1.data(), H.idx1.size() * 4)) != H24_OK) return rc;
   T->idx1 = static_cast<const int32_t *>(p);
+  if ((rc = upload(H.oct_by_triple.data(), H.oct_by_triple.size() * 2)) != H24_OK) return rc;
+  T->oct_by_triple = static_cast<const uint16_t *>(p);
   H24_CUDA_TRY(cudaMalloc(&p, H.raw.size()));
   H24_CUDA_TRY(cudaMemcpy(p, H.raw.data(), H.raw.size(), cudaMemcpyHostToDevice));
   T->cb_raw = static_cast<const int8_t *>(p);

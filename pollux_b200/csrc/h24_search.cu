@@ -75,37 +75,46 @@ constexpr int kATileBytes = 128 * kRowBytes;       // 8192
 constexpr int kAItemBytes = kMTiles * kATileBytes; // 32768
 constexpr int kBTileBytes = kGolayTileN * kRowBytes;  // 8192
 constexpr int kStages = 8;                         // Golay tile ring depth
-constexpr int kW16Chunk = kW16First / kGolayTileN; // 26: first chunk with weight-16 columns
-constexpr int kW16Skip = kW16First - kW16Chunk * kGolayTileN;  // 8 dodecads lead chunk 26
+constexpr int kChunkCols = 64;                     // candidate chunk: half a Golay tile
+constexpr int kChunks = kGolay / kChunkCols;       // 64 per row
+constexpr int kW16Tile = kW16First / kGolayTileN;  // 26: first tile with weight-16 columns
+constexpr int kW16Chunk = kW16First / kChunkCols;  // 52: first chunk with weight-16 columns
+constexpr int kW16Skip = kW16First - kW16Tile * kGolayTileN;  // 8 dodecads lead tile 26
 constexpr int kEpiWarps = 16;                      // 4 M-tiles x 4 TMEM lane quarters
 constexpr int kFirstEpiWarp = 2;                   // warp 0 producer, warp 1 MMA issuer
 constexpr int kScreenThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 576
 constexpr uint32_t kTmemCols = kMTiles * kGolayTileN;  // 512: one accumulator stage per M-tile
-constexpr int kHeavyChunks = 96;                   // flagged chunks (of 102) beyond which the exhaustive scan runs
+constexpr int kHeavyChunks = 192;                  // flagged chunks (of 204) beyond which the exhaustive scan runs
 constexpr int kMaxSegs = 64;                       // input segments per pipeline batch
 constexpr int64_t kBatchAtoms = int64_t(1) << 20;  // atoms per pipeline batch
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s
-static_assert(kW16Chunk == 26 && kW16Skip == 8, "weight-16 block starts 8 columns into chunk 26");
+static_assert(kW16Chunk == 52 && kW16Skip == 8, "weight-16 block starts 8 columns into chunk 52");
 static_assert(kW16First + kOctads == kGolay - 1, "the all-ones word closes the weight-16 block");
 
 // Per-atom constants of the search (prep_kernel -> screen and rescore).
 struct __align__(16) AtomInfo {
   float off[2];  // -3 x_p1, -3 x_p2: added to the slice rows
-  float u;       // max(4 y3, 2 y3): bound for type-3 positions outside {p1, p2}
+  // Bounds of S(c, p) - B(c) = y_p (3 + (-1)^c_p) over the type-3 positions
+  // p outside {p1, p2} (y = -x, y3 >= y4 >= every other y_p):
+  float u0;      // Golay word without p3: max(4 y3, 2 y4)
+  float u1;      // Golay word with p3: max(2 y3, 4 y4, 2 y4)
   float shi;     // sum |hi_i|: added to the |x| row at weight-16 columns
   float t1;      // 4 (|x|_(1) + |x|_(2)): best type-1 score
   float l2s;     // 4 |x|_(8): type-2 parity allowance
   float two_e;   // 2E, or -1 for an atom with a non-finite coordinate
+  float t2lb;    // best type-2 score over the 21 octads through the three largest |x_i|
   uint8_t p[3];  // p1, p2, p3
-  uint8_t pad;
+  uint8_t pad[9];
 };
-static_assert(sizeof(AtomInfo) == 32, "AtomInfo is two 16-byte loads");
+static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 
 struct __align__(1024) ScreenSmem {
   uint8_t a[2][kAItemBytes];          // A operand of two work items
   uint8_t b[kStages][kBTileBytes];    // Golay tile ring
   float rowval[2][kWorkAtoms][kRowsPerAtom];  // per-row bests, by work-item parity
-  float cmax[kGolayTiles][kEpiWarps * 32];    // chunk maxima of each epilogue thread
+  // Chunk maxima of each epilogue thread, rounded up to fp16 (so the flags
+  // stay conservative).
+  __half cmax[kChunks][kEpiWarps * 32];
   uint64_t bar_a_full[2];
   uint64_t bar_a_empty[2];
   uint64_t bar_b_full[kStages];
@@ -358,7 +367,9 @@ __device__ __forceinline__ uint32_t a_offset(int L, int q) {
 // 2 plain, 3 |x|), so that each TMEM lane quarter holds every row type once
 // over the four M-tiles and the epilogue's work spreads evenly over the SM.
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
-                                                   int64_t n_pad, uint8_t *__restrict__ a_tiles,
+                                                   int64_t n_pad, const uint32_t *__restrict__ gmask,
+                                                   const uint16_t *__restrict__ oct_by_triple,
+                                                   uint8_t *__restrict__ a_tiles,
                                                    AtomInfo *__restrict__ info) {
   const int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (a >= n_pad) return;
@@ -382,11 +393,13 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   uint16_t hb[kDim];
   // Three smallest coordinates (lowest position first on ties) and the two
   // largest and eighth largest |x_i|.
-  float s0 = INFINITY, s1 = INFINITY, s2 = INFINITY;
+  float s0 = INFINITY, s1 = INFINITY, s2 = INFINITY, s3 = INFINITY;
   int q0 = 0, q1 = 1, q2 = 2;
   float top[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) top[k] = 0.f;
+  int a0 = 0, a1 = 1, a2 = 2;  // positions of the three largest |x_i|
+  uint32_t negm = 0;
 #pragma unroll
   for (int i = 0; i < kDim; ++i) {
     const __nv_bfloat16 h = __float2bfloat16_rn(v[i]);
@@ -399,12 +412,22 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
     shi += fabsf(hf);
     finite = finite && isfinite(v[i]);
     const float x = v[i];
-    if (x < s2) {
-      if (x < s1) {
-        s2 = s1; q2 = q1;
-        if (x < s0) { s1 = s0; q1 = q0; s0 = x; q0 = i; }
-        else { s1 = x; q1 = i; }
-      } else { s2 = x; q2 = i; }
+    if (x < s3) {
+      if (x < s2) {
+        s3 = s2;
+        if (x < s1) {
+          s2 = s1; q2 = q1;
+          if (x < s0) { s1 = s0; q1 = q0; s0 = x; q0 = i; }
+          else { s1 = x; q1 = i; }
+        } else { s2 = x; q2 = i; }
+      } else { s3 = x; }
+    }
+    negm |= (x < 0.f ? 1u : 0u) << i;
+    if (fabsf(x) > top[2]) {
+      if (fabsf(x) > top[1]) {
+        a2 = a1;
+        if (fabsf(x) > top[0]) { a1 = a0; a0 = i; } else { a1 = i; }
+      } else { a2 = i; }
     }
     float t = fabsf(x);
 #pragma unroll
@@ -424,16 +447,43 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   AtomInfo inf;
   inf.off[0] = -3.f * s0;
   inf.off[1] = -3.f * s1;
-  const float y3 = -s2;
-  inf.u = fmaxf(4.f * y3, 2.f * y3);
+  const float y3 = -s2, y4 = -s3;
+  inf.u0 = fmaxf(4.f * y3, 2.f * y4);
+  inf.u1 = fmaxf(2.f * y3, fmaxf(4.f * y4, 2.f * y4));
   inf.shi = shi;
   inf.t1 = 4.f * (top[0] + top[1]);
   inf.l2s = 4.f * top[7];
   inf.two_e = finite ? 2.f * e : -1.f;
+  // Achievable type-2 score: the best even-parity pattern, 2 T(O) - 4 [odd]
+  // min_O |x|, over the 21 octads that contain the three largest |x_i|.
+  float t2lb = -INFINITY;
+  {
+    // Sort the triple: i < j < k.
+    const int i3 = min(a0, min(a1, a2)), k3 = max(a0, max(a1, a2)), j3 = a0 + a1 + a2 - i3 - k3;
+    const uint4 *row = reinterpret_cast<const uint4 *>(
+        oct_by_triple + (k3 * (k3 - 1) * (k3 - 2) / 6 + j3 * (j3 - 1) / 2 + i3) * kTripleRow);
+    const uint4 r0 = __ldg(row), r1 = __ldg(row + 1), r2 = __ldg(row + 2);
+    const uint32_t ow[12] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w, r2.x, r2.y, r2.z, r2.w};
+#pragma unroll
+    for (int k = 0; k < 21; ++k) {
+      const int o = static_cast<int>((ow[k >> 1] >> (16 * (k & 1))) & 0xFFFFu);
+      const uint32_t om = ~__ldg(gmask + kW16First + o) & 0xFFFFFFu;
+      float t = 0.f, mn = INFINITY;
+#pragma unroll
+    for (int i = 0; i < kDim; ++i)
+      if (om >> i & 1u) {
+        t += fabsf(v[i]);
+        mn = fminf(mn, fabsf(v[i]));
+      }
+      t2lb = fmaxf(t2lb, 2.f * t - ((__popc(om & negm) & 1) ? 4.f * mn : 0.f));
+    }
+  }
+  inf.t2lb = t2lb;
   inf.p[0] = static_cast<uint8_t>(q0);
   inf.p[1] = static_cast<uint8_t>(q1);
   inf.p[2] = static_cast<uint8_t>(q2);
-  inf.pad = 0;
+#pragma unroll
+  for (int k = 0; k < 9; ++k) inf.pad[k] = 0;
   info[a] = inf;
 
   uint8_t *item = a_tiles + (a >> 7) * kAItemBytes;
@@ -470,14 +520,14 @@ struct ScreenArgs {
   const uint8_t *a_tiles;   // [items][kAItemBytes]
   const AtomInfo *info;     // [n_pad]
   const uint8_t *golay;     // [kGolayTiles][kBTileBytes]
-  uint32_t *masks;          // [n][4] flagged chunks per row type
+  uint2 *masks;             // [n][4] flagged 64-column chunks per row type
   float *thr;               // [n] best - 2E
   int64_t n;
   int64_t items;
   int *err;
 };
 
-__global__ void __maxnreg__(112) screen_kernel(const ScreenArgs args) {
+__global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenArgs args) {
   extern __shared__ uint8_t smem_raw[];
   ScreenSmem &S = *reinterpret_cast<ScreenSmem *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -618,7 +668,7 @@ __global__ void __maxnreg__(112) screen_kernel(const ScreenArgs args) {
     for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
       const int64_t atom = it * kWorkAtoms + local;
       const AtomInfo inf = args.info[atom];
-      float *cm = &S.cmax[0][e * 32 + lane];  // chunk t at cm[t * kEpiWarps * 32]
+      __half *cm = &S.cmax[0][e * 32 + lane];  // chunk k at cm[k * kEpiWarps * 32]
       float rowmax = -INFINITY;
 #pragma unroll
       for (int t = 0; t < kGolayTiles; ++t) {
@@ -626,8 +676,8 @@ __global__ void __maxnreg__(112) screen_kernel(const ScreenArgs args) {
         if (lane == 0) got = wait_bar_inl(&S.bar_acc_full[g], t & 1, abort_flag, args.err);
         if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
         tc_fence_after();
-        float m = -INFINITY;
-        if (r != 3 || t >= kW16Chunk) {
+        float m0 = -INFINITY, m1 = -INFINITY;
+        if (r != 3 || t >= kW16Tile) {
           uint32_t x[32];
           // Rolled: an unrolled loop lets the compiler keep several blocks of
           // loaded values live at once (register spills).
@@ -640,24 +690,25 @@ __global__ void __maxnreg__(112) screen_kernel(const ScreenArgs args) {
               __syncwarp();
               if (lane == 0) mbar_arrive(&S.bar_acc_empty[g]);
             }
-            if (r == 3 && t == kW16Chunk && k == 0) {
+            if (r == 3 && t == kW16Tile && k == 0) {
 #pragma unroll
               for (int i = 0; i < kW16Skip; ++i) x[i] = 0xFF800000u;  // dodecad columns
             }
             if (r == 3 && t == kGolayTiles - 1 && k == 3) x[31] = 0xFF800000u;  // all-ones word
-            m = max32(m, x);
+            if (k < 2) m0 = max32(m0, x); else m1 = max32(m1, x);
           }
         } else {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&S.bar_acc_empty[g]);
         }
-        cm[t * kEpiWarps * 32] = m;
-        rowmax = fmaxf(rowmax, m);
+        cm[(2 * t) * kEpiWarps * 32] = __float2half_ru(m0);
+        cm[(2 * t + 1) * kEpiWarps * 32] = __float2half_ru(m1);
+        rowmax = fmaxf(rowmax, fmaxf(m0, m1));
       }
       if (!ok) break;
       // Per-row best, exchanged through shared memory.
-      const float add = r < 2 ? inf.off[r] : (r == 2 ? inf.u : inf.shi);
+      const float add = r < 2 ? inf.off[r] : (r == 2 ? fmaxf(inf.u0, inf.u1) : inf.shi);
       S.rowval[ip][local][r] = r < 2 ? rowmax + add : (r == 3 ? rowmax + inf.shi - inf.l2s : -INFINITY);
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.bar_rows[ip]);
@@ -667,14 +718,17 @@ __global__ void __maxnreg__(112) screen_kernel(const ScreenArgs args) {
       __syncwarp();
       rph ^= 1u << ip;
       const float *rv = S.rowval[ip][local];
-      const float best = fmaxf(fmaxf(rv[0], rv[1]), fmaxf(rv[3], inf.t1));
+      const float best = fmaxf(fmaxf(fmaxf(rv[0], rv[1]), fmaxf(rv[3], inf.t1)), inf.t2lb);
       const float thr = best - inf.two_e;
-      uint32_t mask = 0;
+      uint32_t mlo = 0, mhi = 0;
 #pragma unroll
-      for (int t = 0; t < kGolayTiles; ++t) mask |= (cm[t * kEpiWarps * 32] + add >= thr ? 1u : 0u) << t;
-      if (!(inf.two_e >= 0.f)) mask = 0;
+      for (int k = 0; k < 32; ++k) {
+        mlo |= (__half2float(cm[k * kEpiWarps * 32]) + add >= thr ? 1u : 0u) << k;
+        mhi |= (__half2float(cm[(k + 32) * kEpiWarps * 32]) + add >= thr ? 1u : 0u) << k;
+      }
+      if (!(inf.two_e >= 0.f)) mlo = mhi = 0;
       if (atom < args.n) {
-        args.masks[atom * kRowsPerAtom + r] = mask;
+        args.masks[atom * kRowsPerAtom + r] = make_uint2(mlo, mhi);
         if (r == 0) args.thr[atom] = thr;
       }
       ip ^= 1;
@@ -754,7 +808,7 @@ __device__ __forceinline__ int32_t apply_rule(double best, int bj, int rule) {
 }
 
 struct RescoreArgs {
-  const uint4 *masks;        // [n] flagged chunks per row type
+  const uint4 *masks;        // [2n]: rows 0-1, rows 2-3 (64-bit chunk masks)
   const float *thr;          // [n]
   const AtomInfo *info;      // [n]
   const uint32_t *gmask;     // Golay masks
@@ -768,6 +822,21 @@ struct RescoreArgs {
   int rule;
 };
 
+// trivial_index for a warp whose lane i < 24 holds x_i in xl (all lanes hold
+// the atom in v): the exact fp64 norm only when the fp32 one is within a
+// factor 4 of the pack rule's 1e-8 (its rounding error is far smaller).
+__device__ __forceinline__ int trivial_index_warp(const float (&v)[kDim], float xl, int lane, int rule) {
+  const bool finite = __all_sync(0xffffffffu, lane >= kDim || isfinite(xl));
+  if (!finite) return rule == H24_RULE_TRAIN ? 0 : 1;
+  if (rule == H24_RULE_PACK) {
+    float ss = xl * xl;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (ss < 4e-16f) return trivial_index(v, rule);
+  }
+  return -1;
+}
+
 __device__ __forceinline__ float pick(const float (&v)[kDim], int p) {
   float r = 0.f;
 #pragma unroll
@@ -775,211 +844,251 @@ __device__ __forceinline__ float pick(const float (&v)[kDim], int p) {
   return r;
 }
 
-// Exact score of kissing point j into the lane's running best: one copy of
-// the fp64 loop for all call sites; it reloads the atom (an L1 hit) so that
-// the caller's copy stays in registers.
-__device__ __noinline__ void exact(const float *__restrict__ xg, const int8_t *__restrict__ cb_raw,
-                                   int j, double &bs, int &bj, int &nex) {
+constexpr int kRescoreWarps = 8;
+constexpr int kRescoreBlocksPerSm = 2;
+constexpr int kCandCap = 128;  // fp32 candidates per atom before the fp64 pass
+
+// fp64 score of kissing point j, for candidates beyond the list (exact ties
+// over many codewords): out of line, it reloads the atom.
+__device__ __noinline__ void exact_now(const float *__restrict__ xg, const int8_t *__restrict__ cb_raw,
+                                       int32_t j, double &bs, int &bj, int &nex) {
   float v[kDim];
   load_atom(xg, v);
   better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
   ++nex;
 }
 
-constexpr int kRescoreWarps = 8;
-constexpr int kRescoreBlocksPerSm = 2;
-
 // Persistent: each warp takes atoms a = warp, warp + warps, ...; no block
 // barrier inside the loop, so a slow atom holds up only its own warp.
-// Screening scores of single codewords are recomputed in fp32 from the exact
-// coordinates (error far below E): sum_{i in c} x_i is three lookups in
-// per-atom tables of the partial sums over each byte of the position mask.
+//
+// Pass 1 recomputes the screening score S' of every codeword behind the
+// flagged chunks in fp32 from the exact coordinates (sum_{i in c} x_i is
+// three lookups in per-atom tables of the partial sums over each byte of the
+// position mask) and lists those with S' >= thr = best - 2E.  Pass 2 scores
+// in fp64, in the reference's order, the listed codewords within 2 e' of the
+// largest S', e' = 2^-16 sum|x|, which bounds |S' - sqrt(8) R| with a wide
+// margin; the winner and every codeword tied with it are among them.
 __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     rescore_kernel(const __grid_constant__ Segs sg, const RescoreArgs r) {
   __shared__ float tab[kRescoreWarps][3][256];
+  __shared__ float cand_s[kRescoreWarps][kCandCap];
+  __shared__ int32_t cand_j[kRescoreWarps][kCandCap];
+  __shared__ int cand_n[kRescoreWarps];
   const int lane = threadIdx.x & 31;
-  float(*T)[256] = tab[threadIdx.x >> 5];
+  const int w = threadIdx.x >> 5;
+  float(*T)[256] = tab[w];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
   unsigned long long st_exh = 0, st_exact = 0, st_chunks = 0;
-  for (int64_t a = blockIdx.x * static_cast<int64_t>(kRescoreWarps) + (threadIdx.x >> 5); a < r.n;
-       a += nwarps) {
+  for (int64_t a = blockIdx.x * static_cast<int64_t>(kRescoreWarps) + w; a < r.n; a += nwarps) {
     const float *xg = atom_ptr(sg, a);
     float v[kDim];
     load_atom(xg, v);
-    const int triv = trivial_index(v, r.rule);
-    const uint4 mk = r.masks[a];
-    const int nch = __popc(mk.x) + __popc(mk.y) + __popc(mk.z) + __popc(mk.w);
+    const float xl = lane < kDim ? __ldg(xg + lane) : 0.f;  // lane i: x_i
+    const int triv = trivial_index_warp(v, xl, lane, r.rule);
+    const uint4 mq0 = r.masks[2 * a], mq1 = r.masks[2 * a + 1];
+    const uint64_t mrow[4] = {mq0.x | static_cast<uint64_t>(mq0.y) << 32,
+                              mq0.z | static_cast<uint64_t>(mq0.w) << 32,
+                              mq1.x | static_cast<uint64_t>(mq1.y) << 32,
+                              mq1.z | static_cast<uint64_t>(mq1.w) << 32};
+    const int nch = __popcll(mrow[0]) + __popcll(mrow[1]) + __popcll(mrow[2]) + __popcll(mrow[3]);
     if (triv >= 0) {
       if (lane == 0) r.out[a] = triv;
       continue;
     }
     st_chunks += nch;
-    if (nch > kHeavyChunks) {
-      if (lane == 0) {
-        // Certain origin under the training rule: every score is at most
-        // 2 ||x|| (Cauchy-Schwarz, ||kp|| = 2).
-        double ss = 0.0;
-#pragma unroll
-        for (int i = 0; i < kDim; ++i)
-          ss = __fma_rn(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
-        r.out[a] = 0;
-        if (!(r.rule == H24_RULE_TRAIN && 4.0 * sqrt(ss) * (1.0 + 1e-6) < kCSqNorm)) {
-          r.ovf_list[atomicAdd(r.ovf_count, 1)] = static_cast<int32_t>(a);
-          ++st_exh;
-        }
-      }
-      continue;
-    }
-    const float thr = r.thr[a];
-    const AtomInfo inf = r.info[a];
-    // Partial-sum tables: T[k][s] = sum of x_{8k+i} over the bits i of s.
-    __syncwarp();  // the previous atom's lookups are done
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      float lo5 = 0.f;
-#pragma unroll
-      for (int i = 0; i < 5; ++i)
-        if (lane >> i & 1) lo5 += v[8 * k + i];
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        float hi3 = lo5;
-        if (m & 1) hi3 += v[8 * k + 5];
-        if (m & 2) hi3 += v[8 * k + 6];
-        if (m & 4) hi3 += v[8 * k + 7];
-        T[k][lane + 32 * m] = hi3;
-      }
-    }
-    __syncwarp();
-    float sumx = 0.f, sumabs = 0.f;
-    uint32_t negm = 0;
-#pragma unroll
-    for (int i = 0; i < kDim; ++i) {
-      sumx += v[i];
-      sumabs += fabsf(v[i]);
-      negm |= (v[i] < 0.f ? 1u : 0u) << i;
-    }
-    const auto tsum = [&](uint32_t m) { return T[0][m & 255] + T[1][(m >> 8) & 255] + T[2][m >> 16]; };
+    bool heavy = nch > kHeavyChunks;
+    // Running fp64 best of this lane (list overflow and the fp64 pass).
     double bs = -INFINITY;
     int bj = 0x7FFFFFFF;
     int nex = 0;
-    const int p1 = inf.p[0], p2 = inf.p[1];
-    // Type 3 at the slice positions p1, p2.
-#pragma unroll 1
-    for (int s = 0; s < 2; ++s) {
-      uint32_t m = s ? mk.y : mk.x;
-      const int p = s ? p2 : p1;
-      const float xp = pick(v, p);
-      while (m) {
-        const int b = __ffs(m) - 1;
-        m &= m - 1;
-#pragma unroll 1
-        for (int k = 0; k < 4; ++k) {
-          const int c = b * kGolayTileN + 32 * k + lane;
-          const uint32_t gm = __ldg(r.gmask + c);
-          const float bc = sumx - 2.f * tsum(gm);
-          if (bc - xp * ((gm >> p & 1u) ? 2.f : 4.f) >= thr)
-            exact(xg, r.cb_raw, __ldg(r.idx3 + c * kDim + p), bs, bj, nex);
-        }
-      }
-    }
-    // Type 3 at the other positions, behind flagged chunks of the plain row.
-    {
-      uint32_t m = mk.z;
-      while (m) {
-        const int b = __ffs(m) - 1;
-        m &= m - 1;
-#pragma unroll 1
-        for (int k = 0; k < 4; ++k) {
-          const int c = b * kGolayTileN + 32 * k + lane;
-          const uint32_t gm = __ldg(r.gmask + c);
-          const float bc = sumx - 2.f * tsum(gm);
-          if (bc + inf.u >= thr) {
-            uint32_t hit = 0;
+    if (!heavy) {
+      const float thr = r.thr[a];
+      const AtomInfo inf = r.info[a];
+      __syncwarp();  // the previous atom's table and list reads are done
+      if (lane == 0) cand_n[w] = 0;
+      // Partial-sum tables: T[k][s] = sum of x_{8k+i} over the bits i of s.
 #pragma unroll
-            for (int p = 0; p < kDim; ++p)
-              hit |= (bc - v[p] * ((gm >> p & 1u) ? 2.f : 4.f) >= thr ? 1u : 0u) << p;
-            hit &= ~((1u << p1) | (1u << p2));
-            while (hit) {
-              const int p = __ffs(hit) - 1;
-              hit &= hit - 1;
-              exact(xg, r.cb_raw, __ldg(r.idx3 + c * kDim + p), bs, bj, nex);
-            }
-          }
+      for (int k = 0; k < 3; ++k) {
+        float lo5 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 5; ++i)
+          if (lane >> i & 1) lo5 += v[8 * k + i];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          float hi3 = lo5;
+          if (m & 1) hi3 += v[8 * k + 5];
+          if (m & 2) hi3 += v[8 * k + 6];
+          if (m & 4) hi3 += v[8 * k + 7];
+          T[k][lane + 32 * m] = hi3;
         }
       }
-    }
-    // Type 2, behind flagged chunks of the |x| row: octads first, then the
-    // 128 sign patterns of each surviving octad across the warp.
-    {
-      uint32_t m = mk.w;
-      while (m) {
-        const int b = __ffs(m) - 1;
-        m &= m - 1;
+      __syncwarp();
+      // Sums over the coordinates, lane i holding x_i.
+      float sumx = xl, sumabs = fabsf(xl);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        sumx += __shfl_xor_sync(0xffffffffu, sumx, off);
+        sumabs += __shfl_xor_sync(0xffffffffu, sumabs, off);
+      }
+      const uint32_t negm = __ballot_sync(0xffffffffu, xl < 0.f);
+      const auto tsum = [&](uint32_t m) { return T[0][m & 255] + T[1][(m >> 8) & 255] + T[2][m >> 16]; };
+      const auto push = [&](float sc, int32_t j) {
+        const int k = atomicAdd(&cand_n[w], 1);
+        if (k < kCandCap) {
+          cand_s[w][k] = sc;
+          cand_j[w][k] = j;
+        } else {
+          exact_now(xg, r.cb_raw, j, bs, bj, nex);
+        }
+      };
+      const int p1 = inf.p[0], p2 = inf.p[1], p3 = inf.p[2];
+      // Type 3 at the slice positions p1, p2.
 #pragma unroll 1
-        for (int k = 0; k < 4; ++k) {
-          const int c = b * kGolayTileN + 32 * k + lane;
-          const int o = c - kW16First;
-          uint32_t om = 0;
-          bool cand = false;
-          if (o >= 0 && o < kOctads) {
+      for (int s = 0; s < 2; ++s) {
+        uint64_t m = s ? mrow[1] : mrow[0];
+        const int p = s ? p2 : p1;
+        const float xp = pick(v, p);
+        while (m) {
+          const int b = __ffsll(m) - 1;
+          m &= m - 1;
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int c = b * kChunkCols + 32 * k + lane;
             const uint32_t gm = __ldg(r.gmask + c);
-            om = ~gm & 0xFFFFFFu;
-            const float in_c = tsum(gm & ~negm) - tsum(gm & negm);  // sum_{i in c} |x_i|
-            cand = 2.f * (sumabs - in_c) >= thr;
+            const float sc = sumx - 2.f * tsum(gm) - xp * ((gm >> p & 1u) ? 2.f : 4.f);
+            if (sc >= thr) push(sc, __ldg(r.idx3 + c * kDim + p));
           }
-          uint32_t bal = __ballot_sync(0xffffffffu, cand);
-          while (bal) {
-            const int src = __ffs(bal) - 1;
-            bal &= bal - 1;
-            const int oc = __shfl_sync(0xffffffffu, o, src);
-            const uint32_t omc = __shfl_sync(0xffffffffu, om, src);
-            // The octad's 8 coordinates, lowest position first, to every lane.
-            float ov = 0.f;
-            if (lane < 8) ov = pick(v, static_cast<int>(__fns(omc, 0, lane + 1)));
-            float o8[8];
+        }
+      }
+      // Type 3 at the other positions, behind flagged chunks of the plain row.
+      {
+        uint64_t m = mrow[2];
+        while (m) {
+          const int b = __ffsll(m) - 1;
+          m &= m - 1;
+#pragma unroll 1
+          for (int k = 0; k < 2; ++k) {
+            const int c = b * kChunkCols + 32 * k + lane;
+            const uint32_t gm = __ldg(r.gmask + c);
+            const float bc = sumx - 2.f * tsum(gm);
+            if (bc + ((gm >> p3 & 1u) ? inf.u1 : inf.u0) >= thr) {
+              uint32_t hit = 0;
 #pragma unroll
-            for (int k2 = 0; k2 < 8; ++k2) o8[k2] = __shfl_sync(0xffffffffu, ov, k2);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const int pid = lane + 32 * t;
-              float sc = (__popc(pid) & 1) ? -o8[7] : o8[7];
-#pragma unroll
-              for (int k2 = 0; k2 < 7; ++k2) sc += (pid >> k2 & 1) ? -o8[k2] : o8[k2];
-              if (2.f * sc >= thr) exact(xg, r.cb_raw, __ldg(r.idx2 + oc * 128 + pid), bs, bj, nex);
+              for (int p = 0; p < kDim; ++p)
+                hit |= (bc - v[p] * ((gm >> p & 1u) ? 2.f : 4.f) >= thr ? 1u : 0u) << p;
+              hit &= ~((1u << p1) | (1u << p2));
+              while (hit) {
+                const int p = __ffs(hit) - 1;
+                hit &= hit - 1;
+                push(bc - pick(v, p) * ((gm >> p & 1u) ? 2.f : 4.f), __ldg(r.idx3 + c * kDim + p));
+              }
             }
           }
         }
       }
-    }
-    // Type 1: every score is at most t1.
-    if (inf.t1 >= thr && lane < kDim) {
-      const float xa = pick(v, lane);
+      // Type 2, behind flagged chunks of the |x| row: octads whose best
+      // even-parity pattern, 2 T(O) - 4 [odd] min_O |x|, reaches thr; then
+      // their 128 sign patterns across the warp.
+      {
+        uint64_t m = mrow[3];
+        while (m) {
+          const int b = __ffsll(m) - 1;
+          m &= m - 1;
 #pragma unroll 1
-      for (int b2 = lane + 1; b2 < kDim; ++b2) {
-        const float xb = pick(v, b2);
+          for (int k = 0; k < 2; ++k) {
+            const int c = b * kChunkCols + 32 * k + lane;
+            const int o = c - kW16First;
+            uint32_t om = 0;
+            float t2 = -INFINITY;
+            if (o >= 0 && o < kOctads) {
+              const uint32_t gm = __ldg(r.gmask + c);
+              om = ~gm & 0xFFFFFFu;
+              t2 = 2.f * (sumabs - (tsum(gm & ~negm) - tsum(gm & negm)));  // 2 T(O)
+            }
+            uint32_t bal = __ballot_sync(0xffffffffu, t2 >= thr);
+            while (bal) {
+              const int src = __ffs(bal) - 1;
+              bal &= bal - 1;
+              const int oc = __shfl_sync(0xffffffffu, o, src);
+              const uint32_t omc = __shfl_sync(0xffffffffu, om, src);
+              const float t2c = __shfl_sync(0xffffffffu, t2, src);
+              // The octad's 8 coordinates, lowest position first, to every lane.
+              float ov = 0.f;
+              if (lane < 8) ov = pick(v, static_cast<int>(__fns(omc, 0, lane + 1)));
+              // Best even-parity pattern: 2 T(O) - 4 [odd] min_O |x|.
+              // (Over all 32 lanes, so that every lane takes the same branch.)
+              float mn = lane < 8 ? fabsf(ov) : INFINITY;
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const float sc = 4.f * ((s & 1 ? -xa : xa) + (s & 2 ? -xb : xb));
-          if (sc >= thr) exact(xg, r.cb_raw, __ldg(r.idx1 + (lane * kDim + b2) * 4 + s), bs, bj, nex);
+              for (int off = 16; off > 0; off >>= 1) mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+              const bool odd = __popc(__ballot_sync(0xffffffffu, lane < 8 && ov < 0.f)) & 1;
+              if (t2c - (odd ? 4.f * mn : 0.f) < thr) continue;
+              float o8[8];
+#pragma unroll
+              for (int k2 = 0; k2 < 8; ++k2) o8[k2] = __shfl_sync(0xffffffffu, ov, k2);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const int pid = lane + 32 * t;
+                float sc = (__popc(pid) & 1) ? -o8[7] : o8[7];
+#pragma unroll
+                for (int k2 = 0; k2 < 7; ++k2) sc += (pid >> k2 & 1) ? -o8[k2] : o8[k2];
+                if (2.f * sc >= thr) push(2.f * sc, __ldg(r.idx2 + oc * 128 + pid));
+              }
+            }
+          }
         }
       }
-    }
+      // Type 1: every score is at most t1.
+      if (inf.t1 >= thr && lane < kDim) {
+        const float xa = pick(v, lane);
+#pragma unroll 1
+        for (int b2 = lane + 1; b2 < kDim; ++b2) {
+          const float xb = pick(v, b2);
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const double os = __shfl_xor_sync(0xffffffffu, bs, off);
-      const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
-      better(bs, bj, os, oj);
-      nex += __shfl_xor_sync(0xffffffffu, nex, off);
+          for (int s = 0; s < 4; ++s) {
+            const float sc = 4.f * ((s & 1 ? -xa : xa) + (s & 2 ? -xb : xb));
+            if (sc >= thr) push(sc, __ldg(r.idx1 + (lane * kDim + b2) * 4 + s));
+          }
+        }
+      }
+      __syncwarp();
+      const int nc = min(cand_n[w], kCandCap);
+      heavy = cand_n[w] == 0;  // cannot happen while the bound holds
+      if (!heavy) {
+        float smax = -INFINITY;
+        for (int k = lane; k < nc; k += 32) smax = fmaxf(smax, cand_s[w][k]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
+        const float cut = smax - 3.0517578125e-5f * sumabs;  // 2 e'
+        for (int k = lane; k < nc; k += 32) {
+          if (cand_s[w][k] >= cut) {
+            const int j = cand_j[w][k];
+            better(bs, bj, score64(v, r.cb_raw + static_cast<int64_t>(j) * kDim), j);
+            ++nex;
+          }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          const double os = __shfl_xor_sync(0xffffffffu, bs, off);
+          const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+          better(bs, bj, os, oj);
+          nex += __shfl_xor_sync(0xffffffffu, nex, off);
+        }
+        st_exact += nex;
+        if (lane == 0) r.out[a] = apply_rule(bs, bj, r.rule);
+      }
     }
-    st_exact += nex;
-    if (lane == 0) {
-      if (bj == 0x7FFFFFFF) {
-        // No codeword passed (cannot happen when the bound holds): scan all.
-        r.out[a] = 0;
+    if (heavy && lane == 0) {
+      // Too many candidates (exact ties over many codewords): the exhaustive
+      // scan.  Certain origin under the training rule instead when every
+      // score is at most 2 ||x|| (Cauchy-Schwarz, ||kp|| = 2) < c_sq_norm / 2.
+      double ss = 0.0;
+#pragma unroll
+      for (int i = 0; i < kDim; ++i)
+        ss = __fma_rn(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+      r.out[a] = 0;
+      if (!(r.rule == H24_RULE_TRAIN && 4.0 * sqrt(ss) * (1.0 + 1e-6) < kCSqNorm)) {
         r.ovf_list[atomicAdd(r.ovf_count, 1)] = static_cast<int32_t>(a);
         ++st_exh;
-      } else {
-        r.out[a] = apply_rule(bs, bj, r.rule);
       }
     }
   }
@@ -1032,7 +1141,7 @@ int g_sms[64] = {};
 struct Scratch {
   uint8_t *a_tiles;
   AtomInfo *info;
-  uint32_t *masks;
+  uint2 *masks;
   float *thr;
   int32_t *ovf_list;
   int32_t *ovf_count;
@@ -1041,7 +1150,7 @@ constexpr size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255);
 constexpr size_t scratch_bytes(int64_t pad) {
   return up256(static_cast<size_t>(pad) / kWorkAtoms * kAItemBytes) +
          up256(static_cast<size_t>(pad) * sizeof(AtomInfo)) +
-         up256(static_cast<size_t>(pad) * kRowsPerAtom * 4) + up256(static_cast<size_t>(pad) * 4) +
+         up256(static_cast<size_t>(pad) * kRowsPerAtom * 8) + up256(static_cast<size_t>(pad) * 4) +
          up256(static_cast<size_t>(pad) * 4) + 256;
 }
 Scratch carve(uint8_t *base, int64_t pad) {
@@ -1051,8 +1160,8 @@ Scratch carve(uint8_t *base, int64_t pad) {
   o += up256(static_cast<size_t>(pad) / kWorkAtoms * kAItemBytes);
   sc.info = reinterpret_cast<AtomInfo *>(base + o);
   o += up256(static_cast<size_t>(pad) * sizeof(AtomInfo));
-  sc.masks = reinterpret_cast<uint32_t *>(base + o);
-  o += up256(static_cast<size_t>(pad) * kRowsPerAtom * 4);
+  sc.masks = reinterpret_cast<uint2 *>(base + o);
+  o += up256(static_cast<size_t>(pad) * kRowsPerAtom * 8);
   sc.thr = reinterpret_cast<float *>(base + o);
   o += up256(static_cast<size_t>(pad) * 4);
   sc.ovf_list = reinterpret_cast<int32_t *>(base + o);
@@ -1066,8 +1175,8 @@ int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int3
                  const Scratch &sc, int sms, cudaStream_t s) {
   const int64_t items = (nbatch + kWorkAtoms - 1) / kWorkAtoms;
   const int64_t npad = items * kWorkAtoms;
-  prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(sg, nbatch, npad,
-                                                                      sc.a_tiles, sc.info);
+  prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(
+      sg, nbatch, npad, t->golay_mask, t->oct_by_triple, sc.a_tiles, sc.info);
   ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
                 sc.thr, nbatch, items, t->err};
   const int grid = static_cast<int>(items < sms ? items : sms);
@@ -1102,6 +1211,20 @@ int screen_setup(int dev, int *sms) {
     H24_CUDA_TRY(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
     H24_CUDA_TRY(cudaFuncSetAttribute(screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(sizeof(ScreenSmem) + 1024)));
+    // Launch sizes against what each kernel's resources allow.
+    const struct { const void *fn; int threads; const char *name; } ks[] = {
+        {reinterpret_cast<const void *>(screen_kernel), kScreenThreads, "screen_kernel"},
+        {reinterpret_cast<const void *>(rescore_kernel), 32 * kRescoreWarps, "rescore_kernel"},
+        {reinterpret_cast<const void *>(prep_kernel), 256, "prep_kernel"},
+        {reinterpret_cast<const void *>(exhaustive_kernel), 256, "exhaustive_kernel"}};
+    for (const auto &k : ks) {
+      cudaFuncAttributes at;
+      H24_CUDA_TRY(cudaFuncGetAttributes(&at, k.fn));
+      if (at.maxThreadsPerBlock < k.threads)
+        return fail(H24_ERR_STATE, std::string(k.name) + ": " + std::to_string(at.numRegs) +
+                                       " registers allow " + std::to_string(at.maxThreadsPerBlock) +
+                                       " threads per block, launch needs " + std::to_string(k.threads));
+    }
     g_sms[dev] = count;
   }
   *sms = g_sms[dev];
