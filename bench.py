@@ -459,10 +459,28 @@ def run_components(args) -> dict:
                 ts.append(e0.elapsed_time(e1) / calls)
         return statistics.median(ts)
 
+    # INT8 token embedding (PolluxConfig defaults: vocab 50688 x n_embd 1920),
+    # two buffer sets of 389 MB of fp32 each.
+    vocab, d = 50688, 1920
+    emb_w = [torch.randn(vocab, d, device=dev) * 0.02 for _ in range(2)]
+    emb_q = [torch.empty(vocab, d, dtype=torch.int8, device=dev) for _ in range(2)]
+    emb_mu = [torch.empty(vocab, dtype=torch.float16, device=dev) for _ in range(2)]
+    emb_out = [torch.empty(vocab, d, dtype=torch.float16, device=dev) for _ in range(2)]
+
+    def int8_quant(k):
+        N.check(lib.h24_int8_quantize(emb_w[k].data_ptr(), vocab, d, emb_q[k].data_ptr(),
+                                      emb_mu[k].data_ptr(), stream), "int8_quantize")
+
+    def int8_deq(k):
+        N.check(lib.h24_int8_dequant(emb_q[k].data_ptr(), emb_mu[k].data_ptr(), vocab, d,
+                                     emb_out[k].data_ptr(), stream), "int8_dequant")
+
     reps = max(3, args.steps)
     t_pack = timed(pack, sets, reps)
     t_unpack = timed(unpack, sets, reps)
     t_deq = timed(dequant, 2, reps)
+    t_i8q = timed(int8_quant, 2, reps)
+    t_i8d = timed(int8_deq, 2, reps)
     torch.cuda.synchronize()
     for k in range(sets):
         assert torch.equal(backs[k], idxs[k]), "pack/unpack round trip failed"
@@ -476,12 +494,16 @@ def run_components(args) -> dict:
     pack_bytes = n * 4 + packs[0].numel()
     deq_bytes = packs[0].numel() + layers * rows * 2 + layers * rows * in_f * 2
     res = {}
+    i8q_bytes = vocab * d * 5 + vocab * 2      # fp32 in, int8 + fp16 scales out
+    i8d_bytes = vocab * d * 3 + vocab * 2      # int8 + scales in, fp16 out
     for name, t, b in (("pack", t_pack, pack_bytes), ("unpack", t_unpack, pack_bytes),
-                       ("dequant", t_deq, deq_bytes)):
+                       ("dequant", t_deq, deq_bytes), ("int8_quantize", t_i8q, i8q_bytes),
+                       ("int8_dequant", t_i8d, i8d_bytes)):
         gbs = b / (t / 1e3) / 1e9
         res[name] = {"ms": t, "algorithmic_bytes": b, "GB_per_s": gbs, "frac_of_measured_hbm": gbs / peak}
     res["workload"] = ("config5: 18 layers x [7680,1920], 11,059,200 uniform indices; pack int32->18-bit, "
-                       "unpack 18-bit->int32, batched LUT dequant to fp16; back-to-back calls over "
+                       "unpack 18-bit->int32, batched LUT dequant to fp16; INT8 embedding "
+                       "[50688,1920] quantize and dequant; back-to-back calls over "
                        "rotating buffer sets larger than L2, after an L2 flush")
     res["hbm_peak_gbs"] = peak
     return res

@@ -102,6 +102,21 @@ typedef struct h24_dequant_layer {
 int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad_count,
                         void *stream);
 
+/* ---- INT8 token embedding / output head ------------------------------------
+ * Per-row INT8 quantisation (pack._quantize_int8, pack.py:124-136):
+ * mu = max(max_c |w[r][c]|, 1e-8) in fp32, q = clamp(rint(w / mu * 127),
+ * -128, 127), mu16 = fp16(mu).  w: rows x cols fp32 row-major; q: rows x cols
+ * int8; mu16: rows fp16 bits.  A NaN in a row makes its mu NaN and every q 0
+ * (torch's amax and int8 cast). */
+int h24_int8_quantize(const float *w, int64_t rows, int64_t cols, int8_t *q, uint16_t *mu16,
+                      void *stream);
+
+/* INT8 reconstruction (PackedInt8Embedding.materialize / PackedInt8Linear.
+ * materialize, pollux.py:519-528, 545-554): out16 = fp16(q * fp16(mu16 / 127)),
+ * both roundings of the reference kept. */
+int h24_int8_dequant(const int8_t *q, const uint16_t *mu16, int64_t rows, int64_t cols,
+                     uint16_t *out16, void *stream);
+
 /* ---- nearest codeword (castor._leech_nn_kernel / castor_quantize_leech,
  *      castor.py:386-560; pack._quantize_h24_layer search, pack.py:166-177) --
  * x: n atoms of 24 fp32 values (16-byte aligned), out_idx: n int32 indices.

@@ -278,3 +278,25 @@ def sigma16_pack_rule(weight: np.ndarray) -> np.ndarray:
     s = (rms * np.float32(np.sqrt(12.0))).astype(np.float32)
     s = np.maximum(s, np.float32(1e-8))
     return s.astype(np.float16)
+
+
+def int8_quantize(weight: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """numpy restatement of pack._quantize_int8 (pack.py:124-136): per row
+    mu = max(max|w|, fp32(1e-8)) in fp32, q = clamp(round_half_even(
+    fp32(fp32(w / mu) * 127)), -128, 127) as int8 (NaN -> 0), mu as fp16."""
+    w = np.asarray(weight, dtype=np.float32)
+    with np.errstate(invalid="ignore", divide="ignore", over="ignore"):
+        mu = np.max(np.abs(w), axis=-1, keepdims=True)        # NaN propagates
+        mu = np.where(np.isnan(mu), mu, np.maximum(mu, np.float32(1e-8)))
+        t = (w / mu).astype(np.float32) * np.float32(127.0)
+        r = np.clip(np.rint(t), -128, 127)
+        q = np.where(np.isnan(r), 0, r).astype(np.int8)
+        return q, mu[..., 0].astype(np.float16)
+
+
+def int8_dequant(q: np.ndarray, mu16: np.ndarray) -> np.ndarray:
+    """numpy restatement of PackedInt8Embedding/Linear.materialize
+    (pollux.py:519-523): fp16(q * fp16(fp32(mu) / 127)), both roundings."""
+    with np.errstate(invalid="ignore", over="ignore"):
+        s = (np.asarray(mu16, dtype=np.float16).astype(np.float32) / np.float32(127.0)).astype(np.float16)
+        return (np.asarray(q).astype(np.float32) * s.astype(np.float32)[..., None]).astype(np.float16)

@@ -7,8 +7,8 @@ and LUT dequantisation, behind the reference's own Python signatures.
 
 Modules:
   castor         -- castor.py mirror (codebook, quantizer, pack/unpack, helpers)
-  pack           -- pack._quantize_h24_layer mirror
-  packed_linear  -- PackedH24Linear / materialize mirror, batched materialize
+  pack           -- pack._quantize_h24_layer and pack._quantize_int8 mirrors
+  packed_linear  -- PackedH24Linear / PackedInt8* / materialize mirrors, batched materialize
   plx            -- .plx container reader / writer
   shard          -- row sharding across ranks, optional all-gather of packed bytes
   build          -- nvcc build recipe of libh24.so
@@ -25,7 +25,7 @@ _PATCHES = {
     "castor": ["castor_quantize_leech", "pack_indices", "unpack_indices", "centers_to_indices",
                "CastorQuantizeLeech"],
     "pollux": ["castor_quantize_leech", "unpack_indices"],
-    "pack": ["pack_indices", "_quantize_h24_layer"],
+    "pack": ["pack_indices", "_quantize_h24_layer", "_quantize_int8"],
 }
 
 
@@ -44,6 +44,7 @@ def install(modules: dict | None = None) -> list[str]:
         "centers_to_indices": c.centers_to_indices,
         "CastorQuantizeLeech": c.CastorQuantizeLeech,
         "_quantize_h24_layer": p._quantize_h24_layer,
+        "_quantize_int8": p._quantize_int8,
     }
     mods = modules if modules is not None else {k: sys.modules.get(k) for k in _PATCHES}
     done = []
@@ -59,4 +60,8 @@ def install(modules: dict | None = None) -> list[str]:
     if pol is not None and hasattr(pol, "PackedH24Linear"):
         pol.PackedH24Linear.materialize = pl.materialize
         done.append("pollux.PackedH24Linear.materialize")
+    for cls in ("PackedInt8Embedding", "PackedInt8Linear"):
+        if pol is not None and hasattr(pol, cls):
+            getattr(pol, cls).materialize = pl.materialize_int8
+            done.append(f"pollux.{cls}.materialize")
     return done

@@ -474,6 +474,20 @@ int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad
   return launch_dequant(T, nullptr, layers, count, bad_count, as_stream(stream));
 }
 
+int h24_int8_quantize(const float *w, int64_t rows, int64_t cols, int8_t *q, uint16_t *mu16,
+                      void *stream) {
+  if (rows < 0 || cols < 0) return fail(H24_ERR_INVALID, "int8_quantize: negative size");
+  if (rows > 0 && cols > 0 && (!w || !q || !mu16)) return fail(H24_ERR_INVALID, "int8_quantize: null pointer");
+  return launch_int8_quantize(w, rows, cols, q, mu16, as_stream(stream));
+}
+
+int h24_int8_dequant(const int8_t *q, const uint16_t *mu16, int64_t rows, int64_t cols,
+                     uint16_t *out16, void *stream) {
+  if (rows < 0 || cols < 0) return fail(H24_ERR_INVALID, "int8_dequant: negative size");
+  if (rows > 0 && cols > 0 && (!q || !mu16 || !out16)) return fail(H24_ERR_INVALID, "int8_dequant: null pointer");
+  return launch_int8_dequant(q, mu16, rows, cols, out16, as_stream(stream));
+}
+
 int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *stream) {
   H24_TABLES_OR_FAIL(T);
   if (n < 0) return fail(H24_ERR_INVALID, "quantize: negative atom count");

@@ -690,11 +690,11 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
               __syncwarp();
               if (lane == 0) mbar_arrive(&S.bar_acc_empty[g]);
             }
-            if (r == 3 && t == kW16Tile && k == 0) {
+            if (t == kW16Tile && r == 3 && k == 0) {
 #pragma unroll
               for (int i = 0; i < kW16Skip; ++i) x[i] = 0xFF800000u;  // dodecad columns
             }
-            if (r == 3 && t == kGolayTiles - 1 && k == 3) x[31] = 0xFF800000u;  // all-ones word
+            if (t == kGolayTiles - 1 && r == 3 && k == 3) x[31] = 0xFF800000u;  // all-ones word
             if (k < 2) m0 = max32(m0, x); else m1 = max32(m1, x);
           }
         } else {

@@ -1,5 +1,6 @@
 """Drop-in mirror of the reference's ``pack._quantize_h24_layer``
-(pack.py:139-180), the checkpoint -> .plx quantiser, on libh24.
+(pack.py:139-180) and ``pack._quantize_int8`` (pack.py:124-136), the
+checkpoint -> .plx quantisers, on libh24.
 
 ``_quantize_h24_layer(weight, codebook) -> (packed_u8_cpu, sigma_f16_cpu)``:
   * sigma_rows = fp16(clamp_min(sqrt(mean(w^2)+1e-8) * sqrt(12), 1e-8)) per row
@@ -80,3 +81,30 @@ def quantize_layers(weights: list[torch.Tensor]) -> list[tuple[torch.Tensor, tor
         outs.append((packed, sigma))
     _call(dev, "h24_quantize_layers", ctypes.cast(layers, ctypes.c_void_p), len(ws), _stream(dev))
     return outs
+
+
+def quantize_int8_device(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row INT8 quantisation on the GPU: (q int8 with weight's shape, mu
+    fp16 with weight.shape[:-1]) on the weight's CUDA device (the staging
+    device for host tensors)."""
+    w = weight.detach()
+    if w.dim() == 0:
+        raise IndexError("Dimension specified as -1 but tensor has no dimensions")
+    dev = _work_device(w)
+    cols = w.shape[-1]
+    rows = w.numel() // cols if cols else 0
+    wd = _aligned(w.to(device=dev, dtype=torch.float32).reshape(rows, cols))
+    q = torch.empty(rows, cols, dtype=torch.int8, device=dev)
+    mu = torch.empty(rows, dtype=torch.float16, device=dev)
+    if rows and cols:
+        _call(dev, "h24_int8_quantize", wd.data_ptr(), rows, cols, q.data_ptr(), mu.data_ptr(),
+              _stream(dev))
+    return q.reshape(w.shape), mu.reshape(w.shape[:-1])
+
+
+def _quantize_int8(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row INT8 quantization with FP16 per-row operational scales mu
+    (pack._quantize_int8): weight ~ (q / 127) * mu_rows[:, None].  Returns
+    host tensors, as the reference does."""
+    q, mu = quantize_int8_device(weight)
+    return q.cpu(), mu.cpu()

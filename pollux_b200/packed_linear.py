@@ -8,6 +8,10 @@ bit-identical to the reference's two torch multiplications (pollux.py:497-499),
 then drops the packed buffers exactly as the reference does (pollux.py:500-504).
 ``materialize_all`` dequantises every packed layer of a model with one launch
 per 64 layers (the loop of from_packed_checkpoint, pollux.py:748-750).
+
+``PackedInt8Embedding`` / ``PackedInt8Linear`` (pollux.py:510-563) and
+``materialize_int8`` rebuild the INT8 token embedding and output head,
+weight = fp16(q * fp16(mu / 127)), with one launch per tensor.
 """
 from __future__ import annotations
 
@@ -127,3 +131,76 @@ def materialize_all(model: nn.Module) -> int:
         del m.sigma_rows
         m._materialized = True
     return len(mods)
+
+
+def int8_dequant(weight_int8: torch.Tensor, mu_rows: torch.Tensor) -> torch.Tensor:
+    """fp16 weight = q * (mu / 127) per row, both fp16 roundings of the
+    reference (pollux.py:519-523)."""
+    if weight_int8.dtype != torch.int8:
+        raise TypeError(f"weight_int8 must be int8, got {weight_int8.dtype}")
+    if mu_rows.dtype != torch.float16:
+        raise TypeError(f"mu_rows must be float16, got {mu_rows.dtype}")
+    dev = _work_device(weight_int8)
+    cols = weight_int8.shape[-1]
+    rows = weight_int8.numel() // cols if cols else 0
+    if mu_rows.numel() != rows:
+        raise RuntimeError(f"mu_rows has {mu_rows.numel()} scales for {rows} rows")
+    q = _aligned(weight_int8.to(dev).reshape(rows, cols))
+    mu = mu_rows.reshape(-1).to(dev).contiguous()
+    out = torch.empty(rows, cols, dtype=torch.float16, device=dev)
+    if rows and cols:
+        _call(dev, "h24_int8_dequant", q.data_ptr(), mu.data_ptr(), rows, cols, out.data_ptr(),
+              _stream(dev))
+    return out.reshape(weight_int8.shape)
+
+
+def materialize_int8(self) -> None:
+    """PackedInt8Embedding.materialize / PackedInt8Linear.materialize
+    (pollux.py:519-528, 545-554) on libh24."""
+    if self._materialized:
+        return
+    weight = int8_dequant(self.weight_int8, self.mu_rows)
+    self.weight = nn.Parameter(weight.to(self.weight_int8.device), requires_grad=False)
+    del self.weight_int8
+    del self.mu_rows
+    self._materialized = True
+
+
+class PackedInt8Embedding(nn.Module):
+    """Token embedding with INT8 weights and per-row FP16 scales mu (same
+    buffers and forward as pollux.py:510-532)."""
+
+    def __init__(self, num_embeddings: int, embedding_dim: int) -> None:
+        super().__init__()
+        self.num_embeddings = int(num_embeddings)
+        self.embedding_dim = int(embedding_dim)
+        self.register_buffer("weight_int8", torch.zeros(num_embeddings, embedding_dim, dtype=torch.int8))
+        self.register_buffer("mu_rows", torch.ones(num_embeddings, dtype=torch.float16))
+        self._materialized = False
+
+    materialize = materialize_int8
+
+    def forward(self, idx: torch.Tensor) -> torch.Tensor:
+        return F.embedding(idx, self.weight.to(dtype=torch.float32))
+
+
+class PackedInt8Linear(nn.Module):
+    """Output projection with INT8 weights and per-row FP16 scales mu (same
+    buffers and forward as pollux.py:535-558)."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False) -> None:
+        super().__init__()
+        self.in_features = int(in_features)
+        self.out_features = int(out_features)
+        self.register_buffer("weight_int8", torch.zeros(out_features, in_features, dtype=torch.int8))
+        self.register_buffer("mu_rows", torch.ones(out_features, dtype=torch.float16))
+        self._materialized = False
+        if bias:
+            self.bias = nn.Parameter(torch.zeros(out_features))
+        else:
+            self.register_parameter("bias", None)
+
+    materialize = materialize_int8
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return F.linear(x, self.weight.to(dtype=x.dtype), self.bias)

@@ -22,6 +22,9 @@ Fixtures written (all small):
   materialize.npz        PackedH24Linear.materialize outputs (pollux.py:485-504)
   tiny.plx, plx_state.npz  (with --plx) a .plx written by pack._write_plx and
                          the tensors that went into it
+  int8.npz               (with --int8) pack._quantize_int8 and
+                         PackedInt8Embedding/Linear.materialize on seeded and
+                         edge-case matrices (pack.py:124-136, pollux.py:510-563)
 """
 from __future__ import annotations
 
@@ -54,8 +57,13 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--plx", action="store_true", help="only write the .plx fixture")
+    ap.add_argument("--int8", action="store_true", help="only write the INT8 fixture")
     args = ap.parse_args()
     if args.plx:
+        make_plx(args.reference)
+        return
+    if args.int8:
+        make_int8(args.reference)
         return
     sys.path.insert(0, args.reference)
     sys.path.insert(0, REPO)
@@ -172,9 +180,6 @@ def main() -> None:
     print("materialize.npz written")
 
 
-if __name__ == "__main__":
-    main()
-
 
 def make_plx(reference: str) -> None:
     """tiny.plx written by the reference's own pack._write_plx (pack.py:187-247)
@@ -202,5 +207,48 @@ def make_plx(reference: str) -> None:
     print("tiny.plx written")
 
 
-if __name__ == "__main__" and "--plx" in sys.argv:
-    make_plx(sys.argv[sys.argv.index("--reference") + 1])
+
+def make_int8(reference: str) -> None:
+    """int8.npz: the reference's pack._quantize_int8 and the INT8 modules'
+    materialize() on seeded and edge-case matrices."""
+    sys.path.insert(0, reference)
+    import pack as ref_pack  # noqa: E402
+    import pollux as ref_pollux  # noqa: E402
+    g = torch.Generator().manual_seed(31)
+    cases = {
+        "normal": torch.randn(64, 1152, generator=g) * 0.02,
+        "odd": torch.randn(5, 37, generator=g),
+    }
+    # Exact ties at .5: a row with max 1.0 and values i/256 (127 i / 256 is exact).
+    cases["ties"] = torch.arange(-256, 257, dtype=torch.float32).reshape(1, -1) / 256.0
+    e = torch.randn(8, 48, generator=g)
+    e[0] = 0.0                      # zero row: mu clamps to 1e-8
+    e[1, 3] = float("nan")          # NaN row
+    e[2, 5] = float("inf")          # inf row
+    e[3] *= 1e5                     # mu above the fp16 range -> inf
+    e[4] *= 1e-6                    # fp16-subnormal mu
+    e[5, :] = 1e-9                  # below the clamp
+    cases["edge"] = e
+    out = {}
+    for k, w in cases.items():
+        q, mu = ref_pack._quantize_int8(w)
+        out[f"{k}_w"] = w.numpy()
+        out[f"{k}_q"] = q.numpy()
+        out[f"{k}_mu"] = mu.numpy()
+        rows, cols = w.shape
+        emb = ref_pollux.PackedInt8Embedding(rows, cols)
+        emb.weight_int8.copy_(q)
+        emb.mu_rows.copy_(mu)
+        emb.materialize()
+        out[f"{k}_emb"] = emb.weight.detach().numpy()
+        head = ref_pollux.PackedInt8Linear(cols, rows)
+        head.weight_int8.copy_(q)
+        head.mu_rows.copy_(mu)
+        head.materialize()
+        out[f"{k}_head"] = head.weight.detach().numpy()
+    np.savez_compressed(os.path.join(HERE, "int8.npz"), **out)
+    print("int8.npz written")
+
+
+if __name__ == "__main__":
+    main()

@@ -68,9 +68,15 @@ def test_install_rebinds_reference_names():
     class RefPacked:  # stands in for pollux.PackedH24Linear
         def materialize(self):
             raise AssertionError("reference path must not run")
+    class RefEmb:  # stands in for pollux.PackedInt8Embedding
+        def materialize(self):
+            raise AssertionError("reference path must not run")
+    class RefHead(RefEmb):  # pollux.PackedInt8Linear
+        pass
     ref_pollux = types.SimpleNamespace(castor_quantize_leech=None, unpack_indices=None,
-                                       PackedH24Linear=RefPacked)
-    ref_pack = types.SimpleNamespace(pack_indices=None, _quantize_h24_layer=None)
+                                       PackedH24Linear=RefPacked, PackedInt8Embedding=RefEmb,
+                                       PackedInt8Linear=RefHead)
+    ref_pack = types.SimpleNamespace(pack_indices=None, _quantize_h24_layer=None, _quantize_int8=None)
     done = pollux_b200.install({"castor": ref_castor, "pollux": ref_pollux, "pack": ref_pack})
     assert ref_castor.castor_quantize_leech is castor.castor_quantize_leech
     assert ref_castor.unpack_indices is castor.unpack_indices
@@ -78,6 +84,9 @@ def test_install_rebinds_reference_names():
     assert ref_pack._quantize_h24_layer is pack._quantize_h24_layer
     assert RefPacked.materialize is packed_linear.materialize
     assert "pollux.PackedH24Linear.materialize" in done
+    assert ref_pack._quantize_int8 is pack._quantize_int8
+    assert RefEmb.materialize is packed_linear.materialize_int8
+    assert RefHead.materialize is packed_linear.materialize_int8
     assert not isinstance(ref_castor.get_h24_codebook, type(castor.get_h24_codebook))
 
 

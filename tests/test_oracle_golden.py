@@ -122,3 +122,21 @@ def test_bf16_fallback_differs_from_exact(oracle, golden):
     d_ex = oracle.dist2_fp64(x[sample], ex)
     d_ref = oracle.dist2_fp64(x[sample], ref[sample])
     assert (d_ex <= d_ref * (1 + 1e-6)).all()
+
+
+def _same_f16(a, b):
+    """Equal fp16 arrays, NaN positions included (NaN payloads not compared)."""
+    a, b = np.asarray(a, np.float16), np.asarray(b, np.float16)
+    return (np.array_equal(np.isnan(a), np.isnan(b)) and
+            np.array_equal(np.where(np.isnan(a), 0, a).view(np.uint16),
+                           np.where(np.isnan(b), 0, b).view(np.uint16)))
+
+
+def test_int8_oracle_matches_reference(oracle, golden):
+    g = golden("int8.npz")
+    for k in ("normal", "odd", "ties", "edge"):
+        q, mu = oracle.int8_quantize(g[k + "_w"])
+        assert np.array_equal(q, g[k + "_q"]), k
+        assert _same_f16(mu, g[k + "_mu"]), k
+        w16 = oracle.int8_dequant(g[k + "_q"], g[k + "_mu"])
+        assert _same_f16(w16, g[k + "_emb"]) and _same_f16(w16, g[k + "_head"]), k
