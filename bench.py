@@ -475,7 +475,33 @@ def run_components(args) -> dict:
         N.check(lib.h24_int8_dequant(emb_q[k].data_ptr(), emb_mu[k].data_ptr(), vocab, d,
                                      emb_out[k].data_ptr(), stream), "int8_dequant")
 
+    # Decode through the 18 config-5 layers: LUT GEMV straight from the packed
+    # bytes vs a dense fp16 GEMV (cuBLAS) on the materialised weights.
+    xs = {b: torch.randn(b, in_f, device=dev) for b in (1, 8)}
+    ys = {b: torch.empty(b, rows, device=dev) for b in (1, 8)}
+    x16 = {b: xs[b].half() for b in (1, 8)}
+
+    def lut_sweep(b):
+        def run(k):
+            for l in range(layers):
+                N.check(lib.h24_lut_gemv(packs[k].data_ptr() + l * per_layer_bytes, sig_l[l].data_ptr(),
+                                         rows, in_f, xs[b].data_ptr(), b, ys[b].data_ptr(),
+                                         bad.data_ptr(), stream), "lut_gemv")
+        return run
+
+    def dense_sweep(b):
+        def run(k):
+            for l in range(layers):
+                torch.matmul(x16[b], outs[k % 2][l].t())
+        return run
+
     reps = max(3, args.steps)
+    dequant(0)
+    dequant(1)
+    t_lut1 = timed(lut_sweep(1), 2, reps)
+    t_lut8 = timed(lut_sweep(8), 2, reps)
+    t_dense1 = timed(dense_sweep(1), 2, reps)
+    t_dense8 = timed(dense_sweep(8), 2, reps)
     t_pack = timed(pack, sets, reps)
     t_unpack = timed(unpack, sets, reps)
     t_deq = timed(dequant, 2, reps)
@@ -501,6 +527,14 @@ def run_components(args) -> dict:
                        ("int8_dequant", t_i8d, i8d_bytes)):
         gbs = b / (t / 1e3) / 1e9
         res[name] = {"ms": t, "algorithmic_bytes": b, "GB_per_s": gbs, "frac_of_measured_hbm": gbs / peak}
+    wbytes = layers * rows * in_f * 2
+    res["lut_gemv"] = {
+        "what": "y = x @ W.T through all 18 config-5 layers, W never materialised (fp32); "
+                "against torch.matmul of the materialised fp16 weights (cuBLAS)",
+        "batch1_ms": t_lut1, "batch8_ms": t_lut8,
+        "dense_fp16_batch1_ms": t_dense1, "dense_fp16_batch8_ms": t_dense8,
+        "dense_equivalent_GB_per_s_batch1": wbytes / (t_lut1 / 1e3) / 1e9,
+        "packed_bytes": layers * per_layer_bytes, "fp16_weight_bytes": wbytes}
     res["workload"] = ("config5: 18 layers x [7680,1920], 11,059,200 uniform indices; pack int32->18-bit, "
                        "unpack 18-bit->int32, batched LUT dequant to fp16; INT8 embedding "
                        "[50688,1920] quantize and dequant; back-to-back calls over "

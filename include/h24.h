@@ -102,6 +102,17 @@ typedef struct h24_dequant_layer {
 int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad_count,
                         void *stream);
 
+/* Matrix-free LUT GEMV (the "future native kernel" of README.md:88, 155-156;
+ * generate.py:8-18): y[b][o] = sum_i x[b][i] * W[o][i] for b < batch, where W is
+ * the packed layer (rows = out_features) and W[o][i] the fp16 value
+ * PackedH24Linear.materialize would produce; W is never materialised.  x: batch
+ * x in_features fp32 (16-byte aligned rows), y: batch x rows fp32, fp32
+ * products and sums (the order differs from a dense matmul's).  Out-of-range
+ * packed indices count into *bad_count (if non-null) and read as the origin. */
+int h24_lut_gemv(const uint8_t *packed, const uint16_t *sigma16, int64_t rows,
+                 int64_t in_features, const float *x, int64_t batch, float *y,
+                 int32_t *bad_count, void *stream);
+
 /* ---- INT8 token embedding / output head ------------------------------------
  * Per-row INT8 quantisation (pack._quantize_int8, pack.py:124-136):
  * mu = max(max_c |w[r][c]|, 1e-8) in fp32, q = clamp(rint(w / mu * 127),

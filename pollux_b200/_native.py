@@ -41,6 +41,7 @@ SIGNATURES = {
     "h24_unpack_i64": (_I, [_P, _I64, _I64, _P, _P]),
     "h24_dequant": (_I, [_P, _P, _I64, _I64, _P, _P, _P]),
     "h24_dequant_batched": (_I, [_P, _I, _P, _P]),
+    "h24_lut_gemv": (_I, [_P, _P, _I64, _I64, _P, _I64, _P, _P, _P]),
     "h24_int8_quantize": (_I, [_P, _I64, _I64, _P, _P, _P]),
     "h24_int8_dequant": (_I, [_P, _P, _I64, _I64, _P, _P]),
     "h24_quantize": (_I, [_P, _I64, _I, _P, _P]),

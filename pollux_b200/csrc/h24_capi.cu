@@ -474,6 +474,14 @@ int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad
   return launch_dequant(T, nullptr, layers, count, bad_count, as_stream(stream));
 }
 
+int h24_lut_gemv(const uint8_t *packed, const uint16_t *sigma16, int64_t rows,
+                 int64_t in_features, const float *x, int64_t batch, float *y,
+                 int32_t *bad_count, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  return launch_lut_gemv(T, packed, sigma16, rows, in_features, x, batch, y, bad_count,
+                         as_stream(stream));
+}
+
 int h24_int8_quantize(const float *w, int64_t rows, int64_t cols, int8_t *q, uint16_t *mu16,
                       void *stream) {
   if (rows < 0 || cols < 0) return fail(H24_ERR_INVALID, "int8_quantize: negative size");

@@ -112,6 +112,9 @@ int launch_dequant(const Tables *t, const h24_dequant_layer *layers_dev,
                    const h24_dequant_layer *layers_host, int count, int32_t *bad,
                    cudaStream_t s);
 int launch_codebook_f32(const Tables *t, float *out_kissing, cudaStream_t s);
+int launch_lut_gemv(const Tables *t, const uint8_t *packed, const uint16_t *sigma16, int64_t rows,
+                    int64_t in_f, const float *x, int64_t batch, float *y, int32_t *bad,
+                    cudaStream_t s);
 int launch_gather(const Tables *t, const int32_t *idx, int64_t n, int dtype, void *out,
                   cudaStream_t s);
 int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,

@@ -9,6 +9,12 @@ then drops the packed buffers exactly as the reference does (pollux.py:500-504).
 ``materialize_all`` dequantises every packed layer of a model with one launch
 per 64 layers (the loop of from_packed_checkpoint, pollux.py:748-750).
 
+``lut_linear`` computes ``x @ W.T`` straight from the packed indices (the
+README's "future native kernel", README.md:88, 155-156) with W never
+materialised; ``PackedH24Linear.forward`` uses it until the layer is
+materialised, and ``enable_lut_forward`` switches the packed layers of any
+model (the reference's included) to it.
+
 ``PackedInt8Embedding`` / ``PackedInt8Linear`` (pollux.py:510-563) and
 ``materialize_int8`` rebuild the INT8 token embedding and output head,
 weight = fp16(q * fp16(mu / 127)), with one launch per tensor.
@@ -69,6 +75,66 @@ def materialize(self) -> None:
     self._materialized = True
 
 
+LUT_GEMV_MAX_BATCH = 32  # larger batches: dequantise once and use a dense GEMM
+
+
+def lut_linear(x: torch.Tensor, packed: torch.Tensor, sigma_rows: torch.Tensor, out_features: int,
+               in_features: int, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """F.linear(x, W, bias) for the packed H24 weight W ([out_features,
+    in_features], the fp16 values materialize() produces), computed in fp32
+    without materialising W for up to LUT_GEMV_MAX_BATCH input rows; the result
+    has x's dtype."""
+    if x.shape[-1] != in_features:
+        raise RuntimeError(f"mat1 and mat2 shapes cannot be multiplied "
+                           f"({x.numel() // max(1, x.shape[-1])}x{x.shape[-1]} and {in_features}x{out_features})")
+    if sigma_rows.dtype != torch.float16:
+        raise TypeError(f"sigma_rows must be float16, got {sigma_rows.dtype}")
+    lead = x.shape[:-1]
+    batch = x.numel() // in_features if in_features else 0
+    dev = _work_device(x)
+    if batch > LUT_GEMV_MAX_BATCH:
+        w = dequant(packed, sigma_rows, out_features, in_features).float()
+        y = torch.matmul(x.to(device=dev, dtype=torch.float32).reshape(batch, in_features), w.t())
+    else:
+        atoms = h24_linear_atom_count(out_features, in_features)
+        need = ((atoms + 3) // 4) * BYTES_PER_CHUNK
+        flat = packed.reshape(-1)
+        if flat.dtype != torch.uint8 or flat.numel() < need:
+            raise ValueError(f"packed_weights must be uint8 with at least {need} bytes")
+        p = flat.to(dev).contiguous()
+        s = sigma_rows.reshape(-1).to(dev).contiguous()
+        xf = _aligned(x.to(device=dev, dtype=torch.float32).reshape(batch, in_features))
+        y = torch.empty(batch, out_features, dtype=torch.float32, device=dev)
+        bad = torch.zeros(1, dtype=torch.int32, device=dev)
+        if batch:
+            _call(dev, "h24_lut_gemv", p.data_ptr(), s.data_ptr(), out_features, in_features,
+                  xf.data_ptr(), batch, y.data_ptr(), bad.data_ptr(), _stream(dev))
+            _raise_bad(bad)
+    y = y.reshape(*lead, out_features)
+    if bias is not None:
+        y = y + bias.to(y)
+    return y.to(x.dtype)
+
+
+def _lut_forward(self, x: torch.Tensor) -> torch.Tensor:
+    if getattr(self, "_materialized", False):
+        return F.linear(x, self.weight.to(dtype=x.dtype), self.bias)
+    return lut_linear(x, self.packed_weights, self.sigma_rows, self.out_features, self.in_features,
+                      self.bias)
+
+
+def enable_lut_forward(model: nn.Module) -> int:
+    """Make every not-yet-materialised packed H24 layer of ``model`` run its
+    forward through the LUT GEMV (instance attribute, so the reference's
+    PackedH24Linear is covered too); returns the number of layers."""
+    n = 0
+    for m in model.modules():
+        if hasattr(m, "packed_weights") and hasattr(m, "sigma_rows") and not getattr(m, "_materialized", False):
+            m.forward = _lut_forward.__get__(m, type(m))
+            n += 1
+    return n
+
+
 class PackedH24Linear(nn.Module):
     """H24 linear layer with packed uint8 indices + fp16 per-row sigma
     (same buffers, shapes and forward as pollux.py:461-507)."""
@@ -92,7 +158,9 @@ class PackedH24Linear(nn.Module):
     materialize = materialize
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return F.linear(x, self.weight.to(dtype=x.dtype), self.bias)
+        """F.linear with the materialised weight, as the reference; before
+        materialize(), the LUT GEMV over the packed indices."""
+        return _lut_forward(self, x)
 
 
 def materialize_all(model: nn.Module) -> int:
