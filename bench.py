@@ -263,6 +263,26 @@ def run_ours(args) -> None:
     if peak is None:
         peak, peak_src = 1400.0, "fallback sustained bf16 1.4 PFLOP/s"
 
+    # F3: the fused training projection (pollux_step's H24 block) over the same
+    # backbone, all 48 parameters in one call.
+    proj = None
+    if rank == 0 and world == 1:
+        outs_p = [torch.empty_like(w) for w in weights]
+        pairs = list(zip(outs_p, weights))
+        castor.project_h24_many(pairs)
+        torch.cuda.synchronize()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        for _ in range(3):
+            castor.project_h24_many(pairs)
+        p1.record()
+        p1.synchronize()
+        pms = p0.elapsed_time(p1) / 3
+        proj = {"what": "pollux_step H24 block (row RMS, normalise, training-rule search, rescale "
+                        "into p.data) for all 48 config-2 matrices in one fused call",
+                "ms": pms, "G_atoms_per_s": atoms_per_step / (pms / 1e3) / 1e9}
+        del outs_p, pairs
+
     # End-to-end through the public drop-in API with host buffers.
     e2e = None
     if rank == 0 and not args.skip_e2e:
@@ -303,6 +323,7 @@ def run_ours(args) -> None:
             "e2e": e2e,
             "cpu_baseline": cpu,
             "hbm_kernels": comps,
+            "training_projection": proj,
         }
         print(json.dumps(out), flush=True)
     if world > 1:

@@ -102,6 +102,25 @@ typedef struct h24_dequant_layer {
 int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad_count,
                         void *stream);
 
+/* ---- H24 projection of pollux_step (pollux.py:874-884), fused ------------
+ * For every layer: sigma_r = sqrt(mean(latent_r^2) + 1e-8) (fp32; squares
+ * summed in fp64, so torch's fp32 reduction may differ in the last bit),
+ * x = (latent / max(sigma, 1e-8)) / s_lattice, the nearest codeword of each
+ * atom of x under the training rule (castor_quantize_leech), and
+ * out = (codeword * sigma_r) * s_lattice in fp32 (the p.data.copy_ of the
+ * reference).  One search pipeline for all layers, no host synchronisation.
+ * sigma (rows fp32) and idx (rows*in/24 int32) are optional outputs. */
+typedef struct h24_project_layer {
+  const float *latent;
+  float *out;
+  int64_t rows;
+  int64_t in_features;
+  float *sigma;
+  int32_t *idx;
+} h24_project_layer;
+
+int h24_project_layers(const h24_project_layer *layers, int count, void *stream);
+
 /* Matrix-free LUT GEMV (the "future native kernel" of README.md:88, 155-156;
  * generate.py:8-18): y[b][o] = sum_i x[b][i] * W[o][i] for b < batch, where W is
  * the packed layer (rows = out_features) and W[o][i] the fp16 value

@@ -42,6 +42,7 @@ SIGNATURES = {
     "h24_dequant": (_I, [_P, _P, _I64, _I64, _P, _P, _P]),
     "h24_dequant_batched": (_I, [_P, _I, _P, _P]),
     "h24_lut_gemv": (_I, [_P, _P, _I64, _I64, _P, _I64, _P, _P, _P]),
+    "h24_project_layers": (_I, [_P, _I, _P]),
     "h24_int8_quantize": (_I, [_P, _I64, _I64, _P, _P, _P]),
     "h24_int8_dequant": (_I, [_P, _P, _I64, _I64, _P, _P]),
     "h24_quantize": (_I, [_P, _I64, _I, _P, _P]),
@@ -68,6 +69,12 @@ class Layer(ctypes.Structure):
     """Mirror of h24_layer."""
     _fields_ = [("w", _P), ("rows", ctypes.c_int64), ("in_features", ctypes.c_int64),
                 ("sigma16_out", _P), ("packed_out", _P)]
+
+
+class ProjectLayer(ctypes.Structure):
+    """Mirror of h24_project_layer."""
+    _fields_ = [("latent", _P), ("out", _P), ("rows", ctypes.c_int64),
+                ("in_features", ctypes.c_int64), ("sigma", _P), ("idx", _P)]
 
 
 class H24Error(RuntimeError):

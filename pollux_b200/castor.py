@@ -12,6 +12,8 @@ Same names, signatures, argument meaning and error behaviour as the reference:
 * row-RMS helpers ...................... castor.py:309-339
 * castor_quantize_leech ................ castor.py:487-560
 * CastorQuantizeLeech .................. castor.py:563-580
+* project_h24_ / project_h24_many ...... the H24 block of pollux_step (pollux.py:874-884),
+                                         fused and batched over parameters
 
 Device policy: the work always runs on a CUDA device through libh24.  Tensors
 on the host are staged through the current CUDA device and the result is
@@ -339,3 +341,45 @@ def quantize_stats(device=None) -> tuple[int, int, int]:
 def launch_count() -> int:
     """Kernels libh24 has launched in this process."""
     return int(N.load().h24_launch_count())
+
+
+def project_h24_many(pairs, sigma_out: bool = False, idx_out: bool = False):
+    """The H24 projection block of pollux_step (pollux.py:874-884) for many
+    parameters at once: for each (p_data, latent) pair of fp32 CUDA matrices,
+    p_data <- (nearest codeword of latent / sigma / s_lattice) * sigma *
+    s_lattice with sigma = row_rms_from_matrix(latent), in one fused pipeline
+    (h24_project_layers).  Returns per pair a dict with the optional 'sigma'
+    [rows] fp32 and 'idx' [rows*in/24] int32 tensors."""
+    pairs = list(pairs)
+    if not pairs:
+        return []
+    dev = _work_device(pairs[0][1])
+    layers = (N.ProjectLayer * len(pairs))()
+    keep, extras = [], []
+    for i, (p, lat) in enumerate(pairs):
+        if lat.dim() != 2 or p.shape != lat.shape:
+            raise ValueError(f"p and latent must be matching 2-D matrices, got {tuple(p.shape)} and {tuple(lat.shape)}")
+        rows, in_f = lat.shape
+        assert_row_aligned_in_features(in_f)
+        if p.dtype != torch.float32 or not p.is_contiguous() or p.device != dev:
+            raise ValueError("p must be a contiguous fp32 tensor on the latent's device")
+        l = _aligned(lat.detach().to(device=dev, dtype=torch.float32))
+        ex = {}
+        if sigma_out:
+            ex["sigma"] = torch.empty(rows, dtype=torch.float32, device=dev)
+        if idx_out:
+            ex["idx"] = torch.empty(rows * in_f // H24_DIM, dtype=torch.int32, device=dev)
+        keep.append(l)
+        extras.append(ex)
+        layers[i] = N.ProjectLayer(l.data_ptr(), p.data_ptr(), rows, in_f,
+                                   ex["sigma"].data_ptr() if sigma_out else None,
+                                   ex["idx"].data_ptr() if idx_out else None)
+    _call(dev, "h24_project_layers", ctypes.cast(layers, ctypes.c_void_p), len(pairs), _stream(dev))
+    return extras
+
+
+def project_h24_(p_data: torch.Tensor, latent: torch.Tensor) -> torch.Tensor:
+    """In-place p_data.copy_(center) of pollux_step's H24 block for one
+    parameter (see project_h24_many); returns p_data."""
+    project_h24_many([(p_data, latent)])
+    return p_data

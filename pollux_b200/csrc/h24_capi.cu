@@ -474,6 +474,15 @@ int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad
   return launch_dequant(T, nullptr, layers, count, bad_count, as_stream(stream));
 }
 
+int h24_project_layers(const h24_project_layer *layers, int count, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (count < 0 || (count > 0 && !layers)) return fail(H24_ERR_INVALID, "project_layers: bad layer list");
+  for (int i = 0; i < count; ++i)
+    if (layers[i].rows > 0 && layers[i].latent && !aligned16(layers[i].latent))
+      return fail(H24_ERR_INVALID, "project_layers: latent must be 16-byte aligned");
+  return project_layers(T, layers, count, as_stream(stream));
+}
+
 int h24_lut_gemv(const uint8_t *packed, const uint16_t *sigma16, int64_t rows,
                  int64_t in_features, const float *x, int64_t batch, float *y,
                  int32_t *bad_count, void *stream) {

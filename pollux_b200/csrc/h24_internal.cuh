@@ -121,6 +121,7 @@ int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_
              cudaStream_t s);
 int quantize_segments(const Tables *t, const float *const *xs, const int64_t *counts, int nseg,
                       int rule, int32_t *out_idx, cudaStream_t s);
+int project_layers(const Tables *t, const h24_project_layer *layers, int count, cudaStream_t s);
 int launch_int8_quantize(const float *w, int64_t rows, int64_t cols, int8_t *q, uint16_t *mu16,
                          cudaStream_t s);
 int launch_int8_dequant(const int8_t *q, const uint16_t *mu16, int64_t rows, int64_t cols,
