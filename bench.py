@@ -120,14 +120,18 @@ def cpu_baseline(seconds: float = 12.0, chunk: int = 2048) -> dict:
     nthreads = os.cpu_count() or 1
     w = synth.backbone_weights(2, device="cpu", seed=1, shapes=[(3456, 1152)])[0]
     atoms = w.numpy().reshape(-1, 24)
-    done, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds and done + chunk <= atoms.shape[0]:
-        a = atoms[done:done + chunk]
-        idx = O.nearest_fp32_pack_rule(a)
-        O.sigma16_pack_rule(w.numpy()[done // 48: done // 48 + chunk // 48])
-        O.pack_indices(idx)
-        done += chunk
-    dt = time.perf_counter() - t0
+    # Every host thread, also under torchrun (which sets OMP_NUM_THREADS=1).
+    from threadpoolctl import threadpool_limits
+    torch.set_num_threads(nthreads)
+    with threadpool_limits(limits=nthreads):
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds and done + chunk <= atoms.shape[0]:
+            a = atoms[done:done + chunk]
+            idx = O.nearest_fp32_pack_rule(a)
+            O.sigma16_pack_rule(w.numpy()[done // 48: done // 48 + chunk // 48])
+            O.pack_indices(idx)
+            done += chunk
+        dt = time.perf_counter() - t0
     return {"value": done / dt / 1e9, "unit": "G atoms/s", "cores": nthreads, "kind": "port",
             "sample": f"{done} atoms of config-2 layer 0 (QKV 3456x1152), fp32 matmul + argmax "
                       f"+ sigma16 + pack with numpy/BLAS on {nthreads} host threads ({dt:.1f} s); "
