@@ -81,8 +81,9 @@ constexpr int kW16Tile = kW16First / kGolayTileN;  // 26: first tile with weight
 constexpr int kW16Chunk = kW16First / kChunkCols;  // 52: first chunk with weight-16 columns
 constexpr int kW16Skip = kW16First - kW16Tile * kGolayTileN;  // 8 dodecads lead tile 26
 constexpr int kEpiWarps = 16;                      // 4 M-tiles x 4 TMEM lane quarters
-constexpr int kFirstEpiWarp = 2;                   // warp 0 producer, warp 1 MMA issuer
-constexpr int kScreenThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 576
+constexpr int kIssuers = 2;                        // MMA issuer warps, two M-tiles each
+constexpr int kFirstEpiWarp = 1 + kIssuers;        // warp 0 producer, warps 1-2 MMA issuers
+constexpr int kScreenThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 608
 constexpr uint32_t kTmemCols = kMTiles * kGolayTileN;  // 512: one accumulator stage per M-tile
 constexpr int kHeavyChunks = 192;                  // flagged chunks (of 204) beyond which the exhaustive scan runs
 constexpr int kMaxSegs = 64;                       // input segments per pipeline batch
@@ -116,13 +117,13 @@ struct __align__(1024) ScreenSmem {
   // stay conservative).
   __half cmax[kChunks][kEpiWarps * 32];
   uint64_t bar_a_full[2];
-  uint64_t bar_a_empty[2];
+  uint64_t bar_a_empty[2];          // one commit per issuer
   uint64_t bar_b_full[kStages];
   uint64_t bar_b_empty[kStages];
   uint64_t bar_acc_full[kMTiles];
   uint64_t bar_acc_empty[kMTiles];
   uint64_t bar_rows[2];
-  uint64_t bar_final;
+  uint64_t bar_final[kIssuers];     // each issuer's last MMAs
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -302,18 +303,22 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 #define H24_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), \
                   "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
 
-// 32 lanes x 32 consecutive 32-bit TMEM columns, waited for in the same
-// statement (so no use of r can be scheduled before the wait).
-__device__ __forceinline__ void tmem_ld32_wait(uint32_t taddr, uint32_t *r) {
+// 32 lanes x 64 consecutive 32-bit TMEM columns, waited for in the same
+// statement.
+__device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, uint32_t *r) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
-      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24)
+      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24), H24_R8(32), H24_R8(40), H24_R8(48),
+        H24_R8(56)
       : "r"(taddr)
       : "memory");
 }
+
 #undef H24_R8
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -538,18 +543,18 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.bar_a_full[i], 1);
-      mbar_init(&S.bar_a_empty[i], 1);
+      mbar_init(&S.bar_a_empty[i], kIssuers);
       mbar_init(&S.bar_rows[i], kEpiWarps);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.bar_b_full[s], 1);
-      mbar_init(&S.bar_b_empty[s], 1);
+      mbar_init(&S.bar_b_empty[s], kIssuers);
     }
     for (int g = 0; g < kMTiles; ++g) {
       mbar_init(&S.bar_acc_full[g], 1);
       mbar_init(&S.bar_acc_empty[g], 4);  // the four warps of M-tile g
     }
-    mbar_init(&S.bar_final, 1);
+    for (int i = 0; i < kIssuers; ++i) mbar_init(&S.bar_final[i], 1);
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -605,10 +610,13 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
             }
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer --------------------------------------------
+  } else if (warp <= kIssuers) {
+    // ---------------- MMA issuers ---------------------------------------------
     // Per Golay tile, one M128 N128 K32 product (two K=16 MMAs) for each of
-    // the four M-tiles into TMEM stage g (columns 128 g).
+    // the four M-tiles into TMEM stage g (columns 128 g).  MMA issue blocks
+    // until the tensor core accepts the instruction, so two issuers (M-tiles
+    // 0-1 and 2-3) let one wait on its barriers while the other's MMAs run.
+    const int g0 = (warp - 1) * (kMTiles / kIssuers);
     if (lane == 0) {
       const uint32_t a0 = smem_u32(S.a[0]), b0 = smem_u32(S.b[0]);
       constexpr uint64_t kKStep = 256 >> 4;  // next 16 K: two 16-byte chunks, descriptor units
@@ -622,7 +630,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
           if (!wait_bar(&S.bar_b_full[bs], bph, abort_flag, args.err)) { ok = false; break; }
           tc_fence_after();
           const uint64_t bd = smem_desc(b0 + static_cast<uint32_t>(bs) * kBTileBytes);
-          for (int g = 0; g < kMTiles; ++g) {
+          for (int g = g0; g < g0 + kMTiles / kIssuers; ++g) {
             // Use t of stage g (32 per work item, so parity t & 1) waits for
             // the release of use t - 1.
             if (!wait_bar(&S.bar_acc_empty[g], (t & 1) ^ 1, abort_flag, args.err)) { ok = false; break; }
@@ -644,9 +652,9 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       }
       if (issued) {
         // All MMAs of this CTA complete before TMEM is released.
-        mma_commit(&S.bar_final);
+        mma_commit(&S.bar_final[warp - 1]);
         const unsigned long long t0 = global_ns();
-        while (!mbar_try_wait(&S.bar_final, 0) && global_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(&S.bar_final[warp - 1], 0) && global_ns() - t0 < kWaitLimitNs) {
         }
       }
     }
@@ -678,14 +686,14 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         tc_fence_after();
         float m0 = -INFINITY, m1 = -INFINITY;
         if (r != 3 || t >= kW16Tile) {
-          uint32_t x[32];
-          // Rolled: an unrolled loop lets the compiler keep several blocks of
+          uint32_t x[64];
+          // Rolled: an unrolled loop lets the compiler keep both blocks of
           // loaded values live at once (register spills).
 #pragma unroll 1
-          for (int k = 0; k < 4; ++k) {
-            tmem_ld32_wait(t_row + static_cast<uint32_t>(32 * k), x);
-            if (k == 3) {
-              // All four loads done: hand the stage back to the MMA issuer.
+          for (int k = 0; k < 2; ++k) {
+            tmem_ld64_wait(t_row + static_cast<uint32_t>(64 * k), x);
+            if (k == 1) {
+              // Both loads done: hand the stage back to the MMA issuer.
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&S.bar_acc_empty[g]);
@@ -694,8 +702,9 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
 #pragma unroll
               for (int i = 0; i < kW16Skip; ++i) x[i] = 0xFF800000u;  // dodecad columns
             }
-            if (t == kGolayTiles - 1 && r == 3 && k == 3) x[31] = 0xFF800000u;  // all-ones word
-            if (k < 2) m0 = max32(m0, x); else m1 = max32(m1, x);
+            if (t == kGolayTiles - 1 && r == 3 && k == 1) x[63] = 0xFF800000u;  // all-ones word
+            const float mk = max32(max32(-INFINITY, x), x + 32);
+            if (k == 0) m0 = mk; else m1 = mk;
           }
         } else {
           tc_fence_before();
