@@ -99,3 +99,16 @@ def test_unpack_capacity_below_count(C, oracle):
         u = C.unpack_indices(p, n)
         ref = oracle.unpack_indices(p.cpu().numpy(), n)
         assert np.array_equal(u.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("rows,in_f", [(4608, 1152), (5461, 72), (3, 96)])
+def test_pinned_host_layer_pipelined_equals_device_path(C, rows, in_f):
+    # Pinned fp32 host weights are copied in row chunks on a side stream while
+    # earlier chunks are searched; bytes and sigma must not change.
+    from pollux_b200 import pack
+    gen = torch.Generator().manual_seed(rows)
+    w = torch.randn(rows, in_f, generator=gen) * 0.02
+    cb = C.get_h24_codebook("cuda", torch.float32)
+    p_pin, s_pin = pack._quantize_h24_layer(w.pin_memory(), cb)
+    p_dev, s_dev = pack._quantize_h24_layer(w.cuda(), cb)
+    assert torch.equal(p_pin, p_dev) and torch.equal(s_pin.view(torch.int16), s_dev.view(torch.int16))
