@@ -956,7 +956,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       for (int s = 0; s < 2; ++s) {
         uint64_t m = s ? mrow[1] : mrow[0];
         const int p = s ? p2 : p1;
-        const float xp = pick(v, p);
+        const float xp = __shfl_sync(0xffffffffu, xl, p);
         while (m) {
           const int b = __ffsll(m) - 1;
           m &= m - 1;
@@ -1022,8 +1022,9 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
               const uint32_t omc = __shfl_sync(0xffffffffu, om, src);
               const float t2c = __shfl_sync(0xffffffffu, t2, src);
               // The octad's 8 coordinates, lowest position first, to every lane.
-              float ov = 0.f;
-              if (lane < 8) ov = pick(v, static_cast<int>(__fns(omc, 0, lane + 1)));
+              const int pos = lane < 8 ? static_cast<int>(__fns(omc, 0, lane + 1)) : 0;
+              float ov = __shfl_sync(0xffffffffu, xl, pos);
+              if (lane >= 8) ov = 0.f;
               // Best even-parity pattern: 2 T(O) - 4 [odd] min_O |x|.
               // (Over all 32 lanes, so that every lane takes the same branch.)
               float mn = lane < 8 ? fabsf(ov) : INFINITY;
