@@ -1015,23 +1015,29 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
               t2 = 2.f * (sumabs - (tsum(gm & ~negm) - tsum(gm & negm)));  // 2 T(O)
             }
             uint32_t bal = __ballot_sync(0xffffffffu, t2 >= thr);
+            if (bal) {
+              // Best even-parity pattern of every lane's octad at once:
+              // 2 T(O) - 4 [odd number of negative x_i in O] min_O |x|.
+              float mn = INFINITY;
+              uint32_t mm = om;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int pos = __ffs(mm) - 1;  // -1 (any lane) once om is exhausted
+                mm &= mm - 1;
+                mn = fminf(mn, fabsf(__shfl_sync(0xffffffffu, xl, pos & 31)));
+              }
+              const bool odd = __popc(om & negm) & 1;
+              bal = __ballot_sync(0xffffffffu, t2 - (odd ? 4.f * mn : 0.f) >= thr);
+            }
             while (bal) {
               const int src = __ffs(bal) - 1;
               bal &= bal - 1;
               const int oc = __shfl_sync(0xffffffffu, o, src);
               const uint32_t omc = __shfl_sync(0xffffffffu, om, src);
-              const float t2c = __shfl_sync(0xffffffffu, t2, src);
               // The octad's 8 coordinates, lowest position first, to every lane.
               const int pos = lane < 8 ? static_cast<int>(__fns(omc, 0, lane + 1)) : 0;
               float ov = __shfl_sync(0xffffffffu, xl, pos);
               if (lane >= 8) ov = 0.f;
-              // Best even-parity pattern: 2 T(O) - 4 [odd] min_O |x|.
-              // (Over all 32 lanes, so that every lane takes the same branch.)
-              float mn = lane < 8 ? fabsf(ov) : INFINITY;
-#pragma unroll
-              for (int off = 16; off > 0; off >>= 1) mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
-              const bool odd = __popc(__ballot_sync(0xffffffffu, lane < 8 && ov < 0.f)) & 1;
-              if (t2c - (odd ? 4.f * mn : 0.f) < thr) continue;
               float o8[8];
 #pragma unroll
               for (int k2 = 0; k2 < 8; ++k2) o8[k2] = __shfl_sync(0xffffffffu, ov, k2);
@@ -1068,23 +1074,46 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         for (int k = lane; k < nc; k += 32) smax = fmaxf(smax, cand_s[w][k]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
-        const float cut = smax - 3.0517578125e-5f * sumabs;  // 2 e'
+        const float two_ep = 3.0517578125e-5f * sumabs;  // 2 e'
+        const float cut = smax - two_ep;
+        int nin = 0, jin = 0;
         for (int k = lane; k < nc; k += 32) {
           if (cand_s[w][k] >= cut) {
-            const int j = cand_j[w][k];
-            better(bs, bj, score64(v, r.cb_raw + static_cast<int64_t>(j) * kDim), j);
-            ++nex;
+            ++nin;
+            jin = cand_j[w][k];
           }
         }
+        // One codeword within 2 e' of the largest S' (and no list overflow):
+        // it is the unique winner.  The training rule's origin test
+        // 2 R < c_sq_norm, with sqrt(8) R within e' of S', is decided from
+        // S' unless S' / sqrt(2) lies within 2 e' of c_sq_norm.
+        const uint32_t who = __ballot_sync(0xffffffffu, nin > 0);
+        const int src = (__ffs(who) - 1) & 31;
+        const int nsrc = __shfl_sync(0xffffffffu, nin, src);
+        const int jsrc = __shfl_sync(0xffffffffu, jin, src);
+        const float origin_gap = smax * 0.70710678f - static_cast<float>(kCSqNorm);
+        const bool quick = __popc(who) == 1 && nsrc == 1 && cand_n[w] <= kCandCap &&
+                           (r.rule != H24_RULE_TRAIN || fabsf(origin_gap) > two_ep);
+        if (quick) {
+          if (lane == 0) r.out[a] = (r.rule == H24_RULE_TRAIN && origin_gap < 0.f) ? 0 : jsrc + 1;
+        } else {
+          for (int k = lane; k < nc; k += 32) {
+            if (cand_s[w][k] >= cut) {
+              const int j = cand_j[w][k];
+              better(bs, bj, score64(v, r.cb_raw + static_cast<int64_t>(j) * kDim), j);
+              ++nex;
+            }
+          }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-          const double os = __shfl_xor_sync(0xffffffffu, bs, off);
-          const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
-          better(bs, bj, os, oj);
-          nex += __shfl_xor_sync(0xffffffffu, nex, off);
+          for (int off = 16; off > 0; off >>= 1) {
+            const double os = __shfl_xor_sync(0xffffffffu, bs, off);
+            const int oj = __shfl_xor_sync(0xffffffffu, bj, off);
+            better(bs, bj, os, oj);
+            nex += __shfl_xor_sync(0xffffffffu, nex, off);
+          }
+          st_exact += nex;
+          if (lane == 0) r.out[a] = apply_rule(bs, bj, r.rule);
         }
-        st_exact += nex;
-        if (lane == 0) r.out[a] = apply_rule(bs, bj, r.rule);
       }
     }
     if (heavy && lane == 0) {
