@@ -853,6 +853,26 @@ __device__ __forceinline__ float pick(const float (&v)[kDim], int p) {
   return r;
 }
 
+// What the rescore reads of one atom, staged in shared memory by cp.async one
+// atom ahead of its use.
+struct AtomStage {
+  float x[kDim];
+  uint4 masks[2];
+  AtomInfo info;
+  float thr;
+  float pad[3];
+};
+static_assert(sizeof(AtomStage) == 192, "AtomStage is twelve 16-byte chunks");
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
 constexpr int kRescoreWarps = 8;
 constexpr int kRescoreBlocksPerSm = 2;
 constexpr int kCandCap = 128;  // fp32 candidates per atom before the fp64 pass
@@ -883,18 +903,47 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   __shared__ float cand_s[kRescoreWarps][kCandCap];
   __shared__ int32_t cand_j[kRescoreWarps][kCandCap];
   __shared__ int cand_n[kRescoreWarps];
+  __shared__ AtomStage stage[kRescoreWarps][2];
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
   float(*T)[256] = tab[w];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
   unsigned long long st_exh = 0, st_exact = 0, st_chunks = 0;
-  for (int64_t a = blockIdx.x * static_cast<int64_t>(kRescoreWarps) + w; a < r.n; a += nwarps) {
+  // Lanes 0-11 copy one 16-byte chunk each of atom a's stage (thr: 4 bytes).
+  const auto prefetch = [&](int64_t a, int s) {
+    if (a < r.n && lane < 12) {
+      AtomStage &d = stage[w][s];
+      if (lane < 6) cp_async16(d.x + 4 * lane, atom_ptr(sg, a) + 4 * lane);
+      else if (lane < 8) cp_async16(&d.masks[lane - 6], r.masks + 2 * a + (lane - 6));
+      else if (lane < 11) cp_async16(reinterpret_cast<uint4 *>(&d.info) + (lane - 8),
+                                     reinterpret_cast<const uint4 *>(r.info + a) + (lane - 8));
+      else cp_async4(&d.thr, r.thr + a);
+    }
+    cp_async_commit();
+  };
+  int sb = 0;
+  prefetch(blockIdx.x * static_cast<int64_t>(kRescoreWarps) + w, 0);
+  for (int64_t a = blockIdx.x * static_cast<int64_t>(kRescoreWarps) + w; a < r.n; a += nwarps, sb ^= 1) {
+    // The other stage was last read by the previous atom: every lane is done
+    // with it before the next atom's copies overwrite it.
+    __syncwarp();
+    prefetch(a + nwarps, sb ^ 1);
+    cp_async_wait1();
+    __syncwarp();
+    const AtomStage &A = stage[w][sb];
     const float *xg = atom_ptr(sg, a);
     float v[kDim];
-    load_atom(xg, v);
-    const float xl = lane < kDim ? __ldg(xg + lane) : 0.f;  // lane i: x_i
+#pragma unroll
+    for (int q = 0; q < 6; ++q) {
+      const float4 f = reinterpret_cast<const float4 *>(A.x)[q];
+      v[4 * q] = f.x;
+      v[4 * q + 1] = f.y;
+      v[4 * q + 2] = f.z;
+      v[4 * q + 3] = f.w;
+    }
+    const float xl = lane < kDim ? A.x[lane] : 0.f;  // lane i: x_i
     const int triv = trivial_index_warp(v, xl, lane, r.rule);
-    const uint4 mq0 = r.masks[2 * a], mq1 = r.masks[2 * a + 1];
+    const uint4 mq0 = A.masks[0], mq1 = A.masks[1];
     const uint64_t mrow[4] = {mq0.x | static_cast<uint64_t>(mq0.y) << 32,
                               mq0.z | static_cast<uint64_t>(mq0.w) << 32,
                               mq1.x | static_cast<uint64_t>(mq1.y) << 32,
@@ -911,8 +960,8 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     int bj = 0x7FFFFFFF;
     int nex = 0;
     if (!heavy) {
-      const float thr = r.thr[a];
-      const AtomInfo inf = r.info[a];
+      const float thr = A.thr;
+      const AtomInfo inf = A.info;
       __syncwarp();  // the previous atom's table and list reads are done
       if (lane == 0) cand_n[w] = 0;
       // Partial-sum tables: T[k][s] = sum of x_{8k+i} over the bits i of s.
