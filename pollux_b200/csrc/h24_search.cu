@@ -26,15 +26,17 @@
 //   1. prep_kernel      per atom: the four bf16 rows, written straight into
 //                       the UMMA shared-memory layout of the screening A
 //                       operand, and the per-atom constants (AtomInfo).
-//   2. screen_kernel    persistent tcgen05 kernel, one CTA per SM, 128 atoms
-//                       (four M=128 tiles of 32 atoms x 4 rows) per work item;
+//   2. screen_kernel    persistent tcgen05 kernel, one CTA per SM, 64 atoms
+//                       (two M=128 tiles of 32 atoms x 4 rows) per work item;
 //                       the Golay operand streams through a shared-memory ring
-//                       in tiles of 128 columns; M128 N128 K32 MMAs into four
-//                       TMEM accumulator stages.  16 epilogue warps keep, per
-//                       row, the maximum of each 128-column chunk; at the end
-//                       of a work item they form the atom's best achievable
-//                       screening score and flag every chunk that may hold a
-//                       codeword within 2E of it (one 32-bit mask per row).
+//                       in tiles of 128 columns; M128 N128 K32 MMAs into two
+//                       TMEM accumulator stages per M-tile, so that the MMAs
+//                       of one Golay tile run while the epilogue reads the
+//                       previous one.  16 epilogue warps keep, per row, the
+//                       maximum of each 64-column chunk; at the end of a work
+//                       item they form the atom's best achievable screening
+//                       score and flag every chunk that may hold a codeword
+//                       within 2E of it (one 64-bit mask per row).
 //   3. rescore_kernel   one warp per atom: fp32 scores (from per-atom
 //                       partial-sum tables) of the codewords behind the
 //                       flagged chunks, then fp64 scores in the reference's
@@ -68,29 +70,56 @@
 namespace h24 {
 namespace {
 
-constexpr int kWorkAtoms = 128;                    // atoms per CTA work item
+constexpr int kWorkAtoms = 64;                     // atoms per CTA work item
 constexpr int kRowsPerAtom = 4;                    // slice p1, slice p2, plain, |x|
-constexpr int kMTiles = kWorkAtoms * kRowsPerAtom / 128;  // 4
+constexpr int kMTiles = kWorkAtoms * kRowsPerAtom / 128;  // 2
 constexpr int kATileBytes = 128 * kRowBytes;       // 8192
-constexpr int kAItemBytes = kMTiles * kATileBytes; // 32768
+constexpr int kAItemBytes = kMTiles * kATileBytes; // 16384
 constexpr int kBTileBytes = kGolayTileN * kRowBytes;  // 8192
 constexpr int kStages = 8;                         // Golay tile ring depth
 constexpr int kChunkCols = 64;                     // candidate chunk: half a Golay tile
-constexpr int kChunks = kGolay / kChunkCols;       // 64 per row
 constexpr int kW16Tile = kW16First / kGolayTileN;  // 26: first tile with weight-16 columns
 constexpr int kW16Chunk = kW16First / kChunkCols;  // 52: first chunk with weight-16 columns
 constexpr int kW16Skip = kW16First - kW16Tile * kGolayTileN;  // 8 dodecads lead tile 26
-constexpr int kEpiWarps = 16;                      // 4 M-tiles x 4 TMEM lane quarters
-constexpr int kIssuers = 2;                        // MMA issuer warps, two M-tiles each
-constexpr int kFirstEpiWarp = 1 + kIssuers;        // warp 0 producer, warps 1-2 MMA issuers
-constexpr int kScreenThreads = 32 * (kFirstEpiWarp + kEpiWarps);  // 608
-constexpr uint32_t kTmemCols = kMTiles * kGolayTileN;  // 512: one accumulator stage per M-tile
+constexpr int kAccStages = 2;                      // TMEM accumulator stages per M-tile
+constexpr int kEpiWarps = kMTiles * 4;            // 8: (M-tile, lane quarter)
+constexpr int kProducerWarp = kEpiWarps;           // warp 8: TMA producer
+constexpr int kIssuerWarp = kEpiWarps + 1;         // warps 9-10: MMA issuer of M-tile 0, 1
+constexpr int kScreenThreads = 32 * (kEpiWarps + 1 + kMTiles);  // 352
+constexpr uint32_t kTmemCols = kMTiles * kAccStages * kGolayTileN;  // 512
 constexpr int kHeavyChunks = 192;                  // flagged chunks (of 204) beyond which the exhaustive scan runs
 constexpr int kMaxSegs = 64;                       // input segments per pipeline batch
 constexpr int64_t kBatchAtoms = int64_t(1) << 20;  // atoms per pipeline batch
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s
 static_assert(kW16Chunk == 52 && kW16Skip == 8, "weight-16 block starts 8 columns into chunk 52");
 static_assert(kW16First + kOctads == kGolay - 1, "the all-ones word closes the weight-16 block");
+static_assert(kGolayTiles % (2 * kAccStages) == 0, "each stage is used an even number of times per item");
+
+// Row type held by TMEM lane quarter q of M-tile g, and its inverse.  The two
+// |x| rows (their loads are skipped for 26 of the 32 Golay tiles) sit in lane
+// quarters 1 and 2, read by the SM sub-partitions that also run the two MMA
+// issuer warps (warp w runs on sub-partition w % 4 and reads quarter w % 4).
+__host__ __device__ constexpr int row_of_quarter(int g, int q) {
+  return g == 0 ? ((0x2130 >> (4 * q)) & 0xF) : ((q + 1) & 3);
+}
+__host__ __device__ constexpr int quarter_of_row(int g, int r) {
+  return g == 0 ? ((0x1320 >> (4 * r)) & 0xF) : ((r + 3) & 3);
+}
+static_assert(row_of_quarter(0, quarter_of_row(0, 1)) == 1 && row_of_quarter(0, quarter_of_row(0, 2)) == 2 &&
+                  row_of_quarter(0, quarter_of_row(0, 3)) == 3 && row_of_quarter(1, quarter_of_row(1, 0)) == 0 &&
+                  row_of_quarter(1, quarter_of_row(1, 3)) == 3 && quarter_of_row(0, 3) == 1 &&
+                  quarter_of_row(1, 3) == 2,
+              "quarter <-> row type maps are inverse, |x| rows in quarters 1 and 2");
+
+// Chunk of bit b of a row's 64-bit flag mask: bits 32 s + i and 32 s + 16 + i
+// hold the chunks 2 t and 2 t + 1 of Golay tile t = 2 i + s (the tiles of
+// accumulator stage s fill one 32-bit half of the mask).
+__host__ __device__ constexpr int chunk_of_bit(int b) {
+  return 4 * (b & 15) + 2 * (b >> 5) + ((b >> 4) & 1);
+}
+static_assert(chunk_of_bit(0) == 0 && chunk_of_bit(16) == 1 && chunk_of_bit(32) == 2 &&
+                  chunk_of_bit(48) == 3 && chunk_of_bit(1) == 4 && chunk_of_bit(63) == 63,
+              "mask bit order");
 
 // Per-atom constants of the search (prep_kernel -> screen and rescore).
 struct __align__(16) AtomInfo {
@@ -112,18 +141,19 @@ static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 struct __align__(1024) ScreenSmem {
   uint8_t a[2][kAItemBytes];          // A operand of two work items
   uint8_t b[kStages][kBTileBytes];    // Golay tile ring
-  float rowval[2][kWorkAtoms][kRowsPerAtom];  // per-row bests, by work-item parity
-  // Chunk maxima of each epilogue thread, rounded up to fp16 (so the flags
-  // stay conservative).
-  __half cmax[kChunks][kEpiWarps * 32];
+  // Per Golay tile and epilogue thread slot (M-tile, lane quarter, lane): the
+  // maxima of the tile's two 64-column chunks, rounded up to fp16 (so the
+  // flags stay conservative).  Each slot is written and read by one thread.
+  __half2 cmax[kGolayTiles][kWorkAtoms * kRowsPerAtom];
+  float rowval[2][kWorkAtoms][kRowsPerAtom];  // row maxima, by work-item parity
   uint64_t bar_a_full[2];
   uint64_t bar_a_empty[2];          // one commit per issuer
   uint64_t bar_b_full[kStages];
-  uint64_t bar_b_empty[kStages];
-  uint64_t bar_acc_full[kMTiles];
-  uint64_t bar_acc_empty[kMTiles];
+  uint64_t bar_b_empty[kStages];    // one arrival per epilogue warp
+  uint64_t bar_acc_full[kMTiles][kAccStages];
+  uint64_t bar_acc_empty[kMTiles][kAccStages];
   uint64_t bar_rows[2];
-  uint64_t bar_final[kIssuers];     // each issuer's last MMAs
+  uint64_t bar_final[kMTiles];      // each issuer's last MMAs
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -282,7 +312,7 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) <<
                             ((128u >> 4) << 24);
 
 // D (TMEM) += A x B, both from shared-memory descriptors; accumulate == 0
-// overwrites D.
+// overwrites D.  Issued by a single thread.
 __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                             uint32_t accumulate) {
   asm volatile(
@@ -293,6 +323,7 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uin
       : "memory");
 }
 
+// Arrival on `bar` once the MMAs issued so far by this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -303,18 +334,14 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 #define H24_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), \
                   "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
 
-// 32 lanes x 64 consecutive 32-bit TMEM columns, waited for in the same
-// statement.
-__device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, uint32_t *r) {
+// 32 lanes x 128 consecutive 32-bit TMEM columns, waited for in the same
+// statement (one load latency per 128 columns).
+__device__ __forceinline__ void tmem_ld128_wait(uint32_t taddr, uint32_t *r) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
-      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24), H24_R8(32), H24_R8(40), H24_R8(48),
-        H24_R8(56)
+      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24), H24_R8(32), H24_R8(40), H24_R8(48), H24_R8(56), H24_R8(64), H24_R8(72), H24_R8(80), H24_R8(88), H24_R8(96), H24_R8(104), H24_R8(112), H24_R8(120)
       : "r"(taddr)
       : "memory");
 }
@@ -367,10 +394,9 @@ __device__ __forceinline__ uint32_t a_offset(int L, int q) {
   return static_cast<uint32_t>((L >> 3) * 512 + q * 128 + (L & 7) * 16);
 }
 
-// Atom a of work item w = a / 128 sits in M-tile g = (a / 32) % 4 at lane
-// 32 * ((r - g) mod 4) + a % 32 for row type r (0 slice p1, 1 slice p2,
-// 2 plain, 3 |x|), so that each TMEM lane quarter holds every row type once
-// over the four M-tiles and the epilogue's work spreads evenly over the SM.
+// Atom a of work item w = a / 64 sits in M-tile g = (a / 32) % 2 at lane
+// 32 * quarter_of_row(g, r) + a % 32 for row type r (0 slice p1, 1 slice p2,
+// 2 plain, 3 |x|).
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
                                                    int64_t n_pad, const uint32_t *__restrict__ gmask,
                                                    const uint16_t *__restrict__ oct_by_triple,
@@ -491,8 +517,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   for (int k = 0; k < 9; ++k) inf.pad[k] = 0;
   info[a] = inf;
 
-  uint8_t *item = a_tiles + (a >> 7) * kAItemBytes;
-  const int g = static_cast<int>((a >> 5) & 3), l = static_cast<int>(a & 31);
+  uint8_t *item = a_tiles + (a / kWorkAtoms) * kAItemBytes;
+  const int g = static_cast<int>((a >> 5) & (kMTiles - 1)), l = static_cast<int>(a & 31);
 #pragma unroll
   for (int r = 0; r < kRowsPerAtom; ++r) {
     uint32_t w[16];
@@ -510,7 +536,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
 #pragma unroll
     for (int k = 12; k < 16; ++k) w[k] = 0;
     uint8_t *tile = item + g * kATileBytes;
-    const int L = 32 * ((r - g) & 3) + l;
+    const int L = 32 * quarter_of_row(g, r) + l;
 #pragma unroll
     for (int q = 0; q < 4; ++q)
       *reinterpret_cast<uint4 *>(tile + a_offset(L, q)) =
@@ -543,23 +569,25 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.bar_a_full[i], 1);
-      mbar_init(&S.bar_a_empty[i], kIssuers);
+      mbar_init(&S.bar_a_empty[i], kMTiles);
       mbar_init(&S.bar_rows[i], kEpiWarps);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.bar_b_full[s], 1);
-      mbar_init(&S.bar_b_empty[s], kIssuers);
+      mbar_init(&S.bar_b_empty[s], kEpiWarps);
     }
     for (int g = 0; g < kMTiles; ++g) {
-      mbar_init(&S.bar_acc_full[g], 1);
-      mbar_init(&S.bar_acc_empty[g], 4);  // the four warps of M-tile g
+      for (int s = 0; s < kAccStages; ++s) {
+        mbar_init(&S.bar_acc_full[g][s], 1);
+        mbar_init(&S.bar_acc_empty[g][s], 4);  // the four lane-quarter warps of M-tile g
+      }
+      mbar_init(&S.bar_final[g], 1);
     }
-    for (int i = 0; i < kIssuers; ++i) mbar_init(&S.bar_final[i], 1);
     S.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == kIssuerWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&S.tmem_base)),
                  "r"(kTmemCols)
@@ -571,7 +599,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
   tc_fence_after();
   const uint32_t tmem_base = S.tmem_base;
 
-  if (warp == 0) {
+  if (warp == kProducerWarp) {
     // ---------------- producer: A of each work item, Golay tiles ----------
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
@@ -610,13 +638,14 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
             }
       }
     }
-  } else if (warp <= kIssuers) {
-    // ---------------- MMA issuers ---------------------------------------------
-    // Per Golay tile, one M128 N128 K32 product (two K=16 MMAs) for each of
-    // the four M-tiles into TMEM stage g (columns 128 g).  MMA issue blocks
-    // until the tensor core accepts the instruction, so two issuers (M-tiles
-    // 0-1 and 2-3) let one wait on its barriers while the other's MMAs run.
-    const int g0 = (warp - 1) * (kMTiles / kIssuers);
+  } else if (warp >= kIssuerWarp) {
+    // ---------------- MMA issuers, one per M-tile -----------------------------
+    // Golay tile t goes into accumulator stage s = t % 2 of M-tile g (TMEM
+    // columns 128 (2 g + s)): one M128 N128 K32 product, two K=16 MMAs.  Stage
+    // s is used 16 times per work item, so the release awaited before use
+    // u = t / 2 has parity (u & 1) ^ 1.  The Golay ring slot goes back to the
+    // producer through the epilogue warps, which see the MMAs complete.
+    const int g = warp - kIssuerWarp;
     if (lane == 0) {
       const uint32_t a0 = smem_u32(S.a[0]), b0 = smem_u32(S.b[0]);
       constexpr uint64_t kKStep = 256 >> 4;  // next 16 K: two 16-byte chunks, descriptor units
@@ -626,24 +655,21 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
         if (!wait_bar(&S.bar_a_full[ab], aph, abort_flag, args.err)) { ok = false; break; }
         tc_fence_after();
-        for (int t = 0; ok && t < kGolayTiles; ++t) {
+        const uint64_t ad = smem_desc(a0 + static_cast<uint32_t>(ab * kAItemBytes + g * kATileBytes));
+        for (int t = 0; t < kGolayTiles; ++t) {
+          const int s = t & 1;
           if (!wait_bar(&S.bar_b_full[bs], bph, abort_flag, args.err)) { ok = false; break; }
+          if (!wait_bar(&S.bar_acc_empty[g][s], ((t >> 1) & 1) ^ 1, abort_flag, args.err)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint64_t bd = smem_desc(b0 + static_cast<uint32_t>(bs) * kBTileBytes);
-          for (int g = g0; g < g0 + kMTiles / kIssuers; ++g) {
-            // Use t of stage g (32 per work item, so parity t & 1) waits for
-            // the release of use t - 1.
-            if (!wait_bar(&S.bar_acc_empty[g], (t & 1) ^ 1, abort_flag, args.err)) { ok = false; break; }
-            tc_fence_after();
-            const uint64_t ad = smem_desc(a0 + static_cast<uint32_t>(ab * kAItemBytes + g * kATileBytes));
-            const uint32_t d = tmem_base + static_cast<uint32_t>(g * kGolayTileN);
-            mma_bf16_ss(d, ad, bd, 0);
-            mma_bf16_ss(d, ad + kKStep, bd + kKStep, 1);
-            mma_commit(&S.bar_acc_full[g]);
-            issued = true;
-          }
-          if (!ok) break;
-          mma_commit(&S.bar_b_empty[bs]);
+          const uint32_t d = tmem_base + static_cast<uint32_t>((g * kAccStages + s) * kGolayTileN);
+          mma_bf16_ss(d, ad, bd, 0);
+          mma_bf16_ss(d, ad + kKStep, bd + kKStep, 1);
+          mma_commit(&S.bar_acc_full[g][s]);
+          issued = true;
           if (++bs == kStages) { bs = 0; bph ^= 1; }
         }
         if (!ok) break;
@@ -652,73 +678,66 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       }
       if (issued) {
         // All MMAs of this CTA complete before TMEM is released.
-        mma_commit(&S.bar_final[warp - 1]);
+        mma_commit(&S.bar_final[g]);
         const unsigned long long t0 = global_ns();
-        while (!mbar_try_wait(&S.bar_final[warp - 1], 0) && global_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try_wait(&S.bar_final[g], 0) && global_ns() - t0 < kWaitLimitNs) {
         }
       }
     }
   } else {
-    // ---------------- epilogue: one thread per (atom, row type) -------------
-    // Warp w may only access TMEM lanes 32*(w%4)..+31: warps of M-tile g
-    // (e / 4) cover its four lane quarters, quarter q holding row type
-    // (q + g) mod 4 of atoms 32 g .. 32 g + 31 of the work item.
-    const int e = warp - kFirstEpiWarp;
-    const int g = e >> 2;
+    // ---------------- epilogue: one thread per (atom, row type) --------------
+    // Warp w reads TMEM lane quarter q = w % 4 of M-tile g = w / 4: row type
+    // row_of_quarter(g, q) of atoms 32 g .. 32 g + 31 of the work item, the
+    // Golay tiles alternating between the two accumulator stages.
     const int q = warp & 3;
-    const int r = (q + g) & 3;
+    const int g = warp >> 2;
+    const int r = row_of_quarter(g, q);
     const int local = 32 * g + lane;
-    const uint32_t t_row =
-        tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(g * kGolayTileN);
+    const int slot = (g * 4 + q) * 32 + lane;
+    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                           static_cast<uint32_t>(g * kAccStages * kGolayTileN);
     bool ok = true;
     int ip = 0;
     uint32_t rph = 0;  // bit i: parity of the next phase of bar_rows[i]
     for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
       const int64_t atom = it * kWorkAtoms + local;
       const AtomInfo inf = args.info[atom];
-      __half *cm = &S.cmax[0][e * 32 + lane];  // chunk k at cm[k * kEpiWarps * 32]
       float rowmax = -INFINITY;
-#pragma unroll
+#pragma unroll 1
       for (int t = 0; t < kGolayTiles; ++t) {
+        const int s = t & 1;
         bool got = true;
-        if (lane == 0) got = wait_bar_inl(&S.bar_acc_full[g], t & 1, abort_flag, args.err);
+        if (lane == 0) got = wait_bar_inl(&S.bar_acc_full[g][s], (t >> 1) & 1, abort_flag, args.err);
         if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
         tc_fence_after();
+        // The MMAs of tile t are complete: its Golay ring slot may be refilled.
+        if (lane == 0) mbar_arrive(&S.bar_b_empty[t % kStages]);
         float m0 = -INFINITY, m1 = -INFINITY;
         if (r != 3 || t >= kW16Tile) {
-          uint32_t x[64];
-          // Rolled: an unrolled loop lets the compiler keep both blocks of
-          // loaded values live at once (register spills).
-#pragma unroll 1
-          for (int k = 0; k < 2; ++k) {
-            tmem_ld64_wait(t_row + static_cast<uint32_t>(64 * k), x);
-            if (k == 1) {
-              // Both loads done: hand the stage back to the MMA issuer.
-              tc_fence_before();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(&S.bar_acc_empty[g]);
-            }
-            if (t == kW16Tile && r == 3 && k == 0) {
+          uint32_t x[128];
+          tmem_ld128_wait(t_row + static_cast<uint32_t>(s * kGolayTileN), x);
+          // Loaded: hand the stage back to the MMA issuer.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.bar_acc_empty[g][s]);
+          if (r == 3 && t == kW16Tile) {
 #pragma unroll
-              for (int i = 0; i < kW16Skip; ++i) x[i] = 0xFF800000u;  // dodecad columns
-            }
-            if (t == kGolayTiles - 1 && r == 3 && k == 1) x[63] = 0xFF800000u;  // all-ones word
-            const float mk = max32(max32(-INFINITY, x), x + 32);
-            if (k == 0) m0 = mk; else m1 = mk;
+            for (int j = 0; j < kW16Skip; ++j) x[j] = 0xFF800000u;  // dodecad columns
           }
+          if (r == 3 && t == kGolayTiles - 1) x[127] = 0xFF800000u;  // all-ones word
+          m0 = max32(max32(-INFINITY, x), x + 32);
+          m1 = max32(max32(-INFINITY, x + 64), x + 96);
         } else {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&S.bar_acc_empty[g]);
+          if (lane == 0) mbar_arrive(&S.bar_acc_empty[g][s]);
         }
-        cm[(2 * t) * kEpiWarps * 32] = __float2half_ru(m0);
-        cm[(2 * t + 1) * kEpiWarps * 32] = __float2half_ru(m1);
+        S.cmax[t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
         rowmax = fmaxf(rowmax, fmaxf(m0, m1));
       }
       if (!ok) break;
-      // Per-row best, exchanged through shared memory.
-      const float add = r < 2 ? inf.off[r] : (r == 2 ? fmaxf(inf.u0, inf.u1) : inf.shi);
-      S.rowval[ip][local][r] = r < 2 ? rowmax + add : (r == 3 ? rowmax + inf.shi - inf.l2s : -INFINITY);
+      // Row maxima of the atom's four rows, exchanged through shared memory.
+      S.rowval[ip][local][r] = rowmax;
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.bar_rows[ip]);
       bool got = true;
@@ -727,17 +746,27 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       __syncwarp();
       rph ^= 1u << ip;
       const float *rv = S.rowval[ip][local];
-      const float best = fmaxf(fmaxf(fmaxf(rv[0], rv[1]), fmaxf(rv[3], inf.t1)), inf.t2lb);
+      const float best = fmaxf(fmaxf(fmaxf(rv[0] + inf.off[0], rv[1] + inf.off[1]),
+                                     fmaxf(rv[3] + inf.shi - inf.l2s, inf.t1)),
+                               inf.t2lb);
       const float thr = best - inf.two_e;
-      uint32_t mlo = 0, mhi = 0;
+      const float add = r < 2 ? inf.off[r] : (r == 2 ? fmaxf(inf.u0, inf.u1) : inf.shi);
+      // A chunk is flagged when (its fp16 maximum) + add >= thr in fp32.  In
+      // fp16: maximum >= th with th <= thr - add, lowered by 2^-18 (|thr| +
+      // |add|) against the fp32 roundings and rounded down to fp16, so every
+      // chunk flagged in fp32 is flagged here (a few more may be).  th stays
+      // finite so that chunks without columns (maximum -inf) stay unflagged.
+      const float theta = (thr - add) - (fabsf(thr) + fabsf(add)) * 3.814697265625e-6f;
+      const __half2 th2 = __half2half2(__float2half_rd(fmaxf(theta, -65504.f)));
+      uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        mlo |= (__half2float(cm[k * kEpiWarps * 32]) + add >= thr ? 1u : 0u) << k;
-        mhi |= (__half2float(cm[(k + 32) * kEpiWarps * 32]) + add >= thr ? 1u : 0u) << k;
+      for (int i = kGolayTiles / 2 - 1; i >= 0; --i) {
+        w0 = (w0 << 1) | (__hge2_mask(S.cmax[2 * i][slot], th2) & 0x00010001u);
+        w1 = (w1 << 1) | (__hge2_mask(S.cmax[2 * i + 1][slot], th2) & 0x00010001u);
       }
-      if (!(inf.two_e >= 0.f)) mlo = mhi = 0;
+      if (!(inf.two_e >= 0.f)) w0 = w1 = 0;
       if (atom < args.n) {
-        args.masks[atom * kRowsPerAtom + r] = make_uint2(mlo, mhi);
+        args.masks[atom * kRowsPerAtom + r] = make_uint2(w0, w1);
         if (r == 0) args.thr[atom] = thr;
       }
       ip ^= 1;
@@ -747,12 +776,13 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) {
+  if (warp == kIssuerWarp) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(kTmemCols)
                  : "memory");
   }
 }
+
 
 // ---------------------------------------------------------------------------
 // 3. rescore (one warp per atom) and 4. exhaustive fallback
@@ -1007,7 +1037,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         const int p = s ? p2 : p1;
         const float xp = __shfl_sync(0xffffffffu, xl, p);
         while (m) {
-          const int b = __ffsll(m) - 1;
+          const int b = chunk_of_bit(__ffsll(m) - 1);
           m &= m - 1;
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
@@ -1022,7 +1052,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       {
         uint64_t m = mrow[2];
         while (m) {
-          const int b = __ffsll(m) - 1;
+          const int b = chunk_of_bit(__ffsll(m) - 1);
           m &= m - 1;
 #pragma unroll 1
           for (int k = 0; k < 2; ++k) {
@@ -1050,7 +1080,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       {
         uint64_t m = mrow[3];
         while (m) {
-          const int b = __ffsll(m) - 1;
+          const int b = chunk_of_bit(__ffsll(m) - 1);
           m &= m - 1;
 #pragma unroll 1
           for (int k = 0; k < 2; ++k) {
