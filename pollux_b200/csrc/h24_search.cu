@@ -876,13 +876,6 @@ __device__ __forceinline__ int trivial_index_warp(const float (&v)[kDim], float 
   return -1;
 }
 
-__device__ __forceinline__ float pick(const float (&v)[kDim], int p) {
-  float r = 0.f;
-#pragma unroll
-  for (int i = 0; i < kDim; ++i) r = i == p ? v[i] : r;
-  return r;
-}
-
 // What the rescore reads of one atom, staged in shared memory by cp.async one
 // atom ahead of its use.
 struct AtomStage {
@@ -907,12 +900,28 @@ constexpr int kRescoreWarps = 8;
 constexpr int kRescoreBlocksPerSm = 2;
 constexpr int kCandCap = 128;  // fp32 candidates per atom before the fp64 pass
 
-// fp64 score of kissing point j, for candidates beyond the list (exact ties
+// A listed candidate is held as (type << 24) | its offset in that type's
+// index table (idx3: 24 c + p, idx2: 128 o + sign pattern, idx1: 4 (24 a + b)
+// + signs); the kissing-point index is looked up only for the candidates
+// that reach the fp64 pass.
+constexpr uint32_t kCandType3 = 3u << 24, kCandType2 = 2u << 24, kCandType1 = 1u << 24;
+__device__ __forceinline__ int32_t cand_index(const int32_t *__restrict__ idx3,
+                                              const int32_t *__restrict__ idx2,
+                                              const int32_t *__restrict__ idx1, uint32_t code) {
+  const uint32_t off = code & 0xFFFFFFu;
+  const uint32_t type = code >> 24;
+  return __ldg((type == 3 ? idx3 : (type == 2 ? idx2 : idx1)) + off);
+}
+
+// fp64 score of a listed candidate beyond the list's capacity (exact ties
 // over many codewords): out of line, it reloads the atom.
 __device__ __noinline__ void exact_now(const float *__restrict__ xg, const int8_t *__restrict__ cb_raw,
-                                       int32_t j, double &bs, int &bj, int &nex) {
+                                       const int32_t *__restrict__ idx3, const int32_t *__restrict__ idx2,
+                                       const int32_t *__restrict__ idx1, uint32_t code, double &bs,
+                                       int &bj, int &nex) {
   float v[kDim];
   load_atom(xg, v);
+  const int32_t j = cand_index(idx3, idx2, idx1, code);
   better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
   ++nex;
 }
@@ -931,11 +940,15 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     rescore_kernel(const __grid_constant__ Segs sg, const RescoreArgs r) {
   __shared__ float tab[kRescoreWarps][3][256];
   __shared__ float cand_s[kRescoreWarps][kCandCap];
-  __shared__ int32_t cand_j[kRescoreWarps][kCandCap];
+  __shared__ uint32_t cand_c[kRescoreWarps][kCandCap];
   __shared__ int cand_n[kRescoreWarps];
   __shared__ AtomStage stage[kRescoreWarps][2];
+  extern __shared__ uint32_t gmask_s[];  // [kGolay] Golay masks, staged once per block
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < kGolay / 4; i += blockDim.x)
+    reinterpret_cast<uint4 *>(gmask_s)[i] = __ldg(reinterpret_cast<const uint4 *>(r.gmask) + i);
+  __syncthreads();
   float(*T)[256] = tab[w];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
   unsigned long long st_exh = 0, st_exact = 0, st_chunks = 0;
@@ -962,15 +975,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     __syncwarp();
     const AtomStage &A = stage[w][sb];
     const float *xg = atom_ptr(sg, a);
-    float v[kDim];
-#pragma unroll
-    for (int q = 0; q < 6; ++q) {
-      const float4 f = reinterpret_cast<const float4 *>(A.x)[q];
-      v[4 * q] = f.x;
-      v[4 * q + 1] = f.y;
-      v[4 * q + 2] = f.z;
-      v[4 * q + 3] = f.w;
-    }
+    const float(&v)[kDim] = A.x;  // the atom, read from the stage when needed
     const float xl = lane < kDim ? A.x[lane] : 0.f;  // lane i: x_i
     const int triv = trivial_index_warp(v, xl, lane, r.rule);
     const uint4 mq0 = A.masks[0], mq1 = A.masks[1];
@@ -997,16 +1002,19 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       // Partial-sum tables: T[k][s] = sum of x_{8k+i} over the bits i of s.
 #pragma unroll
       for (int k = 0; k < 3; ++k) {
+        const float4 f0 = reinterpret_cast<const float4 *>(A.x)[2 * k];
+        const float4 f1 = reinterpret_cast<const float4 *>(A.x)[2 * k + 1];
+        const float v8[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
         float lo5 = 0.f;
 #pragma unroll
         for (int i = 0; i < 5; ++i)
-          if (lane >> i & 1) lo5 += v[8 * k + i];
+          if (lane >> i & 1) lo5 += v8[i];
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
           float hi3 = lo5;
-          if (m & 1) hi3 += v[8 * k + 5];
-          if (m & 2) hi3 += v[8 * k + 6];
-          if (m & 4) hi3 += v[8 * k + 7];
+          if (m & 1) hi3 += v8[5];
+          if (m & 2) hi3 += v8[6];
+          if (m & 4) hi3 += v8[7];
           T[k][lane + 32 * m] = hi3;
         }
       }
@@ -1020,13 +1028,13 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       }
       const uint32_t negm = __ballot_sync(0xffffffffu, xl < 0.f);
       const auto tsum = [&](uint32_t m) { return T[0][m & 255] + T[1][(m >> 8) & 255] + T[2][m >> 16]; };
-      const auto push = [&](float sc, int32_t j) {
+      const auto push = [&](float sc, uint32_t code) {
         const int k = atomicAdd(&cand_n[w], 1);
         if (k < kCandCap) {
           cand_s[w][k] = sc;
-          cand_j[w][k] = j;
+          cand_c[w][k] = code;
         } else {
-          exact_now(xg, r.cb_raw, j, bs, bj, nex);
+          exact_now(xg, r.cb_raw, r.idx3, r.idx2, r.idx1, code, bs, bj, nex);
         }
       };
       const int p1 = inf.p[0], p2 = inf.p[1], p3 = inf.p[2];
@@ -1042,9 +1050,9 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
 #pragma unroll
           for (int k = 0; k < 2; ++k) {
             const int c = b * kChunkCols + 32 * k + lane;
-            const uint32_t gm = __ldg(r.gmask + c);
+            const uint32_t gm = gmask_s[c];
             const float sc = sumx - 2.f * tsum(gm) - xp * ((gm >> p & 1u) ? 2.f : 4.f);
-            if (sc >= thr) push(sc, __ldg(r.idx3 + c * kDim + p));
+            if (sc >= thr) push(sc, kCandType3 | static_cast<uint32_t>(c * kDim + p));
           }
         }
       }
@@ -1057,18 +1065,26 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
 #pragma unroll 1
           for (int k = 0; k < 2; ++k) {
             const int c = b * kChunkCols + 32 * k + lane;
-            const uint32_t gm = __ldg(r.gmask + c);
+            const uint32_t gm = gmask_s[c];
             const float bc = sumx - 2.f * tsum(gm);
             if (bc + ((gm >> p3 & 1u) ? inf.u1 : inf.u0) >= thr) {
               uint32_t hit = 0;
 #pragma unroll
-              for (int p = 0; p < kDim; ++p)
-                hit |= (bc - v[p] * ((gm >> p & 1u) ? 2.f : 4.f) >= thr ? 1u : 0u) << p;
+              for (int q = 0; q < 6; ++q) {
+                const float4 f = reinterpret_cast<const float4 *>(A.x)[q];
+                const float f4[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int p = 4 * q + e;
+                  hit |= (bc - f4[e] * ((gm >> p & 1u) ? 2.f : 4.f) >= thr ? 1u : 0u) << p;
+                }
+              }
               hit &= ~((1u << p1) | (1u << p2));
               while (hit) {
                 const int p = __ffs(hit) - 1;
                 hit &= hit - 1;
-                push(bc - pick(v, p) * ((gm >> p & 1u) ? 2.f : 4.f), __ldg(r.idx3 + c * kDim + p));
+                push(bc - A.x[p] * ((gm >> p & 1u) ? 2.f : 4.f),
+                     kCandType3 | static_cast<uint32_t>(c * kDim + p));
               }
             }
           }
@@ -1089,7 +1105,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
             uint32_t om = 0;
             float t2 = -INFINITY;
             if (o >= 0 && o < kOctads) {
-              const uint32_t gm = __ldg(r.gmask + c);
+              const uint32_t gm = gmask_s[c];
               om = ~gm & 0xFFFFFFu;
               t2 = 2.f * (sumabs - (tsum(gm & ~negm) - tsum(gm & negm)));  // 2 T(O)
             }
@@ -1114,19 +1130,20 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
               const int oc = __shfl_sync(0xffffffffu, o, src);
               const uint32_t omc = __shfl_sync(0xffffffffu, om, src);
               // The octad's 8 coordinates, lowest position first, to every lane.
-              const int pos = lane < 8 ? static_cast<int>(__fns(omc, 0, lane + 1)) : 0;
-              float ov = __shfl_sync(0xffffffffu, xl, pos);
-              if (lane >= 8) ov = 0.f;
               float o8[8];
+              uint32_t mo = omc;
 #pragma unroll
-              for (int k2 = 0; k2 < 8; ++k2) o8[k2] = __shfl_sync(0xffffffffu, ov, k2);
+              for (int k2 = 0; k2 < 8; ++k2) {
+                o8[k2] = __shfl_sync(0xffffffffu, xl, (__ffs(mo) - 1) & 31);
+                mo &= mo - 1;
+              }
 #pragma unroll
               for (int t = 0; t < 4; ++t) {
                 const int pid = lane + 32 * t;
                 float sc = (__popc(pid) & 1) ? -o8[7] : o8[7];
 #pragma unroll
                 for (int k2 = 0; k2 < 7; ++k2) sc += (pid >> k2 & 1) ? -o8[k2] : o8[k2];
-                if (2.f * sc >= thr) push(2.f * sc, __ldg(r.idx2 + oc * 128 + pid));
+                if (2.f * sc >= thr) push(2.f * sc, kCandType2 | static_cast<uint32_t>(oc * 128 + pid));
               }
             }
           }
@@ -1134,14 +1151,14 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       }
       // Type 1: every score is at most t1.
       if (inf.t1 >= thr && lane < kDim) {
-        const float xa = pick(v, lane);
+        const float xa = A.x[lane];
 #pragma unroll 1
         for (int b2 = lane + 1; b2 < kDim; ++b2) {
-          const float xb = pick(v, b2);
+          const float xb = A.x[b2];
 #pragma unroll
           for (int s = 0; s < 4; ++s) {
             const float sc = 4.f * ((s & 1 ? -xa : xa) + (s & 2 ? -xb : xb));
-            if (sc >= thr) push(sc, __ldg(r.idx1 + (lane * kDim + b2) * 4 + s));
+            if (sc >= thr) push(sc, kCandType1 | static_cast<uint32_t>((lane * kDim + b2) * 4 + s));
           }
         }
       }
@@ -1159,7 +1176,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         for (int k = lane; k < nc; k += 32) {
           if (cand_s[w][k] >= cut) {
             ++nin;
-            jin = cand_j[w][k];
+            jin = static_cast<int>(cand_c[w][k]);
           }
         }
         // One codeword within 2 e' of the largest S' (and no list overflow):
@@ -1174,11 +1191,14 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         const bool quick = __popc(who) == 1 && nsrc == 1 && cand_n[w] <= kCandCap &&
                            (r.rule != H24_RULE_TRAIN || fabsf(origin_gap) > two_ep);
         if (quick) {
-          if (lane == 0) r.out[a] = (r.rule == H24_RULE_TRAIN && origin_gap < 0.f) ? 0 : jsrc + 1;
+          if (lane == 0)
+            r.out[a] = (r.rule == H24_RULE_TRAIN && origin_gap < 0.f)
+                           ? 0
+                           : cand_index(r.idx3, r.idx2, r.idx1, static_cast<uint32_t>(jsrc)) + 1;
         } else {
           for (int k = lane; k < nc; k += 32) {
             if (cand_s[w][k] >= cut) {
-              const int j = cand_j[w][k];
+              const int j = cand_index(r.idx3, r.idx2, r.idx1, cand_c[w][k]);
               better(bs, bj, score64(v, r.cb_raw + static_cast<int64_t>(j) * kDim), j);
               ++nex;
             }
@@ -1314,8 +1334,8 @@ int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int3
                  rule};
   const int64_t rblocks = (nbatch + kRescoreWarps - 1) / kRescoreWarps;
   const int64_t rcap = static_cast<int64_t>(sms) * kRescoreBlocksPerSm;
-  rescore_kernel<<<static_cast<unsigned>(rblocks < rcap ? rblocks : rcap), 32 * kRescoreWarps, 0,
-                   s>>>(sg, ra);
+  rescore_kernel<<<static_cast<unsigned>(rblocks < rcap ? rblocks : rcap), 32 * kRescoreWarps,
+                   kGolay * sizeof(uint32_t), s>>>(sg, ra);
   exhaustive_kernel<<<2 * sms, 256, 0, s>>>(sg, rule, sc.ovf_list, sc.ovf_count, t->cb_raw, ob);
   count_launches(4);
   H24_CUDA_TRY(cudaGetLastError());
@@ -1329,6 +1349,8 @@ int screen_setup(int dev, int *sms) {
     H24_CUDA_TRY(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
     H24_CUDA_TRY(cudaFuncSetAttribute(screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(sizeof(ScreenSmem) + 1024)));
+    H24_CUDA_TRY(cudaFuncSetAttribute(rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(kGolay * sizeof(uint32_t))));
     // Launch sizes against what each kernel's resources allow.
     const struct { const void *fn; int threads; const char *name; } ks[] = {
         {reinterpret_cast<const void *>(screen_kernel), kScreenThreads, "screen_kernel"},
