@@ -897,7 +897,7 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 constexpr int kRescoreWarps = 8;
-constexpr int kRescoreBlocksPerSm = 2;
+constexpr int kRescoreBlocksPerSm = 3;
 constexpr int kCandCap = 128;  // fp32 candidates per atom before the fp64 pass
 
 // A listed candidate is held as (type << 24) | its offset in that type's
@@ -913,17 +913,21 @@ __device__ __forceinline__ int32_t cand_index(const int32_t *__restrict__ idx3,
   return __ldg((type == 3 ? idx3 : (type == 2 ? idx2 : idx1)) + off);
 }
 
-// fp64 score of a listed candidate beyond the list's capacity (exact ties
-// over many codewords): out of line, it reloads the atom.
-__device__ __noinline__ void exact_now(const float *__restrict__ xg, const int8_t *__restrict__ cb_raw,
+// Running fp64 best of one lane over the candidates beyond the list's
+// capacity (exact ties over many codewords), kept in shared memory.
+struct LaneBest {
+  double s;
+  int j;
+  int n;  // fp64 scores taken
+};
+
+// fp64 score of a listed candidate beyond the list's capacity: out of line.
+__device__ __noinline__ void exact_now(const float (&x)[kDim], const int8_t *__restrict__ cb_raw,
                                        const int32_t *__restrict__ idx3, const int32_t *__restrict__ idx2,
-                                       const int32_t *__restrict__ idx1, uint32_t code, double &bs,
-                                       int &bj, int &nex) {
-  float v[kDim];
-  load_atom(xg, v);
+                                       const int32_t *__restrict__ idx1, uint32_t code, LaneBest &lb) {
   const int32_t j = cand_index(idx3, idx2, idx1, code);
-  better(bs, bj, score64(v, cb_raw + static_cast<int64_t>(j) * kDim), j);
-  ++nex;
+  better(lb.s, lb.j, score64(x, cb_raw + static_cast<int64_t>(j) * kDim), j);
+  ++lb.n;
 }
 
 // Persistent: each warp takes atoms a = warp, warp + warps, ...; no block
@@ -943,6 +947,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   __shared__ uint32_t cand_c[kRescoreWarps][kCandCap];
   __shared__ int cand_n[kRescoreWarps];
   __shared__ AtomStage stage[kRescoreWarps][2];
+  __shared__ LaneBest lbest[kRescoreWarps][32];
   extern __shared__ uint32_t gmask_s[];  // [kGolay] Golay masks, staged once per block
   const int lane = threadIdx.x & 31;
   const int w = threadIdx.x >> 5;
@@ -951,7 +956,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   __syncthreads();
   float(*T)[256] = tab[w];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
-  unsigned long long st_exh = 0, st_exact = 0, st_chunks = 0;
+  uint32_t st_exh = 0, st_exact = 0, st_chunks = 0;
   // Lanes 0-11 copy one 16-byte chunk each of atom a's stage (thr: 4 bytes).
   const auto prefetch = [&](int64_t a, int s) {
     if (a < r.n && lane < 12) {
@@ -974,15 +979,11 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     cp_async_wait1();
     __syncwarp();
     const AtomStage &A = stage[w][sb];
-    const float *xg = atom_ptr(sg, a);
     const float(&v)[kDim] = A.x;  // the atom, read from the stage when needed
     const float xl = lane < kDim ? A.x[lane] : 0.f;  // lane i: x_i
     const int triv = trivial_index_warp(v, xl, lane, r.rule);
-    const uint4 mq0 = A.masks[0], mq1 = A.masks[1];
-    const uint64_t mrow[4] = {mq0.x | static_cast<uint64_t>(mq0.y) << 32,
-                              mq0.z | static_cast<uint64_t>(mq0.w) << 32,
-                              mq1.x | static_cast<uint64_t>(mq1.y) << 32,
-                              mq1.z | static_cast<uint64_t>(mq1.w) << 32};
+    // Row r's 64-bit chunk mask, read from the stage when its row is processed.
+    const uint64_t *mrow = reinterpret_cast<const uint64_t *>(A.masks);
     const int nch = __popcll(mrow[0]) + __popcll(mrow[1]) + __popcll(mrow[2]) + __popcll(mrow[3]);
     if (triv >= 0) {
       if (lane == 0) r.out[a] = triv;
@@ -990,15 +991,15 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     }
     st_chunks += nch;
     bool heavy = nch > kHeavyChunks;
-    // Running fp64 best of this lane (list overflow and the fp64 pass).
-    double bs = -INFINITY;
-    int bj = 0x7FFFFFFF;
-    int nex = 0;
     if (!heavy) {
       const float thr = A.thr;
       const AtomInfo inf = A.info;
       __syncwarp();  // the previous atom's table and list reads are done
       if (lane == 0) cand_n[w] = 0;
+      LaneBest &lb = lbest[w][lane];
+      lb.s = -INFINITY;
+      lb.j = 0x7FFFFFFF;
+      lb.n = 0;
       // Partial-sum tables: T[k][s] = sum of x_{8k+i} over the bits i of s.
 #pragma unroll
       for (int k = 0; k < 3; ++k) {
@@ -1034,7 +1035,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
           cand_s[w][k] = sc;
           cand_c[w][k] = code;
         } else {
-          exact_now(xg, r.cb_raw, r.idx3, r.idx2, r.idx1, code, bs, bj, nex);
+          exact_now(v, r.cb_raw, r.idx3, r.idx2, r.idx1, code, lb);
         }
       };
       const int p1 = inf.p[0], p2 = inf.p[1], p3 = inf.p[2];
@@ -1196,6 +1197,8 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
                            ? 0
                            : cand_index(r.idx3, r.idx2, r.idx1, static_cast<uint32_t>(jsrc)) + 1;
         } else {
+          double bs = lb.s;
+          int bj = lb.j, nex = lb.n;
           for (int k = lane; k < nc; k += 32) {
             if (cand_s[w][k] >= cut) {
               const int j = cand_index(r.idx3, r.idx2, r.idx1, cand_c[w][k]);
@@ -1231,9 +1234,9 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     }
   }
   if (lane == 0) {
-    if (st_exh) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[0]), st_exh);
-    if (st_exact) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[1]), st_exact);
-    if (st_chunks) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[2]), st_chunks);
+    if (st_exh) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[0]), static_cast<unsigned long long>(st_exh));
+    if (st_exact) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[1]), static_cast<unsigned long long>(st_exact));
+    if (st_chunks) atomicAdd(reinterpret_cast<unsigned long long *>(&r.stats[2]), static_cast<unsigned long long>(st_chunks));
   }
 }
 
