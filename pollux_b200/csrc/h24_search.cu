@@ -169,10 +169,6 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
@@ -251,21 +247,23 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
   return wait_slow(bar, parity, abort_flag, err);
 }
 
-// Fully inlined form of wait_bar for loops that keep many values in
-// registers (no call, so nothing is saved around it).
-__device__ __forceinline__ bool wait_bar_inl(uint64_t *bar, uint32_t parity,
-                                             volatile int *abort_flag, int *err) {
-  if (mbar_test(bar, parity)) return true;
-  const unsigned long long t0 = global_ns();
-  for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (global_ns() - t0 > kWaitLimitNs) {
-      *abort_flag = 1;
-      atomicExch(err, H24_ERR_TIMEOUT);
-      return false;
-    }
-  }
+// One arrival on `bar` from lane 0 of a converged warp: a predicated
+// instruction rather than a branch around it.
+__device__ __forceinline__ void mbar_arrive_lane0(uint64_t *bar, int lane) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.eq.u32 p, %1, 0;\n\t"
+      "@p mbarrier.arrive.shared::cta.b64 _, [%0];\n\t}" ::"r"(smem_u32(bar)),
+      "r"(lane)
+      : "memory");
+}
+
+// wait_bar for a whole converged warp, every lane polling (no divergent
+// region); the result is the same on all lanes.
+__device__ __forceinline__ bool wait_bar_warp(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                              int *err) {
+  if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
+  return __all_sync(0xffffffffu, wait_slow(bar, parity, abort_flag, err));
 }
 
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
@@ -706,12 +704,13 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
 #pragma unroll 1
       for (int t = 0; t < kGolayTiles; ++t) {
         const int s = t & 1;
-        bool got = true;
-        if (lane == 0) got = wait_bar_inl(&S.bar_acc_full[g][s], (t >> 1) & 1, abort_flag, args.err);
-        if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
+        if (!wait_bar_warp(&S.bar_acc_full[g][s], (t >> 1) & 1, abort_flag, args.err)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         // The MMAs of tile t are complete: its Golay ring slot may be refilled.
-        if (lane == 0) mbar_arrive(&S.bar_b_empty[t % kStages]);
+        mbar_arrive_lane0(&S.bar_b_empty[t % kStages], lane);
         float m0 = -INFINITY, m1 = -INFINITY;
         if (r != 3 || t >= kW16Tile) {
           uint32_t x[128];
@@ -719,7 +718,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
           // Loaded: hand the stage back to the MMA issuer.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&S.bar_acc_empty[g][s]);
+          mbar_arrive_lane0(&S.bar_acc_empty[g][s], lane);
           if (r == 3 && t == kW16Tile) {
 #pragma unroll
             for (int j = 0; j < kW16Skip; ++j) x[j] = 0xFF800000u;  // dodecad columns
@@ -730,7 +729,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         } else {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&S.bar_acc_empty[g][s]);
+          mbar_arrive_lane0(&S.bar_acc_empty[g][s], lane);
         }
         S.cmax[t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
         rowmax = fmaxf(rowmax, fmaxf(m0, m1));
@@ -739,11 +738,11 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       // Row maxima of the atom's four rows, exchanged through shared memory.
       S.rowval[ip][local][r] = rowmax;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&S.bar_rows[ip]);
-      bool got = true;
-      if (lane == 0) got = wait_bar_inl(&S.bar_rows[ip], (rph >> ip) & 1u, abort_flag, args.err);
-      if (!__shfl_sync(0xffffffffu, got, 0)) { ok = false; break; }
-      __syncwarp();
+      mbar_arrive_lane0(&S.bar_rows[ip], lane);
+      if (!wait_bar_warp(&S.bar_rows[ip], (rph >> ip) & 1u, abort_flag, args.err)) {
+        ok = false;
+        break;
+      }
       rph ^= 1u << ip;
       const float *rv = S.rowval[ip][local];
       const float best = fmaxf(fmaxf(fmaxf(rv[0] + inf.off[0], rv[1] + inf.off[1]),
