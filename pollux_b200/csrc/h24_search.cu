@@ -310,21 +310,27 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) <<
                             ((128u >> 4) << 24);
 
 // D (TMEM) += A x B, both from shared-memory descriptors; accumulate == 0
-// overwrites D.  Issued by a single thread.
+// overwrites D.  Executed by a whole converged warp (every lane, warp-uniform
+// operands); the lane chosen by elect.sync issues it, the same lane every
+// time since the warp is fully active.
 __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                             uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
       : "memory");
 }
 
-// Arrival on `bar` once the MMAs issued so far by this thread complete.
+// Arrival on `bar` once the MMAs issued so far by the elected lane complete
+// (whole converged warp, as mma_bf16_ss).
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
           smem_u32(bar))
       : "memory");
 }
@@ -644,43 +650,44 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     // u = t / 2 has parity (u & 1) ^ 1.  The Golay ring slot goes back to the
     // producer through the epilogue warps, which see the MMAs complete.
     const int g = warp - kIssuerWarp;
-    if (lane == 0) {
-      const uint32_t a0 = smem_u32(S.a[0]), b0 = smem_u32(S.b[0]);
-      constexpr uint64_t kKStep = 256 >> 4;  // next 16 K: two 16-byte chunks, descriptor units
-      int bs = 0, ab = 0;
-      uint32_t bph = 0, aph = 0;
-      bool ok = true, issued = false;
-      for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
-        if (!wait_bar(&S.bar_a_full[ab], aph, abort_flag, args.err)) { ok = false; break; }
+    // The whole warp runs the loop (converged, uniform values); barrier waits
+    // are polled by every lane and the MMAs are issued by the elected lane.
+    const uint32_t a0 = smem_u32(S.a[0]), b0 = smem_u32(S.b[0]);
+    constexpr uint64_t kKStep = 256 >> 4;  // next 16 K: two 16-byte chunks, descriptor units
+    int bs = 0, ab = 0;
+    uint32_t bph = 0, aph = 0;
+    bool ok = true, issued = false;
+    for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
+      if (!wait_bar_warp(&S.bar_a_full[ab], aph, abort_flag, args.err)) { ok = false; break; }
+      tc_fence_after();
+      const uint64_t ad = smem_desc(a0 + static_cast<uint32_t>(ab * kAItemBytes + g * kATileBytes));
+      for (int t = 0; t < kGolayTiles; ++t) {
+        const int s = t & 1;
+        if (!wait_bar_warp(&S.bar_b_full[bs], bph, abort_flag, args.err) ||
+            !wait_bar_warp(&S.bar_acc_empty[g][s], ((t >> 1) & 1) ^ 1, abort_flag, args.err)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint64_t ad = smem_desc(a0 + static_cast<uint32_t>(ab * kAItemBytes + g * kATileBytes));
-        for (int t = 0; t < kGolayTiles; ++t) {
-          const int s = t & 1;
-          if (!wait_bar(&S.bar_b_full[bs], bph, abort_flag, args.err)) { ok = false; break; }
-          if (!wait_bar(&S.bar_acc_empty[g][s], ((t >> 1) & 1) ^ 1, abort_flag, args.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t bd = smem_desc(b0 + static_cast<uint32_t>(bs) * kBTileBytes);
-          const uint32_t d = tmem_base + static_cast<uint32_t>((g * kAccStages + s) * kGolayTileN);
-          mma_bf16_ss(d, ad, bd, 0);
-          mma_bf16_ss(d, ad + kKStep, bd + kKStep, 1);
-          mma_commit(&S.bar_acc_full[g][s]);
-          issued = true;
-          if (++bs == kStages) { bs = 0; bph ^= 1; }
-        }
-        if (!ok) break;
-        mma_commit(&S.bar_a_empty[ab]);
-        if (++ab == 2) { ab = 0; aph ^= 1; }
+        const uint64_t bd = smem_desc(b0 + static_cast<uint32_t>(bs) * kBTileBytes);
+        const uint32_t d = tmem_base + static_cast<uint32_t>((g * kAccStages + s) * kGolayTileN);
+        mma_bf16_ss(d, ad, bd, 0);
+        mma_bf16_ss(d, ad + kKStep, bd + kKStep, 1);
+        mma_commit(&S.bar_acc_full[g][s]);
+        issued = true;
+        if (++bs == kStages) { bs = 0; bph ^= 1; }
       }
-      if (issued) {
-        // All MMAs of this CTA complete before TMEM is released.
-        mma_commit(&S.bar_final[g]);
-        const unsigned long long t0 = global_ns();
-        while (!mbar_try_wait(&S.bar_final[g], 0) && global_ns() - t0 < kWaitLimitNs) {
-        }
+      if (!ok) break;
+      mma_commit(&S.bar_a_empty[ab]);
+      if (++ab == 2) { ab = 0; aph ^= 1; }
+    }
+    if (issued) {
+      // All MMAs of this CTA complete before TMEM is released.
+      mma_commit(&S.bar_final[g]);
+      const unsigned long long t0 = global_ns();
+      while (!mbar_try_wait(&S.bar_final[g], 0) && global_ns() - t0 < kWaitLimitNs) {
       }
+      __syncwarp();
     }
   } else {
     // ---------------- epilogue: one thread per (atom, row type) --------------
