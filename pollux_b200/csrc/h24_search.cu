@@ -39,12 +39,15 @@
 //                       within 2E of it (one 64-bit mask per row).
 //   3. rescore_kernel   one warp per atom: fp32 scores (from per-atom
 //                       partial-sum tables) of the codewords behind the
-//                       flagged chunks, then fp64 scores in the reference's
-//                       order for those within 2E of the best, lowest index on
-//                       ties, and the origin rule.
+//                       flagged chunks; a unique best within the fp32 error
+//                       bound is the winner, otherwise fp64 scores in the
+//                       reference's order for those within the bound, lowest
+//                       index on ties; then the origin rule.
 //   4. exhaustive_kernel  fp64 scan of all codewords for atoms with more than
 //                       kHeavyChunks flagged chunks (exact ties over many
 //                       codewords).
+//   5. decode_kernel    kissing-point index of each rescore winner, looked up
+//                       in bulk from its candidate code.
 //
 // Why the flags are sufficient: let S~_j be a screening score with
 // |S~_j - sqrt(8) R_j| <= E for every codeword j (R_j the exact score; E from
@@ -134,7 +137,9 @@ struct __align__(16) AtomInfo {
   float two_e;   // 2E, or -1 for an atom with a non-finite coordinate
   float t2lb;    // best type-2 score over the 21 octads through the three largest |x_i|
   uint8_t p[3];  // p1, p2, p3
-  uint8_t pad[9];
+  uint8_t pad0;
+  float thr;     // best - 2E, written by the screen
+  uint8_t pad[4];
 };
 static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 
@@ -517,8 +522,10 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   inf.p[0] = static_cast<uint8_t>(q0);
   inf.p[1] = static_cast<uint8_t>(q1);
   inf.p[2] = static_cast<uint8_t>(q2);
+  inf.pad0 = 0;
+  inf.thr = -INFINITY;
 #pragma unroll
-  for (int k = 0; k < 9; ++k) inf.pad[k] = 0;
+  for (int k = 0; k < 4; ++k) inf.pad[k] = 0;
   info[a] = inf;
 
   uint8_t *item = a_tiles + (a / kWorkAtoms) * kAItemBytes;
@@ -553,10 +560,9 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
 // ---------------------------------------------------------------------------
 struct ScreenArgs {
   const uint8_t *a_tiles;   // [items][kAItemBytes]
-  const AtomInfo *info;     // [n_pad]
+  AtomInfo *info;           // [n_pad]; the screen fills in thr
   const uint8_t *golay;     // [kGolayTiles][kBTileBytes]
   uint2 *masks;             // [n][4] flagged 64-column chunks per row type
-  float *thr;               // [n] best - 2E
   int64_t n;
   int64_t items;
   int *err;
@@ -773,7 +779,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       if (!(inf.two_e >= 0.f)) w0 = w1 = 0;
       if (atom < args.n) {
         args.masks[atom * kRowsPerAtom + r] = make_uint2(w0, w1);
-        if (r == 0) args.thr[atom] = thr;
+        if (r == 0) args.info[atom].thr = thr;
       }
       ip ^= 1;
     }
@@ -854,8 +860,7 @@ __device__ __forceinline__ int32_t apply_rule(double best, int bj, int rule) {
 
 struct RescoreArgs {
   const uint4 *masks;        // [2n]: rows 0-1, rows 2-3 (64-bit chunk masks)
-  const float *thr;          // [n]
-  const AtomInfo *info;      // [n]
+  const AtomInfo *info;      // [n], thr included
   const uint32_t *gmask;     // Golay masks
   const int32_t *idx3, *idx2, *idx1;
   const int8_t *cb_raw;
@@ -870,34 +875,40 @@ struct RescoreArgs {
 // trivial_index for a warp whose lane i < 24 holds x_i in xl (all lanes hold
 // the atom in v): the exact fp64 norm only when the fp32 one is within a
 // factor 4 of the pack rule's 1e-8 (its rounding error is far smaller).
+__device__ __forceinline__ float warp_max(float v) {
+  float m;
+  asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
+  return m;
+}
+
+__device__ __forceinline__ float warp_max_abs(float v) {
+  float m;
+  asm("redux.sync.max.abs.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
+  return m;
+}
+
 __device__ __forceinline__ int trivial_index_warp(const float (&v)[kDim], float xl, int lane, int rule) {
   const bool finite = __all_sync(0xffffffffu, lane >= kDim || isfinite(xl));
   if (!finite) return rule == H24_RULE_TRAIN ? 0 : 1;
-  if (rule == H24_RULE_PACK) {
-    float ss = xl * xl;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    if (ss < 4e-16f) return trivial_index(v, rule);
-  }
+  // ||x|| >= max |x_i|: only an atom whose |x_i| are all below 2e-8 can have
+  // ||x|| < 1e-8, and only such an atom needs the exact fp64 norm.
+  if (rule == H24_RULE_PACK && warp_max_abs(xl) < 2e-8f) return trivial_index(v, rule);
   return -1;
 }
 
 // What the rescore reads of one atom, staged in shared memory by cp.async one
-// atom ahead of its use.
+// atom ahead of its use: eleven 16-byte chunks, chunk k copied by lane k.
 struct AtomStage {
   float x[kDim];
   uint4 masks[2];
   AtomInfo info;
-  float thr;
-  float pad[3];
 };
-static_assert(sizeof(AtomStage) == 192, "AtomStage is twelve 16-byte chunks");
+static_assert(sizeof(AtomStage) == 176 && offsetof(AtomStage, masks) == 96 &&
+                  offsetof(AtomStage, info) == 128,
+              "AtomStage is eleven 16-byte chunks: coordinates, masks, constants");
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
@@ -911,6 +922,7 @@ constexpr int kCandCap = 128;  // fp32 candidates per atom before the fp64 pass
 // + signs); the kissing-point index is looked up only for the candidates
 // that reach the fp64 pass.
 constexpr uint32_t kCandType3 = 3u << 24, kCandType2 = 2u << 24, kCandType1 = 1u << 24;
+constexpr uint32_t kPendingIndex = 0x80000000u;  // output entry holding a candidate code
 __device__ __forceinline__ int32_t cand_index(const int32_t *__restrict__ idx3,
                                               const int32_t *__restrict__ idx2,
                                               const int32_t *__restrict__ idx1, uint32_t code) {
@@ -963,15 +975,14 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   float(*T)[256] = tab[w];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
   uint32_t st_exh = 0, st_exact = 0, st_chunks = 0;
-  // Lanes 0-11 copy one 16-byte chunk each of atom a's stage (thr: 4 bytes).
+  // Lanes 0-10 copy one 16-byte chunk each of atom a's stage.
   const auto prefetch = [&](int64_t a, int s) {
-    if (a < r.n && lane < 12) {
-      AtomStage &d = stage[w][s];
-      if (lane < 6) cp_async16(d.x + 4 * lane, atom_ptr(sg, a) + 4 * lane);
-      else if (lane < 8) cp_async16(&d.masks[lane - 6], r.masks + 2 * a + (lane - 6));
-      else if (lane < 11) cp_async16(reinterpret_cast<uint4 *>(&d.info) + (lane - 8),
-                                     reinterpret_cast<const uint4 *>(r.info + a) + (lane - 8));
-      else cp_async4(&d.thr, r.thr + a);
+    if (a < r.n) {
+      const uint4 *xa = reinterpret_cast<const uint4 *>(atom_ptr(sg, a));
+      const uint4 *src = lane < 6 ? xa + lane
+                                  : (lane < 8 ? r.masks + 2 * a + (lane - 6)
+                                              : reinterpret_cast<const uint4 *>(r.info + a) + (lane - 8));
+      if (lane < 11) cp_async16(reinterpret_cast<uint4 *>(&stage[w][s]) + lane, src);
     }
     cp_async_commit();
   };
@@ -998,7 +1009,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     st_chunks += nch;
     bool heavy = nch > kHeavyChunks;
     if (!heavy) {
-      const float thr = A.thr;
+      const float thr = A.info.thr;
       const AtomInfo inf = A.info;
       __syncwarp();  // the previous atom's table and list reads are done
       if (lane == 0) cand_n[w] = 0;
@@ -1027,14 +1038,11 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       }
       __syncwarp();
       // Sums over the coordinates, lane i holding x_i.
-      float sumx = xl, sumabs = fabsf(xl);
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        sumx += __shfl_xor_sync(0xffffffffu, sumx, off);
-        sumabs += __shfl_xor_sync(0xffffffffu, sumabs, off);
-      }
       const uint32_t negm = __ballot_sync(0xffffffffu, xl < 0.f);
       const auto tsum = [&](uint32_t m) { return T[0][m & 255] + T[1][(m >> 8) & 255] + T[2][m >> 16]; };
+      // Sum of x and of |x|, read from the tables.
+      const float sumx = tsum(0xFFFFFFu);
+      const float sumabs = sumx - 2.f * tsum(negm);
       const auto push = [&](float sc, uint32_t code) {
         const int k = atomicAdd(&cand_n[w], 1);
         if (k < kCandCap) {
@@ -1175,8 +1183,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       if (!heavy) {
         float smax = -INFINITY;
         for (int k = lane; k < nc; k += 32) smax = fmaxf(smax, cand_s[w][k]);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
+        smax = warp_max(smax);
         const float two_ep = 3.0517578125e-5f * sumabs;  // 2 e'
         const float cut = smax - two_ep;
         int nin = 0, jin = 0;
@@ -1198,10 +1205,11 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         const bool quick = __popc(who) == 1 && nsrc == 1 && cand_n[w] <= kCandCap &&
                            (r.rule != H24_RULE_TRAIN || fabsf(origin_gap) > two_ep);
         if (quick) {
+          // The winner's kissing-point index is looked up by decode_kernel.
           if (lane == 0)
             r.out[a] = (r.rule == H24_RULE_TRAIN && origin_gap < 0.f)
                            ? 0
-                           : cand_index(r.idx3, r.idx2, r.idx1, static_cast<uint32_t>(jsrc)) + 1;
+                           : static_cast<int32_t>(kPendingIndex | static_cast<uint32_t>(jsrc));
         } else {
           double bs = lb.s;
           int bj = lb.j, nex = lb.n;
@@ -1281,6 +1289,19 @@ __global__ void __launch_bounds__(256) exhaustive_kernel(const __grid_constant__
   }
 }
 
+// Replaces every pending output entry of the rescore (bit 31 set: the code of
+// the winning listed candidate) by its kissing-point index + 1.
+__global__ void __launch_bounds__(256) decode_kernel(int32_t *__restrict__ out, int64_t n,
+                                                     const int32_t *__restrict__ idx3,
+                                                     const int32_t *__restrict__ idx2,
+                                                     const int32_t *__restrict__ idx1) {
+  for (int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; a < n;
+       a += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t v = static_cast<uint32_t>(out[a]);
+    if (v & kPendingIndex) out[a] = cand_index(idx3, idx2, idx1, v & ~kPendingIndex) + 1;
+  }
+}
+
 std::mutex g_mu;
 int g_sms[64] = {};
 
@@ -1289,7 +1310,6 @@ struct Scratch {
   uint8_t *a_tiles;
   AtomInfo *info;
   uint2 *masks;
-  float *thr;
   int32_t *ovf_list;
   int32_t *ovf_count;
 };
@@ -1297,8 +1317,7 @@ constexpr size_t up256(size_t v) { return (v + 255) & ~static_cast<size_t>(255);
 constexpr size_t scratch_bytes(int64_t pad) {
   return up256(static_cast<size_t>(pad) / kWorkAtoms * kAItemBytes) +
          up256(static_cast<size_t>(pad) * sizeof(AtomInfo)) +
-         up256(static_cast<size_t>(pad) * kRowsPerAtom * 8) + up256(static_cast<size_t>(pad) * 4) +
-         up256(static_cast<size_t>(pad) * 4) + 256;
+         up256(static_cast<size_t>(pad) * kRowsPerAtom * 8) + up256(static_cast<size_t>(pad) * 4) + 256;
 }
 Scratch carve(uint8_t *base, int64_t pad) {
   Scratch sc;
@@ -1309,15 +1328,13 @@ Scratch carve(uint8_t *base, int64_t pad) {
   o += up256(static_cast<size_t>(pad) * sizeof(AtomInfo));
   sc.masks = reinterpret_cast<uint2 *>(base + o);
   o += up256(static_cast<size_t>(pad) * kRowsPerAtom * 8);
-  sc.thr = reinterpret_cast<float *>(base + o);
-  o += up256(static_cast<size_t>(pad) * 4);
   sc.ovf_list = reinterpret_cast<int32_t *>(base + o);
   o += up256(static_cast<size_t>(pad) * 4);
   sc.ovf_count = reinterpret_cast<int32_t *>(base + o);
   return sc;
 }
 
-// The four kernels of one batch (the overflow counter must be zero).
+// The five kernels of one batch (the overflow counter must be zero).
 int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int32_t *ob,
                  const Scratch &sc, int sms, cudaStream_t s) {
   const int64_t items = (nbatch + kWorkAtoms - 1) / kWorkAtoms;
@@ -1325,7 +1342,7 @@ int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int3
   prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(
       sg, nbatch, npad, t->golay_mask, t->oct_by_triple, sc.a_tiles, sc.info);
   ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
-                sc.thr, nbatch, items, t->err};
+                nbatch, items, t->err};
   const int grid = static_cast<int>(items < sms ? items : sms);
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   if (timing_enabled()) {
@@ -1338,7 +1355,7 @@ int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int3
     cudaEventRecord(ev1, s);
     timing_record(ev0, ev1);
   }
-  RescoreArgs ra{reinterpret_cast<const uint4 *>(sc.masks), sc.thr, sc.info, t->golay_mask, t->idx3,
+  RescoreArgs ra{reinterpret_cast<const uint4 *>(sc.masks), sc.info, t->golay_mask, t->idx3,
                  t->idx2, t->idx1, t->cb_raw, ob, sc.ovf_list, sc.ovf_count, t->stats, nbatch,
                  rule};
   const int64_t rblocks = (nbatch + kRescoreWarps - 1) / kRescoreWarps;
@@ -1346,7 +1363,10 @@ int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int3
   rescore_kernel<<<static_cast<unsigned>(rblocks < rcap ? rblocks : rcap), 32 * kRescoreWarps,
                    kGolay * sizeof(uint32_t), s>>>(sg, ra);
   exhaustive_kernel<<<2 * sms, 256, 0, s>>>(sg, rule, sc.ovf_list, sc.ovf_count, t->cb_raw, ob);
-  count_launches(4);
+  const int64_t dblocks = (nbatch + 255) / 256;
+  decode_kernel<<<static_cast<unsigned>(dblocks < 8 * sms ? dblocks : 8 * sms), 256, 0, s>>>(
+      ob, nbatch, t->idx3, t->idx2, t->idx1);
+  count_launches(5);
   H24_CUDA_TRY(cudaGetLastError());
   return H24_OK;
 }
@@ -1365,7 +1385,8 @@ int screen_setup(int dev, int *sms) {
         {reinterpret_cast<const void *>(screen_kernel), kScreenThreads, "screen_kernel"},
         {reinterpret_cast<const void *>(rescore_kernel), 32 * kRescoreWarps, "rescore_kernel"},
         {reinterpret_cast<const void *>(prep_kernel), 256, "prep_kernel"},
-        {reinterpret_cast<const void *>(exhaustive_kernel), 256, "exhaustive_kernel"}};
+        {reinterpret_cast<const void *>(exhaustive_kernel), 256, "exhaustive_kernel"},
+        {reinterpret_cast<const void *>(decode_kernel), 256, "decode_kernel"}};
     for (const auto &k : ks) {
       cudaFuncAttributes at;
       H24_CUDA_TRY(cudaFuncGetAttributes(&at, k.fn));
