@@ -189,6 +189,15 @@ int h24_quantize_segments(const float *const *xs, const int64_t *counts, int nse
 int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features,
                        uint16_t *sigma16_out, uint8_t *packed_out, void *stream);
 
+/* h24_quantize_layer with the weight and both outputs in host memory (the
+ * call shape of pack._quantize_h24_layer on a CPU weight, pack.py:139-180,
+ * which returns host tensors).  The rows are processed in chunks: the
+ * host-to-device copy of one chunk overlaps the search of the previous one
+ * (page-locked host memory gives the overlap; pageable memory works too).
+ * Returns once sigma16_out and packed_out are written. */
+int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features,
+                            uint16_t *sigma16_out, uint8_t *packed_out, void *stream);
+
 /* One layer of h24_quantize_layers. */
 typedef struct h24_layer {
   const float *w;

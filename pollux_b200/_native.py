@@ -47,6 +47,7 @@ SIGNATURES = {
     "h24_int8_dequant": (_I, [_P, _P, _I64, _I64, _P, _P]),
     "h24_quantize": (_I, [_P, _I64, _I, _P, _P]),
     "h24_quantize_layer": (_I, [_P, _I64, _I64, _P, _P, _P]),
+    "h24_quantize_layer_host": (_I, [_P, _I64, _I64, _P, _P, _P]),
     "h24_quantize_segments": (_I, [_P, _P, _I, _I, _P, _P]),
     "h24_quantize_noalloc": (_I, [_P, _I64, _I, _P, _P]),
     "h24_quantize_layers": (_I, [_P, _I, _P]),

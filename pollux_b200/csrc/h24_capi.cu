@@ -283,6 +283,7 @@ int build_device_tables(int dev, Tables *T) {
   H24_CUDA_TRY(cudaMemPoolCreate(&T->pool, &props));
   uint64_t keep = ~uint64_t(0);
   H24_CUDA_TRY(cudaMemPoolSetAttribute(T->pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  H24_CUDA_TRY(cudaStreamCreateWithFlags(&T->copy_stream, cudaStreamNonBlocking));
   std::memcpy(T->fingerprint, H.fingerprint, sizeof(T->fingerprint));
   T->device = dev;
   return H24_OK;
@@ -578,6 +579,92 @@ int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16
                        uint8_t *packed_out, void *stream) {
   h24_layer L{w, rows, in_features, sigma16_out, packed_out};
   return h24_quantize_layers(&L, 1, stream);
+}
+
+// Host-memory form of h24_quantize_layer.  The rows are cut into chunks of
+// whole 4-atom pack groups; chunk k+1 is copied host-to-device on the copy
+// stream while chunk k is searched on the caller's stream, and both outputs
+// come back when all chunks are done.  Returns after the outputs are written.
+int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features, uint16_t *sigma16_out,
+                            uint8_t *packed_out, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (rows < 0 || in_features <= 0 || (rows * in_features) % kDim != 0)
+    return fail(H24_ERR_INVALID, "quantize_layer_host: rows*in_features must be a multiple of 24");
+  if (rows == 0) return H24_OK;
+  if (!w || !sigma16_out || !packed_out) return fail(H24_ERR_INVALID, "quantize_layer_host: null pointer");
+  cudaStream_t s = as_stream(stream);
+  const int64_t atoms = rows * in_features / kDim;
+  const size_t packed_bytes = static_cast<size_t>((atoms + 3) / 4) * 9;
+  // Chunk rows: a multiple of rg rows holds a whole number of 4-atom groups.
+  int64_t g = in_features, h = 96;
+  while (h) { const int64_t t2 = g % h; g = h; h = t2; }
+  const int64_t rg = 96 / g;
+  constexpr int64_t kChunkAtoms = 49152;
+  int64_t crows = (kChunkAtoms * kDim / in_features) / rg * rg;
+  if (crows < rg) crows = rg;
+  auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
+  const size_t off_sig = up(static_cast<size_t>(rows * in_features) * sizeof(float));
+  const size_t off_pk = off_sig + up(static_cast<size_t>(rows) * 2);
+  const size_t off_idx = off_pk + up(packed_bytes);
+  uint8_t *buf = nullptr;
+  H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&buf),
+                                       off_idx + up(static_cast<size_t>(atoms) * 4), T->pool, s));
+  float *wd = reinterpret_cast<float *>(buf);
+  uint16_t *sig = reinterpret_cast<uint16_t *>(buf + off_sig);
+  uint8_t *pk = buf + off_pk;
+  int32_t *idx = reinterpret_cast<int32_t *>(buf + off_idx);
+  std::vector<cudaEvent_t> evs;
+  int rc = H24_OK;
+  auto event = [&](cudaEvent_t *e) -> int {
+    cudaError_t ce = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaEventCreate");
+    evs.push_back(*e);
+    return H24_OK;
+  };
+  // The copy stream starts after the buffer exists on the caller's stream.
+  cudaEvent_t ready;
+  rc = event(&ready);
+  if (rc == H24_OK) {
+    cudaError_t ce = cudaEventRecord(ready, s);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(T->copy_stream, ready, 0);
+    if (ce != cudaSuccess) rc = cuda_fail(ce, "copy stream order");
+  }
+  for (int64_t r0 = 0; r0 < rows && rc == H24_OK; r0 += crows) {
+    const int64_t nr = rows - r0 < crows ? rows - r0 : crows;
+    const int64_t e0 = r0 * in_features;
+    const int64_t a0 = e0 / kDim, na = nr * in_features / kDim;
+    cudaEvent_t copied;
+    rc = event(&copied);
+    if (rc != H24_OK) break;
+    cudaError_t ce = cudaMemcpyAsync(wd + e0, w + e0, static_cast<size_t>(nr * in_features) * sizeof(float),
+                                     cudaMemcpyHostToDevice, T->copy_stream);
+    if (ce == cudaSuccess) ce = cudaEventRecord(copied, T->copy_stream);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s, copied, 0);
+    if (ce != cudaSuccess) { rc = cuda_fail(ce, "chunk copy"); break; }
+    rc = launch_sigma16(wd + e0, nr, in_features, sig + r0, s);
+    const float *xs = wd + e0;
+    if (rc == H24_OK) rc = quantize_segments(T, &xs, &na, 1, H24_RULE_PACK, idx + a0, s);
+    if (rc == H24_OK) rc = launch_pack_i32(idx + a0, na, pk + a0 / 4 * 9, s);
+  }
+  if (rc == H24_OK) {
+    cudaError_t ce = cudaMemcpyAsync(sigma16_out, sig, static_cast<size_t>(rows) * 2, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(packed_out, pk, packed_bytes, cudaMemcpyDeviceToHost, s);
+    if (ce != cudaSuccess) rc = cuda_fail(ce, "output copy");
+  }
+  // Every copy-stream operation is ordered before the free (also after an
+  // error part way through the chunks).
+  cudaEvent_t drained = nullptr;
+  if (cudaEventCreateWithFlags(&drained, cudaEventDisableTiming) == cudaSuccess) {
+    evs.push_back(drained);
+    if (cudaEventRecord(drained, T->copy_stream) == cudaSuccess) cudaStreamWaitEvent(s, drained, 0);
+  }
+  const cudaError_t fe = cudaFreeAsync(buf, s);
+  const cudaError_t se = cudaStreamSynchronize(s);
+  for (cudaEvent_t e : evs) cudaEventDestroy(e);
+  if (rc != H24_OK) return rc;
+  if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync");
+  if (se != cudaSuccess) return cuda_fail(se, "cudaStreamSynchronize");
+  return H24_OK;
 }
 
 int h24_gather_codewords(const int32_t *idx, int64_t n, int dtype, void *out, void *stream) {

@@ -78,6 +78,9 @@ struct Tables {
   int *err = nullptr;
   // Stream-ordered pool for per-call scratch (kept warm between calls).
   cudaMemPool_t pool = nullptr;
+  // Non-blocking stream for the host-to-device copies of host-pointer entry
+  // points, so that the copy of one chunk overlaps the search of the previous.
+  cudaStream_t copy_stream = nullptr;
 };
 
 // Returns the tables of the current device, building them on first use.

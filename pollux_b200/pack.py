@@ -35,6 +35,16 @@ def _quantize_h24_layer(weight: torch.Tensor, codebook: torch.Tensor) -> tuple[t
     rows, in_f = w.shape
     atoms = w.numel() // H24_DIM
     dev = _work_device(w)
+    if w.device.type == "cpu" and w.dtype == torch.float32 and w.is_contiguous():
+        # Host fp32 weight: the chunked host entry overlaps the copy of one
+        # chunk with the search of the previous one and fills host outputs.
+        pin = w.is_pinned()
+        packed = torch.empty(((atoms + 3) // 4) * BYTES_PER_CHUNK, dtype=torch.uint8, pin_memory=pin)
+        sigma = torch.empty(rows, dtype=torch.float16, pin_memory=pin)
+        if rows:
+            _call(dev, "h24_quantize_layer_host", w.data_ptr(), rows, in_f, sigma.data_ptr(),
+                  packed.data_ptr(), _stream(dev))
+        return packed, sigma
     wd = _aligned(w.to(device=dev, dtype=torch.float32))
     packed = torch.empty(((atoms + 3) // 4) * BYTES_PER_CHUNK, dtype=torch.uint8, device=dev)
     sigma = torch.empty(rows, dtype=torch.float16, device=dev)

@@ -101,14 +101,19 @@ def test_unpack_capacity_below_count(C, oracle):
         assert np.array_equal(u.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("rows,in_f", [(4608, 1152), (5461, 72), (3, 96)])
-def test_pinned_host_layer_pipelined_equals_device_path(C, rows, in_f):
-    # Pinned fp32 host weights are copied in row chunks on a side stream while
-    # earlier chunks are searched; bytes and sigma must not change.
+@pytest.mark.parametrize("rows,in_f", [(4608, 1152), (5461, 72), (3, 96), (30012, 40), (7, 24)])
+@pytest.mark.parametrize("pinned", [True, False])
+def test_host_layer_pipelined_equals_device_path(C, rows, in_f, pinned):
+    # fp32 host weights go through h24_quantize_layer_host: row chunks of whole
+    # 4-atom pack groups (atoms straddle rows when in_f is not a multiple of
+    # 24) copied on a side stream while earlier chunks are searched; bytes and
+    # sigma must equal the device-resident path.
     from pollux_b200 import pack
     gen = torch.Generator().manual_seed(rows)
     w = torch.randn(rows, in_f, generator=gen) * 0.02
     cb = C.get_h24_codebook("cuda", torch.float32)
-    p_pin, s_pin = pack._quantize_h24_layer(w.pin_memory(), cb)
+    p_host, s_host = pack._quantize_h24_layer(w.pin_memory() if pinned else w, cb)
     p_dev, s_dev = pack._quantize_h24_layer(w.cuda(), cb)
-    assert torch.equal(p_pin, p_dev) and torch.equal(s_pin.view(torch.int16), s_dev.view(torch.int16))
+    assert p_host.device.type == "cpu" and s_host.device.type == "cpu"
+    assert p_host.is_pinned() == pinned
+    assert torch.equal(p_host, p_dev) and torch.equal(s_host.view(torch.int16), s_dev.view(torch.int16))
