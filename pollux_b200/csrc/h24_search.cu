@@ -881,6 +881,18 @@ __device__ __forceinline__ float warp_max(float v) {
   return m;
 }
 
+__device__ __forceinline__ float warp_min(float v) {
+  float m;
+  asm("redux.sync.min.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
+  return m;
+}
+
+__device__ __forceinline__ uint32_t warp_or(uint32_t v) {
+  uint32_t m;
+  asm("redux.sync.or.b32 %0, %1, 0xffffffff;" : "=r"(m) : "r"(v));
+  return m;
+}
+
 __device__ __forceinline__ float warp_max_abs(float v) {
   float m;
   asm("redux.sync.max.abs.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
@@ -1105,10 +1117,16 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
           }
         }
       }
-      // Type 2, behind flagged chunks of the |x| row: octads whose best
-      // even-parity pattern, 2 T(O) - 4 [odd] min_O |x|, reaches thr; then
-      // their 128 sign patterns across the warp.
+      // Type 2, behind flagged chunks of the |x| row.  For an octad O with
+      // 2 T(O) >= thr, the lanes holding its coordinates give, by warp
+      // reductions, the parity of its negative coordinates, its smallest and
+      // second smallest |x_i| (m1, m2) and the signs of its best even-parity
+      // pattern, of score 2 T(O) - 4 [odd] m1.  Every other pattern of O
+      // scores at least 4 (m2 - m1) (odd) or 4 (m1 + m2) (even) less; when
+      // that gap is clear of fp64 rounding those patterns can neither win nor
+      // tie, and only the best one is listed; else all 128 are scored.
       {
+        const float tie_gap = 9.094947e-13f * sumabs;  // 2^-40 sum|x|
         uint64_t m = mrow[3];
         while (m) {
           const int b = chunk_of_bit(__ffsll(m) - 1);
@@ -1125,26 +1143,32 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
               t2 = 2.f * (sumabs - (tsum(gm & ~negm) - tsum(gm & negm)));  // 2 T(O)
             }
             uint32_t bal = __ballot_sync(0xffffffffu, t2 >= thr);
-            if (bal) {
-              // Best even-parity pattern of every lane's octad at once:
-              // 2 T(O) - 4 [odd number of negative x_i in O] min_O |x|.
-              float mn = INFINITY;
-              uint32_t mm = om;
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const int pos = __ffs(mm) - 1;  // -1 (any lane) once om is exhausted
-                mm &= mm - 1;
-                mn = fminf(mn, fabsf(__shfl_sync(0xffffffffu, xl, pos & 31)));
-              }
-              const bool odd = __popc(om & negm) & 1;
-              bal = __ballot_sync(0xffffffffu, t2 - (odd ? 4.f * mn : 0.f) >= thr);
-            }
             while (bal) {
               const int src = __ffs(bal) - 1;
               bal &= bal - 1;
               const int oc = __shfl_sync(0xffffffffu, o, src);
               const uint32_t omc = __shfl_sync(0xffffffffu, om, src);
-              // The octad's 8 coordinates, lowest position first, to every lane.
+              const float t2c = __shfl_sync(0xffffffffu, t2, src);
+              // Lane i < 24 holds x_i; omc has 24 bits, so in_o is false on
+              // lanes 24-31.
+              const bool in_o = (omc >> lane & 1u) != 0;
+              const bool odd = __popc(__ballot_sync(0xffffffffu, in_o && xl < 0.f)) & 1;
+              const float ax = in_o ? fabsf(xl) : INFINITY;
+              const float m1 = warp_min(ax);
+              const float t2x = odd ? t2c - 4.f * m1 : t2c;
+              if (t2x < thr) continue;
+              const int kmin = __ffs(__ballot_sync(0xffffffffu, ax == m1)) - 1;  // lowest on ties
+              const float m2 = warp_min(lane == kmin ? INFINITY : ax);
+              if ((odd ? 4.f * (m2 - m1) : 4.f * (m1 + m2)) > tie_gap) {
+                // Pattern bit k (k < 7): the coordinate of rank k in O (rank
+                // 0 = lowest position) is negative; rank 7 follows from parity.
+                const uint32_t rank = __popc(omc & ((1u << lane) - 1u));
+                uint32_t pid = warp_or(in_o && xl < 0.f ? 1u << rank : 0u);
+                if (odd) pid ^= 1u << __popc(omc & ((1u << kmin) - 1u));
+                if (lane == 0) push(t2x, kCandType2 | static_cast<uint32_t>(oc * 128 + (pid & 0x7Fu)));
+                continue;
+              }
+              // Exact ties within O: every sign pattern, across the warp.
               float o8[8];
               uint32_t mo = omc;
 #pragma unroll

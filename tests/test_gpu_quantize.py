@@ -87,6 +87,30 @@ def test_edge_atoms(C, oracle):
         assert np.array_equal(ours, oracle.nearest_exact(atoms, rule)), rule
 
 
+def test_octad_pattern_ties(C, oracle):
+    # Atoms dominated by one octad with an odd number of negative coordinates
+    # whose two smallest |x_i| are equal (two best sign patterns tie exactly:
+    # the rescore scores every pattern) or one ulp apart (one best pattern,
+    # listed alone).
+    rng = np.random.default_rng(7)
+    raw = oracle.raw_kissing_points()
+    type2 = np.where((raw != 0).sum(1) == 8)[0]
+    atoms = []
+    for j in rng.choice(type2, 96, replace=False):
+        supp = np.where(raw[j] != 0)[0]
+        x = rng.normal(0, 0.05, 24).astype(np.float32)
+        x[supp] = np.sign(raw[j][supp]) * rng.uniform(1.0, 2.0, 8).astype(np.float32)
+        a, b = rng.choice(supp, 2, replace=False)
+        x[a] = -np.float32(0.5) * np.sign(x[a])
+        x[b] = np.float32(0.5) * np.sign(x[b])
+        y = x.copy()
+        y[b] = np.nextafter(np.float32(0.5), np.float32(1.0)) * np.sign(y[b])
+        atoms += [x, y]
+    atoms = np.stack(atoms)
+    for rule in (0, 1):
+        assert np.array_equal(q(C, atoms, rule), oracle.nearest_exact(atoms, rule)), rule
+
+
 def test_non_finite_atoms(C):
     atoms = np.zeros((4, 24), np.float32)
     atoms[0, 3] = np.nan
