@@ -1083,7 +1083,9 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
           }
         }
       }
-      // Type 3 at the other positions, behind flagged chunks of the plain row.
+      // Type 3 at the other positions, behind flagged chunks of the plain row:
+      // each column whose bound reaches thr is broadcast, and lane i < 24
+      // scores position i.
       {
         uint64_t m = mrow[2];
         while (m) {
@@ -1094,25 +1096,15 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
             const int c = b * kChunkCols + 32 * k + lane;
             const uint32_t gm = gmask_s[c];
             const float bc = sumx - 2.f * tsum(gm);
-            if (bc + ((gm >> p3 & 1u) ? inf.u1 : inf.u0) >= thr) {
-              uint32_t hit = 0;
-#pragma unroll
-              for (int q = 0; q < 6; ++q) {
-                const float4 f = reinterpret_cast<const float4 *>(A.x)[q];
-                const float f4[4] = {f.x, f.y, f.z, f.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int p = 4 * q + e;
-                  hit |= (bc - f4[e] * ((gm >> p & 1u) ? 2.f : 4.f) >= thr ? 1u : 0u) << p;
-                }
-              }
-              hit &= ~((1u << p1) | (1u << p2));
-              while (hit) {
-                const int p = __ffs(hit) - 1;
-                hit &= hit - 1;
-                push(bc - A.x[p] * ((gm >> p & 1u) ? 2.f : 4.f),
-                     kCandType3 | static_cast<uint32_t>(c * kDim + p));
-              }
+            uint32_t bal = __ballot_sync(0xffffffffu, bc + ((gm >> p3 & 1u) ? inf.u1 : inf.u0) >= thr);
+            while (bal) {
+              const int src = __ffs(bal) - 1;
+              bal &= bal - 1;
+              const uint32_t gmc = __shfl_sync(0xffffffffu, gm, src);
+              const float bcc = __shfl_sync(0xffffffffu, bc, src);
+              const float sc = bcc - xl * ((gmc >> lane & 1u) ? 2.f : 4.f);
+              if (lane < kDim && lane != p1 && lane != p2 && sc >= thr)
+                push(sc, kCandType3 | static_cast<uint32_t>((b * kChunkCols + 32 * k + src) * kDim + lane));
             }
           }
         }
