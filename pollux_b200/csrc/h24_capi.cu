@@ -54,7 +54,7 @@ struct HostTables {
   std::vector<uint16_t> golay;     // [kGolay][32] bf16 bits, tiled (Tables::golay_tiled)
   std::vector<uint32_t> golay_mask;  // [kGolay]
   std::vector<int32_t> idx3, idx2, idx1;
-  std::vector<uint16_t> oct_by_triple;  // [kTriples][kTripleRow]
+  std::vector<uint32_t> oct_by_triple;  // [kTriples][kTripleRow][2]
   std::vector<uint32_t> nib;       // [kCount][4] dequant codes
   float fingerprint[16];
   bool ok = false;
@@ -162,7 +162,7 @@ bool build_structure(HostTables &H) {
   for (const int32_t v : H.idx1) t1 += v >= 0;
   if (t1 != 276 * 4) { H.err = "missing type-1 point"; return false; }
   // The 21 octads through each position triple (Steiner system S(5,8,24)).
-  H.oct_by_triple.assign(static_cast<size_t>(kTriples) * kTripleRow, 0);
+  H.oct_by_triple.assign(static_cast<size_t>(kTriples) * kTripleRow * 2, 0);
   {
     std::vector<int> fill(kTriples, 0);
     const auto c3 = [](int k) { return k * (k - 1) * (k - 2) / 6; };
@@ -175,7 +175,13 @@ bool build_structure(HostTables &H) {
             if ((om >> i & 1) && (om >> j & 1) && (om >> k & 1)) {
               const int t = c3(k) + c2(j) + i;
               if (fill[t] >= 21) { H.err = "more than 21 octads through a triple"; return false; }
-              H.oct_by_triple[static_cast<size_t>(t) * kTripleRow + fill[t]++] = static_cast<uint16_t>(o);
+              uint32_t rest = 0;
+              int nr = 0;
+              for (int q = 0; q < kDim; ++q)
+                if ((om >> q & 1) && q != i && q != j && q != k) rest |= static_cast<uint32_t>(q) << (5 * nr++);
+              const size_t e = (static_cast<size_t>(t) * kTripleRow + fill[t]++) * 2;
+              H.oct_by_triple[e] = om;
+              H.oct_by_triple[e + 1] = rest;
             }
     }
     for (int t = 0; t < kTriples; ++t)
@@ -262,8 +268,8 @@ int build_device_tables(int dev, Tables *T) {
   T->idx2 = static_cast<const int32_t *>(p);
   if ((rc = upload(H.idx1.data(), H.idx1.size() * 4)) != H24_OK) return rc;
   T->idx1 = static_cast<const int32_t *>(p);
-  if ((rc = upload(H.oct_by_triple.data(), H.oct_by_triple.size() * 2)) != H24_OK) return rc;
-  T->oct_by_triple = static_cast<const uint16_t *>(p);
+  if ((rc = upload(H.oct_by_triple.data(), H.oct_by_triple.size() * 4)) != H24_OK) return rc;
+  T->oct_by_triple = static_cast<const uint2 *>(p);
   H24_CUDA_TRY(cudaMalloc(&p, H.raw.size()));
   H24_CUDA_TRY(cudaMemcpy(p, H.raw.data(), H.raw.size(), cudaMemcpyHostToDevice));
   T->cb_raw = static_cast<const int8_t *>(p);

@@ -32,7 +32,7 @@ constexpr int kW16First = 3336;               // first weight-16 Golay column
 constexpr int kGolayTileN = 128;              // Golay columns per MMA tile
 constexpr int kGolayTiles = kGolay / kGolayTileN;  // 32
 constexpr int kTriples = 2024;                // C(24, 3)
-constexpr int kTripleRow = 24;                // 21 octads per triple, padded to 48 bytes
+constexpr int kTripleRow = 22;                // 21 octads per triple (+1 pad: 176-byte rows)
 constexpr int kKPad = 32;                     // K padded 24 -> 32 (bf16)
 constexpr int kRowBytes = kKPad * 2;          // 64 bytes per operand row
 
@@ -61,9 +61,11 @@ struct Tables {
   const int32_t *idx3 = nullptr;
   const int32_t *idx2 = nullptr;
   const int32_t *idx1 = nullptr;
-  // The 21 octads (ids o as in idx2) through each position triple i < j < k,
-  // row C(k,3) + C(j,2) + i of kTripleRow entries (the last 3 unused).
-  const uint16_t *oct_by_triple = nullptr;
+  // The 21 octads through each position triple i < j < k, row C(k,3) +
+  // C(j,2) + i of kTripleRow entries (the last unused): .x = the octad's
+  // position mask, .y = its five positions outside the triple, 5 bits each
+  // (lowest first).
+  const uint2 *oct_by_triple = nullptr;
   // raw int8 coordinates [kKissing][24] (kissing point j = codebook row j+1).
   const int8_t *cb_raw = nullptr;
   // Dequant codes [kCount][4] u32 words (16 bytes per codeword, row 0 is the

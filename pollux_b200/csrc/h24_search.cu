@@ -407,10 +407,13 @@ __device__ __forceinline__ uint32_t a_offset(int L, int q) {
 // 32 * quarter_of_row(g, r) + a % 32 for row type r (0 slice p1, 1 slice p2,
 // 2 plain, 3 |x|).
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
-                                                   int64_t n_pad, const uint32_t *__restrict__ gmask,
-                                                   const uint16_t *__restrict__ oct_by_triple,
+                                                   int64_t n_pad,
+                                                   const uint2 *__restrict__ oct_by_triple,
                                                    uint8_t *__restrict__ a_tiles,
                                                    AtomInfo *__restrict__ info) {
+  // |x_i| of each thread's atom, [position][thread]: a warp's accesses hit 32
+  // distinct banks whatever the positions.
+  __shared__ float absx[kDim][256];
   const int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (a >= n_pad) return;
   float v[kDim];
@@ -498,24 +501,24 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   // min_O |x|, over the 21 octads that contain the three largest |x_i|.
   float t2lb = -INFINITY;
   {
+#pragma unroll
+    for (int i = 0; i < kDim; ++i) absx[i][threadIdx.x] = fabsf(v[i]);
     // Sort the triple: i < j < k.
     const int i3 = min(a0, min(a1, a2)), k3 = max(a0, max(a1, a2)), j3 = a0 + a1 + a2 - i3 - k3;
-    const uint4 *row = reinterpret_cast<const uint4 *>(
-        oct_by_triple + (k3 * (k3 - 1) * (k3 - 2) / 6 + j3 * (j3 - 1) / 2 + i3) * kTripleRow);
-    const uint4 r0 = __ldg(row), r1 = __ldg(row + 1), r2 = __ldg(row + 2);
-    const uint32_t ow[12] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w, r2.x, r2.y, r2.z, r2.w};
-#pragma unroll
+    const uint2 *row = oct_by_triple + (k3 * (k3 - 1) * (k3 - 2) / 6 + j3 * (j3 - 1) / 2 + i3) * kTripleRow;
+    // The triple's |x| are the three largest: top[0..2].
+    const float tri = top[0] + top[1] + top[2];
+#pragma unroll 3
     for (int k = 0; k < 21; ++k) {
-      const int o = static_cast<int>((ow[k >> 1] >> (16 * (k & 1))) & 0xFFFFu);
-      const uint32_t om = ~__ldg(gmask + kW16First + o) & 0xFFFFFFu;
-      float t = 0.f, mn = INFINITY;
+      const uint2 e = __ldg(row + k);
+      float t = tri, mn = top[2];
 #pragma unroll
-    for (int i = 0; i < kDim; ++i)
-      if (om >> i & 1u) {
-        t += fabsf(v[i]);
-        mn = fminf(mn, fabsf(v[i]));
+      for (int q = 0; q < 5; ++q) {
+        const float ax = absx[(e.y >> (5 * q)) & 31u][threadIdx.x];
+        t += ax;
+        mn = fminf(mn, ax);
       }
-      t2lb = fmaxf(t2lb, 2.f * t - ((__popc(om & negm) & 1) ? 4.f * mn : 0.f));
+      t2lb = fmaxf(t2lb, 2.f * t - ((__popc(e.x & negm) & 1) ? 4.f * mn : 0.f));
     }
   }
   inf.t2lb = t2lb;
@@ -1356,7 +1359,7 @@ int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int3
   const int64_t items = (nbatch + kWorkAtoms - 1) / kWorkAtoms;
   const int64_t npad = items * kWorkAtoms;
   prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(
-      sg, nbatch, npad, t->golay_mask, t->oct_by_triple, sc.a_tiles, sc.info);
+      sg, nbatch, npad, t->oct_by_triple, sc.a_tiles, sc.info);
   ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
                 nbatch, items, t->err};
   const int grid = static_cast<int>(items < sms ? items : sms);
