@@ -159,7 +159,7 @@ int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *st
  * Same result as h24_quantize for callers that must not allocate device
  * memory at call time (code under an external memory manager that owns every
  * device allocation, or latency-critical loops).  All per-call scratch lives
- * in one fixed device array of about 10.5 MB inside the library, so the call
+ * in one fixed device array of about 10.6 MiB inside the library, so the call
  * makes no cudaMalloc, cudaMallocAsync or cudaFree.  Limits: at most 32768
  * atoms per call (more is H24_ERR_INVALID); the codebook tables must already
  * be resident (call h24_init(device) once at set-up, else H24_ERR_STATE); the

@@ -1504,7 +1504,7 @@ int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_
 namespace {
 
 constexpr int64_t kNoAllocMaxAtoms = 32768;
-constexpr size_t kNoAllocBytes = scratch_bytes(kNoAllocMaxAtoms);  // about 11 MB
+constexpr size_t kNoAllocBytes = scratch_bytes(kNoAllocMaxAtoms);  // 11,141,376 B, about 10.6 MiB
 static_assert(kNoAllocMaxAtoms % kWorkAtoms == 0, "whole CTA work items");
 static_assert(kNoAllocBytes < (size_t(16) << 20), "modest fixed footprint");
 
