@@ -157,7 +157,7 @@ struct __align__(1024) ScreenSmem {
   uint64_t bar_b_empty[kStages];    // one arrival per epilogue warp
   uint64_t bar_acc_full[kMTiles][kAccStages];
   uint64_t bar_acc_empty[kMTiles][kAccStages];
-  uint64_t bar_rows[2];
+  uint64_t bar_rows[kMTiles][2];    // the four warps of an M-tile, by work-item parity
   uint64_t bar_final[kMTiles];      // each issuer's last MMAs
   uint32_t tmem_base;
   int abort_flag;
@@ -583,7 +583,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.bar_a_full[i], 1);
       mbar_init(&S.bar_a_empty[i], kMTiles);
-      mbar_init(&S.bar_rows[i], kEpiWarps);
+      for (int g = 0; g < kMTiles; ++g) mbar_init(&S.bar_rows[g][i], 4);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.bar_b_full[s], 1);
@@ -712,7 +712,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
                            static_cast<uint32_t>(g * kAccStages * kGolayTileN);
     bool ok = true;
     int ip = 0;
-    uint32_t rph = 0;  // bit i: parity of the next phase of bar_rows[i]
+    uint32_t rph = 0;  // bit i: parity of the next phase of bar_rows[g][i]
     for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
       const int64_t atom = it * kWorkAtoms + local;
       const AtomInfo inf = args.info[atom];
@@ -754,8 +754,8 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       // Row maxima of the atom's four rows, exchanged through shared memory.
       S.rowval[ip][local][r] = rowmax;
       __syncwarp();
-      mbar_arrive_lane0(&S.bar_rows[ip], lane);
-      if (!wait_bar_warp(&S.bar_rows[ip], (rph >> ip) & 1u, abort_flag, args.err)) {
+      mbar_arrive_lane0(&S.bar_rows[g][ip], lane);
+      if (!wait_bar_warp(&S.bar_rows[g][ip], (rph >> ip) & 1u, abort_flag, args.err)) {
         ok = false;
         break;
       }
