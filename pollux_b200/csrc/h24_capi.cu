@@ -107,10 +107,32 @@ bool build_structure(HostTables &H) {
     const int wa = __builtin_popcount(a), wb = __builtin_popcount(b);
     return wa != wb ? wa < wb : a < b;
   });
+  // Complement-paired column order (see h24_internal.cuh): the first half
+  // from the zero word, the octads (as complements of the sorted weight-16
+  // words) and the smaller dodecad of each pair; column c + 2048 = ~column c.
+  {
+    std::vector<uint32_t> w16, dodec;
+    for (const uint32_t w : golay) {
+      const int wt = __builtin_popcount(w);
+      if (wt == 16) w16.push_back(w);
+      if (wt == 12 && w < (~w & 0xFFFFFFu)) dodec.push_back(w);
+    }
+    if (w16.size() != static_cast<size_t>(kOctads) || dodec.size() != static_cast<size_t>(kGolayHalf - 1 - kOctads)) {
+      H.err = "unexpected Golay weight distribution";
+      return false;
+    }
+    std::vector<uint32_t> order;
+    order.push_back(0);
+    for (const uint32_t w : w16) order.push_back(~w & 0xFFFFFFu);
+    for (const uint32_t w : dodec) order.push_back(w);
+    for (int c = 0; c < kGolayHalf; ++c) order.push_back(~order[c] & 0xFFFFFFu);
+    golay.swap(order);
+  }
   std::unordered_map<uint32_t, int> col;
   for (int c = 0; c < kGolay; ++c) col[golay[c]] = c;
-  if (__builtin_popcount(golay[kW16First]) != 16 || __builtin_popcount(golay[kW16First - 1]) != 12 ||
-      __builtin_popcount(golay[kGolay - 1]) != 24 || __builtin_popcount(golay[kW16First + kOctads - 1]) != 16) {
+  if (col.size() != static_cast<size_t>(kGolay) || __builtin_popcount(golay[kW16First]) != 16 ||
+      __builtin_popcount(golay[kGolayHalf]) != 24 || __builtin_popcount(golay[kW16First + kOctads - 1]) != 16 ||
+      __builtin_popcount(golay[kW16First + kOctads]) != 12 || __builtin_popcount(golay[kOctads]) != 8) {
     H.err = "unexpected Golay weight distribution";
     return false;
   }

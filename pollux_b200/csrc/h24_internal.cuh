@@ -23,12 +23,18 @@ constexpr int kCount = 196561;
 //           number of minus signs;
 //   type 3  (-3, +-1^23): one of the 4096 Golay codewords c and a position p;
 //           coordinate i != p is (-1)^c_i and coordinate p is -3.
-// The Golay codewords are kept in order of (weight, bit pattern): column 0 is
-// the zero word, 1-759 the octads, 760-3335 the dodecads, 3336-4094 the
-// weight-16 words (complements of the octads), 4095 the all-ones word.
+// The Golay code is closed under complement, and column c + 2048 holds the
+// complement of column c: columns 0-2047 are the zero word (0), the 759
+// octads (1-759, in the order of their complements when sorted by bit
+// pattern) and one dodecad of each complementary pair (760-2047, the smaller
+// bit pattern, ascending); columns 2048-4095 are the all-ones word, the
+// weight-16 words (2049-2807, complement of octad o at 2049 + o) and the
+// other dodecads.  Every screening row r gives r(~c) = -r(c), so the screen
+// multiplies only the first 2048 columns.
 constexpr int kGolay = 4096;
+constexpr int kGolayHalf = kGolay / 2;        // columns c and c + 2048 are complements
 constexpr int kOctads = 759;
-constexpr int kW16First = 3336;               // first weight-16 Golay column
+constexpr int kW16First = kGolayHalf + 1;     // 2049: first weight-16 Golay column
 constexpr int kGolayTileN = 128;              // Golay columns per MMA tile
 constexpr int kGolayTiles = kGolay / kGolayTileN;  // 32
 constexpr int kTriples = 2024;                // C(24, 3)

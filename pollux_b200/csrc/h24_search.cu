@@ -81,9 +81,9 @@ constexpr int kAItemBytes = kMTiles * kATileBytes; // 16384
 constexpr int kBTileBytes = kGolayTileN * kRowBytes;  // 8192
 constexpr int kStages = 8;                         // Golay tile ring depth
 constexpr int kChunkCols = 64;                     // candidate chunk: half a Golay tile
-constexpr int kW16Tile = kW16First / kGolayTileN;  // 26: first tile with weight-16 columns
-constexpr int kW16Chunk = kW16First / kChunkCols;  // 52: first chunk with weight-16 columns
-constexpr int kW16Skip = kW16First - kW16Tile * kGolayTileN;  // 8 dodecads lead tile 26
+constexpr int kScreenTiles = kGolayHalf / kGolayTileN;  // 16 Golay tiles multiplied per work item
+constexpr int kOctTiles = (kOctads + 1 + kGolayTileN - 1) / kGolayTileN;  // 6: tiles holding octad columns
+constexpr int kOctTailCol = kOctads + 1 - (kOctTiles - 1) * kGolayTileN;  // 120: dodecads from here in tile 5
 constexpr int kAccStages = 2;                      // TMEM accumulator stages per M-tile
 constexpr int kEpiWarps = kMTiles * 4;            // 8: (M-tile, lane quarter)
 constexpr int kProducerWarp = kEpiWarps;           // warp 8: TMA producer
@@ -94,9 +94,9 @@ constexpr int kHeavyChunks = 192;                  // flagged chunks (of 204) be
 constexpr int kMaxSegs = 64;                       // input segments per pipeline batch
 constexpr int64_t kBatchAtoms = int64_t(1) << 20;  // atoms per pipeline batch
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s
-static_assert(kW16Chunk == 52 && kW16Skip == 8, "weight-16 block starts 8 columns into chunk 52");
-static_assert(kW16First + kOctads == kGolay - 1, "the all-ones word closes the weight-16 block");
-static_assert(kGolayTiles % (2 * kAccStages) == 0, "each stage is used an even number of times per item");
+static_assert(kOctTiles == 6 && kOctTailCol == 120, "octad columns 1-759 fill tiles 0-5 up to column 120 of tile 5");
+static_assert(kScreenTiles % (2 * kAccStages) == 0, "each stage is used an even number of times per item");
+static_assert(kScreenTiles % kStages == 0, "a work item's Golay tiles fill the ring a whole number of times");
 
 // Row type held by TMEM lane quarter q of M-tile g, and its inverse.  The two
 // |x| rows (their loads are skipped for 26 of the 32 Golay tiles) sit in lane
@@ -361,6 +361,25 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// min(m, the 32 fp32 values held as raw bits): a tree of 3-input min.
+__device__ __forceinline__ float min32(float m, const uint32_t *r) {
+  float t[11];
+#pragma unroll
+  for (int k = 0; k < 10; ++k)
+    t[k] = fmin3(__uint_as_float(r[3 * k]), __uint_as_float(r[3 * k + 1]),
+                 __uint_as_float(r[3 * k + 2]));
+  t[10] = fmin3(__uint_as_float(r[30]), __uint_as_float(r[31]), m);
+  const float u0 = fmin3(t[0], t[1], t[2]), u1 = fmin3(t[3], t[4], t[5]);
+  const float u2 = fmin3(t[6], t[7], t[8]);
+  return fmin3(fmin3(u0, u1, u2), t[9], t[10]);
 }
 
 // max(m, the 32 fp32 values held as raw bits): a tree of 3-input max.
@@ -628,7 +647,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         bulk_g2s(S.a[ab], args.a_tiles + it * kAItemBytes, kAItemBytes, &S.bar_a_full[ab], once);
         last_a[ab] = static_cast<int>(aph);
         if (++ab == 2) { ab = 0; aph ^= 1; }
-        for (int t = 0; t < kGolayTiles; ++t) {
+        for (int t = 0; t < kScreenTiles; ++t) {
           if (!wait_bar(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err)) { ok = false; break; }
           mbar_arrive_expect_tx(&S.bar_b_full[bs], kBTileBytes);
           bulk_g2s(S.b[bs], args.golay + t * kBTileBytes, kBTileBytes, &S.bar_b_full[bs], keep);
@@ -670,7 +689,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       if (!wait_bar_warp(&S.bar_a_full[ab], aph, abort_flag, args.err)) { ok = false; break; }
       tc_fence_after();
       const uint64_t ad = smem_desc(a0 + static_cast<uint32_t>(ab * kAItemBytes + g * kATileBytes));
-      for (int t = 0; t < kGolayTiles; ++t) {
+      for (int t = 0; t < kScreenTiles; ++t) {
         const int s = t & 1;
         if (!wait_bar_warp(&S.bar_b_full[bs], bph, abort_flag, args.err) ||
             !wait_bar_warp(&S.bar_acc_empty[g][s], ((t >> 1) & 1) ^ 1, abort_flag, args.err)) {
@@ -717,8 +736,10 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       const int64_t atom = it * kWorkAtoms + local;
       const AtomInfo inf = args.info[atom];
       float rowmax = -INFINITY;
+      // Tile t holds columns 128 t .. 128 t + 127; the complements of its two
+      // chunks form logical tile t + 16, whose maxima are minus the minima.
 #pragma unroll 1
-      for (int t = 0; t < kGolayTiles; ++t) {
+      for (int t = 0; t < kScreenTiles; ++t) {
         const int s = t & 1;
         if (!wait_bar_warp(&S.bar_acc_full[g][s], (t >> 1) & 1, abort_flag, args.err)) {
           ok = false;
@@ -727,28 +748,36 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         tc_fence_after();
         // The MMAs of tile t are complete: its Golay ring slot may be refilled.
         mbar_arrive_lane0(&S.bar_b_empty[t % kStages], lane);
-        float m0 = -INFINITY, m1 = -INFINITY;
-        if (r != 3 || t >= kW16Tile) {
+        float m0 = -INFINITY, m1 = -INFINITY, n0 = INFINITY, n1 = INFINITY;
+        if (r != 3 || t < kOctTiles) {
           uint32_t x[128];
           tmem_ld128_wait(t_row + static_cast<uint32_t>(s * kGolayTileN), x);
           // Loaded: hand the stage back to the MMA issuer.
           tc_fence_before();
           __syncwarp();
           mbar_arrive_lane0(&S.bar_acc_empty[g][s], lane);
-          if (r == 3 && t == kW16Tile) {
+          if (r == 3) {
+            // The |x| row counts only at the weight-16 words, the complements
+            // of the octad columns 1-759: minima over those alone.
+            if (t == 0) x[0] = 0x7F800000u;  // zero word (its complement: all ones)
+            if (t == kOctTiles - 1) {
 #pragma unroll
-            for (int j = 0; j < kW16Skip; ++j) x[j] = 0xFF800000u;  // dodecad columns
+              for (int j = kOctTailCol; j < kGolayTileN; ++j) x[j] = 0x7F800000u;  // dodecads
+            }
+          } else {
+            m0 = max32(max32(-INFINITY, x), x + 32);
+            m1 = max32(max32(-INFINITY, x + 64), x + 96);
           }
-          if (r == 3 && t == kGolayTiles - 1) x[127] = 0xFF800000u;  // all-ones word
-          m0 = max32(max32(-INFINITY, x), x + 32);
-          m1 = max32(max32(-INFINITY, x + 64), x + 96);
+          n0 = min32(min32(INFINITY, x), x + 32);
+          n1 = min32(min32(INFINITY, x + 64), x + 96);
         } else {
           tc_fence_before();
           __syncwarp();
           mbar_arrive_lane0(&S.bar_acc_empty[g][s], lane);
         }
         S.cmax[t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
-        rowmax = fmaxf(rowmax, fmaxf(m0, m1));
+        S.cmax[t + kScreenTiles][slot] = __halves2half2(__float2half_ru(-n0), __float2half_ru(-n1));
+        rowmax = fmaxf(fmaxf(rowmax, fmaxf(m0, m1)), fmaxf(-n0, -n1));
       }
       if (!ok) break;
       // Row maxima of the atom's four rows, exchanged through shared memory.
