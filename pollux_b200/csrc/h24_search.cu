@@ -15,8 +15,9 @@
 //   type 2 (octad O, signs s):  S = 2 sum_{i in O} s_i x_i
 //                     <= 2 T(O),  T(O) = sum_{i in O} |x_i|;
 //   type 1 (a, b, signs):  S = 4 (s_a x_a + s_b x_b) <= 4 (|x_a| + |x_b|).
-// Per atom four rows go through one GEMM against the 4096 Golay sign columns
-// ((-1)^c_k, bf16): "slice" rows x with x_p1 or x_p2 zeroed (p1, p2, p3 =
+// Per atom four rows go through one GEMM against the Golay sign columns
+// ((-1)^c_k, bf16), of which only one column of each complementary pair is
+// multiplied (every row r gives r(~c) = -r(c)): "slice" rows x with x_p1 or x_p2 zeroed (p1, p2, p3 =
 // the positions of the three smallest coordinates), which give the exact
 // type-3 scores of the codewords (c, p1) and (c, p2) up to the constant
 // -3 x_p; the plain row, which gives B(c); and the row |x|, whose value at the
@@ -28,12 +29,13 @@
 //                       operand, and the per-atom constants (AtomInfo).
 //   2. screen_kernel    persistent tcgen05 kernel, one CTA per SM, 64 atoms
 //                       (two M=128 tiles of 32 atoms x 4 rows) per work item;
-//                       the Golay operand streams through a shared-memory ring
-//                       in tiles of 128 columns; M128 N128 K32 MMAs into two
-//                       TMEM accumulator stages per M-tile, so that the MMAs
-//                       of one Golay tile run while the epilogue reads the
-//                       previous one.  16 epilogue warps keep, per row, the
-//                       maximum of each 64-column chunk; at the end of a work
+//                       the 2048 representative Golay columns stream through a
+//                       shared-memory ring in 16 tiles of 128; M128 N128 K32
+//                       MMAs into two TMEM accumulator stages per M-tile, so
+//                       that the MMAs of one Golay tile run while the epilogue
+//                       reads the previous one.  8 epilogue warps keep, per
+//                       row, the maximum of each 64-column chunk and, as minus
+//                       the minimum, that of its complement chunk; at the end of a work
 //                       item they form the atom's best achievable screening
 //                       score and flag every chunk that may hold a codeword
 //                       within 2E of it (one 64-bit mask per row).
