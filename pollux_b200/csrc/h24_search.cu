@@ -21,7 +21,8 @@
 // the positions of the three smallest coordinates), which give the exact
 // type-3 scores of the codewords (c, p1) and (c, p2) up to the constant
 // -3 x_p; the plain row, which gives B(c); and the row |x|, whose value at the
-// weight-16 column c is 2 T(O) - sum|x| for the octad O = complement of c.
+// weight-16 column c is 2 T(O) - sum|x| for the octad O = complement of c
+// (minus its value at the octad column O).
 //
 // Pipeline per batch of atoms (one CUDA stream, no host synchronisation):
 //   1. prep_kernel      per atom: the four bf16 rows, written straight into
@@ -101,7 +102,8 @@ static_assert(kScreenTiles % (2 * kAccStages) == 0, "each stage is used an even 
 static_assert(kScreenTiles % kStages == 0, "a work item's Golay tiles fill the ring a whole number of times");
 
 // Row type held by TMEM lane quarter q of M-tile g, and its inverse.  The two
-// |x| rows (their loads are skipped for 26 of the 32 Golay tiles) sit in lane
+// |x| rows (loaded only for the 6 of the 16 multiplied tiles that hold octad
+// columns) sit in lane
 // quarters 1 and 2, read by the SM sub-partitions that also run the two MMA
 // issuer warps (warp w runs on sub-partition w % 4 and reads quarter w % 4).
 __host__ __device__ constexpr int row_of_quarter(int g, int q) {
@@ -148,7 +150,8 @@ static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 struct __align__(1024) ScreenSmem {
   uint8_t a[2][kAItemBytes];          // A operand of two work items
   uint8_t b[kStages][kBTileBytes];    // Golay tile ring
-  // Per Golay tile and epilogue thread slot (M-tile, lane quarter, lane): the
+  // Per logical Golay tile (all 32: the 16 multiplied ones and their
+  // complements) and epilogue thread slot (M-tile, lane quarter, lane): the
   // maxima of the tile's two 64-column chunks, rounded up to fp16 (so the
   // flags stay conservative).  Each slot is written and read by one thread.
   __half2 cmax[kGolayTiles][kWorkAtoms * kRowsPerAtom];
