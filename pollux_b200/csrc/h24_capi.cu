@@ -627,7 +627,7 @@ int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features, u
   int64_t g = in_features, h = 96;
   while (h) { const int64_t t2 = g % h; g = h; h = t2; }
   const int64_t rg = 96 / g;
-  constexpr int64_t kChunkAtoms = 49152;
+  constexpr int64_t kChunkAtoms = 73728;
   int64_t crows = (kChunkAtoms * kDim / in_features) / rg * rg;
   if (crows < rg) crows = rg;
   auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };

@@ -101,7 +101,7 @@ def test_unpack_capacity_below_count(C, oracle):
         assert np.array_equal(u.cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("rows,in_f", [(4608, 1152), (5461, 72), (3, 96), (30012, 40), (7, 24)])
+@pytest.mark.parametrize("rows,in_f", [(4608, 1152), (5461, 72), (3, 96), (60012, 40), (7, 24)])
 @pytest.mark.parametrize("pinned", [True, False])
 def test_host_layer_pipelined_equals_device_path(C, rows, in_f, pinned):
     # fp32 host weights go through h24_quantize_layer_host: row chunks of whole
