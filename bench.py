@@ -1,27 +1,28 @@
 #!/usr/bin/env python3
 """Benchmark of the H24 hot path on B200 (one JSON line on rank 0).
 
-Workload (config 2 of the benchmark plan): a synthetic Pollux-1152 backbone,
-12 layers x {QKV [3456,1152], O [1152,1152], up [4608,1152], down [1152,4608]}
-fp32 N(0, 0.02^2) from seed 1: 48 matrices, 7,962,624 atoms of 24 values.
-One step = the whole path over the backbone:
-  1. pack-rule quantisation of every matrix: per-row fp16 sigma, nearest
-     codeword (tcgen05 screening + fp64 rescore), 18-bit pack
-     (pack._quantize_h24_layer, pack.py:139-180), one shared pipeline;
-  2. LUT dequant of every packed matrix back to fp16 (materialize,
-     pollux.py:485-504), one launch.
-value = atoms quantised per second (whole job; N ranks each run their own
-backbone -- weak scaling, no collective on the path).
+Workload (config 3 of the benchmark plan): a synthetic Pollux-1920 backbone,
+18 layers x {QKV [5760,1920], O [1920,1920], up [7680,1920], down [1920,7680]}
+bf16 N(0, 0.02^2) from seed 2: 72 matrices, 33,177,600 atoms of 24 values.
+One step = whole-backbone pack-rule quantisation: per-row fp16 sigma, nearest
+codeword (tcgen05 screening + rescore) and 18-bit pack of every matrix
+(pack._quantize_h24_layer, pack.py:139-180, over pack_checkpoint's loop,
+pack.py:268-283), in one shared pipeline, reading the bf16 weights as they are.
+With N ranks (torchrun), rank r quantises rows shard_rows(rows, in, N, r) of
+every matrix (strong scaling: the backbone is fixed, no collective on the
+path); the optional NCCL all-gather of the packed shards is timed on its own.
+value = backbone atoms quantised per second, whole job.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 --impl reference times the reference's algorithm on the host cores: the CPU
 port in oracle/ of pack._quantize_h24_layer's fp32 matmul + argmax search, row
-scale and 18-bit pack, on a bounded sample of the same atoms.
+scale and 18-bit pack, each step a bounded sample of the same atoms.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -42,10 +43,16 @@ sys.path.insert(0, HERE)
 SCREEN_FLOP_PER_ATOM = 4 * 2048 * 2 * 24
 # An exhaustive search (x . kp_j for all 196,560 kissing points), for context.
 EXHAUSTIVE_FLOP_PER_ATOM = 2 * 24 * 196_560
-METRIC = "G atoms/s quantized (config-2 backbone: quantize + sigma + 18-bit pack, then LUT dequant)"
-WORKLOAD = ("config2: synthetic Pollux-1152 backbone, 12 layers x [3456x1152, 1152x1152, "
-            "4608x1152, 1152x4608] fp32 N(0,0.02^2) seed 1 (rank r: seed 1+r); step = pack-rule "
-            "quantize + sigma16 + 18-bit pack of all 48 matrices, then unpack + LUT dequant to fp16")
+# Bytes the rescore must read per atom: its 24 coordinates (bf16), four 64-bit
+# chunk masks, the 48-byte per-atom constants; and write: one int32 index.
+RESCORE_BYTES_PER_ATOM_BF16 = 48 + 32 + 48 + 4
+CONFIG = 3
+METRIC = ("G atoms/s quantized (config-3 bf16 Pollux-1920 backbone: whole-backbone sigma16 + "
+          "nearest codeword + 18-bit pack)")
+WORKLOAD = ("config3: synthetic Pollux-1920 backbone, 18 layers x [5760x1920, 1920x1920, "
+            "7680x1920, 1920x7680] bf16 N(0,0.02^2) seed 2 (33,177,600 atoms); rank r of N "
+            "quantises rows shard_rows(rows, in, N, r) of every matrix; step = pack-rule sigma16 "
+            "+ nearest codeword + 18-bit pack of those rows of all 72 matrices")
 
 
 def _env_int(name, default):
@@ -53,6 +60,14 @@ def _env_int(name, default):
         return int(os.environ.get(name, default))
     except ValueError:
         return default
+
+
+def _peaks() -> dict:
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
 
 
 # ---------------------------------------------------------------------------
@@ -115,49 +130,108 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference's pack-rule algorithm restated in oracle/
 # ---------------------------------------------------------------------------
-def cpu_baseline(seconds: float = 12.0, chunk: int = 2048) -> dict:
+def _cpu_threads():
+    import torch
+    from threadpoolctl import threadpool_limits
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)  # also under torchrun, which sets OMP_NUM_THREADS=1
+    return n, threadpool_limits(limits=n)
+
+
+def cpu_sample(seconds: float, chunk: int = 2048) -> dict:
+    """The reference's pack-rule path (pack.py:139-180 on CPU tensors) on the
+    first rows of config-3 matrix 0, restated in oracle/: fp32 matmul + argmax
+    over the codebook (numpy/BLAS), the row scales of the reference's torch
+    expression on CPU, and the 18-bit pack; whole rows, as many as fit in
+    about ``seconds``."""
     import torch
     from oracle import oracle as O
     from pollux_b200 import synth
-    nthreads = os.cpu_count() or 1
-    w = synth.backbone_weights(2, device="cpu", seed=1, shapes=[(3456, 1152)])[0]
-    atoms = w.numpy().reshape(-1, 24)
-    # Every host thread, also under torchrun (which sets OMP_NUM_THREADS=1).
-    from threadpoolctl import threadpool_limits
-    torch.set_num_threads(nthreads)
-    with threadpool_limits(limits=nthreads):
-        done, t0 = 0, time.perf_counter()
-        while time.perf_counter() - t0 < seconds and done + chunk <= atoms.shape[0]:
-            a = atoms[done:done + chunk]
-            idx = O.nearest_fp32_pack_rule(a)
-            O.sigma16_pack_rule(w.numpy()[done // 48: done // 48 + chunk // 48])
+    nthreads, limit = _cpu_threads()
+    w = synth.backbone_weights(CONFIG, device="cpu", shapes=[synth.CONFIG3_LAYER_SHAPES[0]])[0]
+    wf = w.float().numpy()
+    apr = wf.shape[1] // 24
+    rows_per_chunk = max(1, chunk // apr)
+    with limit:
+        done_rows, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds and done_rows + rows_per_chunk <= wf.shape[0]:
+            blk = wf[done_rows:done_rows + rows_per_chunk]
+            idx = O.nearest_fp32_pack_rule(blk.reshape(-1, 24))
+            O.sigma16_pack_rule_cpu_torch(blk)
             O.pack_indices(idx)
-            done += chunk
+            done_rows += rows_per_chunk
         dt = time.perf_counter() - t0
-    return {"value": done / dt / 1e9, "unit": "G atoms/s", "cores": nthreads, "kind": "port",
-            "sample": f"{done} atoms of config-2 layer 0 (QKV 3456x1152), fp32 matmul + argmax "
-                      f"+ sigma16 + pack with numpy/BLAS on {nthreads} host threads ({dt:.1f} s); "
-                      f"torch threads {torch.get_num_threads()}"}
+    atoms = done_rows * apr
+    return {"value": atoms / dt / 1e9, "unit": "G atoms/s", "cores": nthreads, "kind": "port",
+            "seconds": dt, "atoms": atoms,
+            "sample": f"{atoms} atoms ({done_rows} rows) of config-3 matrix 0 (QKV [5760,1920], bf16 "
+                      f"widened to fp32): fp32 matmul + argmax over the codebook, sigma16, 18-bit pack "
+                      f"(oracle port of pack._quantize_h24_layer) with numpy/BLAS on {nthreads} host "
+                      f"threads in {dt:.1f} s; torch threads {torch.get_num_threads()}"}
+
+
+def cpu_stress_agreement(x_sample: np.ndarray, cat_sample: np.ndarray, ours: np.ndarray) -> dict:
+    """Config 4 on the host: the exact fp64 oracle and the reference's
+    training-rule semantics (bf16-rounded scores, castor.py:549-557) on a
+    stratified sample of the stress atoms, timed, and the GPU's indices
+    checked against them: index agreement per category, and the largest
+    squared-distance excess of the GPU's codeword over the reference's choice
+    (negative: the GPU's is nearer)."""
+    from oracle import oracle as O
+    from pollux_b200 import synth
+    nthreads, limit = _cpu_threads()
+    with limit:
+        t0 = time.perf_counter()
+        exact = O.nearest_exact(x_sample, O.RULE_TRAIN)
+        t_exact = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        ref = O.nearest_bf16_train_rule(x_sample)
+        t_ref = time.perf_counter() - t0
+    out = {"sample_atoms": int(x_sample.shape[0]), "cores": nthreads,
+           "oracle_exact_atoms_per_s": x_sample.shape[0] / t_exact,
+           "reference_bf16_port_atoms_per_s": x_sample.shape[0] / t_ref,
+           "agreement_vs_exact_fp64": float(np.mean(ours == exact)),
+           "agreement_vs_reference_bf16": float(np.mean(ours == ref)), "per_category": {}}
+    diff = ours != ref
+    if diff.any():
+        d_o = O.dist2_fp64(x_sample[diff], ours[diff])
+        d_r = O.dist2_fp64(x_sample[diff], ref[diff])
+        out["max_rel_excess_vs_reference_bf16"] = float(np.max((d_o - d_r) / np.maximum(d_r, 1e-30)))
+    else:
+        out["max_rel_excess_vs_reference_bf16"] = 0.0
+    for k, name in enumerate(synth.STRESS_CATEGORIES):
+        m = cat_sample == k
+        out["per_category"][name] = {"atoms": int(m.sum()),
+                                     "agreement_vs_exact_fp64": float(np.mean(ours[m] == exact[m])),
+                                     "agreement_vs_reference_bf16": float(np.mean(ours[m] == ref[m]))}
+    return out
 
 
 def run_reference(args) -> None:
+    """The reference arm: each step one bounded sample of the workload through
+    the CPU port of the reference's path, on all host threads; rank 0 only."""
     rank = _env_int("RANK", 0)
     if rank != 0:
         return
-    per_step, total_atoms = [], 0
     from oracle import oracle as O
     O.build()
+    per_step = []
+    seconds = max(1.0, min(4.0, 90.0 / max(1, args.steps + args.warmup)))
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline(seconds=max(2.0, 60.0 / max(1, args.steps + args.warmup)))
+        r = cpu_sample(seconds)
         if i >= args.warmup:
             per_step.append(r)
-    value = statistics.median(r["value"] for r in per_step)
+    secs = sum(r["seconds"] for r in per_step)
+    atoms = sum(r["atoms"] for r in per_step)
+    value = atoms / secs / 1e9
     out = {"metric": METRIC, "value": value, "unit": "G atoms/s", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": 7_962_624 / (value * 1e9) * 1e3, "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "ms_per_step": secs / len(per_step) * 1e3, "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
            "impl": "reference",
-           "config": {"workload": WORKLOAD, "atoms_per_step": 7_962_624},
+           "config": {"workload": WORKLOAD, "atoms_per_step": atoms // len(per_step),
+                      "step": "one bounded sample of whole rows of config-3 matrix 0 per step "
+                              "(the full backbone would take hours on the host)"},
            "cpu_baseline": {**per_step[-1], "value": value},
            "e2e": {"value": value, "unit": "G atoms/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
@@ -167,6 +241,17 @@ def run_reference(args) -> None:
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def _kernel_times(N) -> dict:
+    """Summed event-timed ms and launch count of each instrumented kernel."""
+    out = {}
+    for name, k in (("screen_kernel", N.KERNEL_SCREEN), ("rescore_kernel", N.KERNEL_RESCORE),
+                    ("prep_kernel", N.KERNEL_PREP)):
+        ms, n = ctypes.c_double(0), ctypes.c_int64(0)
+        N.check(N.load().h24_timing_read_kernel(k, ctypes.byref(ms), ctypes.byref(n)), "timing")
+        out[name] = (ms.value, int(n.value))
+    return out
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -180,49 +265,59 @@ def run_ours(args) -> None:
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
-    from pollux_b200 import castor, pack, packed_linear, synth
+    from pollux_b200 import castor, pack, shard, synth
     from pollux_b200 import _native as N
-    import ctypes
 
-    shapes = synth.backbone_shapes(2)
-    weights = synth.backbone_weights(2, device=dev, seed=1 + rank)
-    atoms_per_step = sum(o * i // 24 for o, i in shapes)
-    packed_bytes = sum(((o * i // 24 + 3) // 4) * 9 for o, i in shapes)
-    fp16_bytes = sum(o * i * 2 for o, i in shapes)
-
-    outs16 = [torch.empty(o, i, dtype=torch.float16, device=dev) for o, i in shapes]
-    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    shapes = synth.backbone_shapes(CONFIG)
+    weights = synth.backbone_weights(CONFIG, device=dev)  # identical on every rank (seeded)
+    atoms_total = sum(o * i // 24 for o, i in shapes)
+    ranges = [shard.shard_rows(o, i, world, rank) for o, i in shapes]
+    parts = [(w, r0, r1) for w, (r0, r1) in zip(weights, ranges)]
+    atoms_rank = sum((r1 - r0) * i // 24 for (r0, r1), (o, i) in zip(ranges, shapes))
+    # This rank's packed bytes and scales of all 72 matrices in one buffer each,
+    # padded to the largest rank's size (the all-gather's equal-size blocks).
+    def sizes(r):
+        pb = sb = 0
+        for o, i in shapes:
+            s0, s1 = shard.shard_rows(o, i, world, r)
+            b0, b1 = shard.packed_range(s0, s1, i)
+            pb += b1 - b0
+            sb += s1 - s0
+        return pb, sb
+    all_sizes = [sizes(r) for r in range(world)]
+    max_pb = max(p for p, _ in all_sizes)
+    max_sb = max(s for _, s in all_sizes)
+    pbuf = torch.zeros(max_pb, dtype=torch.uint8, device=dev)
+    sbuf = torch.zeros(max_sb, dtype=torch.float16, device=dev)
+    outs, po, so = [], 0, 0
+    for (o, i), (r0, r1) in zip(shapes, ranges):
+        b0, b1 = shard.packed_range(r0, r1, i)
+        outs.append((pbuf[po:po + b1 - b0], sbuf[so:so + r1 - r0]))
+        po += b1 - b0
+        so += r1 - r0
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        res = pack.quantize_layers(weights)
-        layers = (N.DequantLayer * len(res))()
-        for k, ((p, s), o) in enumerate(zip(res, outs16)):
-            layers[k] = N.DequantLayer(p.data_ptr(), s.data_ptr(), o.data_ptr(), o.shape[0], o.shape[1])
-        castor._call(dev, "h24_dequant_batched", ctypes.cast(layers, ctypes.c_void_p), len(res),
-                     bad.data_ptr(), stream.cuda_stream)
-        return res
+        pack.quantize_layer_rows(parts, outs)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
 
     for _ in range(args.warmup):
-        res = step()
+        step()
     torch.cuda.synchronize()
     castor.device_check(dev)
-
-    # Round-trip check outside the timed region: unpack(packed) re-packs to the
-    # same bytes and dequant found no out-of-range index.
-    p0, _s0 = res[0]
-    n0 = shapes[0][0] * shapes[0][1] // 24
+    # Checks outside the timed region: every index in range and unpack(pack)
+    # the identity on matrix 0's shard.
+    p0, _ = outs[0]
+    n0 = (ranges[0][1] - ranges[0][0]) * shapes[0][1] // 24
     idx0 = castor.unpack_indices(p0, n0)
+    assert int(idx0.max()) <= 196560 and int(idx0.min()) >= 0
     assert torch.equal(castor.pack_indices(idx0), p0), "pack/unpack round trip failed"
-    assert int(bad.item()) == 0, "dequant saw out-of-range indices"
-    assert int(idx0.max()) <= 196560
 
     N.load().h24_timing_enable(1)
-    N.load().h24_timing_read(None, None)
+    _kernel_times(N)
     castor.quantize_stats(dev)
     launches0 = castor.launch_count()
     clocks = ClockSampler(local)
@@ -239,9 +334,7 @@ def run_ours(args) -> None:
     barrier()
     clk = clocks.stop()
     launches = castor.launch_count() - launches0
-    ms = ctypes.c_double(0)
-    nlaunch = ctypes.c_int64(0)
-    N.load().h24_timing_read(ctypes.byref(ms), ctypes.byref(nlaunch))
+    ktimes = _kernel_times(N)
     N.load().h24_timing_enable(0)
     exhaustive, exact_scores, chunks = castor.quantize_stats(dev)
     elapsed_ms = t_start.elapsed_time(t_stop)
@@ -250,141 +343,253 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
-    value = world * atoms_per_step * args.steps / (elapsed_ms / 1e3) / 1e9
+    value = atoms_total * args.steps / (elapsed_ms / 1e3) / 1e9
 
-    # Roofline of the dominant kernel (tensor-core screening): algorithmic
-    # FLOPs per launch over its mean CUDA-event duration.
-    screen_launches = max(1, int(nlaunch.value))
-    screen_ms = ms.value / screen_launches
-    flops_per_launch = SCREEN_FLOP_PER_ATOM * atoms_per_step * args.steps / screen_launches
-    achieved_tflops = flops_per_launch / (screen_ms / 1e3) / 1e12
-    peaks = {}
-    try:
-        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
-            peaks = json.load(f)
-    except (OSError, ValueError):
-        pass
-    peak = peaks.get("bf16_tflops_sustained")
-    peak_src = "measured sustained bf16 (MEASURED_PEAKS.json)"
-    if peak is None:
-        peak, peak_src = 1400.0, "fallback sustained bf16 1.4 PFLOP/s"
+    # Per-kernel shares and rooflines (this rank's launches, CUDA events on the
+    # launching stream over the timed region).
+    peaks = _peaks()
+    peak_t = peaks.get("bf16_tflops_sustained")
+    peak_t_src = "measured sustained bf16 (MEASURED_PEAKS.json)"
+    if peak_t is None:
+        peak_t, peak_t_src = 1400.0, "fallback sustained bf16 1.4 PFLOP/s"
+    peak_b = peaks.get("hbm_gbs")
+    peak_b_src = "measured HBM copy (MEASURED_PEAKS.json)"
+    if peak_b is None:
+        peak_b, peak_b_src = 6650.0, "fallback HBM 6.65 TB/s"
+    atoms_timed = atoms_rank * args.steps
+    kern = {}
+    for name, (ms, n) in ktimes.items():
+        kern[name] = {"ms_total": ms, "launches": n, "ms_per_launch": ms / max(1, n),
+                      "share_of_step": ms / max(1e-9, elapsed_ms), "atoms_per_launch": atoms_timed / max(1, n)}
+    scr = kern["screen_kernel"]
+    screen_tflops = SCREEN_FLOP_PER_ATOM * scr["atoms_per_launch"] / (scr["ms_per_launch"] / 1e3) / 1e12
+    screen_roof = {"bound": "tensor", "kernel": "screen_kernel", "achieved": screen_tflops,
+                   "peak": peak_t, "unit": "TFLOP/s", "frac": screen_tflops / peak_t,
+                   "peak_source": peak_t_src, "flop_per_atom": SCREEN_FLOP_PER_ATOM,
+                   "launch_ms_mean": scr["ms_per_launch"], "launches": scr["launches"],
+                   "traffic": None}
+    res_ = kern["rescore_kernel"]
+    rescore_gbs = RESCORE_BYTES_PER_ATOM_BF16 * res_["atoms_per_launch"] / (res_["ms_per_launch"] / 1e3) / 1e9
+    rescore_roof = {"bound": "hbm", "kernel": "rescore_kernel", "achieved": rescore_gbs, "peak": peak_b,
+                    "unit": "GB/s", "frac": rescore_gbs / peak_b, "peak_source": peak_b_src,
+                    "bytes_per_atom": RESCORE_BYTES_PER_ATOM_BF16,
+                    "launch_ms_mean": res_["ms_per_launch"], "launches": res_["launches"],
+                    "traffic": None,
+                    "note": "the rescore's memory floor; it runs issue-bound far above it"}
+    dominant = max(("screen_kernel", "rescore_kernel"), key=lambda k: kern[k]["ms_total"])
+    roofline = screen_roof if dominant == "screen_kernel" else rescore_roof
 
-    # F3: the fused training projection (pollux_step's H24 block) over the same
-    # backbone, all 48 parameters in one call.
-    proj = None
-    if rank == 0 and world == 1:
-        outs_p = [torch.empty_like(w) for w in weights]
-        pairs = list(zip(outs_p, weights))
-        castor.project_h24_many(pairs)
+    # Optional collective: the packed shards and scales gathered on every rank
+    # (one all_gather_into_tensor each, NCCL over NVLink), timed on its own.
+    gather = None
+    if world > 1:
+        pall = torch.empty(world * max_pb, dtype=torch.uint8, device=dev)
+        sall = torch.empty(world * max_sb, dtype=torch.float16, device=dev)
+        for _ in range(2):
+            dist.all_gather_into_tensor(pall, pbuf)
+            dist.all_gather_into_tensor(sall, sbuf)
         torch.cuda.synchronize()
-        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        p0.record()
-        for _ in range(3):
-            castor.project_h24_many(pairs)
-        p1.record()
-        p1.synchronize()
-        pms = p0.elapsed_time(p1) / 3
-        proj = {"what": "pollux_step H24 block (row RMS, normalise, training-rule search, rescale "
-                        "into p.data) for all 48 config-2 matrices in one fused call",
-                "ms": pms, "G_atoms_per_s": atoms_per_step / (pms / 1e3) / 1e9}
-        del outs_p, pairs
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        g0.record(stream)
+        for _ in range(reps):
+            dist.all_gather_into_tensor(pall, pbuf)
+            dist.all_gather_into_tensor(sall, sbuf)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gms = torch.tensor([g0.elapsed_time(g1) / reps], device=dev)
+        dist.all_reduce(gms, op=dist.ReduceOp.MAX)
+        # The gathered bytes of matrix 0 equal the single-GPU bytes.
+        whole_p, whole_s = pack.quantize_layers([weights[0]])[0]
+        got_p, got_s = [], []
+        for r in range(world):
+            s0, s1 = shard.shard_rows(*shapes[0], world, r)
+            b0, b1 = shard.packed_range(s0, s1, shapes[0][1])
+            got_p.append(pall[r * max_pb: r * max_pb + b1 - b0])
+            got_s.append(sall[r * max_sb: r * max_sb + s1 - s0])
+        ok = torch.equal(torch.cat(got_p), whole_p) and torch.equal(torch.cat(got_s), whole_s)
+        gather = {"what": "all_gather_into_tensor of every rank's packed shards (and one of its "
+                          "fp16 scales) of all 72 matrices, NCCL",
+                  "ms": float(gms.item()), "bytes_gathered": world * (max_pb + 2 * max_sb),
+                  "matrix0_equals_single_gpu_bytes": bool(ok),
+                  "share_of_quantize_step": float(gms.item()) / ms_per_step}
+        del pall, sall
 
-    # End-to-end through the public drop-in API with host buffers, on every
-    # rank at once (each its own backbone); the job's step time is the
-    # slowest rank's, and bytes and atoms are the whole job's.
     e2e = None
     if not args.skip_e2e:
         barrier()
-        e2e = run_e2e(args, weights, shapes, dev)
+        e2e = run_e2e(args, weights, shapes, ranges, dev, world)
         if world > 1:
             t = torch.tensor([e2e["ms_per_step"]], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e["ms_per_step"] = float(t.item())
-            e2e["value"] = world * atoms_per_step / (e2e["ms_per_step"] / 1e3) / 1e9
-            e2e["h2d_bytes_per_step"] *= world
-            e2e["d2h_bytes_per_step"] *= world
             e2e["timing"] = "wall clock per rank around synchronised steps, max over ranks"
+            for key in ("h2d_bytes_per_step", "d2h_bytes_per_step"):
+                t = torch.tensor([e2e[key]], dtype=torch.float64, device=dev)
+                dist.all_reduce(t)
+                e2e[key] = int(t.item())
+        e2e["value"] = atoms_total / (e2e["ms_per_step"] / 1e3) / 1e9
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.skip_cpu:
-        cpu = cpu_baseline()
-    comps = None
-    if rank == 0 and world == 1 and not args.skip_components:
-        comps = run_components(args)
+    extras = {}
+    if rank == 0 and world == 1:
+        del parts, outs
+        torch.cuda.empty_cache()
+        stress = None
+        if not args.skip_stress:
+            stress, sample = run_stress(args, dev)
+        if not args.skip_cpu:
+            extras["cpu_baseline"] = cpu_sample(12.0)
+            if stress is not None:
+                stress["host_check"] = cpu_stress_agreement(*sample)
+        extras["stress"] = stress
+        if not args.skip_components:
+            extras["hbm_kernels"] = run_components(args)
+            extras["training_projection"] = run_projection(dev)
 
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "G atoms/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "atoms_per_step": atoms_per_step,
-                       "matrices": len(shapes), "packed_bytes_per_step": packed_bytes,
-                       "fp16_bytes_per_step": fp16_bytes,
-                       "l2": "inputs larger than L2: 764 MB of fp32 weights read per step",
-                       "compute": "bf16 x bf16 -> fp32 tcgen05 screening, fp64 rescore"},
-            "roofline": {"bound": "tensor", "kernel": "screen_kernel",
-                         "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved_tflops / peak, "peak_source": peak_src,
-                         "flop_per_atom": SCREEN_FLOP_PER_ATOM,
-                         "launch_ms_mean": screen_ms, "launches": screen_launches,
-                         "traffic": None},
+            "config": {"workload": WORKLOAD, "atoms_per_step": atoms_total, "matrices": len(shapes),
+                       "atoms_per_rank": atoms_rank,
+                       "packed_bytes_per_step": sum(((o * i // 24 + 3) // 4) * 9 for o, i in shapes),
+                       "weight_bytes_per_step": sum(o * i * 2 for o, i in shapes),
+                       "l2": "inputs larger than L2: 1.59 GB of bf16 weights read per step",
+                       "compute": "bf16 weights read natively; bf16 x bf16 -> fp32 tcgen05 screening, "
+                                  "fp32/fp64 rescore; sigma in torch's CUDA mean order"},
+            "roofline": roofline,
+            "rooflines": {"screen_kernel": screen_roof, "rescore_kernel": rescore_roof},
+            "kernels": kern,
             "gpu_launches": launches,
             "clocks": clk,
             "search_stats": {"exhaustive_atoms": exhaustive, "exact_scores": exact_scores,
-                             "flagged_chunks": chunks,
-                             # Throughput restated as the FLOPs an exhaustive
-                             # x . kp_j scan would need (context, not a roofline).
+                             "flagged_chunks": chunks, "atoms": atoms_timed,
                              "exhaustive_scan_equivalent_tflops":
                                  value * 1e9 * EXHAUSTIVE_FLOP_PER_ATOM / 1e12},
+            "allgather": gather,
             "e2e": e2e,
-            "cpu_baseline": cpu,
-            "hbm_kernels": comps,
-            "training_projection": proj,
+            "cpu_baseline": extras.get("cpu_baseline"),
+            "stress": extras.get("stress"),
+            "hbm_kernels": extras.get("hbm_kernels"),
+            "training_projection": extras.get("training_projection"),
         }
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def run_e2e(args, weights, shapes, dev) -> dict:
-    """Same step through the public API with host (pinned) buffers: the
-    drop-in pack._quantize_h24_layer per matrix (returns packed bytes and
-    sigma on the host, as the reference does), then materialize of every layer
-    from those host tensors; the H2D/D2H copies are inside the timed region."""
+def run_e2e(args, weights, shapes, ranges, dev, world) -> dict:
+    """The same step through the public API with host buffers: bf16 weights in
+    page-locked host memory, each matrix through the drop-in
+    pack._quantize_h24_layer (one GPU; it returns host tensors, as the
+    reference does) or, on N ranks, pack.quantize_layer_rows_host for this
+    rank's rows; the host-to-device copies of the weights and the copies of
+    the packed bytes and scales back are inside the timed region."""
     import torch
-    from pollux_b200 import pack, packed_linear, castor
-    cb = castor.get_h24_codebook(dev, torch.float32)
+    from pollux_b200 import castor, pack
+    cb = castor.get_h24_codebook("cpu", torch.float32)
     host_w = [w.cpu().pin_memory() for w in weights]
     torch.cuda.synchronize()
 
     def e2e_step():
-        res = [pack._quantize_h24_layer(w, cb) for w in host_w]
-        mods = []
-        for (o, i), (p, s) in zip(shapes, res):
-            m = packed_linear.PackedH24Linear(i, o)
-            m.packed_weights = p.to(dev, non_blocking=True)
-            m.sigma_rows = s.to(dev, non_blocking=True)
-            mods.append(m)
-        n = packed_linear.materialize_all(torch.nn.ModuleList(mods))
-        check = torch.stack([m.weight[0, 0] for m in mods]).float().sum().item()
-        return n, check, res
+        if world == 1:
+            return [pack._quantize_h24_layer(w, cb) for w in host_w]
+        return [pack.quantize_layer_rows_host(w, r0, r1) for w, (r0, r1) in zip(host_w, ranges)]
 
     for _ in range(max(1, min(args.warmup, 2))):
         e2e_step()
-    torch.cuda.synchronize()
     steps = max(1, min(args.steps, 5))
     t0 = time.perf_counter()
     for _ in range(steps):
-        _, _, res = e2e_step()
-    torch.cuda.synchronize()
+        res = e2e_step()
     dt = (time.perf_counter() - t0) / steps
-    atoms = sum(o * i // 24 for o, i in shapes)
-    h2d = sum(w.numel() * 4 for w in host_w) + sum(p.numel() + s.numel() * 2 for p, s in res)
-    d2h = sum(p.numel() + s.numel() * 2 for p, s in res) + 4
-    return {"value": atoms / dt / 1e9, "unit": "G atoms/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": dt * 1e3, "steps": steps,
-            "api": "pollux_b200.pack._quantize_h24_layer + packed_linear.materialize_all"}
+    h2d = sum((r1 - r0) * i * 2 for (r0, r1), (o, i) in zip(ranges, shapes))
+    d2h = sum(p.numel() + s.numel() * 2 for p, s in res)
+    del host_w
+    return {"unit": "G atoms/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": dt * 1e3, "steps": steps,
+            "api": ("pollux_b200.pack._quantize_h24_layer per matrix (bf16 host weights)" if world == 1
+                    else "pollux_b200.pack.quantize_layer_rows_host per matrix, this rank's rows")}
+
+
+def run_stress(args, dev):
+    """Config 4: 2^24 stress atoms (seed 3) through the training rule
+    (castor_quantize_leech's search): throughput, plus the GPU's choice on the
+    reference's own stress fixtures (tests/golden/stress.npz: 4,096 atoms with
+    the indices of pack.py's fp32 path and of castor's bf16 path) as the
+    largest relative squared-distance excess over the reference's choice.
+    Returns the report and a stratified sample for the host check."""
+    import torch
+    from pollux_b200 import castor, synth
+    n = 1 << 24
+    cb = castor.get_h24_codebook(dev, torch.float32)
+    x, cat = synth.stress_atoms(n, cb, seed=3, device=dev, return_category=True)
+    castor.quantize_indices(x[:1 << 16], 0)
+    torch.cuda.synchronize()
+    castor.quantize_stats(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        idx = castor.quantize_indices(x, 0)
+    e1.record()
+    e1.synchronize()
+    castor.device_check(dev)
+    ms = e0.elapsed_time(e1) / reps
+    exh, exact_scores, chunks = castor.quantize_stats(dev)
+    rep = {"atoms": n, "rule": "training (castor_quantize_leech)", "ms": ms,
+           "G_atoms_per_s": n / (ms / 1e3) / 1e9,
+           "exhaustive_atoms_per_call": exh / reps, "exact_fp64_scores_per_atom": exact_scores / (reps * n),
+           "flagged_chunks_per_atom": chunks / (reps * n)}
+    # Against the reference's fixtures: fp64 squared distances on the GPU.
+    g = np.load(os.path.join(HERE, "tests", "golden", "stress.npz"))
+    xg = torch.from_numpy(g["atoms"]).to(dev)
+    cb64 = cb.double()
+    for rule, key in ((1, "pack_rule_idx"), (0, "train_bf16_idx")):
+        ours = castor.quantize_indices(xg, rule).long()
+        ref = torch.from_numpy(g[key]).to(dev).long()
+        d_o = ((xg.double() - cb64[ours]) ** 2).sum(1)
+        d_r = ((xg.double() - cb64[ref]) ** 2).sum(1)
+        rel = (d_o - d_r) / d_r.clamp_min(1e-30)
+        rep[f"golden_{key}"] = {"agreement": float((ours == ref).float().mean()),
+                                "max_rel_excess": float(rel.max()),
+                                "min_rel_excess": float(rel.min())}
+    # Stratified sample for the host check: 2^14 atoms of each category.
+    gsel = torch.Generator(device=dev).manual_seed(4)
+    sel = []
+    for k in range(len(synth.STRESS_CATEGORIES)):
+        pos = torch.nonzero(cat == k).flatten()
+        sel.append(pos[torch.randperm(pos.numel(), generator=gsel, device=dev)[:1 << 14]])
+    sel = torch.cat(sel)
+    sample = (x[sel].cpu().numpy(), cat[sel].cpu().numpy(), idx[sel].cpu().numpy().astype(np.int64))
+    del x, cat, idx
+    torch.cuda.empty_cache()
+    return rep, sample
+
+
+def run_projection(dev) -> dict:
+    """F3: the fused H24 block of pollux_step (row RMS, normalise, training-rule
+    search, rescale into p.data) for the 48 config-2 matrices in one call."""
+    import torch
+    from pollux_b200 import castor, synth
+    weights = synth.backbone_weights(2, device=dev)
+    outs_p = [torch.empty_like(w) for w in weights]
+    pairs = list(zip(outs_p, weights))
+    castor.project_h24_many(pairs)
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    for _ in range(3):
+        castor.project_h24_many(pairs)
+    p1.record()
+    p1.synchronize()
+    pms = p0.elapsed_time(p1) / 3
+    atoms = sum(w.numel() // 24 for w in weights)
+    return {"what": "pollux_step H24 block for all 48 config-2 fp32 matrices in one fused call",
+            "ms": pms, "G_atoms_per_s": atoms / (pms / 1e3) / 1e9}
 
 
 def run_search_only(args) -> None:
@@ -397,14 +602,15 @@ def run_search_only(args) -> None:
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(7)
     x = torch.randn(args.search_atoms, 24, generator=g, device=dev) * 1.4142135
-    import ctypes
+    if args.search_dtype == "bf16":
+        x = x.to(torch.bfloat16)
     from pollux_b200 import _native as N
     for _ in range(args.warmup):
         castor.quantize_indices(x, 1)
     torch.cuda.synchronize()
     castor.quantize_stats(dev)
     N.load().h24_timing_enable(1)
-    N.load().h24_timing_read(None, None)
+    _kernel_times(N)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(args.steps):
@@ -412,16 +618,17 @@ def run_search_only(args) -> None:
     t1.record()
     torch.cuda.synchronize()
     castor.device_check(dev)
-    screen_ms, nscreen = ctypes.c_double(0), ctypes.c_int64(0)
-    N.load().h24_timing_read(ctypes.byref(screen_ms), ctypes.byref(nscreen))
+    kt = _kernel_times(N)
     N.load().h24_timing_enable(0)
     exhaustive, exact_scores, chunks = castor.quantize_stats(dev)
     ms = t0.elapsed_time(t1) / args.steps
     atoms_s = args.search_atoms / (ms / 1e3)
     n = args.search_atoms * args.steps
-    print(json.dumps({"search_atoms": args.search_atoms, "ms_per_call": ms,
+    print(json.dumps({"search_atoms": args.search_atoms, "dtype": args.search_dtype, "ms_per_call": ms,
                       "G_atoms_per_s": atoms_s / 1e9,
-                      "screen_ms_per_call": screen_ms.value / args.steps,
+                      "screen_ms_per_call": kt["screen_kernel"][0] / args.steps,
+                      "rescore_ms_per_call": kt["rescore_kernel"][0] / args.steps,
+                      "prep_ms_per_call": kt["prep_kernel"][0] / args.steps,
                       "exhaustive_per_atom": exhaustive / n, "exact_scores_per_atom": exact_scores / n,
                       "flagged_chunks_per_atom": chunks / n}), flush=True)
 
@@ -534,6 +741,10 @@ def run_components(args) -> dict:
         return run
 
     reps = max(3, args.steps)
+    # Fill every packed buffer before anything reads them.
+    for k in range(sets):
+        pack(k)
+    torch.cuda.synchronize()
     dequant(0)
     dequant(1)
     t_lut1 = timed(lut_sweep(1), 2, reps)
@@ -582,6 +793,10 @@ def run_components(args) -> dict:
 
 
 def main():
+    # libh24 is built from this checkout's sources (incremental; a no-op when
+    # the library is current).
+    from pollux_b200 import build as _build
+    _build.build()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
@@ -589,8 +804,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-stress", action="store_true")
     ap.add_argument("--search-atoms", type=int, default=0,
                     help="profile mode: time only the search on this many atoms")
+    ap.add_argument("--search-dtype", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--components", action="store_true",
                     help="time the HBM-bound kernels (pack/unpack/dequant) on config 5 only")
     ap.add_argument("--skip-components", action="store_true")

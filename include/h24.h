@@ -102,9 +102,21 @@ typedef struct h24_dequant_layer {
 int h24_dequant_batched(const h24_dequant_layer *layers, int count, int32_t *bad_count,
                         void *stream);
 
+/* ---- per-row RMS scales (castor.row_rms_from_matrix, castor.py:309-313;
+ *      the sigma_rows of pack._quantize_h24_layer, pack.py:164) -------------
+ * w: rows x in_features, fp32 or bf16 (dtype H24_DTYPE_F32 / H24_DTYPE_BF16;
+ * bf16 is widened exactly, as weight.float() does), 16-byte aligned.
+ * sigma_out[r] = sqrt(mean(w_r^2) + 1e-8) in fp32, and sigma16_out[r] =
+ * fp16(clamp_min(sigma * sqrt(12), 1e-8)) as fp16 bits; either output may be
+ * NULL.  The fp32 mean is summed in the order torch's CUDA reduction uses for
+ * a contiguous [rows, in_features] tensor, so both are bit-identical to the
+ * reference run on a CUDA device (pack.py's default). */
+int h24_row_rms(const void *w, int64_t rows, int64_t in_features, int dtype, float *sigma_out,
+                uint16_t *sigma16_out, void *stream);
+
 /* ---- H24 projection of pollux_step (pollux.py:874-884), fused ------------
- * For every layer: sigma_r = sqrt(mean(latent_r^2) + 1e-8) (fp32; squares
- * summed in fp64, so torch's fp32 reduction may differ in the last bit),
+ * For every layer: sigma_r = sqrt(mean(latent_r^2) + 1e-8) (fp32, as
+ * h24_row_rms computes it),
  * x = (latent / max(sigma, 1e-8)) / s_lattice, the nearest codeword of each
  * atom of x under the training rule (castor_quantize_leech), and
  * out = (codeword * sigma_r) * s_lattice in fp32 (the p.data.copy_ of the
@@ -155,6 +167,12 @@ int h24_int8_dequant(const int8_t *q, const uint16_t *mu16, int64_t rows, int64_
  * maximum; an fp64 rescore picks the winner. */
 int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *stream);
 
+/* h24_quantize for atoms of element type `dtype` (H24_DTYPE_F32 or
+ * H24_DTYPE_BF16; bf16 coordinates are widened exactly to fp32, as the
+ * reference's .float() does before its search, castor.py:516, pack.py:159).
+ * x: n atoms of 24 elements, 16-byte aligned. */
+int h24_quantize_typed(const void *x, int64_t n, int dtype, int rule, int32_t *out_idx, void *stream);
+
 /* ---- allocation-free nearest codeword (no counterpart in the reference) --
  * Same result as h24_quantize for callers that must not allocate device
  * memory at call time (code under an external memory manager that owns every
@@ -172,7 +190,7 @@ int h24_quantize_noalloc(const float *x, int64_t n, int rule, int32_t *out_idx, 
  * Segment i holds counts[i] atoms of 24 fp32 values at xs[i] (device
  * pointers, 16-byte aligned; `xs` and `counts` are host arrays read before the
  * call returns).  out_idx receives the indices of all segments back to back.
- * One screening launch covers up to 4M atoms of up to 64 segments, so many
+ * One screening launch covers up to 1M atoms of up to 64 segments, so many
  * small matrices fill the GPU like one large one (the per-parameter loop of
  * pollux_step, pollux.py:828-884). */
 int h24_quantize_segments(const float *const *xs, const int64_t *counts, int nseg, int rule,
@@ -182,10 +200,8 @@ int h24_quantize_segments(const float *const *xs, const int64_t *counts, int nse
  * w: rows x in_features fp32 row-major (16-byte aligned), rows*in_features a
  * multiple of 24; atoms are consecutive runs of 24 values of the flattened
  * matrix (pack.py:161).  Writes sigma16_out[rows] =
- * fp16(clamp_min(sqrt(mean(w^2)+1e-8) * sqrt(12), 1e-8)) and the packed
- * indices packed_out[((rows*in/24+3)/4)*9] of the pack rule.  Each row's mean
- * of fp32 squares is summed in fp64 and rounded once to fp32, so sigma16 can
- * differ from torch's fp32 reduction by one fp16 ulp on a boundary row. */
+ * fp16(clamp_min(sqrt(mean(w^2)+1e-8) * sqrt(12), 1e-8)) (as h24_row_rms)
+ * and the packed indices packed_out[((rows*in/24+3)/4)*9] of the pack rule. */
 int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features,
                        uint16_t *sigma16_out, uint8_t *packed_out, void *stream);
 
@@ -194,7 +210,9 @@ int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features,
  * which returns host tensors).  The rows are processed in chunks: the
  * host-to-device copy of one chunk overlaps the search of the previous one
  * (page-locked host memory gives the overlap; pageable memory works too).
- * Returns once sigma16_out and packed_out are written. */
+ * Returns once sigma16_out and packed_out are written; H24_ERR_TIMEOUT if a
+ * bounded wait of the screening kernel ran out (the outputs are then
+ * incomplete). */
 int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features,
                             uint16_t *sigma16_out, uint8_t *packed_out, void *stream);
 
@@ -212,17 +230,60 @@ typedef struct h24_layer {
  * array read before the call returns. */
 int h24_quantize_layers(const h24_layer *layers, int count, void *stream);
 
+/* ---- row ranges, fp32 or bf16 weights ----------------------------------
+ * Rows [row_begin, row_end) of one rows x in_features weight matrix: the
+ * unit of row sharding across GPUs (each rank quantises its own rows of
+ * every matrix; the ranks' outputs concatenate into the single-GPU bytes).
+ * `w` points at the WHOLE matrix (elements of the call's dtype); sigma16_out
+ * receives row_end - row_begin fp16 scales and packed_out the
+ * ((row_end - row_begin) * in_features / 24 + 3) / 4 * 9 packed bytes of
+ * those rows.  The range must start on a 4-atom group (row_begin *
+ * in_features a multiple of 96) and end on one or at the matrix end.  The
+ * row scales are those of the whole matrix, bit for bit (h24_row_rms). */
+typedef struct h24_layer_rows {
+  const void *w;
+  int64_t rows;
+  int64_t in_features;
+  int64_t row_begin;
+  int64_t row_end;
+  uint16_t *sigma16_out;
+  uint8_t *packed_out;
+} h24_layer_rows;
+
+/* Pack-rule quantisation of `count` device-resident row ranges with one shared
+ * search pipeline (the H24 branch of pack_checkpoint's loop, pack.py:268-283,
+ * on this rank's rows).  dtype: H24_DTYPE_F32 or H24_DTYPE_BF16 (a bf16
+ * checkpoint is read as it is and widened exactly, pack.py:159).  `layers` is
+ * a host array read before the call returns. */
+int h24_quantize_layer_rows(const h24_layer_rows *layers, int count, int dtype, void *stream);
+
+/* One row range of a weight in HOST memory (pack._quantize_h24_layer on a CPU
+ * weight, pack.py:139-180, which returns host tensors): the rows are copied
+ * in chunks whose transfer overlaps the search of the previous chunk, and
+ * sigma16_out / packed_out (host memory) are written before the call returns.
+ * Returns H24_ERR_TIMEOUT if a bounded wait of the screening kernel ran out
+ * (the outputs are then incomplete). */
+int h24_quantize_layer_rows_host(const h24_layer_rows *layer, int dtype, void *stream);
+
 /* ---- codeword gather (index_select of castor.py:533, 559) ---------------
  * out[a][0..23] = codebook[idx[a]] converted to `dtype` (H24_DTYPE_*). */
 int h24_gather_codewords(const int32_t *idx, int64_t n, int dtype, void *out, void *stream);
 
 /* ---- instrumentation ----------------------------------------------------
- * When enabled, every h24_quantize / h24_quantize_layer call records CUDA
- * events around its tensor-core screening kernel on the caller's stream.
+ * When enabled, every quantize call records CUDA events on the caller's
+ * stream around its prep, tensor-core screening and rescore kernels.
  * h24_timing_read synchronises on the recorded events and returns the summed
  * milliseconds and the number of launches since the last read. */
 int h24_timing_enable(int enable);
 int h24_timing_read(double *ms, int64_t *launches);
+
+/* Per-kernel form of h24_timing_read: the events recorded around each launch
+ * of `kernel` (H24_KERNEL_*) since its last read. */
+#define H24_KERNEL_SCREEN 0   /* tcgen05 screening GEMM */
+#define H24_KERNEL_RESCORE 1  /* candidate rescore */
+#define H24_KERNEL_PREP 2     /* per-atom preparation */
+#define H24_KERNEL_COUNT 3
+int h24_timing_read_kernel(int kernel, double *ms, int64_t *launches);
 
 /* Counters accumulated by the quantize calls on the current device since the
  * previous read (reading resets them; synchronises `stream`): atoms resolved
@@ -238,6 +299,16 @@ int64_t h24_launch_count(void);
  * calls on the current device: H24_ERR_TIMEOUT if a bounded wait inside the
  * screening kernel ran out (the word is then cleared), else H24_OK. */
 int h24_check(void *stream);
+
+/* Test hook for the failure path (no counterpart in the reference, which has
+ * no bounded waits): the next `launches` screening launches leave one Golay
+ * tile of their first work item unloaded, so the waits behind it run out.
+ * `wait_limit_ns` becomes the limit of every bounded wait of the screen from
+ * now on (0 restores the default of 4 s).  A stalled launch drains its copies
+ * and tensor-core work, frees its TMEM and returns; its atoms' indices are
+ * then meaningless and h24_check (or a synchronising call) reports
+ * H24_ERR_TIMEOUT.  No fault, trap or endless wait is involved. */
+int h24_debug_stall_screen(int launches, uint64_t wait_limit_ns);
 
 #ifdef __cplusplus
 }

@@ -269,15 +269,153 @@ def dequant_numpy(packed: np.ndarray, sigma16: np.ndarray, rows: int, in_feature
     return w.reshape(rows, in_features)
 
 
-def sigma16_pack_rule(weight: np.ndarray) -> np.ndarray:
-    """fp16 row scale of pack.py:164: fp32 squares summed in fp64, the mean
-    rounded once to fp32 (the reference reduces in fp32 in torch's order)."""
+# Row scales.  The reference computes sigma = sqrt(w.pow(2).mean(-1) + 1e-8)
+# (castor.py:309-313) and sigma16 = fp16(clamp_min(sigma * sqrt(12), 1e-8))
+# (pack.py:164) with torch ops, so the fp32 mean depends on the device torch
+# reduces on.  Restated here for both devices of the reference:
+#   * CUDA (pack.py's default --device): torch's CUDA reduction order, from
+#     PyTorch 2.11's ATen/native/cuda/Reduce.cuh (setReduceConfig,
+#     input_vectorized_thread_reduce_impl, thread_reduce_impl, block_x_reduce,
+#     block_y_reduce) and MeanOps (ATen/native/SharedReduceOps.h): mean =
+#     sum * (fp32(rows) / fp32(rows * n)); restated in numpy below;
+#   * CPU: the same torch expression run on CPU tensors (torch's CPU mean is a
+#     cascade sum divided by n).
+def _last_pow2(v: int) -> int:
+    p = 1
+    while p * 2 <= v:
+        p *= 2
+    return p
+
+
+def torch_cuda_mean_plan(rows: int, n: int) -> dict:
+    """Launch plan torch's CUDA reduction picks for mean(dim=-1) of a
+    contiguous fp32 [rows, n] tensor (Reduce.cuh setReduceConfig, vt0 = 4)."""
+    vec = n >= 128
+    dim0 = n // 4 if vec else n
+    d0 = _last_pow2(dim0) if dim0 < 512 else 512
+    d1 = _last_pow2(rows) if rows < 512 else 512
+    bw = min(d0, 32)
+    bh = min(d1, 512 // bw)
+    bw = min(d0, 512 // bh)
+    vpt = -(-n // bw)
+    split = vpt >= min(16 * bh, 256)
+    factor = np.float32(np.float32(rows) / np.float32(rows * n))
+    return {"vec": vec, "bw": bw, "bh": bh, "split": split, "factor": factor}
+
+
+def _tree(v: np.ndarray, width: int) -> np.ndarray:
+    """Column 0 of the halving tree v[:, :off] += v[:, off:2 off] over the
+    first `width` columns (width a power of two), in fp32."""
+    v = v[:, :width].copy()
+    off = width // 2
+    while off > 0:
+        v[:, :off] = v[:, :off] + v[:, off:2 * off]
+        off //= 2
+    return v[:, 0]
+
+
+def row_sumsq_cuda_order(w: np.ndarray, matrix_rows: int | None = None, first_row: int = 0) -> np.ndarray:
+    """fp32 sum of squares of each row in torch's CUDA mean order; the rows are
+    rows first_row.. of a matrix of matrix_rows rows (default: just these)."""
+    sq = np.asarray(w, dtype=np.float32)
+    sq = (sq * sq).astype(np.float32)
+    R, n = sq.shape
+    plan = torch_cuda_mean_plan(matrix_rows if matrix_rows is not None else R, n)
+    bw, bh, split = plan["bw"], plan["bh"], plan["split"]
+    lanes = bw * bh if split else bw       # thread t = x + y * bw shares the row
+    out = np.empty(R, dtype=np.float32)
+    if plan["vec"]:
+        shifts = ((first_row + np.arange(R)) * n) % 4
+        for shift in np.unique(shifts):
+            rows_s = np.nonzero(shifts == shift)[0]
+            x = sq[rows_s]
+            acc = np.zeros((len(rows_s), lanes, 4), dtype=np.float32)
+            base = 0
+            if shift:
+                base = 4 - int(shift)
+                for t in range(int(shift), 4):          # head: lanes shift..3 of y = 0
+                    acc[:, t, 0] = x[:, t - int(shift)]
+            end = n - base
+            nvec = end // 4
+            xv = x[:, base:base + 4 * nvec].reshape(len(rows_s), nvec, 4)
+            for i0 in range(0, nvec, lanes):
+                i1 = min(i0 + lanes, nvec)
+                acc[:, :i1 - i0, :] = acc[:, :i1 - i0, :] + xv[:, i0:i1, :]
+            tail = end - end % 4
+            for t in range(end % 4):                   # tail: lanes 0.. of y = 0
+                acc[:, t, 0] = acc[:, t, 0] + x[:, base + tail + t]
+            v = ((acc[:, :, 0] + acc[:, :, 1]) + acc[:, :, 2]) + acc[:, :, 3]
+            out[rows_s] = _combine_lanes(v, bw, bh, split)
+    else:
+        acc = np.zeros((R, lanes, 4), dtype=np.float32)
+        for t in range(lanes):
+            i = t
+            while i + 3 * lanes < n:
+                for k in range(4):
+                    acc[:, t, k] = acc[:, t, k] + sq[:, i + k * lanes]
+                i += 4 * lanes
+            for k in range(4):
+                if i >= n:
+                    break
+                acc[:, t, k] = acc[:, t, k] + sq[:, i]
+                i += lanes
+        v = ((acc[:, :, 0] + acc[:, :, 1]) + acc[:, :, 2]) + acc[:, :, 3]
+        out = _combine_lanes(v, bw, bh, split)
+    return out
+
+
+def _combine_lanes(v: np.ndarray, bw: int, bh: int, split: bool) -> np.ndarray:
+    """block_x_reduce (shared memory down to 32 lanes, then shuffles with
+    halving offsets) per block row, then block_y_reduce when the block rows
+    share a matrix row."""
+    groups = bh if split else 1
+    heads = []
+    for y in range(groups):
+        g = v[:, y * bw:(y + 1) * bw]
+        if bw > 32:
+            g = g.copy()
+            off = bw // 2
+            while off >= 32:
+                g[:, :off] = g[:, :off] + g[:, off:2 * off]
+                off //= 2
+            heads.append(_tree(g, 32))
+        else:
+            heads.append(_tree(g, bw))
+    if not split:
+        return heads[0]
+    return _tree(np.stack(heads, axis=1), bh)
+
+
+def row_rms_cuda_order(weight: np.ndarray, matrix_rows: int | None = None, first_row: int = 0) -> np.ndarray:
+    """castor.row_rms_from_matrix (castor.py:309-313) as torch computes it on
+    a CUDA tensor: fp32 sqrt(sum * factor + 1e-8)."""
     w = np.asarray(weight, dtype=np.float32)
-    ms = (w * w).astype(np.float64).mean(axis=1)
-    rms = np.sqrt((ms.astype(np.float32) + np.float32(1e-8)).astype(np.float32)).astype(np.float32)
-    s = (rms * np.float32(np.sqrt(12.0))).astype(np.float32)
-    s = np.maximum(s, np.float32(1e-8))
+    plan = torch_cuda_mean_plan(matrix_rows if matrix_rows is not None else w.shape[0], w.shape[1])
+    mean = (row_sumsq_cuda_order(w, matrix_rows, first_row) * plan["factor"]).astype(np.float32)
+    return np.sqrt((mean + np.float32(1e-8)).astype(np.float32)).astype(np.float32)
+
+
+def sigma16_from_rms(rms: np.ndarray) -> np.ndarray:
+    """pack.py:164 after the row RMS: fp16(clamp_min(rms * fp32(sqrt 12), 1e-8)),
+    NaN kept."""
+    s = (np.asarray(rms, dtype=np.float32) * np.float32(np.sqrt(12.0))).astype(np.float32)
+    s = np.where(np.isnan(s), s, np.maximum(s, np.float32(1e-8)))
     return s.astype(np.float16)
+
+
+def sigma16_pack_rule(weight: np.ndarray, matrix_rows: int | None = None, first_row: int = 0) -> np.ndarray:
+    """fp16 row scales of pack.py:164 as the reference computes them on its
+    default CUDA device (torch's CUDA mean order)."""
+    return sigma16_from_rms(row_rms_cuda_order(weight, matrix_rows, first_row))
+
+
+def sigma16_pack_rule_cpu_torch(weight) -> np.ndarray:
+    """fp16 row scales of pack.py:164 with the reference's torch expression run
+    on CPU tensors (the reference with --device cpu)."""
+    import torch
+    w = torch.as_tensor(np.asarray(weight)).float()
+    rms = torch.sqrt(w.pow(2).mean(dim=-1) + 1e-8)
+    return (rms * float(np.sqrt(12.0))).clamp_min(1e-8).to(torch.float16).numpy()
 
 
 def int8_quantize(weight: np.ndarray) -> tuple[np.ndarray, np.ndarray]:

@@ -23,6 +23,7 @@ H24_ERR_STATE = 5
 RULE_TRAIN = 0
 RULE_PACK = 1
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+KERNEL_SCREEN, KERNEL_RESCORE, KERNEL_PREP = 0, 1, 2
 
 # Every symbol include/h24.h declares, with (restype, argtypes).
 _P = ctypes.c_void_p
@@ -51,12 +52,18 @@ SIGNATURES = {
     "h24_quantize_segments": (_I, [_P, _P, _I, _I, _P, _P]),
     "h24_quantize_noalloc": (_I, [_P, _I64, _I, _P, _P]),
     "h24_quantize_layers": (_I, [_P, _I, _P]),
+    "h24_quantize_typed": (_I, [_P, _I64, _I, _I, _P, _P]),
+    "h24_quantize_layer_rows": (_I, [_P, _I, _I, _P]),
+    "h24_quantize_layer_rows_host": (_I, [_P, _I, _P]),
+    "h24_row_rms": (_I, [_P, _I64, _I64, _I, _P, _P, _P]),
     "h24_launch_count": (ctypes.c_int64, []),
     "h24_gather_codewords": (_I, [_P, _I64, _I, _P, _P]),
     "h24_timing_enable": (_I, [_I]),
     "h24_timing_read": (_I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
+    "h24_timing_read_kernel": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "h24_quantize_stats": (_I, [ctypes.POINTER(ctypes.c_int64)] * 3 + [_P]),
     "h24_check": (_I, [_P]),
+    "h24_debug_stall_screen": (_I, [_I, ctypes.c_uint64]),
 }
 
 
@@ -69,6 +76,13 @@ class DequantLayer(ctypes.Structure):
 class Layer(ctypes.Structure):
     """Mirror of h24_layer."""
     _fields_ = [("w", _P), ("rows", ctypes.c_int64), ("in_features", ctypes.c_int64),
+                ("sigma16_out", _P), ("packed_out", _P)]
+
+
+class LayerRows(ctypes.Structure):
+    """Mirror of h24_layer_rows."""
+    _fields_ = [("w", _P), ("rows", ctypes.c_int64), ("in_features", ctypes.c_int64),
+                ("row_begin", ctypes.c_int64), ("row_end", ctypes.c_int64),
                 ("sigma16_out", _P), ("packed_out", _P)]
 
 

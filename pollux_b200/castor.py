@@ -241,8 +241,13 @@ def quantize_indices(x: torch.Tensor, rule: int = N.RULE_TRAIN) -> torch.Tensor:
     dev = _work_device(xf)
     out = torch.empty(n, dtype=torch.int32, device=dev)
     if n:
-        xd = _aligned(xf.to(device=dev, dtype=torch.float32))
-        _call(dev, "h24_quantize", xd.data_ptr(), n, int(rule), out.data_ptr(), _stream(dev))
+        # fp32 and bf16 atoms are read as they are (bf16 widens exactly, as
+        # the reference's .float() does); other dtypes go through fp32.
+        if xf.dtype == torch.bfloat16:
+            xd, code = _aligned(xf.to(device=dev)), N.DTYPE_BF16
+        else:
+            xd, code = _aligned(xf.to(device=dev, dtype=torch.float32)), N.DTYPE_F32
+        _call(dev, "h24_quantize_typed", xd.data_ptr(), n, code, int(rule), out.data_ptr(), _stream(dev))
     return out
 
 
@@ -291,6 +296,10 @@ def castor_quantize_leech(latent: torch.Tensor, codebook: torch.Tensor, chunk_si
     _check_codebook(codebook)
     idx = quantize_indices(x, N.RULE_TRAIN)
     out = _gather(idx, codebook, latent.dtype)
+    # One synchronisation per call, as the reference's own .item() has
+    # (castor.py:522): a timed-out wait of the screen raises here instead of
+    # returning unsearched codewords.
+    device_check(idx.device)
     return out.view(orig_shape).to(latent.device)
 
 

@@ -353,7 +353,8 @@ const Tables *tables_if_ready() {
 namespace {
 std::mutex g_timing_mu;
 bool g_timing = false;
-std::vector<std::pair<cudaEvent_t, cudaEvent_t>> g_events;
+// Recorded (start, stop) event pairs per instrumented kernel (H24_KERNEL_*).
+std::vector<std::pair<cudaEvent_t, cudaEvent_t>> g_events[H24_KERNEL_COUNT];
 }  // namespace
 
 namespace {
@@ -367,50 +368,9 @@ bool timing_enabled() {
   return g_timing;
 }
 
-void timing_record(cudaEvent_t start, cudaEvent_t stop) {
+void timing_record(int kernel, cudaEvent_t start, cudaEvent_t stop) {
   std::lock_guard<std::mutex> lk(g_timing_mu);
-  g_events.emplace_back(start, stop);
-}
-
-// ---------------------------------------------------------------------------
-// pack-rule row scale: sigma16 = fp16(clamp_min(sqrt(mean(w^2)+1e-8)*sqrt(12), 1e-8))
-// (pack.py:164, castor.py:309-313).  The fp32 squares are summed in fp64 and
-// the mean rounded once to fp32; torch's own fp32 reduction order differs, so
-// sigma16 can differ by one fp16 ulp on rows whose value sits on a rounding
-// boundary.
-// ---------------------------------------------------------------------------
-namespace {
-__global__ void sigma16_kernel(const float *__restrict__ w, int64_t rows, int64_t in_f,
-                               uint16_t *__restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-  if (row >= rows) return;
-  const float *p = w + row * in_f;
-  double acc = 0.0;
-  for (int64_t i = lane; i < in_f; i += 32) {
-    const float v = __ldg(p + i);
-    acc += static_cast<double>(__fmul_rn(v, v));  // weight.pow(2) rounds to fp32
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
-    const float mean = static_cast<float>(acc / static_cast<double>(in_f));
-    const float rms = sqrtf(mean + 1e-8f);
-    float s = rms * 3.4641016151377544f;
-    s = fmaxf(s, 1e-8f);
-    out[row] = __half_as_ushort(__float2half_rn(s));
-  }
-}
-}  // namespace
-
-int launch_sigma16(const float *w, int64_t rows, int64_t in_f, uint16_t *sigma16, cudaStream_t s) {
-  if (rows <= 0) return H24_OK;
-  const int64_t threads = rows * 32;
-  sigma16_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(w, rows, in_f,
-                                                                             sigma16);
-  H24_CUDA_TRY(cudaGetLastError());
-  count_launches(1);
-  return H24_OK;
+  g_events[kernel].emplace_back(start, stop);
 }
 
 }  // namespace h24
@@ -425,6 +385,21 @@ using namespace h24;
   if (!T) return H24_ERR_STATE
 
 static cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
+
+// Reads the device error word of T's device after the work on `s` (which it
+// synchronises) and clears it: H24_ERR_TIMEOUT if a bounded wait inside the
+// screening kernel ran out, else H24_OK.
+static int take_device_error(const Tables *T, cudaStream_t s) {
+  int err = 0;
+  H24_CUDA_TRY(cudaMemcpyAsync(&err, T->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+  H24_CUDA_TRY(cudaStreamSynchronize(s));
+  if (err != 0) {
+    H24_CUDA_TRY(cudaMemsetAsync(T->err, 0, sizeof(int), s));
+    H24_CUDA_TRY(cudaStreamSynchronize(s));
+    return fail(H24_ERR_TIMEOUT, "a bounded wait in the screening kernel ran out");
+  }
+  return H24_OK;
+}
 
 extern "C" {
 
@@ -545,6 +520,24 @@ int h24_quantize(const float *x, int64_t n, int rule, int32_t *out_idx, void *st
   return quantize(T, x, n, rule, out_idx, as_stream(stream));
 }
 
+int h24_quantize_typed(const void *x, int64_t n, int dtype, int rule, int32_t *out_idx, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (n < 0) return fail(H24_ERR_INVALID, "quantize: negative atom count");
+  if (rule != H24_RULE_TRAIN && rule != H24_RULE_PACK)
+    return fail(H24_ERR_INVALID, "quantize: unknown rule");
+  if (n == 0) return H24_OK;
+  if (!x || !out_idx) return fail(H24_ERR_INVALID, "quantize: null pointer");
+  if (!aligned16(x)) return fail(H24_ERR_INVALID, "quantize: x must be 16-byte aligned");
+  return quantize_segments(T, &x, &n, 1, dtype, rule, out_idx, as_stream(stream));
+}
+
+int h24_row_rms(const void *w, int64_t rows, int64_t in_features, int dtype, float *sigma_out,
+                uint16_t *sigma16_out, void *stream) {
+  if (rows < 0) return fail(H24_ERR_INVALID, "row_rms: negative row count");
+  if (rows > 0 && (!w || (!sigma_out && !sigma16_out))) return fail(H24_ERR_INVALID, "row_rms: null pointer");
+  return launch_row_rms(w, dtype, rows, in_features, rows, 0, sigma_out, sigma16_out, as_stream(stream));
+}
+
 int h24_quantize_segments(const float *const *xs, const int64_t *counts, int nseg, int rule,
                           int32_t *out_idx, void *stream) {
   H24_TABLES_OR_FAIL(T);
@@ -555,52 +548,95 @@ int h24_quantize_segments(const float *const *xs, const int64_t *counts, int nse
   int64_t total = 0;
   for (int i = 0; i < nseg; ++i) total += counts[i] > 0 ? counts[i] : 0;
   if (total > 0 && !out_idx) return fail(H24_ERR_INVALID, "quantize_segments: null output");
-  return quantize_segments(T, xs, counts, nseg, rule, out_idx, as_stream(stream));
+  std::vector<const void *> xv(xs, xs + nseg);
+  return quantize_segments(T, xv.data(), counts, nseg, H24_DTYPE_F32, rule, out_idx, as_stream(stream));
 }
 
-static int validate_layer(const h24_layer &L) {
+// A validated row range of one layer: rows [r0, r1) of a rows x in matrix,
+// whose atoms start on a 4-index group and end on one (or at the matrix end).
+struct RowRange {
+  const uint8_t *w;  // the whole matrix
+  int64_t rows, in, r0, r1;
+  uint16_t *sigma16;
+  uint8_t *packed;
+  int64_t atoms() const { return (r1 - r0) * in / kDim; }
+};
+
+static int validate_rows(const h24_layer_rows &L, size_t esize, bool host, RowRange *out) {
   if (L.rows < 0 || L.in_features <= 0 || (L.rows * L.in_features) % kDim != 0)
     return fail(H24_ERR_INVALID, "quantize_layer: rows*in_features must be a multiple of 24");
-  if (L.rows > 0 && (!L.w || !L.sigma16_out || !L.packed_out))
-    return fail(H24_ERR_INVALID, "quantize_layer: null pointer");
-  if (L.rows > 0 && !aligned16(L.w))
-    return fail(H24_ERR_INVALID, "quantize_layer: w must be 16-byte aligned");
+  if (L.row_begin < 0 || L.row_end < L.row_begin || L.row_end > L.rows)
+    return fail(H24_ERR_INVALID, "quantize_layer: row range outside the matrix");
+  const int64_t a0 = L.row_begin * L.in_features, a1 = L.row_end * L.in_features;
+  if (a0 % (4 * kDim) != 0 || (L.row_end != L.rows && a1 % (4 * kDim) != 0))
+    return fail(H24_ERR_INVALID,
+                "quantize_layer: a row range must start and end on a whole 9-byte group of 4 atoms");
+  if (L.row_end > L.row_begin) {
+    if (!L.w || !L.sigma16_out || !L.packed_out) return fail(H24_ERR_INVALID, "quantize_layer: null pointer");
+    if (!host && !aligned16(L.w)) return fail(H24_ERR_INVALID, "quantize_layer: w must be 16-byte aligned");
+  }
+  *out = RowRange{static_cast<const uint8_t *>(L.w), L.rows, L.in_features, L.row_begin, L.row_end,
+                  L.sigma16_out, L.packed_out};
+  (void)esize;
   return H24_OK;
 }
 
-int h24_quantize_layers(const h24_layer *layers, int count, void *stream) {
-  H24_TABLES_OR_FAIL(T);
-  if (count < 0 || (count > 0 && !layers)) return fail(H24_ERR_INVALID, "quantize_layers: bad list");
-  cudaStream_t s = as_stream(stream);
-  std::vector<const float *> xs;
+// Pack-rule quantisation of device-resident row ranges: row scales, one
+// shared search pipeline over all ranges, then the 18-bit pack of each.
+static int quantize_ranges(const Tables *T, const std::vector<RowRange> &R, int dtype, cudaStream_t s) {
+  const size_t esize = dtype == H24_DTYPE_BF16 ? 2 : 4;
+  std::vector<const void *> xs;
   std::vector<int64_t> counts;
   int64_t total = 0;
-  for (int i = 0; i < count; ++i) {
-    int rc = validate_layer(layers[i]);
-    if (rc != H24_OK) return rc;
-    const int64_t atoms = layers[i].rows * layers[i].in_features / kDim;
-    xs.push_back(layers[i].w);
-    counts.push_back(atoms);
-    total += atoms;
+  for (const RowRange &r : R) {
+    xs.push_back(r.w + static_cast<size_t>(r.r0 * r.in) * esize);
+    counts.push_back(r.atoms());
+    total += r.atoms();
   }
   if (total == 0) return H24_OK;
-  for (int i = 0; i < count; ++i) {
-    int rc = launch_sigma16(layers[i].w, layers[i].rows, layers[i].in_features,
-                            layers[i].sigma16_out, s);
+  for (const RowRange &r : R) {
+    int rc = launch_row_rms(r.w + static_cast<size_t>(r.r0 * r.in) * esize, dtype, r.r1 - r.r0, r.in, r.rows,
+                            r.r0, nullptr, r.sigma16, s);
     if (rc != H24_OK) return rc;
   }
   int32_t *idx = nullptr;
   H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&idx),
                                        static_cast<size_t>(total) * sizeof(int32_t), T->pool, s));
-  int rc = quantize_segments(T, xs.data(), counts.data(), count, H24_RULE_PACK, idx, s);
+  int rc = quantize_segments(T, xs.data(), counts.data(), static_cast<int>(xs.size()), dtype,
+                             H24_RULE_PACK, idx, s);
   int64_t off = 0;
-  for (int i = 0; i < count && rc == H24_OK; ++i) {
-    rc = launch_pack_i32(idx + off, counts[i], layers[i].packed_out, s);
+  for (size_t i = 0; i < R.size() && rc == H24_OK; ++i) {
+    rc = launch_pack_i32(idx + off, counts[i], R[i].packed, s);
     off += counts[i];
   }
   cudaError_t e = cudaFreeAsync(idx, s);
   if (rc == H24_OK && e != cudaSuccess) rc = cuda_fail(e, "cudaFreeAsync");
   return rc;
+}
+
+int h24_quantize_layer_rows(const h24_layer_rows *layers, int count, int dtype, void *stream) {
+  H24_TABLES_OR_FAIL(T);
+  if (count < 0 || (count > 0 && !layers)) return fail(H24_ERR_INVALID, "quantize_layers: bad list");
+  if (dtype != H24_DTYPE_F32 && dtype != H24_DTYPE_BF16)
+    return fail(H24_ERR_INVALID, "quantize_layers: weights must be fp32 or bf16");
+  const size_t esize = dtype == H24_DTYPE_BF16 ? 2 : 4;
+  std::vector<RowRange> R(count);
+  for (int i = 0; i < count; ++i) {
+    int rc = validate_rows(layers[i], esize, false, &R[i]);
+    if (rc != H24_OK) return rc;
+  }
+  // Segments of the pipeline must be 16-byte aligned: a range starting inside
+  // the matrix starts at a multiple of 96 elements, so it is if w is.
+  return quantize_ranges(T, R, dtype, as_stream(stream));
+}
+
+int h24_quantize_layers(const h24_layer *layers, int count, void *stream) {
+  if (count < 0 || (count > 0 && !layers)) return fail(H24_ERR_INVALID, "quantize_layers: bad list");
+  std::vector<h24_layer_rows> L(count);
+  for (int i = 0; i < count; ++i)
+    L[i] = h24_layer_rows{layers[i].w, layers[i].rows, layers[i].in_features, 0, layers[i].rows,
+                          layers[i].sigma16_out, layers[i].packed_out};
+  return h24_quantize_layer_rows(L.data(), count, H24_DTYPE_F32, stream);
 }
 
 int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16_t *sigma16_out,
@@ -609,18 +645,23 @@ int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16
   return h24_quantize_layers(&L, 1, stream);
 }
 
-// Host-memory form of h24_quantize_layer.  The rows are cut into chunks of
-// whole 4-atom pack groups; chunk k+1 is copied host-to-device on the copy
-// stream while chunk k is searched on the caller's stream, and both outputs
-// come back when all chunks are done.  Returns after the outputs are written.
-int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features, uint16_t *sigma16_out,
-                            uint8_t *packed_out, void *stream) {
+// Host-memory form: the range's rows are cut into chunks of whole 4-atom pack
+// groups; chunk k+1 is copied host-to-device on the copy stream while chunk k
+// is searched on the caller's stream; the row scales run once the last chunk
+// has landed, and both outputs come back before the call returns.
+int h24_quantize_layer_rows_host(const h24_layer_rows *layer, int dtype, void *stream) {
   H24_TABLES_OR_FAIL(T);
-  if (rows < 0 || in_features <= 0 || (rows * in_features) % kDim != 0)
-    return fail(H24_ERR_INVALID, "quantize_layer_host: rows*in_features must be a multiple of 24");
-  if (rows == 0) return H24_OK;
-  if (!w || !sigma16_out || !packed_out) return fail(H24_ERR_INVALID, "quantize_layer_host: null pointer");
+  if (!layer) return fail(H24_ERR_INVALID, "quantize_layer_host: null layer");
+  if (dtype != H24_DTYPE_F32 && dtype != H24_DTYPE_BF16)
+    return fail(H24_ERR_INVALID, "quantize_layer_host: weights must be fp32 or bf16");
+  const size_t esize = dtype == H24_DTYPE_BF16 ? 2 : 4;
+  RowRange RR;
+  int rc = validate_rows(*layer, esize, true, &RR);
+  if (rc != H24_OK) return rc;
+  if (RR.r1 == RR.r0) return H24_OK;
   cudaStream_t s = as_stream(stream);
+  const int64_t in_features = RR.in, rows = RR.r1 - RR.r0;
+  const uint8_t *w = RR.w + static_cast<size_t>(RR.r0 * in_features) * esize;
   const int64_t atoms = rows * in_features / kDim;
   const size_t packed_bytes = static_cast<size_t>((atoms + 3) / 4) * 9;
   // Chunk rows: a multiple of rg rows holds a whole number of 4-atom groups.
@@ -631,18 +672,20 @@ int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features, u
   int64_t crows = (kChunkAtoms * kDim / in_features) / rg * rg;
   if (crows < rg) crows = rg;
   auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
-  const size_t off_sig = up(static_cast<size_t>(rows * in_features) * sizeof(float));
+  // The device copy keeps the rows' alignment within 16 bytes of the whole
+  // matrix (the row scales' summation order depends on it).
+  const size_t lead = (static_cast<size_t>(RR.r0 * in_features) * esize) & 15u;
+  const size_t off_sig = up(lead + static_cast<size_t>(rows * in_features) * esize);
   const size_t off_pk = off_sig + up(static_cast<size_t>(rows) * 2);
   const size_t off_idx = off_pk + up(packed_bytes);
   uint8_t *buf = nullptr;
   H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&buf),
                                        off_idx + up(static_cast<size_t>(atoms) * 4), T->pool, s));
-  float *wd = reinterpret_cast<float *>(buf);
+  uint8_t *wd = buf + lead;
   uint16_t *sig = reinterpret_cast<uint16_t *>(buf + off_sig);
   uint8_t *pk = buf + off_pk;
   int32_t *idx = reinterpret_cast<int32_t *>(buf + off_idx);
   std::vector<cudaEvent_t> evs;
-  int rc = H24_OK;
   auto event = [&](cudaEvent_t *e) -> int {
     cudaError_t ce = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaEventCreate");
@@ -664,19 +707,19 @@ int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features, u
     cudaEvent_t copied;
     rc = event(&copied);
     if (rc != H24_OK) break;
-    cudaError_t ce = cudaMemcpyAsync(wd + e0, w + e0, static_cast<size_t>(nr * in_features) * sizeof(float),
+    cudaError_t ce = cudaMemcpyAsync(wd + e0 * esize, w + e0 * esize, static_cast<size_t>(nr * in_features) * esize,
                                      cudaMemcpyHostToDevice, T->copy_stream);
     if (ce == cudaSuccess) ce = cudaEventRecord(copied, T->copy_stream);
     if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s, copied, 0);
     if (ce != cudaSuccess) { rc = cuda_fail(ce, "chunk copy"); break; }
-    rc = launch_sigma16(wd + e0, nr, in_features, sig + r0, s);
-    const float *xs = wd + e0;
-    if (rc == H24_OK) rc = quantize_segments(T, &xs, &na, 1, H24_RULE_PACK, idx + a0, s);
+    const void *xs = wd + e0 * esize;
+    rc = quantize_segments(T, &xs, &na, 1, dtype, H24_RULE_PACK, idx + a0, s);
     if (rc == H24_OK) rc = launch_pack_i32(idx + a0, na, pk + a0 / 4 * 9, s);
   }
+  if (rc == H24_OK) rc = launch_row_rms(wd, dtype, rows, in_features, RR.rows, RR.r0, nullptr, sig, s);
   if (rc == H24_OK) {
-    cudaError_t ce = cudaMemcpyAsync(sigma16_out, sig, static_cast<size_t>(rows) * 2, cudaMemcpyDeviceToHost, s);
-    if (ce == cudaSuccess) ce = cudaMemcpyAsync(packed_out, pk, packed_bytes, cudaMemcpyDeviceToHost, s);
+    cudaError_t ce = cudaMemcpyAsync(RR.sigma16, sig, static_cast<size_t>(rows) * 2, cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(RR.packed, pk, packed_bytes, cudaMemcpyDeviceToHost, s);
     if (ce != cudaSuccess) rc = cuda_fail(ce, "output copy");
   }
   // Every copy-stream operation is ordered before the free (also after an
@@ -692,7 +735,15 @@ int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features, u
   if (rc != H24_OK) return rc;
   if (fe != cudaSuccess) return cuda_fail(fe, "cudaFreeAsync");
   if (se != cudaSuccess) return cuda_fail(se, "cudaStreamSynchronize");
-  return H24_OK;
+  // The call has synchronised: report (and clear) a timed-out wait of the
+  // screening kernel instead of returning incomplete indices.
+  return take_device_error(T, s);
+}
+
+int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features, uint16_t *sigma16_out,
+                            uint8_t *packed_out, void *stream) {
+  h24_layer_rows L{w, rows, in_features, 0, rows, sigma16_out, packed_out};
+  return h24_quantize_layer_rows_host(&L, H24_DTYPE_F32, stream);
 }
 
 int h24_gather_codewords(const int32_t *idx, int64_t n, int dtype, void *out, void *stream) {
@@ -708,11 +759,12 @@ int h24_timing_enable(int enable) {
   return H24_OK;
 }
 
-int h24_timing_read(double *ms, int64_t *launches) {
+int h24_timing_read_kernel(int kernel, double *ms, int64_t *launches) {
+  if (kernel < 0 || kernel >= H24_KERNEL_COUNT) return fail(H24_ERR_INVALID, "timing: unknown kernel");
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
   {
     std::lock_guard<std::mutex> lk(g_timing_mu);
-    ev.swap(g_events);
+    ev.swap(g_events[kernel]);
   }
   double total = 0.0;
   int rc = H24_OK;
@@ -728,6 +780,10 @@ int h24_timing_read(double *ms, int64_t *launches) {
   if (ms) *ms = total;
   if (launches) *launches = static_cast<int64_t>(ev.size());
   return rc;
+}
+
+int h24_timing_read(double *ms, int64_t *launches) {
+  return h24_timing_read_kernel(H24_KERNEL_SCREEN, ms, launches);
 }
 
 int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *exact_scores, int64_t *flagged_chunks,
@@ -748,15 +804,7 @@ int64_t h24_launch_count(void) { return g_launches.load(std::memory_order_relaxe
 
 int h24_check(void *stream) {
   H24_TABLES_OR_FAIL(T);
-  cudaStream_t s = as_stream(stream);
-  int err = 0;
-  H24_CUDA_TRY(cudaMemcpyAsync(&err, T->err, sizeof(int), cudaMemcpyDeviceToHost, s));
-  H24_CUDA_TRY(cudaStreamSynchronize(s));
-  if (err != 0) {
-    H24_CUDA_TRY(cudaMemsetAsync(T->err, 0, sizeof(int), s));
-    return fail(H24_ERR_TIMEOUT, "a bounded wait in the screening kernel ran out");
-  }
-  return H24_OK;
+  return take_device_error(T, as_stream(stream));
 }
 
 }  // extern "C"

@@ -130,21 +130,27 @@ int launch_gather(const Tables *t, const int32_t *idx, int64_t n, int dtype, voi
                   cudaStream_t s);
 int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
              cudaStream_t s);
-int quantize_segments(const Tables *t, const float *const *xs, const int64_t *counts, int nseg,
-                      int rule, int32_t *out_idx, cudaStream_t s);
+// Atoms of segment i: counts[i] x 24 elements at xs[i], of type `dtype`
+// (H24_DTYPE_F32 or H24_DTYPE_BF16), 16-byte aligned.
+int quantize_segments(const Tables *t, const void *const *xs, const int64_t *counts, int nseg,
+                      int dtype, int rule, int32_t *out_idx, cudaStream_t s);
 int project_layers(const Tables *t, const h24_project_layer *layers, int count, cudaStream_t s);
 int launch_int8_quantize(const float *w, int64_t rows, int64_t cols, int8_t *q, uint16_t *mu16,
                          cudaStream_t s);
 int launch_int8_dequant(const int8_t *q, const uint16_t *mu16, int64_t rows, int64_t cols,
                         uint16_t *out, cudaStream_t s);
-int launch_sigma16(const float *w, int64_t rows, int64_t in_f, uint16_t *sigma16,
-                   cudaStream_t s);
+// Row scales of `rows` rows of n elements at w (fp32 or bf16), which are rows
+// first_row.. of a 16-byte aligned matrix of matrix_rows rows, in the
+// reference's arithmetic (h24_rowrms.cu): sigma32 = sqrt(mean(w^2) + 1e-8),
+// sigma16 = fp16(clamp_min(sigma32 * sqrt(12), 1e-8)); either may be null.
+int launch_row_rms(const void *w, int dtype, int64_t rows, int64_t n, int64_t matrix_rows,
+                   int64_t first_row, float *sigma32, uint16_t *sigma16, cudaStream_t s);
 
 // Number of kernels this library has launched (all devices, all threads).
 void count_launches(int64_t k);
 
 // Instrumentation of the screening kernel.
 bool timing_enabled();
-void timing_record(cudaEvent_t start, cudaEvent_t stop);
+void timing_record(int kernel, cudaEvent_t start, cudaEvent_t stop);
 
 }  // namespace h24

@@ -5,10 +5,10 @@
 //   idx      = nearest codeword of every 24-atom of x, training rule (h24_search.cu)
 //   p_rc     = fp32( fp32(cb32[idx][c % 24] * sigma_r) * fp32(s_lattice) )
 // (normalize_matrix_by_row_rms, castor.py:316-333; castor_quantize_leech,
-// castor.py:487-560; scale_matrix_by_row_rms, castor.py:336-339).  The
-// squares are summed in fp64, so sigma is the correctly rounded fp32 value of
-// the fp32 mean of fp32 squares; torch's fp32 reduction may differ from it in
-// the last bit.
+// castor.py:487-560; scale_matrix_by_row_rms, castor.py:336-339).  sigma is
+// computed by the row-scale kernel of h24_rowrms.cu, in the summation order of
+// torch's CUDA mean, so it is bit-identical to row_rms_from_matrix on a CUDA
+// latent.
 #include "h24_internal.cuh"
 
 namespace h24 {
@@ -34,10 +34,10 @@ __device__ __forceinline__ int find_layer(const ProjBatch &b, int64_t v, const i
   return lo;
 }
 
-// One warp per row of every layer: sigma (fp32 squares summed in fp64) and
-// the row's atoms of x into the shared scratch.
+// One warp per row of every layer: the row's atoms of x into the shared
+// scratch, from the row's sigma (already computed).
 __global__ void __launch_bounds__(kThreads) project_prep_kernel(const __grid_constant__ ProjBatch b,
-                                                                float *__restrict__ sigma,
+                                                                const float *__restrict__ sigma,
                                                                 float *__restrict__ xs) {
   const int lane = threadIdx.x & 31;
   const int64_t total = b.row_start[b.count];
@@ -48,20 +48,9 @@ __global__ void __launch_bounds__(kThreads) project_prep_kernel(const __grid_con
     const h24_project_layer &L = b.layer[li];
     const int64_t r = gr - b.row_start[li];
     const float *row = L.latent + r * L.in_features;
-    double ss = 0.0;
-    for (int64_t c = lane; c < L.in_features; c += 32) {
-      const float v = __ldg(row + c);
-      ss += static_cast<double>(__fmul_rn(v, v));
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    const float mean = static_cast<float>(ss / static_cast<double>(L.in_features));
-    const float sg = __fsqrt_rn(__fadd_rn(mean, 1e-8f));
+    const float sg = sigma[gr];
     const float sgc = fmaxf(sg, 1e-8f);
-    if (lane == 0) {
-      sigma[gr] = sg;
-      if (L.sigma) L.sigma[r] = sg;
-    }
+    if (lane == 0 && L.sigma) L.sigma[r] = sg;
     float *xrow = xs + (b.atom_start[li] + r * (L.in_features / kDim)) * kDim;
     for (int64_t c = lane; c < L.in_features; c += 32)
       xrow[c] = __fdiv_rn(__fdiv_rn(__ldg(row + c), sgc), kSLatticeF);
@@ -139,9 +128,17 @@ int project_layers(const Tables *t, const h24_project_layer *layers, int count, 
     float *xs = reinterpret_cast<float *>(scratch + off_x);
     int32_t *idx = reinterpret_cast<int32_t *>(scratch + off_idx);
     int rc = H24_OK;
-    project_prep_kernel<<<grid_for(rows, kWarps), kThreads, 0, s>>>(b, sigma, xs);
-    cudaError_t le = cudaGetLastError();
-    if (le != cudaSuccess) rc = cuda_fail(le, "project_prep launch");
+    for (int i = 0; i < b.count && rc == H24_OK; ++i) {
+      if (!aligned16(b.layer[i].latent)) rc = fail(H24_ERR_INVALID, "project: latent must be 16-byte aligned");
+      else rc = launch_row_rms(b.layer[i].latent, H24_DTYPE_F32, b.layer[i].rows, b.layer[i].in_features,
+                               b.layer[i].rows, 0, sigma + b.row_start[i], nullptr, s);
+    }
+    cudaError_t le = cudaSuccess;
+    if (rc == H24_OK) {
+      project_prep_kernel<<<grid_for(rows, kWarps), kThreads, 0, s>>>(b, sigma, xs);
+      le = cudaGetLastError();
+      if (le != cudaSuccess) rc = cuda_fail(le, "project_prep launch");
+    }
     if (rc == H24_OK) {
       count_launches(1);
       rc = quantize(t, xs, atoms, H24_RULE_TRAIN, idx, s);

@@ -68,6 +68,7 @@
 // rescore.  The type-2 contribution to `best` is max_O 2 T~(O) - 4 |x|_(8),
 // |x|_(8) the 8th largest |x_i|: flipping the sign of the smallest |x_i| of
 // O, which is at most |x|_(8), repairs the parity of any octad.
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -96,7 +97,7 @@ constexpr uint32_t kTmemCols = kMTiles * kAccStages * kGolayTileN;  // 512
 constexpr int kHeavyChunks = 192;                  // flagged chunks (of 204) beyond which the exhaustive scan runs
 constexpr int kMaxSegs = 64;                       // input segments per pipeline batch
 constexpr int64_t kBatchAtoms = int64_t(1) << 20;  // atoms per pipeline batch
-constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s
+constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s (default)
 static_assert(kOctTiles == 6 && kOctTailCol == 120, "octad columns 1-759 fill tiles 0-5 up to column 120 of tile 5");
 static_assert(kScreenTiles % (2 * kAccStages) == 0, "each stage is used an even number of times per item");
 static_assert(kScreenTiles % kStages == 0, "a work item's Golay tiles fill the ring a whole number of times");
@@ -233,16 +234,16 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Slow path of wait_bar.  Gives up after kWaitLimitNs or when another role of
+// Slow path of wait_bar.  Gives up after `limit` ns or when another role of
 // the CTA has aborted; on a timeout it raises the CTA abort flag and the
 // device error word.
 __device__ __noinline__ bool wait_slow(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                       int *err) {
+                                       int *err, unsigned long long limit) {
   const unsigned long long t0 = global_ns();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit) {
       *abort_flag = 1;
       atomicExch(err, H24_ERR_TIMEOUT);
       return false;
@@ -252,9 +253,9 @@ __device__ __noinline__ bool wait_slow(uint64_t *bar, uint32_t parity, volatile 
 
 // Waits for the phase of `bar` with the given parity (inline fast path).
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                         int *err) {
+                                         int *err, unsigned long long limit) {
   if (mbar_test(bar, parity)) return true;
-  return wait_slow(bar, parity, abort_flag, err);
+  return wait_slow(bar, parity, abort_flag, err, limit);
 }
 
 // One arrival on `bar` from lane 0 of a converged warp: a predicated
@@ -271,9 +272,9 @@ __device__ __forceinline__ void mbar_arrive_lane0(uint64_t *bar, int lane) {
 // wait_bar for a whole converged warp, every lane polling (no divergent
 // region); the result is the same on all lanes.
 __device__ __forceinline__ bool wait_bar_warp(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                              int *err) {
+                                              int *err, unsigned long long limit) {
   if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
-  return __all_sync(0xffffffffu, wait_slow(bar, parity, abort_flag, err));
+  return __all_sync(0xffffffffu, wait_slow(bar, parity, abort_flag, err, limit));
 }
 
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
@@ -404,20 +405,54 @@ __device__ __forceinline__ float max32(float m, const uint32_t *r) {
 // 1. prep
 // ---------------------------------------------------------------------------
 // Input atoms of one pipeline batch: segment i holds atoms [start[i],
-// start[i+1]) of the batch, stored contiguously at x[i] (24 fp32 per atom).
+// start[i+1]) of the batch, stored contiguously at x[i] (24 elements per
+// atom, all of the batch's element type: fp32, or bf16 widened exactly to
+// fp32 on load, as the reference's weight.float() does, pack.py:159).
 struct Segs {
-  const float *x[kMaxSegs];
+  const void *x[kMaxSegs];
   int64_t start[kMaxSegs + 1];
   int count;
 };
 
-__device__ __forceinline__ const float *atom_ptr(const Segs &sg, int64_t a) {
+template <typename T>
+__device__ __forceinline__ const T *atom_ptr(const Segs &sg, int64_t a) {
   int lo = 0, hi = sg.count - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (sg.start[mid] <= a) lo = mid; else hi = mid - 1;
   }
-  return sg.x[lo] + (a - sg.start[lo]) * kDim;
+  return static_cast<const T *>(sg.x[lo]) + (a - sg.start[lo]) * kDim;
+}
+
+// 16-byte chunks of one atom of element type T (6 for fp32, 3 for bf16).
+template <typename T>
+constexpr int atom_chunks() { return static_cast<int>(kDim * sizeof(T) / 16); }
+
+// bf16 bit pattern (low 16 bits of h) widened to fp32: exact.
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t h) { return __uint_as_float(h << 16); }
+
+// The 24 coordinates of an atom as fp32, from 16-byte loads; `stream` marks
+// data read once (evict-first loads).
+template <typename T, bool stream>
+__device__ __forceinline__ void load_atom_t(const T *__restrict__ p, float (&v)[kDim]) {
+  const uint4 *src = reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+  for (int q = 0; q < atom_chunks<T>(); ++q) {
+    const uint4 u = stream ? __ldcs(src + q) : __ldg(src + q);
+    if constexpr (sizeof(T) == 4) {
+      v[4 * q + 0] = __uint_as_float(u.x);
+      v[4 * q + 1] = __uint_as_float(u.y);
+      v[4 * q + 2] = __uint_as_float(u.z);
+      v[4 * q + 3] = __uint_as_float(u.w);
+    } else {
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[8 * q + 2 * k] = bf16_bits_to_float(w[k] & 0xFFFFu);
+        v[8 * q + 2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+      }
+    }
+  }
 }
 
 // Byte offset of M-tile lane L, 16-byte K chunk q in an A tile (UMMA
@@ -430,6 +465,7 @@ __device__ __forceinline__ uint32_t a_offset(int L, int q) {
 // Atom a of work item w = a / 64 sits in M-tile g = (a / 32) % 2 at lane
 // 32 * quarter_of_row(g, r) + a % 32 for row type r (0 slice p1, 1 slice p2,
 // 2 plain, 3 |x|).
+template <typename T>
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
                                                    int64_t n_pad,
                                                    const uint2 *__restrict__ oct_by_triple,
@@ -442,15 +478,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   if (a >= n_pad) return;
   float v[kDim];
   if (a < n) {
-    const float4 *src = reinterpret_cast<const float4 *>(atom_ptr(sg, a));
-#pragma unroll
-    for (int q = 0; q < 6; ++q) {
-      const float4 f = __ldcs(src + q);
-      v[4 * q + 0] = f.x;
-      v[4 * q + 1] = f.y;
-      v[4 * q + 2] = f.z;
-      v[4 * q + 3] = f.w;
-    }
+    load_atom_t<T, true>(atom_ptr<T>(sg, a), v);
   } else {
 #pragma unroll
     for (int i = 0; i < kDim; ++i) v[i] = 0.f;
@@ -593,6 +621,8 @@ struct ScreenArgs {
   int64_t n;
   int64_t items;
   int *err;
+  unsigned long long wait_limit_ns;  // limit of every bounded wait
+  int stall_tile;  // test hook: CTA 0 leaves this Golay tile of its first item unloaded (-1: none)
 };
 
 __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenArgs args) {
@@ -647,13 +677,19 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       for (int s = 0; s < kStages; ++s) last_b[s] = -1;
       bool ok = true;
       for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
-        if (!wait_bar(&S.bar_a_empty[ab], aph ^ 1, abort_flag, args.err)) { ok = false; break; }
+        if (!wait_bar(&S.bar_a_empty[ab], aph ^ 1, abort_flag, args.err, args.wait_limit_ns)) { ok = false; break; }
         mbar_arrive_expect_tx(&S.bar_a_full[ab], kAItemBytes);
         bulk_g2s(S.a[ab], args.a_tiles + it * kAItemBytes, kAItemBytes, &S.bar_a_full[ab], once);
         last_a[ab] = static_cast<int>(aph);
         if (++ab == 2) { ab = 0; aph ^= 1; }
         for (int t = 0; t < kScreenTiles; ++t) {
-          if (!wait_bar(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err)) { ok = false; break; }
+          if (!wait_bar(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err, args.wait_limit_ns)) { ok = false; break; }
+          if (t == args.stall_tile && it == 0) {
+            // Test hook: this tile's barrier is never signalled, so the waits
+            // behind it run out, exercising the timeout path.
+            if (++bs == kStages) { bs = 0; bph ^= 1; }
+            continue;
+          }
           mbar_arrive_expect_tx(&S.bar_b_full[bs], kBTileBytes);
           bulk_g2s(S.b[bs], args.golay + t * kBTileBytes, kBTileBytes, &S.bar_b_full[bs], keep);
           last_b[bs] = static_cast<int>(bph);
@@ -666,12 +702,12 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         for (int s = 0; s < kStages; ++s)
           if (last_b[s] >= 0)
             while (!mbar_try_wait(&S.bar_b_full[s], static_cast<uint32_t>(last_b[s])) &&
-                   global_ns() - t0 < kWaitLimitNs) {
+                   global_ns() - t0 < args.wait_limit_ns) {
             }
         for (int i = 0; i < 2; ++i)
           if (last_a[i] >= 0)
             while (!mbar_try_wait(&S.bar_a_full[i], static_cast<uint32_t>(last_a[i])) &&
-                   global_ns() - t0 < kWaitLimitNs) {
+                   global_ns() - t0 < args.wait_limit_ns) {
             }
       }
     }
@@ -691,13 +727,13 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     uint32_t bph = 0, aph = 0;
     bool ok = true, issued = false;
     for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
-      if (!wait_bar_warp(&S.bar_a_full[ab], aph, abort_flag, args.err)) { ok = false; break; }
+      if (!wait_bar_warp(&S.bar_a_full[ab], aph, abort_flag, args.err, args.wait_limit_ns)) { ok = false; break; }
       tc_fence_after();
       const uint64_t ad = smem_desc(a0 + static_cast<uint32_t>(ab * kAItemBytes + g * kATileBytes));
       for (int t = 0; t < kScreenTiles; ++t) {
         const int s = t & 1;
-        if (!wait_bar_warp(&S.bar_b_full[bs], bph, abort_flag, args.err) ||
-            !wait_bar_warp(&S.bar_acc_empty[g][s], ((t >> 1) & 1) ^ 1, abort_flag, args.err)) {
+        if (!wait_bar_warp(&S.bar_b_full[bs], bph, abort_flag, args.err, args.wait_limit_ns) ||
+            !wait_bar_warp(&S.bar_acc_empty[g][s], ((t >> 1) & 1) ^ 1, abort_flag, args.err, args.wait_limit_ns)) {
           ok = false;
           break;
         }
@@ -718,7 +754,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       // All MMAs of this CTA complete before TMEM is released.
       mma_commit(&S.bar_final[g]);
       const unsigned long long t0 = global_ns();
-      while (!mbar_try_wait(&S.bar_final[g], 0) && global_ns() - t0 < kWaitLimitNs) {
+      while (!mbar_try_wait(&S.bar_final[g], 0) && global_ns() - t0 < args.wait_limit_ns) {
       }
       __syncwarp();
     }
@@ -746,7 +782,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
 #pragma unroll 1
       for (int t = 0; t < kScreenTiles; ++t) {
         const int s = t & 1;
-        if (!wait_bar_warp(&S.bar_acc_full[g][s], (t >> 1) & 1, abort_flag, args.err)) {
+        if (!wait_bar_warp(&S.bar_acc_full[g][s], (t >> 1) & 1, abort_flag, args.err, args.wait_limit_ns)) {
           ok = false;
           break;
         }
@@ -789,7 +825,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       S.rowval[ip][local][r] = rowmax;
       __syncwarp();
       mbar_arrive_lane0(&S.bar_rows[g][ip], lane);
-      if (!wait_bar_warp(&S.bar_rows[g][ip], (rph >> ip) & 1u, abort_flag, args.err)) {
+      if (!wait_bar_warp(&S.bar_rows[g][ip], (rph >> ip) & 1u, abort_flag, args.err, args.wait_limit_ns)) {
         ok = false;
         break;
       }
@@ -857,18 +893,6 @@ __device__ __forceinline__ void better(double &bs, int &bj, double s, int j) {
   if (s > bs || (s == bs && j < bj)) {
     bs = s;
     bj = j;
-  }
-}
-
-__device__ __forceinline__ void load_atom(const float *__restrict__ p, float (&v)[kDim]) {
-  const float4 *src = reinterpret_cast<const float4 *>(p);
-#pragma unroll
-  for (int q = 0; q < 6; ++q) {
-    const float4 f = __ldg(src + q);
-    v[4 * q] = f.x;
-    v[4 * q + 1] = f.y;
-    v[4 * q + 2] = f.z;
-    v[4 * q + 3] = f.w;
   }
 }
 
@@ -1007,6 +1031,7 @@ __device__ __noinline__ void exact_now(const float (&x)[kDim], const int8_t *__r
 // in fp64, in the reference's order, the listed codewords within 2 e' of the
 // largest S', e' = 2^-16 sum|x|, which bounds |S' - sqrt(8) R| with a wide
 // margin; the winner and every codeword tied with it are among them.
+template <typename In>
 __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     rescore_kernel(const __grid_constant__ Segs sg, const RescoreArgs r) {
   __shared__ float tab[kRescoreWarps][3][256];
@@ -1024,14 +1049,18 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   float(*T)[256] = tab[w];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
   uint32_t st_exh = 0, st_exact = 0, st_chunks = 0;
-  // Lanes 0-10 copy one 16-byte chunk each of atom a's stage.
+  // Lanes 0-10 copy one 16-byte chunk each of atom a's stage (a bf16 atom
+  // fills only the first three chunks of the coordinates, as bit patterns,
+  // and is widened in place once it has landed).
+  constexpr int kXChunks = atom_chunks<In>();
   const auto prefetch = [&](int64_t a, int s) {
     if (a < r.n) {
-      const uint4 *xa = reinterpret_cast<const uint4 *>(atom_ptr(sg, a));
+      const uint4 *xa = reinterpret_cast<const uint4 *>(atom_ptr<In>(sg, a));
       const uint4 *src = lane < 6 ? xa + lane
                                   : (lane < 8 ? r.masks + 2 * a + (lane - 6)
                                               : reinterpret_cast<const uint4 *>(r.info + a) + (lane - 8));
-      if (lane < 11) cp_async16(reinterpret_cast<uint4 *>(&stage[w][s]) + lane, src);
+      if (lane < 11 && (lane < kXChunks || lane >= 6))
+        cp_async16(reinterpret_cast<uint4 *>(&stage[w][s]) + lane, src);
     }
     cp_async_commit();
   };
@@ -1044,6 +1073,14 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     prefetch(a + nwarps, sb ^ 1);
     cp_async_wait1();
     __syncwarp();
+    if constexpr (sizeof(In) == 2) {
+      // Widen the 24 bf16 patterns at the start of the coordinates in place.
+      float *xs = stage[w][sb].x;
+      const uint32_t h = lane < kDim ? reinterpret_cast<const uint16_t *>(xs)[lane] : 0u;
+      __syncwarp();
+      if (lane < kDim) xs[lane] = bf16_bits_to_float(h);
+      __syncwarp();
+    }
     const AtomStage &A = stage[w][sb];
     const float(&v)[kDim] = A.x;  // the atom, read from the stage when needed
     const float xl = lane < kDim ? A.x[lane] : 0.f;  // lane i: x_i
@@ -1307,6 +1344,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   }
 }
 
+template <typename T>
 __global__ void __launch_bounds__(256) exhaustive_kernel(const __grid_constant__ Segs sg, int rule,
                                                          const int32_t *__restrict__ ovf_list,
                                                          const int32_t *__restrict__ ovf_count,
@@ -1318,7 +1356,7 @@ __global__ void __launch_bounds__(256) exhaustive_kernel(const __grid_constant__
   for (int e = blockIdx.x; e < count; e += gridDim.x) {
     const int64_t a = ovf_list[e];
     float v[kDim];
-    load_atom(atom_ptr(sg, a), v);
+    load_atom_t<T, false>(atom_ptr<T>(sg, a), v);
     double bs = -INFINITY;
     int bj = 0x7FFFFFFF;
     for (int j = threadIdx.x; j < kKissing; j += blockDim.x)
@@ -1358,6 +1396,18 @@ __global__ void __launch_bounds__(256) decode_kernel(int32_t *__restrict__ out, 
 std::mutex g_mu;
 int g_sms[64] = {};
 
+// Limit of the screen's bounded waits, and the number of coming screening
+// launches that leave one Golay tile unloaded (h24_debug_stall_screen).
+std::atomic<unsigned long long> g_wait_limit_ns{kWaitLimitNs};
+std::atomic<int> g_stall_launches{0};
+
+int take_stall() {
+  int n = g_stall_launches.load();
+  while (n > 0 && !g_stall_launches.compare_exchange_weak(n, n - 1)) {
+  }
+  return n > 0 ? 3 : -1;
+}
+
 // Per-atom scratch of one pipeline batch of up to `pad` atoms.
 struct Scratch {
   uint8_t *a_tiles;
@@ -1388,40 +1438,53 @@ Scratch carve(uint8_t *base, int64_t pad) {
 }
 
 // The five kernels of one batch (the overflow counter must be zero).
-int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int32_t *ob,
-                 const Scratch &sc, int sms, cudaStream_t s) {
+template <typename T>
+int launch_batch_t(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int32_t *ob,
+                   const Scratch &sc, int sms, cudaStream_t s) {
   const int64_t items = (nbatch + kWorkAtoms - 1) / kWorkAtoms;
   const int64_t npad = items * kWorkAtoms;
-  prep_kernel<<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(
+  // Optional instrumentation: events around the prep, screen and rescore.
+  const bool timed = timing_enabled();
+  cudaEvent_t ev[6] = {};
+  if (timed)
+    for (auto &e : ev) cudaEventCreate(&e);
+  if (timed) cudaEventRecord(ev[0], s);
+  prep_kernel<T><<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(
       sg, nbatch, npad, t->oct_by_triple, sc.a_tiles, sc.info);
+  if (timed) cudaEventRecord(ev[1], s);
   ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
-                nbatch, items, t->err};
+                nbatch, items, t->err, g_wait_limit_ns.load(), take_stall()};
   const int grid = static_cast<int>(items < sms ? items : sms);
-  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-  if (timing_enabled()) {
-    cudaEventCreate(&ev0);
-    cudaEventCreate(&ev1);
-    cudaEventRecord(ev0, s);
-  }
+  if (timed) cudaEventRecord(ev[2], s);
   screen_kernel<<<grid, kScreenThreads, sizeof(ScreenSmem) + 1024, s>>>(sa);
-  if (ev1) {
-    cudaEventRecord(ev1, s);
-    timing_record(ev0, ev1);
-  }
+  if (timed) cudaEventRecord(ev[3], s);
   RescoreArgs ra{reinterpret_cast<const uint4 *>(sc.masks), sc.info, t->golay_mask, t->idx3,
                  t->idx2, t->idx1, t->cb_raw, ob, sc.ovf_list, sc.ovf_count, t->stats, nbatch,
                  rule};
   const int64_t rblocks = (nbatch + kRescoreWarps - 1) / kRescoreWarps;
   const int64_t rcap = static_cast<int64_t>(sms) * kRescoreBlocksPerSm;
-  rescore_kernel<<<static_cast<unsigned>(rblocks < rcap ? rblocks : rcap), 32 * kRescoreWarps,
-                   kGolay * sizeof(uint32_t), s>>>(sg, ra);
-  exhaustive_kernel<<<2 * sms, 256, 0, s>>>(sg, rule, sc.ovf_list, sc.ovf_count, t->cb_raw, ob);
+  if (timed) cudaEventRecord(ev[4], s);
+  rescore_kernel<T><<<static_cast<unsigned>(rblocks < rcap ? rblocks : rcap), 32 * kRescoreWarps,
+                      kGolay * sizeof(uint32_t), s>>>(sg, ra);
+  if (timed) {
+    cudaEventRecord(ev[5], s);
+    timing_record(H24_KERNEL_PREP, ev[0], ev[1]);
+    timing_record(H24_KERNEL_SCREEN, ev[2], ev[3]);
+    timing_record(H24_KERNEL_RESCORE, ev[4], ev[5]);
+  }
+  exhaustive_kernel<T><<<2 * sms, 256, 0, s>>>(sg, rule, sc.ovf_list, sc.ovf_count, t->cb_raw, ob);
   const int64_t dblocks = (nbatch + 255) / 256;
   decode_kernel<<<static_cast<unsigned>(dblocks < 8 * sms ? dblocks : 8 * sms), 256, 0, s>>>(
       ob, nbatch, t->idx3, t->idx2, t->idx1);
   count_launches(5);
   H24_CUDA_TRY(cudaGetLastError());
   return H24_OK;
+}
+
+int launch_batch(const Tables *t, const Segs &sg, int64_t nbatch, int dtype, int rule, int32_t *ob,
+                 const Scratch &sc, int sms, cudaStream_t s) {
+  return dtype == H24_DTYPE_BF16 ? launch_batch_t<__nv_bfloat16>(t, sg, nbatch, rule, ob, sc, sms, s)
+                                 : launch_batch_t<float>(t, sg, nbatch, rule, ob, sc, sms, s);
 }
 
 int screen_setup(int dev, int *sms) {
@@ -1431,14 +1494,21 @@ int screen_setup(int dev, int *sms) {
     H24_CUDA_TRY(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
     H24_CUDA_TRY(cudaFuncSetAttribute(screen_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(sizeof(ScreenSmem) + 1024)));
-    H24_CUDA_TRY(cudaFuncSetAttribute(rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    H24_CUDA_TRY(cudaFuncSetAttribute(rescore_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(kGolay * sizeof(uint32_t))));
+    H24_CUDA_TRY(cudaFuncSetAttribute(rescore_kernel<__nv_bfloat16>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(kGolay * sizeof(uint32_t))));
     // Launch sizes against what each kernel's resources allow.
     const struct { const void *fn; int threads; const char *name; } ks[] = {
         {reinterpret_cast<const void *>(screen_kernel), kScreenThreads, "screen_kernel"},
-        {reinterpret_cast<const void *>(rescore_kernel), 32 * kRescoreWarps, "rescore_kernel"},
-        {reinterpret_cast<const void *>(prep_kernel), 256, "prep_kernel"},
-        {reinterpret_cast<const void *>(exhaustive_kernel), 256, "exhaustive_kernel"},
+        {reinterpret_cast<const void *>(rescore_kernel<float>), 32 * kRescoreWarps, "rescore_kernel"},
+        {reinterpret_cast<const void *>(rescore_kernel<__nv_bfloat16>), 32 * kRescoreWarps,
+         "rescore_kernel(bf16)"},
+        {reinterpret_cast<const void *>(prep_kernel<float>), 256, "prep_kernel"},
+        {reinterpret_cast<const void *>(prep_kernel<__nv_bfloat16>), 256, "prep_kernel(bf16)"},
+        {reinterpret_cast<const void *>(exhaustive_kernel<float>), 256, "exhaustive_kernel"},
+        {reinterpret_cast<const void *>(exhaustive_kernel<__nv_bfloat16>), 256, "exhaustive_kernel(bf16)"},
         {reinterpret_cast<const void *>(decode_kernel), 256, "decode_kernel"}};
     for (const auto &k : ks) {
       cudaFuncAttributes at;
@@ -1456,8 +1526,11 @@ int screen_setup(int dev, int *sms) {
 
 }  // namespace
 
-int quantize_segments(const Tables *t, const float *const *xs, const int64_t *counts, int nseg,
-                      int rule, int32_t *out_idx, cudaStream_t s) {
+int quantize_segments(const Tables *t, const void *const *xs, const int64_t *counts, int nseg,
+                      int dtype, int rule, int32_t *out_idx, cudaStream_t s) {
+  if (dtype != H24_DTYPE_F32 && dtype != H24_DTYPE_BF16)
+    return fail(H24_ERR_INVALID, "quantize: atoms must be fp32 or bf16");
+  const size_t esize = dtype == H24_DTYPE_BF16 ? 2 : 4;
   int64_t total = 0;
   for (int i = 0; i < nseg; ++i) {
     if (counts[i] < 0) return fail(H24_ERR_INVALID, "quantize: negative segment length");
@@ -1489,7 +1562,7 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
       const int64_t avail = counts[seg] - seg_off;
       if (avail <= 0) { ++seg; seg_off = 0; continue; }
       const int64_t take = avail < batch - nbatch ? avail : batch - nbatch;
-      sg.x[sg.count] = xs[seg] + seg_off * kDim;
+      sg.x[sg.count] = static_cast<const uint8_t *>(xs[seg]) + static_cast<size_t>(seg_off) * kDim * esize;
       nbatch += take;
       sg.start[++sg.count] = nbatch;
       seg_off += take;
@@ -1497,7 +1570,7 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
     }
     cudaError_t e = cudaMemsetAsync(sc.ovf_count, 0, sizeof(int32_t), s);
     if (e != cudaSuccess) { rc = cuda_fail(e, "memset"); break; }
-    rc = launch_batch(t, sg, nbatch, rule, out_idx + done, sc, sms, s);
+    rc = launch_batch(t, sg, nbatch, dtype, rule, out_idx + done, sc, sms, s);
     done += nbatch;
   }
   cudaError_t e = cudaFreeAsync(scratch, s);
@@ -1507,7 +1580,8 @@ int quantize_segments(const Tables *t, const float *const *xs, const int64_t *co
 
 int quantize(const Tables *t, const float *x, int64_t n, int rule, int32_t *out_idx,
              cudaStream_t s) {
-  return quantize_segments(t, &x, &n, 1, rule, out_idx, s);
+  const void *xv = x;
+  return quantize_segments(t, &xv, &n, 1, H24_DTYPE_F32, rule, out_idx, s);
 }
 
 // ===========================================================================
@@ -1579,7 +1653,7 @@ int quantize_noalloc(const Tables *t, const float *x, int64_t n, int rule, int32
   const Scratch sc = carve(scratch, kNoAllocMaxAtoms);
   // The array keeps the previous call's contents: clear the overflow counter.
   H24_CUDA_TRY(cudaMemsetAsync(sc.ovf_count, 0, sizeof(int32_t), s));
-  return launch_batch(t, sg, n, rule, out_idx, sc, sms, s);
+  return launch_batch(t, sg, n, H24_DTYPE_F32, rule, out_idx, sc, sms, s);
 }
 
 }  // namespace
@@ -1604,4 +1678,12 @@ extern "C" int h24_quantize_noalloc(const float *x, int64_t n, int rule, int32_t
                 "quantize_noalloc: codebook tables are not resident on this device; call "
                 "h24_init(device) once at set-up (it allocates them)");
   return quantize_noalloc(t, x, n, rule, out_idx, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h24_debug_stall_screen(int launches, uint64_t wait_limit_ns) {
+  using namespace h24;
+  if (launches < 0) return fail(H24_ERR_INVALID, "debug_stall_screen: negative launch count");
+  g_wait_limit_ns.store(wait_limit_ns ? static_cast<unsigned long long>(wait_limit_ns) : kWaitLimitNs);
+  g_stall_launches.store(launches);
+  return H24_OK;
 }

@@ -41,9 +41,13 @@ def shard_rows(rows: int, in_features: int, world: int, rank: int) -> tuple[int,
 
 
 def packed_range(start: int, end: int, in_features: int) -> tuple[int, int]:
-    """Byte range of rows [start, end) in the packed stream of the whole matrix."""
+    """Byte range of rows [start, end) in the packed stream of the whole matrix
+    (empty for an empty shard, placed at the end of the rows before it)."""
     apr = in_features // H24_DIM
     a0, a1 = start * apr, end * apr
+    if end <= start:
+        b = (a1 + 3) // 4 * BYTES_PER_CHUNK
+        return b, b
     if a0 % 4 != 0:
         raise ValueError("shard does not start on a 4-index group")
     return a0 // 4 * BYTES_PER_CHUNK, (a1 + 3) // 4 * BYTES_PER_CHUNK
@@ -56,15 +60,17 @@ def quantize_layer_sharded(weight: torch.Tensor, world: int = 1, rank: int = 0, 
 
     Returns (packed_shard, sigma_shard, (start, end)) or, with gather=True, the
     whole matrix's (packed, sigma) assembled on every rank.  ``quantize`` maps
-    a 2-D weight to (packed u8, sigma16); the default is the libh24 pipeline
-    (pollux_b200.pack.quantize_layer_device)."""
+    a 2-D block of rows to (packed u8, sigma16); the default is the libh24
+    row-range pipeline (pollux_b200.pack.quantize_layer_rows), which reads the
+    rows in place and computes their scales with the whole matrix's reduction
+    order, so the shards carry exactly the single-GPU bytes."""
     rows, in_f = weight.shape
     start, end = shard_rows(rows, in_f, world, rank)
-    if quantize is None:
-        from .pack import quantize_layer_device as quantize
-    part = weight[start:end]
-    if end > start:
-        packed, sigma = quantize(part)
+    if end > start and quantize is None:
+        from .pack import quantize_layer_rows
+        packed, sigma = quantize_layer_rows([(weight, start, end)])[0]
+    elif end > start:
+        packed, sigma = quantize(weight[start:end])
     else:
         packed = torch.zeros(0, dtype=torch.uint8, device=weight.device)
         sigma = torch.zeros(0, dtype=torch.float16, device=weight.device)

@@ -62,8 +62,14 @@ def backbone_weights(config: int, device="cuda", seed: int | None = None,
     return out
 
 
-def stress_atoms(n: int, codebook_f32: torch.Tensor, seed: int = 3, device="cpu") -> torch.Tensor:
-    """[n, 24] fp32 config-4 atoms.  ``codebook_f32`` is the [196561, 24] table."""
+STRESS_CATEGORIES = ("codeword", "near_origin", "midpoint", "isotropic")
+
+
+def stress_atoms(n: int, codebook_f32: torch.Tensor, seed: int = 3, device="cpu",
+                 return_category: bool = False):
+    """[n, 24] fp32 config-4 atoms.  ``codebook_f32`` is the [196561, 24] table.
+    With return_category, also the category of each atom (an index into
+    STRESS_CATEGORIES)."""
     g = _gen(seed, device)
     cb = codebook_f32.to(device=device, dtype=torch.float32)
     cat = torch.randint(0, 10, (n,), generator=g, device=device)
@@ -80,8 +86,11 @@ def stress_atoms(n: int, codebook_f32: torch.Tensor, seed: int = 3, device="cpu"
     midpoint = (cb[i1] + cb[i2]) * 0.5
     out = torch.where((cat < 4)[:, None], near_codeword,
           torch.where((cat < 6)[:, None], near_origin,
-          torch.where((cat < 8)[:, None], midpoint, iso)))
-    return out.contiguous()
+          torch.where((cat < 8)[:, None], midpoint, iso))).contiguous()
+    if return_category:
+        category = torch.where(cat < 4, 0, torch.where(cat < 6, 1, torch.where(cat < 8, 2, 3)))
+        return out, category
+    return out
 
 
 def config5_layer(seed: int = 5, device="cuda", shape=CONFIG5_SHAPE):
