@@ -300,15 +300,6 @@ int64_t h24_launch_count(void);
  * screening kernel ran out (the word is then cleared), else H24_OK. */
 int h24_check(void *stream);
 
-/* Test hook for the failure path (no counterpart in the reference, which has
- * no bounded waits): the next `launches` screening launches leave one Golay
- * tile of their first work item unloaded, so the waits behind it run out.
- * `wait_limit_ns` becomes the limit of every bounded wait of the screen from
- * now on (0 restores the default of 4 s).  A stalled launch drains its copies
- * and tensor-core work, frees its TMEM and returns; its atoms' indices are
- * then meaningless and h24_check (or a synchronising call) reports
- * H24_ERR_TIMEOUT.  No fault, trap or endless wait is involved. */
-int h24_debug_stall_screen(int launches, uint64_t wait_limit_ns);
 
 #ifdef __cplusplus
 }

@@ -63,7 +63,6 @@ SIGNATURES = {
     "h24_timing_read_kernel": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]),
     "h24_quantize_stats": (_I, [ctypes.POINTER(ctypes.c_int64)] * 3 + [_P]),
     "h24_check": (_I, [_P]),
-    "h24_debug_stall_screen": (_I, [_I, ctypes.c_uint64]),
 }
 
 

@@ -68,7 +68,6 @@
 // rescore.  The type-2 contribution to `best` is max_O 2 T~(O) - 4 |x|_(8),
 // |x|_(8) the 8th largest |x_i|: flipping the sign of the smallest |x_i| of
 // O, which is at most |x|_(8), repairs the parity of any octad.
-#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -622,7 +621,6 @@ struct ScreenArgs {
   int64_t items;
   int *err;
   unsigned long long wait_limit_ns;  // limit of every bounded wait
-  int stall_tile;  // test hook: CTA 0 leaves this Golay tile of its first item unloaded (-1: none)
 };
 
 __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenArgs args) {
@@ -684,12 +682,6 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         if (++ab == 2) { ab = 0; aph ^= 1; }
         for (int t = 0; t < kScreenTiles; ++t) {
           if (!wait_bar(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err, args.wait_limit_ns)) { ok = false; break; }
-          if (t == args.stall_tile && it == 0) {
-            // Test hook: this tile's barrier is never signalled, so the waits
-            // behind it run out, exercising the timeout path.
-            if (++bs == kStages) { bs = 0; bph ^= 1; }
-            continue;
-          }
           mbar_arrive_expect_tx(&S.bar_b_full[bs], kBTileBytes);
           bulk_g2s(S.b[bs], args.golay + t * kBTileBytes, kBTileBytes, &S.bar_b_full[bs], keep);
           last_b[bs] = static_cast<int>(bph);
@@ -1396,17 +1388,6 @@ __global__ void __launch_bounds__(256) decode_kernel(int32_t *__restrict__ out, 
 std::mutex g_mu;
 int g_sms[64] = {};
 
-// Limit of the screen's bounded waits, and the number of coming screening
-// launches that leave one Golay tile unloaded (h24_debug_stall_screen).
-std::atomic<unsigned long long> g_wait_limit_ns{kWaitLimitNs};
-std::atomic<int> g_stall_launches{0};
-
-int take_stall() {
-  int n = g_stall_launches.load();
-  while (n > 0 && !g_stall_launches.compare_exchange_weak(n, n - 1)) {
-  }
-  return n > 0 ? 3 : -1;
-}
 
 // Per-atom scratch of one pipeline batch of up to `pad` atoms.
 struct Scratch {
@@ -1453,7 +1434,7 @@ int launch_batch_t(const Tables *t, const Segs &sg, int64_t nbatch, int rule, in
       sg, nbatch, npad, t->oct_by_triple, sc.a_tiles, sc.info);
   if (timed) cudaEventRecord(ev[1], s);
   ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
-                nbatch, items, t->err, g_wait_limit_ns.load(), take_stall()};
+                nbatch, items, t->err, kWaitLimitNs};
   const int grid = static_cast<int>(items < sms ? items : sms);
   if (timed) cudaEventRecord(ev[2], s);
   screen_kernel<<<grid, kScreenThreads, sizeof(ScreenSmem) + 1024, s>>>(sa);
@@ -1678,12 +1659,4 @@ extern "C" int h24_quantize_noalloc(const float *x, int64_t n, int rule, int32_t
                 "quantize_noalloc: codebook tables are not resident on this device; call "
                 "h24_init(device) once at set-up (it allocates them)");
   return quantize_noalloc(t, x, n, rule, out_idx, static_cast<cudaStream_t>(stream));
-}
-
-extern "C" int h24_debug_stall_screen(int launches, uint64_t wait_limit_ns) {
-  using namespace h24;
-  if (launches < 0) return fail(H24_ERR_INVALID, "debug_stall_screen: negative launch count");
-  g_wait_limit_ns.store(wait_limit_ns ? static_cast<unsigned long long>(wait_limit_ns) : kWaitLimitNs);
-  g_stall_launches.store(launches);
-  return H24_OK;
 }
