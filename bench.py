@@ -482,37 +482,52 @@ def run_ours(args) -> None:
 
 
 def run_e2e(args, weights, shapes, ranges, dev, world) -> dict:
-    """The same step through the public API with host buffers: bf16 weights in
-    page-locked host memory, each matrix through the drop-in
-    pack._quantize_h24_layer (one GPU; it returns host tensors, as the
-    reference does) or, on N ranks, pack.quantize_layer_rows_host for this
-    rank's rows; the host-to-device copies of the weights and the copies of
-    the packed bytes and scales back are inside the timed region."""
+    """The same step through the public API with host buffers: the bf16
+    backbone as a model state_dict in page-locked host memory, packed by
+    pack.quantize_state_dict (pack_checkpoint's tensor loop, pack.py:268-287:
+    packed bytes and fp16 scales returned as host tensors) on one GPU, or on
+    N ranks pack.quantize_layers_host for this rank's rows of every matrix;
+    the host-to-device copies of the weights and the copies of the outputs
+    back are inside the timed region.  The per-matrix drop-in
+    pack._quantize_h24_layer loop is timed too, for context."""
     import torch
     from pollux_b200 import castor, pack
-    cb = castor.get_h24_codebook("cpu", torch.float32)
+    names = [f"layers.{l}.{m}.weight" for l in range(len(shapes) // 4) for m in ("qkv", "o", "up", "down")]
     host_w = [w.cpu().pin_memory() for w in weights]
+    state = dict(zip(names, host_w))
     torch.cuda.synchronize()
 
     def e2e_step():
         if world == 1:
-            return [pack._quantize_h24_layer(w, cb) for w in host_w]
-        return [pack.quantize_layer_rows_host(w, r0, r1) for w, (r0, r1) in zip(host_w, ranges)]
+            out = pack.quantize_state_dict(state)
+            return [(out[n.replace(".weight", ".packed_weights")], out[n.replace(".weight", ".sigma_rows")])
+                    for n in names]
+        return pack.quantize_layers_host([(w, r0, r1) for w, (r0, r1) in zip(host_w, ranges)])
 
-    for _ in range(max(1, min(args.warmup, 2))):
-        e2e_step()
+    def timed(fn, steps):
+        for _ in range(max(1, min(args.warmup, 2))):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            res = fn()
+        return (time.perf_counter() - t0) / steps, res
+
     steps = max(1, min(args.steps, 5))
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        res = e2e_step()
-    dt = (time.perf_counter() - t0) / steps
+    dt, res = timed(e2e_step, steps)
+    per_matrix = None
+    if world == 1:
+        cb = castor.get_h24_codebook("cpu", torch.float32)
+        dtm, res_m = timed(lambda: [pack._quantize_h24_layer(w, cb) for w in host_w], min(steps, 3))
+        assert all(torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]) for a, b in zip(res, res_m))
+        per_matrix = {"api": "pack._quantize_h24_layer per matrix (bf16 host weights)", "ms_per_step": dtm * 1e3}
     h2d = sum((r1 - r0) * i * 2 for (r0, r1), (o, i) in zip(ranges, shapes))
     d2h = sum(p.numel() + s.numel() * 2 for p, s in res)
-    del host_w
+    del host_w, state
     return {"unit": "G atoms/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": dt * 1e3, "steps": steps,
-            "api": ("pollux_b200.pack._quantize_h24_layer per matrix (bf16 host weights)" if world == 1
-                    else "pollux_b200.pack.quantize_layer_rows_host per matrix, this rank's rows")}
+            "api": ("pollux_b200.pack.quantize_state_dict on the 72-matrix bf16 state_dict" if world == 1
+                    else "pollux_b200.pack.quantize_layers_host, this rank's rows of every matrix"),
+            "per_matrix_drop_in": per_matrix}
 
 
 def run_stress(args, dev):

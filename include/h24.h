@@ -257,13 +257,16 @@ typedef struct h24_layer_rows {
  * a host array read before the call returns. */
 int h24_quantize_layer_rows(const h24_layer_rows *layers, int count, int dtype, void *stream);
 
-/* One row range of a weight in HOST memory (pack._quantize_h24_layer on a CPU
- * weight, pack.py:139-180, which returns host tensors): the rows are copied
- * in chunks whose transfer overlaps the search of the previous chunk, and
- * sigma16_out / packed_out (host memory) are written before the call returns.
- * Returns H24_ERR_TIMEOUT if a bounded wait of the screening kernel ran out
- * (the outputs are then incomplete). */
-int h24_quantize_layer_rows_host(const h24_layer_rows *layer, int dtype, void *stream);
+/* Row ranges of weights in HOST memory, outputs in host memory
+ * (pack._quantize_h24_layer on CPU weights, pack.py:139-180, which returns
+ * host tensors; count > 1 runs the H24 branch of pack_checkpoint's whole loop,
+ * pack.py:268-283, as one pipeline).  The rows are copied in chunks whose
+ * transfer overlaps the search of the previous chunk, across matrix
+ * boundaries (page-locked host weights give the overlap; pageable ones work
+ * too), and every sigma16_out / packed_out is written before the call
+ * returns.  Returns H24_ERR_TIMEOUT if a bounded wait of the screening kernel
+ * ran out (the outputs are then incomplete). */
+int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dtype, void *stream);
 
 /* ---- codeword gather (index_select of castor.py:533, 559) ---------------
  * out[a][0..23] = codebook[idx[a]] converted to `dtype` (H24_DTYPE_*). */

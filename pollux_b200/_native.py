@@ -54,7 +54,7 @@ SIGNATURES = {
     "h24_quantize_layers": (_I, [_P, _I, _P]),
     "h24_quantize_typed": (_I, [_P, _I64, _I, _I, _P, _P]),
     "h24_quantize_layer_rows": (_I, [_P, _I, _I, _P]),
-    "h24_quantize_layer_rows_host": (_I, [_P, _I, _P]),
+    "h24_quantize_layer_rows_host": (_I, [_P, _I, _I, _P]),
     "h24_row_rms": (_I, [_P, _I64, _I64, _I, _P, _P, _P]),
     "h24_launch_count": (ctypes.c_int64, []),
     "h24_gather_codewords": (_I, [_P, _I64, _I, _P, _P]),

@@ -645,81 +645,116 @@ int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16
   return h24_quantize_layers(&L, 1, stream);
 }
 
-// Host-memory form: the range's rows are cut into chunks of whole 4-atom pack
-// groups; chunk k+1 is copied host-to-device on the copy stream while chunk k
-// is searched on the caller's stream; the row scales run once the last chunk
-// has landed, and both outputs come back before the call returns.
-int h24_quantize_layer_rows_host(const h24_layer_rows *layer, int dtype, void *stream) {
+// Host-memory form over many row ranges, one pipeline for all of them.  Each
+// range is cut into chunks of whole rows that end on 4-atom groups; chunk k
+// is copied host-to-device into one of kHostSlots device slots on the copy
+// stream while the caller's stream quantises chunk k-1 (row scales with the
+// whole matrix's plan, search, 18-bit pack into the range's device output),
+// across range boundaries, so the transfer hides behind the search.  All
+// outputs come back to the host at the end; the call returns once they are
+// written.
+static constexpr int kHostSlots = 3;
+static constexpr int64_t kHostChunkAtoms = 294912;
+
+int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dtype, void *stream) {
   H24_TABLES_OR_FAIL(T);
-  if (!layer) return fail(H24_ERR_INVALID, "quantize_layer_host: null layer");
+  if (count < 0 || (count > 0 && !layers)) return fail(H24_ERR_INVALID, "quantize_layer_host: bad list");
   if (dtype != H24_DTYPE_F32 && dtype != H24_DTYPE_BF16)
     return fail(H24_ERR_INVALID, "quantize_layer_host: weights must be fp32 or bf16");
   const size_t esize = dtype == H24_DTYPE_BF16 ? 2 : 4;
-  RowRange RR;
-  int rc = validate_rows(*layer, esize, true, &RR);
-  if (rc != H24_OK) return rc;
-  if (RR.r1 == RR.r0) return H24_OK;
-  cudaStream_t s = as_stream(stream);
-  const int64_t in_features = RR.in, rows = RR.r1 - RR.r0;
-  const uint8_t *w = RR.w + static_cast<size_t>(RR.r0 * in_features) * esize;
-  const int64_t atoms = rows * in_features / kDim;
-  const size_t packed_bytes = static_cast<size_t>((atoms + 3) / 4) * 9;
-  // Chunk rows: a multiple of rg rows holds a whole number of 4-atom groups.
-  int64_t g = in_features, h = 96;
-  while (h) { const int64_t t2 = g % h; g = h; h = t2; }
-  const int64_t rg = 96 / g;
-  constexpr int64_t kChunkAtoms = 73728;
-  int64_t crows = (kChunkAtoms * kDim / in_features) / rg * rg;
-  if (crows < rg) crows = rg;
+  std::vector<RowRange> R(count);
+  for (int i = 0; i < count; ++i) {
+    int rc = validate_rows(layers[i], esize, true, &R[i]);
+    if (rc != H24_OK) return rc;
+  }
   auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
-  // The device copy keeps the rows' alignment within 16 bytes of the whole
-  // matrix (the row scales' summation order depends on it).
-  const size_t lead = (static_cast<size_t>(RR.r0 * in_features) * esize) & 15u;
-  const size_t off_sig = up(lead + static_cast<size_t>(rows * in_features) * esize);
-  const size_t off_pk = off_sig + up(static_cast<size_t>(rows) * 2);
-  const size_t off_idx = off_pk + up(packed_bytes);
+  // Chunks: (range, first row, rows).
+  struct Chunk { int li; int64_t c0, c1; };
+  std::vector<Chunk> chunks;
+  std::vector<size_t> out_pk(count), out_sig(count);
+  size_t out_bytes = 0, slot_elems = 0;
+  for (int i = 0; i < count; ++i) {
+    const RowRange &r = R[i];
+    out_pk[i] = out_bytes;
+    out_bytes += up(static_cast<size_t>((r.atoms() + 3) / 4) * 9);
+    out_sig[i] = out_bytes;
+    out_bytes += up(static_cast<size_t>(r.r1 - r.r0) * 2);
+    if (r.r1 == r.r0) continue;
+    int64_t g = r.in, h = 96;
+    while (h) { const int64_t t2 = g % h; g = h; h = t2; }
+    const int64_t rg = 96 / g;  // rows per whole number of 4-atom groups
+    int64_t crows = (kHostChunkAtoms * kDim / r.in) / rg * rg;
+    if (crows < rg) crows = rg;
+    for (int64_t c0 = r.r0; c0 < r.r1; c0 += crows) {
+      const int64_t c1 = c0 + crows < r.r1 ? c0 + crows : r.r1;
+      chunks.push_back({i, c0, c1});
+      slot_elems = std::max(slot_elems, static_cast<size_t>((c1 - c0) * r.in));
+    }
+  }
+  if (chunks.empty()) return H24_OK;
+  cudaStream_t s = as_stream(stream);
+  const size_t slot_bytes = up(slot_elems * esize);
+  const size_t idx_bytes = up(slot_elems / kDim * 4);
+  const size_t off_slots = up(out_bytes);
+  const size_t off_idx = off_slots + kHostSlots * slot_bytes;
   uint8_t *buf = nullptr;
-  H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&buf),
-                                       off_idx + up(static_cast<size_t>(atoms) * 4), T->pool, s));
-  uint8_t *wd = buf + lead;
-  uint16_t *sig = reinterpret_cast<uint16_t *>(buf + off_sig);
-  uint8_t *pk = buf + off_pk;
-  int32_t *idx = reinterpret_cast<int32_t *>(buf + off_idx);
+  H24_CUDA_TRY(cudaMallocFromPoolAsync(reinterpret_cast<void **>(&buf), off_idx + kHostSlots * idx_bytes,
+                                       T->pool, s));
   std::vector<cudaEvent_t> evs;
+  int rc = H24_OK;
   auto event = [&](cudaEvent_t *e) -> int {
     cudaError_t ce = cudaEventCreateWithFlags(e, cudaEventDisableTiming);
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaEventCreate");
     evs.push_back(*e);
     return H24_OK;
   };
-  // The copy stream starts after the buffer exists on the caller's stream.
-  cudaEvent_t ready;
+  cudaEvent_t ready = nullptr, copied[kHostSlots] = {}, freed[kHostSlots] = {};
   rc = event(&ready);
+  for (int k = 0; k < kHostSlots && rc == H24_OK; ++k) {
+    rc = event(&copied[k]);
+    if (rc == H24_OK) rc = event(&freed[k]);
+  }
+  // The copy stream starts after the buffer exists on the caller's stream.
   if (rc == H24_OK) {
     cudaError_t ce = cudaEventRecord(ready, s);
     if (ce == cudaSuccess) ce = cudaStreamWaitEvent(T->copy_stream, ready, 0);
     if (ce != cudaSuccess) rc = cuda_fail(ce, "copy stream order");
   }
-  for (int64_t r0 = 0; r0 < rows && rc == H24_OK; r0 += crows) {
-    const int64_t nr = rows - r0 < crows ? rows - r0 : crows;
-    const int64_t e0 = r0 * in_features;
-    const int64_t a0 = e0 / kDim, na = nr * in_features / kDim;
-    cudaEvent_t copied;
-    rc = event(&copied);
-    if (rc != H24_OK) break;
-    cudaError_t ce = cudaMemcpyAsync(wd + e0 * esize, w + e0 * esize, static_cast<size_t>(nr * in_features) * esize,
-                                     cudaMemcpyHostToDevice, T->copy_stream);
-    if (ce == cudaSuccess) ce = cudaEventRecord(copied, T->copy_stream);
-    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s, copied, 0);
+  for (size_t k = 0; k < chunks.size() && rc == H24_OK; ++k) {
+    const Chunk &c = chunks[k];
+    const RowRange &r = R[c.li];
+    const int sl = static_cast<int>(k % kHostSlots);
+    uint8_t *slot = buf + off_slots + sl * slot_bytes;
+    int32_t *idx = reinterpret_cast<int32_t *>(buf + off_idx + sl * idx_bytes);
+    const int64_t nrow = c.c1 - c.c0, na = nrow * r.in / kDim;
+    // Copy into the slot once the chunk that used it before is quantised.
+    cudaError_t ce = cudaSuccess;
+    if (k >= static_cast<size_t>(kHostSlots)) ce = cudaStreamWaitEvent(T->copy_stream, freed[sl], 0);
+    if (ce == cudaSuccess)
+      ce = cudaMemcpyAsync(slot, r.w + static_cast<size_t>(c.c0 * r.in) * esize,
+                           static_cast<size_t>(nrow * r.in) * esize, cudaMemcpyHostToDevice, T->copy_stream);
+    if (ce == cudaSuccess) ce = cudaEventRecord(copied[sl], T->copy_stream);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s, copied[sl], 0);
     if (ce != cudaSuccess) { rc = cuda_fail(ce, "chunk copy"); break; }
-    const void *xs = wd + e0 * esize;
-    rc = quantize_segments(T, &xs, &na, 1, dtype, H24_RULE_PACK, idx + a0, s);
-    if (rc == H24_OK) rc = launch_pack_i32(idx + a0, na, pk + a0 / 4 * 9, s);
+    uint16_t *sig = reinterpret_cast<uint16_t *>(buf + out_sig[c.li]) + (c.c0 - r.r0);
+    uint8_t *pk = buf + out_pk[c.li] + static_cast<size_t>((c.c0 - r.r0) * r.in / kDim / 4) * 9;
+    rc = launch_row_rms(slot, dtype, nrow, r.in, r.rows, c.c0, nullptr, sig, s);
+    const void *xs = slot;
+    if (rc == H24_OK) rc = quantize_segments(T, &xs, &na, 1, dtype, H24_RULE_PACK, idx, s);
+    if (rc == H24_OK) rc = launch_pack_i32(idx, na, pk, s);
+    if (rc == H24_OK) {
+      ce = cudaEventRecord(freed[sl], s);
+      if (ce != cudaSuccess) rc = cuda_fail(ce, "slot release");
+    }
   }
-  if (rc == H24_OK) rc = launch_row_rms(wd, dtype, rows, in_features, RR.rows, RR.r0, nullptr, sig, s);
-  if (rc == H24_OK) {
-    cudaError_t ce = cudaMemcpyAsync(RR.sigma16, sig, static_cast<size_t>(rows) * 2, cudaMemcpyDeviceToHost, s);
-    if (ce == cudaSuccess) ce = cudaMemcpyAsync(RR.packed, pk, packed_bytes, cudaMemcpyDeviceToHost, s);
+  for (int i = 0; i < count && rc == H24_OK; ++i) {
+    const RowRange &r = R[i];
+    if (r.r1 == r.r0) continue;
+    cudaError_t ce = cudaMemcpyAsync(r.sigma16, buf + out_sig[i], static_cast<size_t>(r.r1 - r.r0) * 2,
+                                     cudaMemcpyDeviceToHost, s);
+    if (ce == cudaSuccess)
+      ce = cudaMemcpyAsync(r.packed, buf + out_pk[i], static_cast<size_t>((r.atoms() + 3) / 4) * 9,
+                           cudaMemcpyDeviceToHost, s);
     if (ce != cudaSuccess) rc = cuda_fail(ce, "output copy");
   }
   // Every copy-stream operation is ordered before the free (also after an
@@ -743,7 +778,7 @@ int h24_quantize_layer_rows_host(const h24_layer_rows *layer, int dtype, void *s
 int h24_quantize_layer_host(const float *w, int64_t rows, int64_t in_features, uint16_t *sigma16_out,
                             uint8_t *packed_out, void *stream) {
   h24_layer_rows L{w, rows, in_features, 0, rows, sigma16_out, packed_out};
-  return h24_quantize_layer_rows_host(&L, H24_DTYPE_F32, stream);
+  return h24_quantize_layer_rows_host(&L, 1, H24_DTYPE_F32, stream);
 }
 
 int h24_gather_codewords(const int32_t *idx, int64_t n, int dtype, void *out, void *stream) {

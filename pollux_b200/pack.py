@@ -57,7 +57,8 @@ def _quantize_h24_layer(weight: torch.Tensor, codebook: torch.Tensor) -> tuple[t
         sigma = torch.empty(rows, dtype=torch.float16, pin_memory=pin)
         if rows:
             L = N.LayerRows(w.data_ptr(), rows, in_f, 0, rows, sigma.data_ptr(), packed.data_ptr())
-            _call(dev, "h24_quantize_layer_rows_host", ctypes.byref(L), _LAYER_DTYPES[w.dtype], _stream(dev))
+            _call(dev, "h24_quantize_layer_rows_host", ctypes.byref(L), 1, _LAYER_DTYPES[w.dtype],
+                  _stream(dev))
         return packed, sigma
     packed, sigma = quantize_layer_device(w)
     packed, sigma = packed.cpu(), sigma.cpu()
@@ -127,18 +128,98 @@ def quantize_layer_rows_host(weight: torch.Tensor, row_begin: int, row_end: int
     """Rows [row_begin, row_end) of a HOST weight (fp32 or bf16, contiguous)
     to host (packed u8, sigma16): only those rows cross PCIe, in chunks that
     overlap the search (page-locked outputs when the weight is pinned)."""
-    w = weight.detach()
-    if w.device.type != "cpu" or w.dtype not in _LAYER_DTYPES or not w.is_contiguous() or w.dim() != 2:
-        raise ValueError("quantize_layer_rows_host wants a contiguous 2-D fp32 or bf16 host tensor")
-    rows, in_f = w.shape
-    atoms = (row_end - row_begin) * in_f // H24_DIM
-    pin = w.is_pinned()
-    packed = torch.empty(((atoms + 3) // 4) * BYTES_PER_CHUNK, dtype=torch.uint8, pin_memory=pin)
-    sigma = torch.empty(max(row_end - row_begin, 0), dtype=torch.float16, pin_memory=pin)
-    dev = _work_device(w)
-    L = N.LayerRows(w.data_ptr(), rows, in_f, row_begin, row_end, sigma.data_ptr(), packed.data_ptr())
-    _call(dev, "h24_quantize_layer_rows_host", ctypes.byref(L), _LAYER_DTYPES[w.dtype], _stream(dev))
-    return packed, sigma
+    return quantize_layers_host([(weight, row_begin, row_end)])[0]
+
+
+def quantize_layers_host(parts: list[tuple[torch.Tensor, int, int]]) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """Rows [begin, end) of each HOST weight (contiguous 2-D fp32 or bf16, all
+    of one dtype) to host (packed u8, sigma16), in one pipeline: the copy of
+    each chunk of rows overlaps the search of the previous one across matrix
+    boundaries (page-locked weights give the overlap).  The outputs are the
+    bytes and scales _quantize_h24_layer returns for those rows."""
+    if not parts:
+        return []
+    dtypes = {w.dtype for w, _, _ in parts}
+    if len(dtypes) != 1 or next(iter(dtypes)) not in _LAYER_DTYPES:
+        raise ValueError("quantize_layers_host wants fp32 or bf16 host weights of one dtype")
+    code = _LAYER_DTYPES[next(iter(dtypes))]
+    dev = _work_device(parts[0][0])
+    layers, outs = [], []
+    for (w, r0, r1) in parts:
+        w = w.detach()
+        if w.device.type != "cpu" or not w.is_contiguous() or w.dim() != 2:
+            raise ValueError("quantize_layers_host wants contiguous 2-D host tensors")
+        rows, in_f = w.shape
+        atoms = max(r1 - r0, 0) * in_f // H24_DIM
+        pin = w.is_pinned()
+        packed = torch.empty(((atoms + 3) // 4) * BYTES_PER_CHUNK, dtype=torch.uint8, pin_memory=pin)
+        sigma = torch.empty(max(r1 - r0, 0), dtype=torch.float16, pin_memory=pin)
+        layers.append(N.LayerRows(w.data_ptr(), rows, in_f, r0, r1, sigma.data_ptr(), packed.data_ptr()))
+        outs.append((packed, sigma))
+    arr = (N.LayerRows * len(layers))(*layers)
+    _call(dev, "h24_quantize_layer_rows_host", ctypes.cast(arr, ctypes.c_void_p), len(layers), code,
+          _stream(dev))
+    return outs
+
+
+def _is_packable_h24(name: str, tensor: torch.Tensor) -> bool:
+    """pack._is_packable_h24 (pack.py:111-117): hidden H24 weight matrices
+    (``*.weight``, >= 2-D, a multiple of 24 elements), not tok_emb, pos_emb or
+    head."""
+    if not name.endswith(".weight"):
+        return False
+    if name.startswith(("tok_emb.", "pos_emb.", "head.")):
+        return False
+    return tensor.dim() >= 2 and tensor.numel() > 0 and tensor.numel() % H24_DIM == 0
+
+
+def quantize_state_dict(state_in: dict, codebook: torch.Tensor | None = None) -> dict:
+    """The tensor loop of pack_checkpoint (pack.py:268-287) on a model
+    state_dict: tok_emb / head to INT8 + fp16 mu (``.weight_int8``,
+    ``.mu_rows``), every packable H24 matrix to packed 18-bit indices + fp16
+    row scales (``.packed_weights``, ``.sigma_rows``), everything else passed
+    through on the host; the entries keep the reference's names and order.
+    All H24 matrices of one dtype go through one pipelined call
+    (host-resident ones overlap their transfer with the search); the result
+    equals _quantize_h24_layer per matrix."""
+    if codebook is not None:
+        _check_codebook(codebook)
+    out: dict = {}
+    h24_names = [n for n, t in state_in.items()
+                 if n not in ("tok_emb.weight", "head.weight") and _is_packable_h24(n, t)]
+    mats = {n: state_in[n].detach() for n in h24_names}
+    for n, m in mats.items():
+        if m.dim() != 2:  # row_rms_from_matrix raises the same (castor.py:311)
+            raise ValueError(f"row_rms_from_matrix expects a 2D weight matrix, got {m.dim()}D.")
+    results: dict = {}
+    host_groups: dict = {}
+    device_list = []
+    for n in h24_names:
+        m = mats[n]
+        if m.device.type == "cpu" and m.dtype in _LAYER_DTYPES and m.is_contiguous():
+            host_groups.setdefault(m.dtype, []).append(n)
+        else:
+            device_list.append(n)
+    for names in host_groups.values():
+        for n, r in zip(names, quantize_layers_host([(mats[n], 0, mats[n].shape[0]) for n in names])):
+            results[n] = r
+    if device_list:
+        res = quantize_layers([mats[n] for n in device_list])
+        for n, (p, s) in zip(device_list, res):
+            results[n] = (p.cpu(), s.cpu())
+        device_check(res[0][0].device)
+    for name, tensor in state_in.items():
+        if name in ("tok_emb.weight", "head.weight"):
+            q, mu = _quantize_int8(tensor)
+            out[name.replace(".weight", ".weight_int8")] = q
+            out[name.replace(".weight", ".mu_rows")] = mu
+        elif name in results:
+            p, s = results[name]
+            out[name.replace(".weight", ".packed_weights")] = p
+            out[name.replace(".weight", ".sigma_rows")] = s
+        else:
+            out[name] = tensor.detach().cpu()
+    return out
 
 
 def quantize_int8_device(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

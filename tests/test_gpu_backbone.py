@@ -116,3 +116,51 @@ def test_row_range_validation(mods):
     (p, s), = P.quantize_layer_rows([(w, 4, 16)])
     whole_p, whole_s = P.quantize_layers([w])[0]
     assert torch.equal(p, whole_p[27:]) and torch.equal(s, whole_s[4:])
+
+
+def test_state_dict_loop_equals_per_matrix_calls(mods):
+    """pack_checkpoint's tensor loop (pack.py:268-287) through
+    quantize_state_dict: every H24 matrix of the (host) state_dict in one
+    pipelined call, INT8 for tok_emb / head, pass-through for the rest; each
+    output equals the per-matrix drop-in call."""
+    C, P, SH, _ = mods
+    g = torch.Generator().manual_seed(5)
+    state = {
+        "tok_emb.weight": torch.randn(300, 192, generator=g) * 0.02,
+        "pos_emb.weight": torch.randn(64, 192, generator=g) * 0.02,
+        "layers.0.qkv.weight": (torch.randn(576, 192, generator=g) * 0.02).to(torch.bfloat16).pin_memory(),
+        "layers.0.o.weight": (torch.randn(192, 192, generator=g) * 0.02).to(torch.bfloat16).pin_memory(),
+        "layers.0.norm.gain": torch.ones(192),
+        "layers.0.up.weight": torch.randn(768, 192, generator=g) * 0.02,        # fp32, pageable
+        "layers.0.down.weight": (torch.randn(192, 768, generator=g) * 0.02).cuda(),  # on the GPU
+        "layers.1.big.weight": (torch.randn(7000, 1920, generator=g) * 0.02).to(torch.bfloat16),
+        "head.weight": torch.randn(300, 192, generator=g) * 0.02,
+    }
+    cb = C.get_h24_codebook("cpu", torch.float32)
+    out = P.quantize_state_dict(state, cb)
+    assert list(out) == ["tok_emb.weight_int8", "tok_emb.mu_rows", "pos_emb.weight",
+                         "layers.0.qkv.packed_weights", "layers.0.qkv.sigma_rows",
+                         "layers.0.o.packed_weights", "layers.0.o.sigma_rows", "layers.0.norm.gain",
+                         "layers.0.up.packed_weights", "layers.0.up.sigma_rows",
+                         "layers.0.down.packed_weights", "layers.0.down.sigma_rows",
+                         "layers.1.big.packed_weights", "layers.1.big.sigma_rows",
+                         "head.weight_int8", "head.mu_rows"]
+    for n, t in state.items():
+        base = n[:-len(".weight")]
+        if n in ("tok_emb.weight", "head.weight"):
+            q, mu = P._quantize_int8(t)
+            assert torch.equal(out[base + ".weight_int8"], q) and torch.equal(out[base + ".mu_rows"], mu)
+        elif n.endswith(".weight") and n != "pos_emb.weight":
+            p, s = P._quantize_h24_layer(t, cb)
+            assert torch.equal(out[base + ".packed_weights"], p.cpu())
+            assert torch.equal(out[base + ".sigma_rows"], s.cpu())
+            assert out[base + ".packed_weights"].device.type == "cpu"
+        else:
+            assert torch.equal(out[n], t)
+    # Row ranges of several host matrices in one pipeline.
+    ws = [state["layers.1.big.weight"], state["layers.0.qkv.weight"]]
+    parts = [(ws[0], *SH.shard_rows(7000, 1920, 3, 1)), (ws[1], *SH.shard_rows(576, 192, 3, 2))]
+    for (w, r0, r1), (p, s) in zip(parts, P.quantize_layers_host(parts)):
+        wp, wsig = P.quantize_layers([w.cuda()])[0]
+        b0, b1 = SH.packed_range(r0, r1, w.shape[1])
+        assert torch.equal(p, wp[b0:b1].cpu()) and torch.equal(s, wsig[r0:r1].cpu())
