@@ -104,8 +104,9 @@ def test_stress_subset_tie_tolerance(oracle, golden):
 
 
 def test_bf16_fallback_differs_from_exact(oracle, golden):
-    """The reference's autocast fallback is not exact (SURVEY: 4.2 % on config 1);
-    the training-rule golden is kept as a one-sided check only."""
+    """The reference's autocast fallback is not exact (it disagrees with the
+    exact argmax on about 4.2 % of config-1 atoms); the training-rule golden is
+    kept as a one-sided check only."""
     from pollux_b200 import synth
     import torch
     c1 = golden("config1.npz")
