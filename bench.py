@@ -655,8 +655,8 @@ def run_components(args) -> dict:
     fp16 in one batched launch.  Each kernel is timed with CUDA events around
     a run of back-to-back calls that rotate over several buffer sets (pack and
     unpack: 8 sets, 552 MB; dequant: 2 sets of 531 MB of output), so no call
-    finds its inputs in L2; the run starts after an L2 flush and a short
-    device-side delay that hides the host's launch overhead."""
+    finds its inputs in L2; the calls are replayed from one CUDA graph after
+    an L2 flush, so the host's launch rate plays no part."""
     import ctypes
     import torch
     from pollux_b200 import castor, synth
@@ -681,16 +681,19 @@ def run_components(args) -> dict:
             for _ in range(2)]
     bad = torch.zeros(1, dtype=torch.int32, device=dev)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev).cuda_stream
     lib = N.load()
     per_layer_bytes = per // 4 * 9
 
+    def cur():
+        """The current stream (a capture stream while a graph is recorded)."""
+        return torch.cuda.current_stream(dev).cuda_stream
+
     def pack(k):
-        N.check(lib.h24_pack(idxs[k].data_ptr(), n, packs[k].data_ptr(), stream), "pack")
+        N.check(lib.h24_pack(idxs[k].data_ptr(), n, packs[k].data_ptr(), cur()), "pack")
 
     def unpack(k):
         N.check(lib.h24_unpack(packs[k].data_ptr(), packs[k].numel() // 9, n, backs[k].data_ptr(),
-                               stream), "unpack")
+                               cur()), "unpack")
 
     descs = []
     for k in range(2):
@@ -702,21 +705,33 @@ def run_components(args) -> dict:
 
     def dequant(k):
         N.check(lib.h24_dequant_batched(ctypes.cast(descs[k % 2], ctypes.c_void_p), layers,
-                                        bad.data_ptr(), stream), "dequant")
+                                        bad.data_ptr(), cur()), "dequant")
 
     def timed(fn, calls, reps):
+        """Median ms per call of `calls` back-to-back calls fn(0..calls-1),
+        captured once into a CUDA graph and replayed after an L2 flush."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # one eager run before capture
+            for k in range(calls):
+                fn(k)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for k in range(calls):
+                fn(k)
         ts = []
         for i in range(reps + 2):
             flush.fill_(i & 0xFF)
-            torch.cuda._sleep(200_000)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            for k in range(calls):
-                fn(k)
+            g.replay()
             e1.record()
             e1.synchronize()
             if i >= 2:
                 ts.append(e0.elapsed_time(e1) / calls)
+        del g
         return statistics.median(ts)
 
     # INT8 token embedding (PolluxConfig defaults: vocab 50688 x n_embd 1920),
@@ -729,11 +744,11 @@ def run_components(args) -> dict:
 
     def int8_quant(k):
         N.check(lib.h24_int8_quantize(emb_w[k].data_ptr(), vocab, d, emb_q[k].data_ptr(),
-                                      emb_mu[k].data_ptr(), stream), "int8_quantize")
+                                      emb_mu[k].data_ptr(), cur()), "int8_quantize")
 
     def int8_deq(k):
         N.check(lib.h24_int8_dequant(emb_q[k].data_ptr(), emb_mu[k].data_ptr(), vocab, d,
-                                     emb_out[k].data_ptr(), stream), "int8_dequant")
+                                     emb_out[k].data_ptr(), cur()), "int8_dequant")
 
     # Decode through the 18 config-5 layers: LUT GEMV straight from the packed
     # bytes vs a dense fp16 GEMV (cuBLAS) on the materialised weights.
@@ -746,13 +761,15 @@ def run_components(args) -> dict:
             for l in range(layers):
                 N.check(lib.h24_lut_gemv(packs[k].data_ptr() + l * per_layer_bytes, sig_l[l].data_ptr(),
                                          rows, in_f, xs[b].data_ptr(), b, ys[b].data_ptr(),
-                                         bad.data_ptr(), stream), "lut_gemv")
+                                         bad.data_ptr(), cur()), "lut_gemv")
         return run
+
+    ys16 = {b: torch.empty(b, rows, dtype=torch.float16, device=dev) for b in (1, 8)}
 
     def dense_sweep(b):
         def run(k):
             for l in range(layers):
-                torch.matmul(x16[b], outs[k % 2][l].t())
+                torch.matmul(x16[b], outs[k % 2][l].t(), out=ys16[b])
         return run
 
     reps = max(3, args.steps)
@@ -793,8 +810,9 @@ def run_components(args) -> dict:
         res[name] = {"ms": t, "algorithmic_bytes": b, "GB_per_s": gbs, "frac_of_measured_hbm": gbs / peak}
     wbytes = layers * rows * in_f * 2
     res["lut_gemv"] = {
-        "what": "y = x @ W.T through all 18 config-5 layers, W never materialised (fp32); "
-                "against torch.matmul of the materialised fp16 weights (cuBLAS)",
+        "what": "y = x @ W.T through all 18 config-5 layers, W never materialised (fp32 x, "
+                "fp32 products); against torch.matmul of the materialised fp16 weights (cuBLAS); "
+                "both sweeps replayed from CUDA graphs",
         "batch1_ms": t_lut1, "batch8_ms": t_lut8,
         "dense_fp16_batch1_ms": t_dense1, "dense_fp16_batch8_ms": t_dense8,
         "dense_equivalent_GB_per_s_batch1": wbytes / (t_lut1 / 1e3) / 1e9,

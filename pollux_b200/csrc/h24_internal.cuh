@@ -111,6 +111,27 @@ int cuda_fail(cudaError_t e, const char *what);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Blocks of `kernel` that one SM holds at once (at least 1).
+template <typename K>
+int blocks_per_sm(K kernel, int threads, size_t dyn_smem) {
+  int per = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, dyn_smem) != cudaSuccess ||
+      per < 1)
+    per = 1;
+  return per;
+}
+
+// Grid of at most one resident wave (SMs x `per_sm` blocks), fewer when the
+// work needs fewer blocks: a grid-stride kernel then finishes in one wave
+// instead of leaving a partial second one.
+inline int wave_grid(int64_t want_blocks, int per_sm) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t cap = static_cast<int64_t>(sms) * per_sm;
+  return static_cast<int>(want_blocks < 1 ? 1 : (want_blocks < cap ? want_blocks : cap));
+}
+
 // Host-side raw codebook generation (h24_codebook.cpp).  out: [kKissing][24].
 bool build_raw_kissing_points(int8_t *out, std::string *err);
 

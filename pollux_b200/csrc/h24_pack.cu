@@ -261,16 +261,13 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const uint8_t *__restr
 }
 
 // Enough warps for the vector tiles (or for one thread per remaining group),
-// capped at 8 blocks per SM.
-int grid_for(int64_t tiles, int64_t rest_groups) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+// capped at one resident wave of `kernel`.
+template <typename K>
+int grid_for(K kernel, int64_t tiles, int64_t rest_groups) {
   int64_t want = (tiles + kWarps - 1) / kWarps;
   const int64_t rest = (rest_groups + kThreads - 1) / kThreads;
   if (rest > want) want = rest;
-  const int64_t cap = static_cast<int64_t>(sms) * 8;
-  return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
+  return wave_grid(want, blocks_per_sm(kernel, kThreads, 0));
 }
 
 template <typename T>
@@ -279,7 +276,7 @@ int launch_pack(const T *idx, int64_t n, uint8_t *out, cudaStream_t s) {
   const bool fast = aligned16(idx) && aligned16(out);
   const int64_t tiles = fast ? n / kWarpIndices : 0;
   const int64_t rest = (n + 3) / 4 - tiles * kWarpGroups;
-  pack_kernel<T><<<grid_for(tiles, rest), kThreads, 0, s>>>(idx, n, out, fast);
+  pack_kernel<T><<<grid_for(pack_kernel<T>, tiles, rest), kThreads, 0, s>>>(idx, n, out, fast);
   H24_CUDA_TRY(cudaGetLastError());
   count_launches(1);
   return H24_OK;
@@ -292,8 +289,8 @@ int launch_unpack(const uint8_t *p, int64_t groups, int64_t n, T *out, cudaStrea
   const int64_t used = (n + 3) / 4 < groups ? (n + 3) / 4 : groups;
   int64_t tiles = 0;
   if (fast) tiles = n / kWarpIndices < groups / kWarpGroups ? n / kWarpIndices : groups / kWarpGroups;
-  unpack_kernel<T><<<grid_for(tiles, used - tiles * kWarpGroups), kThreads, 0, s>>>(p, groups, n,
-                                                                                   out, fast);
+  unpack_kernel<T><<<grid_for(unpack_kernel<T>, tiles, used - tiles * kWarpGroups), kThreads, 0, s>>>(
+      p, groups, n, out, fast);
   H24_CUDA_TRY(cudaGetLastError());
   count_launches(1);
   return H24_OK;

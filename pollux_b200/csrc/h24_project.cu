@@ -88,13 +88,10 @@ __global__ void __launch_bounds__(kThreads) project_store_kernel(const __grid_co
   }
 }
 
-int grid_for(int64_t work, int per_block) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = (work + per_block - 1) / per_block;
-  const int64_t cap = static_cast<int64_t>(sms) * 8;
-  return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
+// One resident wave of `kernel`, or fewer blocks when the work needs fewer.
+template <typename K>
+int grid_for(K kernel, int64_t work, int per_block) {
+  return wave_grid((work + per_block - 1) / per_block, blocks_per_sm(kernel, kThreads, 0));
 }
 
 }  // namespace
@@ -135,7 +132,7 @@ int project_layers(const Tables *t, const h24_project_layer *layers, int count, 
     }
     cudaError_t le = cudaSuccess;
     if (rc == H24_OK) {
-      project_prep_kernel<<<grid_for(rows, kWarps), kThreads, 0, s>>>(b, sigma, xs);
+      project_prep_kernel<<<grid_for(project_prep_kernel, rows, kWarps), kThreads, 0, s>>>(b, sigma, xs);
       le = cudaGetLastError();
       if (le != cudaSuccess) rc = cuda_fail(le, "project_prep launch");
     }
@@ -144,7 +141,7 @@ int project_layers(const Tables *t, const h24_project_layer *layers, int count, 
       rc = quantize(t, xs, atoms, H24_RULE_TRAIN, idx, s);
     }
     if (rc == H24_OK) {
-      project_store_kernel<<<grid_for(atoms * 3, kThreads), kThreads, 0, s>>>(b, sigma, idx, t->cb_raw);
+      project_store_kernel<<<grid_for(project_store_kernel, atoms * 3, kThreads), kThreads, 0, s>>>(b, sigma, idx, t->cb_raw);
       le = cudaGetLastError();
       if (le != cudaSuccess) rc = cuda_fail(le, "project_store launch");
       else count_launches(1);

@@ -57,6 +57,30 @@ def test_large_and_odd_shapes_against_oracle(mods, oracle, shape):
     assert np.array_equal(w16.cpu().numpy().view(np.uint16), oracle.int8_dequant(qo, muo).view(np.uint16))
 
 
+@pytest.mark.parametrize("cols", [1920, 4608])
+def test_near_ties(mods, oracle, cols):
+    """Elements at and around every rounding boundary of w / mu * 127: the
+    kernel's product with fp32(127 / mu) must round like the reference's
+    quotient-then-product on both sides of each half-integer (1920: the
+    register path; 4608: the two-pass path)."""
+    pack, _ = mods
+    rows = 512
+    g = np.random.default_rng(cols)
+    mu = g.uniform(1e-3, 1.0, rows).astype(np.float32)
+    k = g.integers(-127, 127, (rows, cols)).astype(np.float64)
+    delta = g.choice([0.0, 1e-7, -1e-7, 3e-6, -3e-6, 3e-5, -3e-5, 1e-4, -1e-4, 0.25], (rows, cols))
+    w = ((k + 0.5 + delta) * mu[:, None].astype(np.float64) / 127.0).astype(np.float32)
+    # fp32 neighbours of the boundaries, and the row maximum itself.
+    w[:, ::7] = np.nextafter(w[:, ::7], np.float32(np.inf))
+    w[:, 1::7] = np.nextafter(w[:, 1::7], np.float32(-np.inf))
+    w[:, 3] = mu
+    w[:, 5] = -mu
+    q, m = pack.quantize_int8_device(torch.from_numpy(w).cuda())
+    qo, mo = oracle.int8_quantize(w)
+    assert np.array_equal(m.cpu().numpy().view(np.uint16), mo.view(np.uint16))
+    assert np.array_equal(q.cpu().numpy(), qo)
+
+
 def test_unaligned_views(mods, oracle):
     pack, pl = mods
     base = torch.randn(65 * 96 + 1, device="cuda")
