@@ -825,6 +825,48 @@ def run_components(args) -> dict:
     return res
 
 
+def run_lut_only(args) -> None:
+    """Profile mode: the LUT GEMV alone through the 18 config-5 layers (one
+    25 MB packed set, fp32 x of batch --lut-batch), CUDA events around
+    --steps eager sweeps after --warmup sweeps; prints one JSON line."""
+    import torch
+    from pollux_b200 import castor, synth
+    from pollux_b200 import _native as N
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layers = 18
+    rows, in_f = synth.CONFIG5_SHAPE
+    packs, sigs = [], []
+    for l in range(layers):
+        i, sg = synth.config5_layer(seed=5 + l, device=dev)
+        packs.append(castor.pack_indices(i))
+        sigs.append(sg)
+    b = args.lut_batch
+    x = torch.randn(b, in_f, device=dev)
+    y = torch.empty(b, rows, device=dev)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = N.load()
+    st = torch.cuda.current_stream(dev).cuda_stream
+
+    def sweep():
+        for l in range(layers):
+            N.check(lib.h24_lut_gemv(packs[l].data_ptr(), sigs[l].data_ptr(), rows, in_f, x.data_ptr(), b,
+                                     y.data_ptr(), bad.data_ptr(), st), "lut_gemv")
+
+    for _ in range(args.warmup):
+        sweep()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        sweep()
+    e1.record()
+    e1.synchronize()
+    assert int(bad.item()) == 0
+    print(json.dumps({"lut_gemv_batch": b, "layers": layers, "shape": [rows, in_f],
+                      "ms_per_sweep": e0.elapsed_time(e1) / args.steps}), flush=True)
+
+
 def main():
     # libh24 is built from this checkout's sources (incremental; a no-op when
     # the library is current).
@@ -844,8 +886,13 @@ def main():
     ap.add_argument("--components", action="store_true",
                     help="time the HBM-bound kernels (pack/unpack/dequant) on config 5 only")
     ap.add_argument("--skip-components", action="store_true")
+    ap.add_argument("--lut-only", action="store_true",
+                    help="profile mode: time only the LUT GEMV sweep over the config-5 layers")
+    ap.add_argument("--lut-batch", type=int, default=1)
     args = ap.parse_args()
-    if args.search_atoms:
+    if args.lut_only:
+        run_lut_only(args)
+    elif args.search_atoms:
         run_search_only(args)
     elif args.components:
         print(json.dumps(run_components(args)), flush=True)

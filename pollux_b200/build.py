@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_lib")
 BUILD_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(OUT_DIR, "libh24.so")
-SOURCES = ["h24_capi.cu", "h24_pack.cu", "h24_dequant.cu", "h24_int8.cu", "h24_project.cu", "h24_rowrms.cu", "h24_search.cu", "h24_codebook.cpp"]
+SOURCES = ["h24_capi.cu", "h24_pack.cu", "h24_dequant.cu", "h24_lut.cu", "h24_int8.cu", "h24_project.cu", "h24_rowrms.cu", "h24_search.cu", "h24_codebook.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
                      "--expt-relaxed-constexpr", "-Werror", "all-warnings"]

@@ -388,7 +388,7 @@ static cudaStream_t as_stream(void *s) { return static_cast<cudaStream_t>(s); }
 
 // Reads the device error word of T's device after the work on `s` (which it
 // synchronises) and clears it: H24_ERR_TIMEOUT if a bounded wait inside the
-// screening kernel ran out, else H24_OK.
+// screening kernel or the LUT GEMV ran out, else H24_OK.
 static int take_device_error(const Tables *T, cudaStream_t s) {
   int err = 0;
   H24_CUDA_TRY(cudaMemcpyAsync(&err, T->err, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -396,7 +396,7 @@ static int take_device_error(const Tables *T, cudaStream_t s) {
   if (err != 0) {
     H24_CUDA_TRY(cudaMemsetAsync(T->err, 0, sizeof(int), s));
     H24_CUDA_TRY(cudaStreamSynchronize(s));
-    return fail(H24_ERR_TIMEOUT, "a bounded wait in the screening kernel ran out");
+    return fail(H24_ERR_TIMEOUT, "a bounded wait in a tensor-core kernel ran out");
   }
   return H24_OK;
 }

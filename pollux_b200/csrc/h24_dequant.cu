@@ -1,7 +1,6 @@
-// h24_dequant.cu -- LUT dequantisation of packed H24 layers (pollux.py:485-500),
-// the matrix-free LUT GEMV over packed layers (README "future native kernel",
-// README.md:88, 155-156) and the codeword gather of castor_quantize_leech's
-// output (castor.py:533).
+// h24_dequant.cu -- LUT dequantisation of packed H24 layers (pollux.py:485-500)
+// and the codeword gather of castor_quantize_leech's output (castor.py:533).
+// The matrix-free LUT GEMV over the same code table is in h24_lut.cu.
 //
 // Dequant: every weight element of row r takes one of nine fp16 values,
 //   F(v, r) = fp16( fp32( fp16(cb16[v] * sigma16[r]) ) * 0.70710677f ),
@@ -47,14 +46,6 @@ struct WarpSmem {
 };
 static_assert(offsetof(WarpSmem, lists) % 8 == 0 && sizeof(WarpSmem) % 16 == 0,
               "value lists are read as 8-byte pairs");
-
-__device__ __forceinline__ uint16_t dequant_value(int raw, uint16_t sigma_bits) {
-  const __half cb = __float2half_rn(static_cast<float>(raw) * kLeechScaleF);
-  const __half sg = __ushort_as_half(sigma_bits);
-  const __half t = __float2half_rn(__half2float(cb) * __half2float(sg));
-  const __half w = __float2half_rn(__half2float(t) * kSLatticeF);
-  return __half_as_ushort(w);
-}
 
 // Value lists of rows r_lo..r_hi (at most kSlots) into their ring slots, the
 // code orders of h24_capi.cu's table:
@@ -242,119 +233,6 @@ __global__ void codebook_f32_kernel(const int8_t *__restrict__ cb_raw, float *__
     out[i] = static_cast<float>(cb_raw[i]) * kLeechScaleF;
 }
 
-// ---------------------------------------------------------------------------
-// Matrix-free LUT GEMV: y[b][o] = sum_i x[b][i] * W[o][i] with W never
-// materialised.  W[o][i] is the fp16 value materialize() produces (the same
-// code table and value lists as dequant_kernel), widened to fp32; products
-// and sums are fp32.  One warp per output row; each lane takes atoms a, a+32,
-// ...: 18-bit index, one 16-byte code gather, 8 + 8 + 8 weights by byte
-// permutes, 24 fp32 FMAs per input vector (each lane sums at most 24 * 4
-// products per chunk of 128 atoms, then the warp tree).  Reads 2.25 packed bytes and one
-// L2-resident 16-byte code entry per 24 weights instead of 48 bytes of fp16.
-constexpr int kGemvMaxBatch = 8;
-
-// Value-list source pair of list `l` (0, 1, 2) from the row's six words.
-__device__ __forceinline__ uint2 list_pair(const uint32_t (&L)[6], uint32_t l) {
-  return make_uint2(l == 0 ? L[0] : (l == 1 ? L[2] : L[4]), l == 0 ? L[1] : (l == 1 ? L[3] : L[5]));
-}
-
-template <int B>
-__global__ void __launch_bounds__(kThreads) lut_gemv_kernel(const uint8_t *__restrict__ packed,
-                                                            const uint16_t *__restrict__ sigma16,
-                                                            int64_t rows, int apr,
-                                                            const float *__restrict__ x,
-                                                            int64_t in_f, float *__restrict__ y,
-                                                            const uint32_t *__restrict__ codes,
-                                                            int32_t *__restrict__ bad) {
-  const int lane = threadIdx.x & 31;
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
-  constexpr uint32_t kSel = 0x76543210u;
-  constexpr uint32_t kPairs = 0x82641735u;  // (lo, hi) raw pairs of words 0-3 (see build_lists)
-  const int k6 = lane < 6 ? lane : 0;
-  const uint32_t pair = k6 < 4 ? (kPairs >> (8 * k6)) & 0xFFu : (k6 == 4 ? 0x82u : 0x40u);
-  unsigned nbad = 0;
-  for (int64_t o = blockIdx.x * static_cast<int64_t>(kWarpsPerBlock) + (threadIdx.x >> 5); o < rows;
-       o += nwarps) {
-    // The row's value lists: lane k < 6 builds word k, then every lane gets all six.
-    const uint16_t sg = __ldg(sigma16 + o);
-    const uint32_t mine = dequant_value(static_cast<int>(pair & 15u) - 4, sg) |
-                          (static_cast<uint32_t>(dequant_value(static_cast<int>(pair >> 4) - 4, sg)) << 16);
-    uint32_t L[6];
-#pragma unroll
-    for (int k = 0; k < 6; ++k) L[k] = __shfl_sync(0xffffffffu, mine, k);
-    float acc[B];
-#pragma unroll
-    for (int b = 0; b < B; ++b) acc[b] = 0.f;
-    // Chunks of 4 atoms per lane: all index decodes and code gathers of a
-    // chunk are issued before the weights are expanded, so their latencies
-    // overlap.
-    constexpr int kPre = 4;
-    for (int a0 = 0; a0 < apr; a0 += 32 * kPre) {
-      uint4 cw[kPre];
-#pragma unroll
-      for (int j = 0; j < kPre; ++j) {
-        const int a = a0 + lane + 32 * j;
-        cw[j] = make_uint4(0, 0, 0, 0);
-        if (a < apr) {
-          const int64_t A = o * apr + a;
-          const uint8_t *p = packed + 9 * (A >> 2) + 2 * (A & 3);
-          const uint32_t v24 = (static_cast<uint32_t>(__ldg(p)) << 16) |
-                               (static_cast<uint32_t>(__ldg(p + 1)) << 8) | __ldg(p + 2);
-          uint32_t idx = (v24 >> (6 - 2 * (A & 3))) & 0x3FFFFu;
-          if (idx > static_cast<uint32_t>(kKissing)) {
-            ++nbad;
-            idx = 0;
-          }
-          cw[j] = __ldg(reinterpret_cast<const uint4 *>(codes) + idx);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kPre; ++j) {
-        const int a = a0 + lane + 32 * j;
-        if (a >= apr) continue;
-        const uint32_t words[3] = {cw[j].x, cw[j].y, cw[j].z};
-#pragma unroll
-        for (int part = 0; part < 3; ++part) {
-          const uint32_t w = words[part];
-          const uint2 src = list_pair(L, ((w >> 2) & 1u) | ((w >> 5) & 2u));
-          const uint32_t s_lo = __byte_perm(kSel, kSel, w), s_hi = __byte_perm(kSel, kSel, w >> 16);
-          const uint32_t h[4] = {__byte_perm(src.x, src.y, s_lo), __byte_perm(src.x, src.y, s_lo >> 16),
-                                 __byte_perm(src.x, src.y, s_hi), __byte_perm(src.x, src.y, s_hi >> 16)};
-          float wf[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h[e]));
-            wf[2 * e] = f.x;
-            wf[2 * e + 1] = f.y;
-          }
-          const int64_t col = static_cast<int64_t>(a) * kDim + 8 * part;
-#pragma unroll
-          for (int b = 0; b < B; ++b) {
-            const float4 x0 = __ldg(reinterpret_cast<const float4 *>(x + b * in_f + col));
-            const float4 x1 = __ldg(reinterpret_cast<const float4 *>(x + b * in_f + col + 4));
-            acc[b] = fmaf(x0.x, wf[0], acc[b]);
-            acc[b] = fmaf(x0.y, wf[1], acc[b]);
-            acc[b] = fmaf(x0.z, wf[2], acc[b]);
-            acc[b] = fmaf(x0.w, wf[3], acc[b]);
-            acc[b] = fmaf(x1.x, wf[4], acc[b]);
-            acc[b] = fmaf(x1.y, wf[5], acc[b]);
-            acc[b] = fmaf(x1.z, wf[6], acc[b]);
-            acc[b] = fmaf(x1.w, wf[7], acc[b]);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < B; ++b) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], off);
-      if (lane == 0) y[b * rows + o] = acc[b];
-    }
-  }
-  const unsigned total_bad = __reduce_add_sync(0xffffffffu, nbad);
-  if (lane == 0 && total_bad && bad) atomicAdd(bad, static_cast<int32_t>(total_bad));
-}
-
 int sm_count() {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -402,38 +280,6 @@ int launch_dequant(const Tables *t, const h24_dequant_layer * /*layers_dev*/,
     const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks();
     const int grid = static_cast<int>(want < cap ? want : cap);
     dequant_kernel<<<grid, kThreads, 0, s>>>(b, t->cb_nib, bad);
-    H24_CUDA_TRY(cudaGetLastError());
-    count_launches(1);
-  }
-  return H24_OK;
-}
-
-int launch_lut_gemv(const Tables *t, const uint8_t *packed, const uint16_t *sigma16, int64_t rows,
-                    int64_t in_f, const float *x, int64_t batch, float *y, int32_t *bad,
-                    cudaStream_t s) {
-  if (rows < 0 || in_f <= 0 || in_f % kDim != 0 || batch < 0)
-    return fail(H24_ERR_INVALID, "lut_gemv: in_features must be a positive multiple of 24");
-  if (rows == 0 || batch == 0) return H24_OK;
-  if (!packed || !sigma16 || !x || !y) return fail(H24_ERR_INVALID, "lut_gemv: null pointer");
-  if (!aligned16(x)) return fail(H24_ERR_INVALID, "lut_gemv: x must be 16-byte aligned");
-  const int apr = static_cast<int>(in_f / kDim);
-  const int64_t want = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
-  const int grid = static_cast<int>(want < cap ? want : cap);
-  for (int64_t b0 = 0; b0 < batch; b0 += kGemvMaxBatch) {
-    const int64_t nb = batch - b0 < kGemvMaxBatch ? batch - b0 : kGemvMaxBatch;
-    const float *xb = x + b0 * in_f;
-    float *yb = y + b0 * rows;
-#define H24_GEMV(B)                                                                            \
-  case B:                                                                                      \
-    lut_gemv_kernel<B><<<grid, kThreads, 0, s>>>(packed, sigma16, rows, apr, xb, in_f, yb,    \
-                                                 t->cb_nib, bad);                              \
-    break;
-    switch (nb) {
-      H24_GEMV(1) H24_GEMV(2) H24_GEMV(3) H24_GEMV(4) H24_GEMV(5) H24_GEMV(6) H24_GEMV(7) H24_GEMV(8)
-      default: break;
-    }
-#undef H24_GEMV
     H24_CUDA_TRY(cudaGetLastError());
     count_launches(1);
   }

@@ -10,9 +10,11 @@
 // Division and products are IEEE round-to-nearest as in the reference's fp32
 // and fp16 tensor arithmetic (rint = round half to even, torch.round).  Both
 // kernels are HBM-bound: 4 B read + 1 B written per element to quantise,
-// 1 B read + 2 B written to reconstruct.  Rows of up to 2,048 elements are
-// quantised from registers (one read of the row); longer rows take a second
-// pass that hits L1/L2.
+// 1 B read + 2 B written to reconstruct.  Rows of up to 4,096 elements are
+// streamed through shared memory: each warp owns a row at a time and has the
+// next one in flight (cp.async, two buffers per warp), so HBM reads continue
+// while the current row is reduced and quantised; other rows take two passes,
+// the second hitting L1/L2.
 #include "h24_internal.cuh"
 
 namespace h24 {
@@ -20,7 +22,8 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr float kEps = 1e-8f;
-constexpr int kRegVec = 16;  // float4 per lane held in registers: rows of up to 2048 elements
+constexpr int kStreamThreads = 128;  // 4 warps per block in the streaming kernel
+constexpr int kStreamMaxCols = 4096;   // rows that fit the two shared-memory buffers of a warp
 
 // NaN (a NaN or infinite w, or a NaN row scale) becomes 0, as torch's
 // int8 cast of the clamped NaN does.
@@ -45,8 +48,17 @@ __device__ __forceinline__ int8_t quant_fast(float w, float mu, float s) {
   return static_cast<int8_t>(static_cast<int>(r));
 }
 
-// amax propagates NaN.
-__device__ __forceinline__ float max_nan(float a, float b) { return (a != a || b != b) ? NAN : fmaxf(a, b); }
+// amax propagates NaN: max.NaN returns NaN when either input is NaN.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// max_nan(m, |f.x|, |f.y|, |f.z|, |f.w|)
+__device__ __forceinline__ float absmax4(float m, float4 f) {
+  return max_nan(max_nan(m, fabsf(f.x)), max_nan(max_nan(fabsf(f.y), fabsf(f.z)), fabsf(f.w)));
+}
 
 __device__ __forceinline__ float row_mu(float m) { return m != m ? m : fmaxf(m, kEps); }  // clamp_min keeps NaN
 
@@ -54,47 +66,76 @@ __device__ __forceinline__ uint16_t mu_bits(float mu) {
   return mu != mu ? static_cast<uint16_t>(0x7E00) : __half_as_ushort(__float2half_rn(mu));
 }
 
+// Four quant_fast results as packed int8 (element 0 in the low byte).  One
+// test covers the four elements: when any lies within 1e-4 of a half-integer
+// (or is NaN) all four take quant_one.  No clamp: |t| <= 127 (1 + 2^-22)
+// < 127.5, so rint(t) already lies in [-127, 127].
 __device__ __forceinline__ uint32_t quant4(float4 f, float mu, float sc) {
-  const uint32_t b0 = static_cast<uint8_t>(quant_fast(f.x, mu, sc));
-  const uint32_t b1 = static_cast<uint8_t>(quant_fast(f.y, mu, sc));
-  const uint32_t b2 = static_cast<uint8_t>(quant_fast(f.z, mu, sc));
-  const uint32_t b3 = static_cast<uint8_t>(quant_fast(f.w, mu, sc));
-  return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+  const float t0 = __fmul_rn(f.x, sc), t1 = __fmul_rn(f.y, sc);
+  const float t2 = __fmul_rn(f.z, sc), t3 = __fmul_rn(f.w, sc);
+  const float r0 = rintf(t0), r1 = rintf(t1), r2 = rintf(t2), r3 = rintf(t3);
+  const bool far = (fabsf(fabsf(t0 - r0) - 0.5f) > 1e-4f) & (fabsf(fabsf(t1 - r1) - 0.5f) > 1e-4f) &
+                   (fabsf(fabsf(t2 - r2) - 0.5f) > 1e-4f) & (fabsf(fabsf(t3 - r3) - 0.5f) > 1e-4f);
+  int i0, i1, i2, i3;
+  if (far) {
+    i0 = __float2int_rz(r0);
+    i1 = __float2int_rz(r1);
+    i2 = __float2int_rz(r2);
+    i3 = __float2int_rz(r3);
+  } else {
+    i0 = quant_one(f.x, mu);
+    i1 = quant_one(f.y, mu);
+    i2 = quant_one(f.z, mu);
+    i3 = quant_one(f.w, mu);
+  }
+  return __byte_perm(__byte_perm(i0, i1, 0x0040), __byte_perm(i2, i3, 0x0040), 0x5410);
 }
 
-// One warp per row (grid-stride over rows), the row held in registers:
-// rows 16-byte aligned with cols % 4 == 0 and cols <= 2048.
-__global__ void __launch_bounds__(kThreads) int8_quant_reg_kernel(const float *__restrict__ w, int64_t rows,
-                                                                  int64_t cols, int8_t *__restrict__ q,
-                                                                  uint16_t *__restrict__ mu16) {
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+
+// One warp per row (grid-stride over rows) for rows 16-byte aligned with
+// cols % 4 == 0 and cols <= kStreamMaxCols.  The warp's two shared-memory
+// buffers alternate: row i+1 is copied in while row i is reduced and
+// quantised.  Lane l copies and later reads the float4s l, l+32, ... of a
+// row, so each lane waits only for its own copies (cp.async.wait_group).
+__global__ void __launch_bounds__(kStreamThreads) int8_quant_stream_kernel(const float *__restrict__ w,
+                                                                           int64_t rows, int64_t cols,
+                                                                           int8_t *__restrict__ q,
+                                                                           uint16_t *__restrict__ mu16) {
+  extern __shared__ __align__(16) float4 int8_rows[];
   const int lane = threadIdx.x & 31;
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
   const int nv = static_cast<int>(cols / 4);
-  for (int64_t r = blockIdx.x * static_cast<int64_t>(kThreads / 32) + (threadIdx.x >> 5); r < rows;
-       r += nwarps) {
-    const float4 *row4 = reinterpret_cast<const float4 *>(w + r * cols);
-    float4 f[kRegVec];
-#pragma unroll
-    for (int k = 0; k < kRegVec; ++k) {
-      const int c = lane + 32 * k;
-      f[k] = c < nv ? __ldcs(row4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 *buf = int8_rows + static_cast<size_t>(threadIdx.x >> 5) * 2 * nv;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kStreamThreads / 32);
+  int64_t r = blockIdx.x * static_cast<int64_t>(kStreamThreads / 32) + (threadIdx.x >> 5);
+  auto issue = [&](int64_t row, float4 *dst) {
+    if (row < rows) {
+      const float4 *src = reinterpret_cast<const float4 *>(w + row * cols);
+      for (int c = lane; c < nv; c += 32) cp_async16(dst + c, src + c);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");  // one group per row, empty past the end
+  };
+  issue(r, buf);
+  for (int i = 0; r < rows; ++i, r += nwarps) {
+    const float4 *cur = buf + (i & 1) * nv;
+    issue(r + nwarps, buf + ((i + 1) & 1) * nv);
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // this lane's copies of row r landed
     float m = 0.f;
-#pragma unroll
-    for (int k = 0; k < kRegVec; ++k)
-      m = max_nan(m, max_nan(max_nan(fabsf(f[k].x), fabsf(f[k].y)), max_nan(fabsf(f[k].z), fabsf(f[k].w))));
+    for (int c = lane; c < nv; c += 32) m = absmax4(m, cur[c]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
     const float mu = row_mu(m);
     const float sc = __fdiv_rn(127.0f, mu);
     int *q4 = reinterpret_cast<int *>(q + r * cols);
-#pragma unroll
-    for (int k = 0; k < kRegVec; ++k) {
-      const int c = lane + 32 * k;
-      if (c < nv) __stcs(q4 + c, static_cast<int>(quant4(f[k], mu, sc)));
-    }
+    for (int c = lane; c < nv; c += 32) __stcs(q4 + c, static_cast<int>(quant4(cur[c], mu, sc)));
     if (lane == 0) mu16[r] = mu_bits(mu);
+    __syncwarp();
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // One warp per row (grid-stride over rows), two passes over the row.
@@ -110,10 +151,7 @@ __global__ void __launch_bounds__(kThreads) int8_quant_kernel(const float *__res
     float m = 0.f;
     if (vec) {
       const float4 *row4 = reinterpret_cast<const float4 *>(row);
-      for (int64_t c = lane; c < cols / 4; c += 32) {
-        const float4 f = __ldg(row4 + c);
-        m = max_nan(m, max_nan(max_nan(fabsf(f.x), fabsf(f.y)), max_nan(fabsf(f.z), fabsf(f.w))));
-      }
+      for (int64_t c = lane; c < cols / 4; c += 32) m = absmax4(m, __ldg(row4 + c));
     } else {
       for (int64_t c = lane; c < cols; c += 32) m = max_nan(m, fabsf(__ldg(row + c)));
     }
@@ -202,10 +240,16 @@ int launch_int8_quantize(const float *w, int64_t rows, int64_t cols, int8_t *q, 
                          cudaStream_t s) {
   if (rows == 0 || cols == 0) return H24_OK;
   const bool vec = cols % 4 == 0 && aligned16(w) && (reinterpret_cast<uintptr_t>(q) & 3) == 0;
-  if (vec && cols <= 4 * 32 * kRegVec)
-    int8_quant_reg_kernel<<<grid_for(int8_quant_reg_kernel, rows, kThreads / 32), kThreads, 0, s>>>(
-        w, rows, cols, q, mu16);
-  else
+  if (vec && cols <= kStreamMaxCols) {
+    const size_t smem = static_cast<size_t>(kStreamThreads / 32) * 2 * cols * sizeof(float);
+    H24_CUDA_TRY(cudaFuncSetAttribute(int8_quant_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+    H24_CUDA_TRY(cudaFuncSetAttribute(int8_quant_stream_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared));
+    const int grid = wave_grid((rows + kStreamThreads / 32 - 1) / (kStreamThreads / 32),
+                               blocks_per_sm(int8_quant_stream_kernel, kStreamThreads, smem));
+    int8_quant_stream_kernel<<<grid, kStreamThreads, smem, s>>>(w, rows, cols, q, mu16);
+  } else
     int8_quant_kernel<<<grid_for(int8_quant_kernel, rows, kThreads / 32), kThreads, 0, s>>>(
         w, rows, cols, q, mu16, vec);
   H24_CUDA_TRY(cudaGetLastError());

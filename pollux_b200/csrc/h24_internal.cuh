@@ -49,6 +49,19 @@ constexpr float kSLatticeF = 0.7071067811865476f;
 // float(kissing_points[0].pow(2).sum()) of castor.py:522.
 constexpr double kCSqNorm = 3.999999761581421;
 
+#ifdef __CUDACC__
+// fp16 bits of the materialised weight of raw Leech coordinate `raw` (-4..4)
+// in a row with fp16 scale `sigma_bits` (pollux.py:485-500):
+//   fp16( fp32( fp16(cb16 * sigma16) ) * s_lattice ),  cb16 = fp16(raw * fp32(1/sqrt(8))).
+__device__ __forceinline__ uint16_t dequant_value(int raw, uint16_t sigma_bits) {
+  const __half cb = __float2half_rn(static_cast<float>(raw) * kLeechScaleF);
+  const __half sg = __ushort_as_half(sigma_bits);
+  const __half t = __float2half_rn(__half2float(cb) * __half2float(sg));
+  const __half w = __float2half_rn(__half2float(t) * kSLatticeF);
+  return __half_as_ushort(w);
+}
+#endif
+
 // Per-device tables (all device pointers).
 struct Tables {
   int device = -1;

@@ -49,6 +49,21 @@ def test_against_oracle_weight(PL, oracle, out_f, in_f, batch):
     _check(oracle, packed, sig, out_f, in_f, x, y)
 
 
+@pytest.mark.parametrize("offset", [1, 7, 15])
+def test_unaligned_packed_view(PL, offset):
+    """Packed bytes at any address: the kernel reads them in aligned 16-byte
+    blocks and never touches bytes outside the buffer; the result equals the
+    aligned call's bit for bit."""
+    out_f, in_f = 37, 72
+    packed, sig = _layer(out_f, in_f, 11)
+    store = torch.zeros(packed.numel() + offset, dtype=torch.uint8, device="cuda")
+    store[offset:] = packed
+    x = torch.randn(3, in_f, device="cuda")
+    y0 = PL.lut_linear(x, packed, sig, out_f, in_f)
+    y1 = PL.lut_linear(x, store[offset:], sig, out_f, in_f)
+    assert torch.equal(y0, y1)
+
+
 def test_module_forward_before_and_after_materialize(PL, oracle):
     packed, sig = _layer(96, 192, 5)
     m = PL.PackedH24Linear(192, 96, bias=True).cuda()
