@@ -88,10 +88,11 @@ constexpr int kScreenTiles = kGolayHalf / kGolayTileN;  // 16 Golay tiles multip
 constexpr int kOctTiles = (kOctads + 1 + kGolayTileN - 1) / kGolayTileN;  // 6: tiles holding octad columns
 constexpr int kOctTailCol = kOctads + 1 - (kOctTiles - 1) * kGolayTileN;  // 120: dodecads from here in tile 5
 constexpr int kAccStages = 2;                      // TMEM accumulator stages per M-tile
-constexpr int kEpiWarps = kMTiles * 4;            // 8: (M-tile, lane quarter)
-constexpr int kProducerWarp = kEpiWarps;           // warp 8: TMA producer
-constexpr int kIssuerWarp = kEpiWarps + 1;         // warps 9-10: MMA issuer of M-tile 0, 1
-constexpr int kScreenThreads = 32 * (kEpiWarps + 1 + kMTiles);  // 352
+constexpr int kEpiPerStage = kMTiles * 4;         // 8: epilogue warps reading one accumulator stage
+constexpr int kEpiWarps = kEpiPerStage * kAccStages;  // 16: (stage, M-tile, lane quarter)
+constexpr int kProducerWarp = kEpiWarps;           // warp 16: TMA producer
+constexpr int kIssuerWarp = kEpiWarps + 1;         // warps 17-18: MMA issuer of M-tile 0, 1
+constexpr int kScreenThreads = 32 * (kEpiWarps + 1 + kMTiles);  // 608
 constexpr uint32_t kTmemCols = kMTiles * kAccStages * kGolayTileN;  // 512
 constexpr int kHeavyChunks = 192;                  // flagged chunks (of 204) beyond which the exhaustive scan runs
 constexpr int kMaxSegs = 64;                       // input segments per pipeline batch
@@ -155,14 +156,14 @@ struct __align__(1024) ScreenSmem {
   // maxima of the tile's two 64-column chunks, rounded up to fp16 (so the
   // flags stay conservative).  Each slot is written and read by one thread.
   __half2 cmax[kGolayTiles][kWorkAtoms * kRowsPerAtom];
-  float rowval[2][kWorkAtoms][kRowsPerAtom];  // row maxima, by work-item parity
+  float rowval[2][kWorkAtoms][kRowsPerAtom][kAccStages];  // row maxima, by work-item parity and stage
   uint64_t bar_a_full[2];
   uint64_t bar_a_empty[2];          // one commit per issuer
   uint64_t bar_b_full[kStages];
-  uint64_t bar_b_empty[kStages];    // one arrival per epilogue warp
+  uint64_t bar_b_empty[kStages];    // one arrival per epilogue warp of the tile's stage
   uint64_t bar_acc_full[kMTiles][kAccStages];
   uint64_t bar_acc_empty[kMTiles][kAccStages];
-  uint64_t bar_rows[kMTiles][2];    // the four warps of an M-tile, by work-item parity
+  uint64_t bar_rows[kMTiles][2];    // the eight warps of an M-tile, by work-item parity
   uint64_t bar_final[kMTiles];      // each issuer's last MMAs
   uint32_t tmem_base;
   int abort_flag;
@@ -348,14 +349,14 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 #define H24_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), \
                   "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
 
-// 32 lanes x 128 consecutive 32-bit TMEM columns, waited for in the same
-// statement (one load latency per 128 columns).
-__device__ __forceinline__ void tmem_ld128_wait(uint32_t taddr, uint32_t *r) {
+// 32 lanes x 64 consecutive 32-bit TMEM columns, waited for in the same
+// statement.
+__device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, uint32_t *r) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
-      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
-      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24), H24_R8(32), H24_R8(40), H24_R8(48), H24_R8(56), H24_R8(64), H24_R8(72), H24_R8(80), H24_R8(88), H24_R8(96), H24_R8(104), H24_R8(112), H24_R8(120)
+      : H24_R8(0), H24_R8(8), H24_R8(16), H24_R8(24), H24_R8(32), H24_R8(40), H24_R8(48), H24_R8(56)
       : "r"(taddr)
       : "memory");
 }
@@ -635,11 +636,11 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     for (int i = 0; i < 2; ++i) {
       mbar_init(&S.bar_a_full[i], 1);
       mbar_init(&S.bar_a_empty[i], kMTiles);
-      for (int g = 0; g < kMTiles; ++g) mbar_init(&S.bar_rows[g][i], 4);
+      for (int g = 0; g < kMTiles; ++g) mbar_init(&S.bar_rows[g][i], 4 * kAccStages);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.bar_b_full[s], 1);
-      mbar_init(&S.bar_b_empty[s], kEpiWarps);
+      mbar_init(&S.bar_b_empty[s], kEpiPerStage);
     }
     for (int g = 0; g < kMTiles; ++g) {
       for (int s = 0; s < kAccStages; ++s) {
@@ -751,17 +752,21 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       __syncwarp();
     }
   } else {
-    // ---------------- epilogue: one thread per (atom, row type) --------------
-    // Warp w reads TMEM lane quarter q = w % 4 of M-tile g = w / 4: row type
-    // row_of_quarter(g, q) of atoms 32 g .. 32 g + 31 of the work item, the
-    // Golay tiles alternating between the two accumulator stages.
+    // ---------------- epilogue: one thread per (atom, row type, stage) -------
+    // Warp w reads TMEM lane quarter q = w % 4 of M-tile g = (w / 4) % 2 --
+    // row type row_of_quarter(g, q) of atoms 32 g .. 32 g + 31 of the work
+    // item -- in accumulator stage h = w / 8: the Golay tiles t = h, h + 2,
+    // ....  The two warps of a row type thus work a tile apart, one loading
+    // from TMEM while the other reduces, and each builds the half of the row's
+    // flag mask that its tiles fill (bits of stage h: mask word h).
     const int q = warp & 3;
-    const int g = warp >> 2;
+    const int g = (warp >> 2) % kMTiles;
+    const int h = warp / kEpiPerStage;
     const int r = row_of_quarter(g, q);
     const int local = 32 * g + lane;
     const int slot = (g * 4 + q) * 32 + lane;
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                           static_cast<uint32_t>(g * kAccStages * kGolayTileN);
+                           static_cast<uint32_t>((g * kAccStages + h) * kGolayTileN);
     bool ok = true;
     int ip = 0;
     uint32_t rph = 0;  // bit i: parity of the next phase of bar_rows[g][i]
@@ -772,9 +777,8 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       // Tile t holds columns 128 t .. 128 t + 127; the complements of its two
       // chunks form logical tile t + 16, whose maxima are minus the minima.
 #pragma unroll 1
-      for (int t = 0; t < kScreenTiles; ++t) {
-        const int s = t & 1;
-        if (!wait_bar_warp(&S.bar_acc_full[g][s], (t >> 1) & 1, abort_flag, args.err, args.wait_limit_ns)) {
+      for (int t = h; t < kScreenTiles; t += kAccStages) {
+        if (!wait_bar_warp(&S.bar_acc_full[g][h], (t >> 1) & 1, abort_flag, args.err, args.wait_limit_ns)) {
           ok = false;
           break;
         }
@@ -783,38 +787,44 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         mbar_arrive_lane0(&S.bar_b_empty[t % kStages], lane);
         float m0 = -INFINITY, m1 = -INFINITY, n0 = INFINITY, n1 = INFINITY;
         if (r != 3 || t < kOctTiles) {
-          uint32_t x[128];
-          tmem_ld128_wait(t_row + static_cast<uint32_t>(s * kGolayTileN), x);
-          // Loaded: hand the stage back to the MMA issuer.
-          tc_fence_before();
-          __syncwarp();
-          mbar_arrive_lane0(&S.bar_acc_empty[g][s], lane);
+          // The tile's two 64-column chunks, one TMEM load each.
+          uint32_t x[64];
+          tmem_ld64_wait(t_row, x);
           if (r == 3) {
             // The |x| row counts only at the weight-16 words, the complements
             // of the octad columns 1-759: minima over those alone.
             if (t == 0) x[0] = 0x7F800000u;  // zero word (its complement: all ones)
-            if (t == kOctTiles - 1) {
-#pragma unroll
-              for (int j = kOctTailCol; j < kGolayTileN; ++j) x[j] = 0x7F800000u;  // dodecads
-            }
           } else {
             m0 = max32(max32(-INFINITY, x), x + 32);
-            m1 = max32(max32(-INFINITY, x + 64), x + 96);
           }
           n0 = min32(min32(INFINITY, x), x + 32);
-          n1 = min32(min32(INFINITY, x + 64), x + 96);
+          tmem_ld64_wait(t_row + 64u, x);
+          // Loaded: hand the stage back to the MMA issuer.
+          tc_fence_before();
+          __syncwarp();
+          mbar_arrive_lane0(&S.bar_acc_empty[g][h], lane);
+          if (r == 3) {
+            if (t == kOctTiles - 1) {
+#pragma unroll
+              for (int j2 = kOctTailCol - 64; j2 < 64; ++j2) x[j2] = 0x7F800000u;  // dodecads
+            }
+          } else {
+            m1 = max32(max32(-INFINITY, x), x + 32);
+          }
+          n1 = min32(min32(INFINITY, x), x + 32);
         } else {
           tc_fence_before();
           __syncwarp();
-          mbar_arrive_lane0(&S.bar_acc_empty[g][s], lane);
+          mbar_arrive_lane0(&S.bar_acc_empty[g][h], lane);
         }
         S.cmax[t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
         S.cmax[t + kScreenTiles][slot] = __halves2half2(__float2half_ru(-n0), __float2half_ru(-n1));
         rowmax = fmaxf(fmaxf(rowmax, fmaxf(m0, m1)), fmaxf(-n0, -n1));
       }
       if (!ok) break;
-      // Row maxima of the atom's four rows, exchanged through shared memory.
-      S.rowval[ip][local][r] = rowmax;
+      // Row maxima of the atom's four rows (both stages), exchanged through
+      // shared memory.
+      S.rowval[ip][local][r][h] = rowmax;
       __syncwarp();
       mbar_arrive_lane0(&S.bar_rows[g][ip], lane);
       if (!wait_bar_warp(&S.bar_rows[g][ip], (rph >> ip) & 1u, abort_flag, args.err, args.wait_limit_ns)) {
@@ -822,7 +832,9 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         break;
       }
       rph ^= 1u << ip;
-      const float *rv = S.rowval[ip][local];
+      float rv[kRowsPerAtom];
+#pragma unroll
+      for (int k = 0; k < kRowsPerAtom; ++k) rv[k] = fmaxf(S.rowval[ip][local][k][0], S.rowval[ip][local][k][1]);
       const float best = fmaxf(fmaxf(fmaxf(rv[0] + inf.off[0], rv[1] + inf.off[1]),
                                      fmaxf(rv[3] + inf.shi - inf.l2s, inf.t1)),
                                inf.t2lb);
@@ -835,16 +847,16 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       // finite so that chunks without columns (maximum -inf) stay unflagged.
       const float theta = (thr - add) - (fabsf(thr) + fabsf(add)) * 3.814697265625e-6f;
       const __half2 th2 = __half2half2(__float2half_rd(fmaxf(theta, -65504.f)));
-      uint32_t w0 = 0, w1 = 0;
+      // Mask word h: logical tiles 2 i + h (i = 0..15), all of them tiles of
+      // stage h or their complements, whose maxima this warp wrote.
+      uint32_t wh = 0;
 #pragma unroll
-      for (int i = kGolayTiles / 2 - 1; i >= 0; --i) {
-        w0 = (w0 << 1) | (__hge2_mask(S.cmax[2 * i][slot], th2) & 0x00010001u);
-        w1 = (w1 << 1) | (__hge2_mask(S.cmax[2 * i + 1][slot], th2) & 0x00010001u);
-      }
-      if (!(inf.two_e >= 0.f)) w0 = w1 = 0;
+      for (int i = kGolayTiles / 2 - 1; i >= 0; --i)
+        wh = (wh << 1) | (__hge2_mask(S.cmax[2 * i + h][slot], th2) & 0x00010001u);
+      if (!(inf.two_e >= 0.f)) wh = 0;
       if (atom < args.n) {
-        args.masks[atom * kRowsPerAtom + r] = make_uint2(w0, w1);
-        if (r == 0) args.info[atom].thr = thr;
+        reinterpret_cast<uint32_t *>(args.masks)[(atom * kRowsPerAtom + r) * 2 + h] = wh;
+        if (r == 0 && h == 0) args.info[atom].thr = thr;
       }
       ip ^= 1;
     }
