@@ -124,14 +124,30 @@ __global__ void __launch_bounds__(kStreamThreads) int8_quant_stream_kernel(const
     const float4 *cur = buf + (i & 1) * nv;
     issue(r + nwarps, buf + ((i + 1) & 1) * nv);
     asm volatile("cp.async.wait_group 1;" ::: "memory");  // this lane's copies of row r landed
-    float m = 0.f;
-    for (int c = lane; c < nv; c += 32) m = absmax4(m, cur[c]);
+    // Four independent float4 per step in both passes (the trip count is a
+    // runtime value, so the loops are unrolled by hand for latency overlap).
+    float mm[4] = {0.f, 0.f, 0.f, 0.f};
+    int c = lane;
+    for (; c + 96 < nv; c += 128) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mm[k] = absmax4(mm[k], cur[c + 32 * k]);
+    }
+    for (; c < nv; c += 32) mm[0] = absmax4(mm[0], cur[c]);
+    float m = max_nan(max_nan(mm[0], mm[1]), max_nan(mm[2], mm[3]));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, off));
     const float mu = row_mu(m);
     const float sc = __fdiv_rn(127.0f, mu);
     int *q4 = reinterpret_cast<int *>(q + r * cols);
-    for (int c = lane; c < nv; c += 32) __stcs(q4 + c, static_cast<int>(quant4(cur[c], mu, sc)));
+    c = lane;
+    for (; c + 96 < nv; c += 128) {
+      float4 f[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) f[k] = cur[c + 32 * k];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) __stcs(q4 + c + 32 * k, static_cast<int>(quant4(f[k], mu, sc)));
+    }
+    for (; c < nv; c += 32) __stcs(q4 + c, static_cast<int>(quant4(cur[c], mu, sc)));
     if (lane == 0) mu16[r] = mu_bits(mu);
     __syncwarp();
   }
