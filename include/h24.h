@@ -138,8 +138,12 @@ int h24_project_layers(const h24_project_layer *layers, int count, void *stream)
  * the packed layer (rows = out_features) and W[o][i] the fp16 value
  * PackedH24Linear.materialize would produce; W is never materialised.  x: batch
  * x in_features fp32 (16-byte aligned rows), y: batch x rows fp32, fp32
- * products and sums (the order differs from a dense matmul's).  Out-of-range
- * packed indices count into *bad_count (if non-null) and read as the origin. */
+ * products accurate to 2^-14 * sum_i |x[b][i] W[o][i]| (the order differs from
+ * a dense matmul's; 3-8 input rows run on the tensor cores with exact bf16
+ * products).  Out-of-range packed indices count into *bad_count (if non-null)
+ * and read as the origin.  Layers split across several CTAs take a
+ * stream-ordered workspace (8 * rows * 4 bytes per slice, at most 8 slices)
+ * from the library's device memory pool, freed on the same stream. */
 int h24_lut_gemv(const uint8_t *packed, const uint16_t *sigma16, int64_t rows,
                  int64_t in_features, const float *x, int64_t batch, float *y,
                  int32_t *bad_count, void *stream);
