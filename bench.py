@@ -825,6 +825,51 @@ def run_components(args) -> dict:
     return res
 
 
+def run_torch_reference(args) -> None:
+    """Secondary comparator, not a bench line: the reference's own GPU search
+    for the pack rule, pack._quantize_h24_layer on a CUDA tensor (pack.py:
+    159-178: chunks of 4096 atoms, an fp32 torch.matmul against all 196,560
+    kissing points, the row maximum, the norm test), written here as the same
+    torch operations and timed on config-3 matrix 0 ([5760, 1920], 460,800
+    atoms) with CUDA events; also the share of its indices that equal the
+    library's exact ones.  Prints one JSON line."""
+    import math
+    import torch
+    from pollux_b200 import castor, pack, synth
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    kp = castor.get_h24_codebook(dev, torch.float32)[1:].contiguous()
+    w = synth.backbone_weights(3, device=dev, shapes=[synth.CONFIG3_LAYER_SHAPES[0]])[0]
+
+    def search(weight):
+        wf = weight.detach().float()
+        atoms = wf.reshape(-1, 24)
+        sig = (torch.sqrt(wf.pow(2).mean(-1) + 1e-8) * math.sqrt(12.0)).clamp_min(1e-8)
+        idx = torch.zeros(atoms.shape[0], dtype=torch.long, device=dev)
+        for i in range(0, atoms.shape[0], 4096):
+            a = atoms[i:i + 4096]
+            _, best = torch.matmul(a, kp.t()).max(dim=-1)
+            idx[i:i + 4096] = (best + 1).masked_fill(a.norm(dim=-1) < 1e-8, 0)
+        return idx, sig
+
+    search(w[:256])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    idx, _ = search(w)
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    n = w.numel() // 24
+    packed, _ = pack.quantize_layers([w])[0]
+    ours = castor.unpack_indices(packed, n).long()
+    rate = n / (ms / 1e3)
+    print(json.dumps({"what": "the reference's GPU pack-rule search (fp32 matmul chunks of 4096 + max) as torch ops",
+                      "matrix": list(w.shape), "atoms": n, "ms": ms, "G_atoms_per_s": rate / 1e9,
+                      "config3_backbone_s": 33177600 / rate, "tf32": torch.backends.cuda.matmul.allow_tf32,
+                      "index_agreement_with_library": float((ours == idx).float().mean())}), flush=True)
+
+
 def run_lut_only(args) -> None:
     """Profile mode: the LUT GEMV alone through the 18 config-5 layers (one
     25 MB packed set, fp32 x of batch --lut-batch), CUDA events around
@@ -889,8 +934,12 @@ def main():
     ap.add_argument("--lut-only", action="store_true",
                     help="profile mode: time only the LUT GEMV sweep over the config-5 layers")
     ap.add_argument("--lut-batch", type=int, default=1)
+    ap.add_argument("--torch-reference", action="store_true",
+                    help="time the reference's GPU search as torch ops on one config-3 matrix (a comparator)")
     args = ap.parse_args()
-    if args.lut_only:
+    if args.torch_reference:
+        run_torch_reference(args)
+    elif args.lut_only:
         run_lut_only(args)
     elif args.search_atoms:
         run_search_only(args)
