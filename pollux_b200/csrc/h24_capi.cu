@@ -645,16 +645,18 @@ int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16
   return h24_quantize_layers(&L, 1, stream);
 }
 
-// Host-memory form over many row ranges, one pipeline for all of them.  Each
-// range is cut into chunks of whole rows that end on 4-atom groups; chunk k
-// is copied host-to-device into one of kHostSlots device slots on the copy
-// stream while the caller's stream quantises chunk k-1 (row scales with the
-// whole matrix's plan, search, 18-bit pack into the range's device output),
-// across range boundaries, so the transfer hides behind the search.  All
-// outputs come back to the host at the end; the call returns once they are
-// written.
+// Host-memory form over many row ranges, one pipeline for all of them.  The
+// ranges are cut into pieces of whole rows that start on 4-atom groups and
+// gathered, across range boundaries, into batches of up to 2^20 atoms; batch
+// k is copied host-to-device (one copy per piece) into one of kHostSlots
+// device slots on the copy stream while the caller's stream quantises batch
+// k-1 (row scales of each piece with its whole matrix's plan, one search over
+// all the batch's pieces, 18-bit pack into each range's device output), so
+// the transfer hides behind the search.  All outputs come back to the host at
+// the end; the call returns once they are written.
 static constexpr int kHostSlots = 3;
-static constexpr int64_t kHostChunkAtoms = 294912;
+static constexpr int64_t kHostBatchAtoms = int64_t(1) << 20;  // atoms per batch (one search call)
+static constexpr int kHostPieces = 64;                         // row ranges per batch
 
 int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dtype, void *stream) {
   H24_TABLES_OR_FAIL(T);
@@ -668,33 +670,56 @@ int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dt
     if (rc != H24_OK) return rc;
   }
   auto up = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
-  // Chunks: (range, first row, rows).
-  struct Chunk { int li; int64_t c0, c1; };
-  std::vector<Chunk> chunks;
+  // Batches of up to kHostBatchAtoms atoms, each made of pieces: row ranges
+  // of one matrix that start on a whole 4-atom group (rows [c0, c1) of range
+  // li, at byte offset `off` of the batch's slot), at most kHostPieces per
+  // batch.  A batch is one search over all its pieces, so the device works on
+  // batches as large as the device-resident path's whatever the matrix sizes.
+  struct Piece { int li; int64_t c0, c1; size_t off; };
+  struct Batch { size_t first, count; int64_t atoms; size_t bytes; };
+  std::vector<Piece> pieces;
+  std::vector<Batch> batches;
   std::vector<size_t> out_pk(count), out_sig(count);
-  size_t out_bytes = 0, slot_elems = 0;
-  for (int i = 0; i < count; ++i) {
-    const RowRange &r = R[i];
-    out_pk[i] = out_bytes;
-    out_bytes += up(static_cast<size_t>((r.atoms() + 3) / 4) * 9);
-    out_sig[i] = out_bytes;
-    out_bytes += up(static_cast<size_t>(r.r1 - r.r0) * 2);
-    if (r.r1 == r.r0) continue;
-    int64_t g = r.in, h = 96;
-    while (h) { const int64_t t2 = g % h; g = h; h = t2; }
-    const int64_t rg = 96 / g;  // rows per whole number of 4-atom groups
-    int64_t crows = (kHostChunkAtoms * kDim / r.in) / rg * rg;
-    if (crows < rg) crows = rg;
-    for (int64_t c0 = r.r0; c0 < r.r1; c0 += crows) {
-      const int64_t c1 = c0 + crows < r.r1 ? c0 + crows : r.r1;
-      chunks.push_back({i, c0, c1});
-      slot_elems = std::max(slot_elems, static_cast<size_t>((c1 - c0) * r.in));
+  size_t out_bytes = 0;
+  {
+    Batch cur{0, 0, 0, 0};
+    for (int i = 0; i < count; ++i) {
+      const RowRange &r = R[i];
+      out_pk[i] = out_bytes;
+      out_bytes += up(static_cast<size_t>((r.atoms() + 3) / 4) * 9);
+      out_sig[i] = out_bytes;
+      out_bytes += up(static_cast<size_t>(r.r1 - r.r0) * 2);
+      if (r.r1 == r.r0) continue;
+      int64_t g = r.in, h = 96;
+      while (h) { const int64_t t2 = g % h; g = h; h = t2; }
+      const int64_t rg = 96 / g;  // rows per whole number of 4-atom groups
+      for (int64_t c0 = r.r0; c0 < r.r1;) {
+        int64_t fit = (kHostBatchAtoms - cur.atoms) * kDim / r.in / rg * rg;
+        if (cur.count == 0 && fit < rg) fit = rg;  // a row group wider than a batch goes alone
+        if (fit <= 0 || cur.count == static_cast<size_t>(kHostPieces)) {
+          batches.push_back(cur);
+          cur = Batch{pieces.size(), 0, 0, 0};
+          continue;
+        }
+        const int64_t c1 = c0 + fit < r.r1 ? c0 + fit : r.r1;
+        pieces.push_back({i, c0, c1, cur.bytes});
+        cur.atoms += (c1 - c0) * r.in / kDim;
+        cur.bytes += up(static_cast<size_t>((c1 - c0) * r.in) * esize);
+        ++cur.count;
+        c0 = c1;
+      }
     }
+    if (cur.count) batches.push_back(cur);
   }
-  if (chunks.empty()) return H24_OK;
+  if (batches.empty()) return H24_OK;
+  size_t slot_bytes = 0;
+  int64_t batch_atoms = 0;
+  for (const Batch &b : batches) {
+    slot_bytes = std::max(slot_bytes, b.bytes);
+    batch_atoms = std::max(batch_atoms, b.atoms);
+  }
   cudaStream_t s = as_stream(stream);
-  const size_t slot_bytes = up(slot_elems * esize);
-  const size_t idx_bytes = up(slot_elems / kDim * 4);
+  const size_t idx_bytes = up(static_cast<size_t>(batch_atoms) * 4);
   const size_t off_slots = up(out_bytes);
   const size_t off_idx = off_slots + kHostSlots * slot_bytes;
   uint8_t *buf = nullptr;
@@ -720,28 +745,47 @@ int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dt
     if (ce == cudaSuccess) ce = cudaStreamWaitEvent(T->copy_stream, ready, 0);
     if (ce != cudaSuccess) rc = cuda_fail(ce, "copy stream order");
   }
-  for (size_t k = 0; k < chunks.size() && rc == H24_OK; ++k) {
-    const Chunk &c = chunks[k];
-    const RowRange &r = R[c.li];
+  std::vector<const void *> xs;
+  std::vector<int64_t> na;
+  for (size_t k = 0; k < batches.size() && rc == H24_OK; ++k) {
+    const Batch &b = batches[k];
     const int sl = static_cast<int>(k % kHostSlots);
     uint8_t *slot = buf + off_slots + sl * slot_bytes;
     int32_t *idx = reinterpret_cast<int32_t *>(buf + off_idx + sl * idx_bytes);
-    const int64_t nrow = c.c1 - c.c0, na = nrow * r.in / kDim;
-    // Copy into the slot once the chunk that used it before is quantised.
+    // Copy into the slot once the batch that used it before is quantised.
     cudaError_t ce = cudaSuccess;
     if (k >= static_cast<size_t>(kHostSlots)) ce = cudaStreamWaitEvent(T->copy_stream, freed[sl], 0);
-    if (ce == cudaSuccess)
-      ce = cudaMemcpyAsync(slot, r.w + static_cast<size_t>(c.c0 * r.in) * esize,
-                           static_cast<size_t>(nrow * r.in) * esize, cudaMemcpyHostToDevice, T->copy_stream);
+    for (size_t q = b.first; q < b.first + b.count && ce == cudaSuccess; ++q) {
+      const Piece &pc = pieces[q];
+      const RowRange &r = R[pc.li];
+      ce = cudaMemcpyAsync(slot + pc.off, r.w + static_cast<size_t>(pc.c0 * r.in) * esize,
+                           static_cast<size_t>((pc.c1 - pc.c0) * r.in) * esize, cudaMemcpyHostToDevice,
+                           T->copy_stream);
+    }
     if (ce == cudaSuccess) ce = cudaEventRecord(copied[sl], T->copy_stream);
     if (ce == cudaSuccess) ce = cudaStreamWaitEvent(s, copied[sl], 0);
-    if (ce != cudaSuccess) { rc = cuda_fail(ce, "chunk copy"); break; }
-    uint16_t *sig = reinterpret_cast<uint16_t *>(buf + out_sig[c.li]) + (c.c0 - r.r0);
-    uint8_t *pk = buf + out_pk[c.li] + static_cast<size_t>((c.c0 - r.r0) * r.in / kDim / 4) * 9;
-    rc = launch_row_rms(slot, dtype, nrow, r.in, r.rows, c.c0, nullptr, sig, s);
-    const void *xs = slot;
-    if (rc == H24_OK) rc = quantize_segments(T, &xs, &na, 1, dtype, H24_RULE_PACK, idx, s);
-    if (rc == H24_OK) rc = launch_pack_i32(idx, na, pk, s);
+    if (ce != cudaSuccess) { rc = cuda_fail(ce, "batch copy"); break; }
+    xs.clear();
+    na.clear();
+    for (size_t q = b.first; q < b.first + b.count && rc == H24_OK; ++q) {
+      const Piece &pc = pieces[q];
+      const RowRange &r = R[pc.li];
+      uint16_t *sig = reinterpret_cast<uint16_t *>(buf + out_sig[pc.li]) + (pc.c0 - r.r0);
+      rc = launch_row_rms(slot + pc.off, dtype, pc.c1 - pc.c0, r.in, r.rows, pc.c0, nullptr, sig, s);
+      xs.push_back(slot + pc.off);
+      na.push_back((pc.c1 - pc.c0) * r.in / kDim);
+    }
+    if (rc == H24_OK)
+      rc = quantize_segments(T, xs.data(), na.data(), static_cast<int>(xs.size()), dtype, H24_RULE_PACK, idx, s);
+    int64_t a0 = 0;
+    for (size_t q = b.first; q < b.first + b.count && rc == H24_OK; ++q) {
+      const Piece &pc = pieces[q];
+      const RowRange &r = R[pc.li];
+      const int64_t n = (pc.c1 - pc.c0) * r.in / kDim;
+      uint8_t *pk = buf + out_pk[pc.li] + static_cast<size_t>((pc.c0 - r.r0) * r.in / kDim / 4) * 9;
+      rc = launch_pack_i32(idx + a0, n, pk, s);
+      a0 += n;
+    }
     if (rc == H24_OK) {
       ce = cudaEventRecord(freed[sl], s);
       if (ce != cudaSuccess) rc = cuda_fail(ce, "slot release");
