@@ -504,27 +504,45 @@ def run_e2e(args, weights, shapes, ranges, dev, world) -> dict:
                     for n in names]
         return pack.quantize_layers_host([(w, r0, r1) for w, (r0, r1) in zip(host_w, ranges)])
 
-    def timed(fn, steps):
-        for _ in range(max(1, min(args.warmup, 2))):
+    def timed(fn, steps, warm):
+        # The first calls of a process are slower (page-locked output buffers
+        # and the device pool grow to their working set): steady state after
+        # a few.
+        for _ in range(warm):
             fn()
         t0 = time.perf_counter()
         for _ in range(steps):
             res = fn()
         return (time.perf_counter() - t0) / steps, res
 
+    # The page-locked host-to-device bandwidth this box gives at the moment
+    # (PCIe links may be shared with other jobs), for reading the number.
+    dev_w = [torch.empty_like(w, device=dev) for w in host_w]
+    for _ in range(2):
+        for h, d in zip(host_w, dev_w):
+            d.copy_(h, non_blocking=True)
+    torch.cuda.synchronize()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for h, d in zip(host_w, dev_w):
+        d.copy_(h, non_blocking=True)
+    c1.record()
+    c1.synchronize()
+    h2d_gbps = sum(h.numel() * h.element_size() for h in host_w) / (c0.elapsed_time(c1) / 1e3) / 1e9
+    del dev_w
     steps = max(1, min(args.steps, 5))
-    dt, res = timed(e2e_step, steps)
+    dt, res = timed(e2e_step, steps, max(5, args.warmup))
     per_matrix = None
     if world == 1:
         cb = castor.get_h24_codebook("cpu", torch.float32)
-        dtm, res_m = timed(lambda: [pack._quantize_h24_layer(w, cb) for w in host_w], min(steps, 3))
+        dtm, res_m = timed(lambda: [pack._quantize_h24_layer(w, cb) for w in host_w], min(steps, 3), 2)
         assert all(torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]) for a, b in zip(res, res_m))
         per_matrix = {"api": "pack._quantize_h24_layer per matrix (bf16 host weights)", "ms_per_step": dtm * 1e3}
     h2d = sum((r1 - r0) * i * 2 for (r0, r1), (o, i) in zip(ranges, shapes))
     d2h = sum(p.numel() + s.numel() * 2 for p, s in res)
     del host_w, state
     return {"unit": "G atoms/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": dt * 1e3, "steps": steps,
+            "ms_per_step": dt * 1e3, "steps": steps, "h2d_GBps_measured": h2d_gbps,
             "api": ("pollux_b200.pack.quantize_state_dict on the 72-matrix bf16 state_dict" if world == 1
                     else "pollux_b200.pack.quantize_layers_host, this rank's rows of every matrix"),
             "per_matrix_drop_in": per_matrix}

@@ -133,9 +133,10 @@ def quantize_layer_rows_host(weight: torch.Tensor, row_begin: int, row_end: int
 
 def quantize_layers_host(parts: list[tuple[torch.Tensor, int, int]]) -> list[tuple[torch.Tensor, torch.Tensor]]:
     """Rows [begin, end) of each HOST weight (contiguous 2-D fp32 or bf16, all
-    of one dtype) to host (packed u8, sigma16), in one pipeline: the copy of
-    each chunk of rows overlaps the search of the previous one across matrix
-    boundaries (page-locked weights give the overlap).  The outputs are the
+    of one dtype) to host (packed u8, sigma16), in one pipeline: rows of
+    several matrices are gathered into batches of up to 2^20 atoms, and the
+    copy of each batch overlaps the search of the previous one (page-locked
+    weights give the overlap).  The outputs are the
     bytes and scales _quantize_h24_layer returns for those rows."""
     if not parts:
         return []
