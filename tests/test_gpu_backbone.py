@@ -104,6 +104,27 @@ def test_row_shards_concatenate(mods, shape):
     assert torch.equal(ph, whole_p[b0:b1].cpu()) and torch.equal(sh, whole_s[r0:r1].cpu())
 
 
+def test_host_pipeline_many_small_matrices(mods):
+    """More row ranges than one batch holds (the host pipeline closes a batch
+    at 64 pieces), of assorted widths and row starts, through one call: every
+    range's bytes and scales equal the device path's for those rows."""
+    C, P, SH, _ = mods
+    g = torch.Generator().manual_seed(17)
+    shapes = [(8 + (k % 5) * 4, (1 + k % 7) * 24) for k in range(80)]
+    ws = [(torch.randn(o, i, generator=g) * 0.02).to(torch.bfloat16).pin_memory() for o, i in shapes]
+    parts = []
+    for k, w in enumerate(ws):
+        rows, in_f = w.shape
+        world = 1 + k % 3
+        parts.append((w, *SH.shard_rows(rows, in_f, world, world - 1)))
+    res = P.quantize_layers_host(parts)
+    assert len(res) == len(parts)
+    for (w, r0, r1), (p, s) in zip(parts, res):
+        wp, wsig = P.quantize_layers([w.cuda()])[0]
+        b0, b1 = SH.packed_range(r0, r1, w.shape[1])
+        assert torch.equal(p, wp[b0:b1].cpu()) and torch.equal(s, wsig[r0:r1].cpu())
+
+
 def test_row_range_validation(mods):
     C, P, _, _ = mods
     w = torch.randn(16, 72, device="cuda")  # 3 atoms per row: groups end every 4 rows
