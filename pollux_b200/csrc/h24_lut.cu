@@ -404,20 +404,22 @@ __global__ void __launch_bounds__(256) lut_reduce_kernel(const float *__restrict
 }
 
 // ---------------------------------------------------------------------------
-// Batches of 1-2 input rows: one warp per weight row, fp32 FMAs.  W[o][i] is
-// the fp16 value of materialize(), widened to fp32; each lane takes atoms a,
-// a+32, a+64, ...: 18-bit index, one 16-byte code gather, 8 + 8 + 8 weights by
-// byte permutes of the row's fp16 value lists, 24 FMAs per input row; then the
-// warp tree.  At one input row (40 registers, 48 warps per SM) the rows of a
-// layer of up to about 7,000 rows are resident at once, so every warp's
-// gathers are in flight together.  With one or two input rows there are too
-// few products per weight for the tensor-core path's staging to pay.
+// Batches of 1-2 input rows: half a warp per weight row, fp32 FMAs.  W[o][i]
+// is the fp16 value of materialize(), widened to fp32; the 16 lanes of a row
+// take atoms a, a+16, a+32, ..., up to kFmaPre of them with their gathers in
+// flight together: 18-bit index, one 16-byte code gather, 8 + 8 + 8 weights by
+// byte permutes of the row's fp16 value lists, 24 FMAs per input row; then a
+// 16-lane tree.  Two rows per warp (64 registers, four blocks per SM) let
+// every row of a layer of up to ~9,400 rows be resident at once, so the whole
+// layer's gathers are in flight in one wave.  With one or two input rows there are too few products per weight
+// for the tensor-core path's staging to pay.
 constexpr int kFmaThreads = 256;
 constexpr int kFmaWarps = kFmaThreads / 32;
-constexpr int kFmaPre = 3;  // atoms per lane whose gathers are issued together
+constexpr int kFmaRowsPerWarp = 2;
+constexpr int kFmaPre = 5;  // atoms per lane whose gathers are issued together
 
 template <int B>
-__global__ void __launch_bounds__(kFmaThreads, B == 1 ? 6 : 4) lut_fma_kernel(const uint8_t *__restrict__ packed,
+__global__ void __launch_bounds__(kFmaThreads, 4) lut_fma_kernel(const uint8_t *__restrict__ packed,
                                                                  const uint16_t *__restrict__ sigma16,
                                                                  int64_t rows, int apr,
                                                                  const float *__restrict__ x, int64_t in_f,
@@ -425,30 +427,40 @@ __global__ void __launch_bounds__(kFmaThreads, B == 1 ? 6 : 4) lut_fma_kernel(co
                                                                  const uint32_t *__restrict__ codes,
                                                                  int32_t *__restrict__ bad) {
   const int lane = threadIdx.x & 31;
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kFmaWarps;
+  const int sl = lane & 15;        // lane within the row's half warp
+  const int hb = lane & 16;        // first lane of the half
+  const int64_t nrow_slots = static_cast<int64_t>(gridDim.x) * kFmaWarps * kFmaRowsPerWarp;
   constexpr uint32_t kSel = 0x76543210u;
   constexpr uint32_t kPairs = 0x82641735u;  // (lo, hi) raw pairs of words 0-3 of the value lists
-  const int k6 = lane < 6 ? lane : 0;
+  const int k6 = sl < 6 ? sl : 0;
   const uint32_t pair = k6 < 4 ? (kPairs >> (8 * k6)) & 0xFFu : (k6 == 4 ? 0x82u : 0x40u);
   unsigned nbad = 0;
-  for (int64_t o = blockIdx.x * static_cast<int64_t>(kFmaWarps) + (threadIdx.x >> 5); o < rows; o += nwarps) {
-    // The row's fp16 value lists: lane k < 6 builds word k, then every lane gets all six.
-    const uint16_t sg = __ldg(sigma16 + o);
+  const int64_t first = (blockIdx.x * static_cast<int64_t>(kFmaWarps) + (threadIdx.x >> 5)) * kFmaRowsPerWarp +
+                        (lane >> 4);
+  // Every lane runs the same number of iterations (the shuffles below need
+  // the whole warp); a half past the last row computes nothing it keeps.
+  const int64_t iters = (rows + nrow_slots - 1) / nrow_slots;
+  for (int64_t it = 0; it < iters; ++it) {
+    const int64_t o = first + it * nrow_slots;
+    const bool live = o < rows;
+    // The row's fp16 value lists: lane k < 6 of the half builds word k, then
+    // every lane of the half gets all six.
+    const uint16_t sg = live ? __ldg(sigma16 + o) : static_cast<uint16_t>(0);
     const uint32_t mine = dequant_value(static_cast<int>(pair & 15u) - 4, sg) |
                           (static_cast<uint32_t>(dequant_value(static_cast<int>(pair >> 4) - 4, sg)) << 16);
     uint32_t L[6];
 #pragma unroll
-    for (int k = 0; k < 6; ++k) L[k] = __shfl_sync(0xffffffffu, mine, k);
+    for (int k = 0; k < 6; ++k) L[k] = __shfl_sync(0xffffffffu, mine, hb + k);
     float acc[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) acc[b] = 0.f;
-    for (int a0 = 0; a0 < apr; a0 += 32 * kFmaPre) {
+    for (int a0 = 0; a0 < apr; a0 += 16 * kFmaPre) {
       uint4 cw[kFmaPre];
 #pragma unroll
       for (int j = 0; j < kFmaPre; ++j) {
-        const int a = a0 + lane + 32 * j;
+        const int a = a0 + sl + 16 * j;
         cw[j] = make_uint4(0, 0, 0, 0);
-        if (a < apr) {
+        if (live && a < apr) {
           const int64_t A = o * apr + a;
           const uint8_t *p = packed + 9 * (A >> 2) + 2 * (A & 3);
           const uint32_t v24 =
@@ -463,8 +475,8 @@ __global__ void __launch_bounds__(kFmaThreads, B == 1 ? 6 : 4) lut_fma_kernel(co
       }
 #pragma unroll
       for (int j = 0; j < kFmaPre; ++j) {
-        const int a = a0 + lane + 32 * j;
-        if (a >= apr) continue;
+        const int a = a0 + sl + 16 * j;
+        if (!live || a >= apr) continue;
         const uint32_t words[3] = {cw[j].x, cw[j].y, cw[j].z};
         const uint32_t l = ((cw[j].x >> 2) & 1u) | ((cw[j].x >> 5) & 2u);  // the codeword's value list
         const uint32_t s0 = l == 0 ? L[0] : (l == 1 ? L[2] : L[4]);
@@ -502,8 +514,8 @@ __global__ void __launch_bounds__(kFmaThreads, B == 1 ? 6 : 4) lut_fma_kernel(co
 #pragma unroll
     for (int b = 0; b < B; ++b) {
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], off);
-      if (lane == 0) y[b * rows + o] = acc[b];
+      for (int off = 8; off > 0; off >>= 1) acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], off);
+      if (sl == 0 && live) y[b * rows + o] = acc[b];
     }
   }
   const unsigned total_bad = __reduce_add_sync(0xffffffffu, nbad);
@@ -572,7 +584,8 @@ int launch_lut_gemv(const Tables *t, const uint8_t *packed, const uint16_t *sigm
   for (int64_t b0 = 0; b0 < batch && rc == H24_OK; b0 += kMaxB) {
     const int nb = static_cast<int>(batch - b0 < kMaxB ? batch - b0 : kMaxB);
     if (nb <= 2) {
-      const int grid = wave_grid((rows + kFmaWarps - 1) / kFmaWarps,
+      const int64_t per_block = static_cast<int64_t>(kFmaWarps) * kFmaRowsPerWarp;
+      const int grid = wave_grid((rows + per_block - 1) / per_block,
                                  nb == 1 ? blocks_per_sm(lut_fma_kernel<1>, kFmaThreads, 0)
                                          : blocks_per_sm(lut_fma_kernel<2>, kFmaThreads, 0));
       if (nb == 1)
