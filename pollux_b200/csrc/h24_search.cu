@@ -157,6 +157,7 @@ struct __align__(1024) ScreenSmem {
   // flags stay conservative).  Each slot is written and read by one thread.
   __half2 cmax[kGolayTiles][kWorkAtoms * kRowsPerAtom];
   float rowval[2][kWorkAtoms][kRowsPerAtom][kAccStages];  // row maxima, by work-item parity and stage
+  AtomInfo info_st[2][kMTiles][32];   // per-atom constants of the work item, by work-item parity
   uint64_t bar_a_full[2];
   uint64_t bar_a_empty[2];          // one commit per issuer
   uint64_t bar_b_full[kStages];
@@ -175,6 +176,13 @@ struct __align__(1024) ScreenSmem {
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -772,7 +780,17 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     uint32_t rph = 0;  // bit i: parity of the next phase of bar_rows[g][i]
     for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
       const int64_t atom = it * kWorkAtoms + local;
-      const AtomInfo inf = args.info[atom];
+      // One warp per M-tile copies its 32 atoms' constants into shared memory
+      // now; every warp reads them after the item's barrier, so no register
+      // holds them across the tile loop and the copy has the whole item to land.
+      const bool stager = q == 0 && h == 0;
+      if (stager) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k)
+          cp_async16(reinterpret_cast<uint4 *>(&S.info_st[ip][g][lane]) + k,
+                     reinterpret_cast<const uint4 *>(args.info + atom) + k);
+        cp_async_commit();
+      }
       float rowmax = -INFINITY;
       // Tile t holds columns 128 t .. 128 t + 127; the complements of its two
       // chunks form logical tile t + 16, whose maxima are minus the minima.
@@ -821,6 +839,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         S.cmax[t + kScreenTiles][slot] = __halves2half2(__float2half_ru(-n0), __float2half_ru(-n1));
         rowmax = fmaxf(fmaxf(rowmax, fmaxf(m0, m1)), fmaxf(-n0, -n1));
       }
+      if (stager) cp_async_wait_all();  // the constants are in shared memory before the barrier
       if (!ok) break;
       // Row maxima of the atom's four rows (both stages), exchanged through
       // shared memory.
@@ -832,6 +851,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         break;
       }
       rph ^= 1u << ip;
+      const AtomInfo inf = S.info_st[ip][g][lane];
       float rv[kRowsPerAtom];
 #pragma unroll
       for (int k = 0; k < kRowsPerAtom; ++k) rv[k] = fmaxf(S.rowval[ip][local][k][0], S.rowval[ip][local][k][1]);
@@ -984,11 +1004,6 @@ static_assert(sizeof(AtomStage) == 176 && offsetof(AtomStage, masks) == 96 &&
                   offsetof(AtomStage, info) == 128,
               "AtomStage is eleven 16-byte chunks: coordinates, masks, constants");
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 constexpr int kRescoreWarps = 8;
 constexpr int kRescoreBlocksPerSm = 3;
