@@ -151,13 +151,15 @@ static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 struct __align__(1024) ScreenSmem {
   uint8_t a[2][kAItemBytes];          // A operand of two work items
   uint8_t b[kStages][kBTileBytes];    // Golay tile ring
-  // Per logical Golay tile (all 32: the 16 multiplied ones and their
-  // complements) and epilogue thread slot (M-tile, lane quarter, lane): the
-  // maxima of the tile's two 64-column chunks, rounded up to fp16 (so the
-  // flags stay conservative).  Each slot is written and read by one thread.
-  __half2 cmax[kGolayTiles][kWorkAtoms * kRowsPerAtom];
+  // By work-item parity, per logical Golay tile (all 32: the 16 multiplied
+  // ones and their complements) and epilogue thread slot (M-tile, lane
+  // quarter, lane): the maxima of the tile's two 64-column chunks, rounded up
+  // to fp16 (so the flags stay conservative).  Each slot is written and read
+  // by one thread; the flags of a work item are made while the next one is
+  // screened, hence two items.
+  __half2 cmax[2][kGolayTiles][kWorkAtoms * kRowsPerAtom];
   float rowval[2][kWorkAtoms][kRowsPerAtom][kAccStages];  // row maxima, by work-item parity and stage
-  AtomInfo info_st[2][kMTiles][32];   // per-atom constants of the work item, by work-item parity
+  AtomInfo info_st[3][kMTiles][32];   // per-atom constants, by work item modulo 3
   uint64_t bar_a_full[2];
   uint64_t bar_a_empty[2];          // one commit per issuer
   uint64_t bar_b_full[kStages];
@@ -776,18 +778,62 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                            static_cast<uint32_t>((g * kAccStages + h) * kGolayTileN);
     bool ok = true;
-    int ip = 0;
+    int ip = 0;        // work-item parity: cmax, rowval and bar_rows
+    int is = 0;        // work item modulo 3: info_st
     uint32_t rph = 0;  // bit i: parity of the next phase of bar_rows[g][i]
+    // The flags of work item j are made after the tile loop of item j + 1, so
+    // the wait for the M-tile's other warps at item j's barrier has a whole
+    // item of slack.  Order per item j: tile loop (cmax[j % 2]); flags of item
+    // j - 1 (wait for its barrier, read rowval, cmax and constants of j - 1);
+    // rowval[j % 2] written and item j's barrier arrived on.  A warp thus
+    // writes rowval[j % 2] only after every warp of the M-tile has arrived on
+    // item j - 1's barrier, i.e. has read item j - 2's row maxima; and the
+    // stager overwrites the constants of item j - 3 only after every warp has
+    // arrived on item j - 2's barrier, having read them.
+    auto flags = [&](int pp, int ps, int64_t patom) -> bool {
+      if (!wait_bar_warp(&S.bar_rows[g][pp], (rph >> pp) & 1u, abort_flag, args.err, args.wait_limit_ns))
+        return false;
+      rph ^= 1u << pp;
+      const AtomInfo inf = S.info_st[ps][g][lane];
+      float rv[kRowsPerAtom];
+#pragma unroll
+      for (int k = 0; k < kRowsPerAtom; ++k) rv[k] = fmaxf(S.rowval[pp][local][k][0], S.rowval[pp][local][k][1]);
+      const float best = fmaxf(fmaxf(fmaxf(rv[0] + inf.off[0], rv[1] + inf.off[1]),
+                                     fmaxf(rv[3] + inf.shi - inf.l2s, inf.t1)),
+                               inf.t2lb);
+      const float thr = best - inf.two_e;
+      const float add = r < 2 ? inf.off[r] : (r == 2 ? fmaxf(inf.u0, inf.u1) : inf.shi);
+      // A chunk is flagged when (its fp16 maximum) + add >= thr in fp32.  In
+      // fp16: maximum >= th with th <= thr - add, lowered by 2^-18 (|thr| +
+      // |add|) against the fp32 roundings and rounded down to fp16, so every
+      // chunk flagged in fp32 is flagged here (a few more may be).  th stays
+      // finite so that chunks without columns (maximum -inf) stay unflagged.
+      const float theta = (thr - add) - (fabsf(thr) + fabsf(add)) * 3.814697265625e-6f;
+      const __half2 th2 = __half2half2(__float2half_rd(fmaxf(theta, -65504.f)));
+      // Mask word h: logical tiles 2 i + h (i = 0..15), all of them tiles of
+      // stage h or their complements, whose maxima this warp wrote.
+      uint32_t wh = 0;
+#pragma unroll
+      for (int i = kGolayTiles / 2 - 1; i >= 0; --i)
+        wh = (wh << 1) | (__hge2_mask(S.cmax[pp][2 * i + h][slot], th2) & 0x00010001u);
+      if (!(inf.two_e >= 0.f)) wh = 0;
+      if (patom < args.n) {
+        reinterpret_cast<uint32_t *>(args.masks)[(patom * kRowsPerAtom + r) * 2 + h] = wh;
+        if (r == 0 && h == 0) args.info[patom].thr = thr;
+      }
+      return true;
+    };
+    int64_t prev_atom = -1;  // this thread's atom in the previous work item
     for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
       const int64_t atom = it * kWorkAtoms + local;
       // One warp per M-tile copies its 32 atoms' constants into shared memory
-      // now; every warp reads them after the item's barrier, so no register
-      // holds them across the tile loop and the copy has the whole item to land.
+      // now; they are read after the item's barrier, so no register holds
+      // them across the tile loop and the copy has the whole item to land.
       const bool stager = q == 0 && h == 0;
       if (stager) {
 #pragma unroll
         for (int k = 0; k < 3; ++k)
-          cp_async16(reinterpret_cast<uint4 *>(&S.info_st[ip][g][lane]) + k,
+          cp_async16(reinterpret_cast<uint4 *>(&S.info_st[is][g][lane]) + k,
                      reinterpret_cast<const uint4 *>(args.info + atom) + k);
         cp_async_commit();
       }
@@ -835,51 +881,27 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
           __syncwarp();
           mbar_arrive_lane0(&S.bar_acc_empty[g][h], lane);
         }
-        S.cmax[t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
-        S.cmax[t + kScreenTiles][slot] = __halves2half2(__float2half_ru(-n0), __float2half_ru(-n1));
+        S.cmax[ip][t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
+        S.cmax[ip][t + kScreenTiles][slot] = __halves2half2(__float2half_ru(-n0), __float2half_ru(-n1));
         rowmax = fmaxf(fmaxf(rowmax, fmaxf(m0, m1)), fmaxf(-n0, -n1));
       }
       if (stager) cp_async_wait_all();  // the constants are in shared memory before the barrier
       if (!ok) break;
-      // Row maxima of the atom's four rows (both stages), exchanged through
-      // shared memory.
-      S.rowval[ip][local][r][h] = rowmax;
-      __syncwarp();
-      mbar_arrive_lane0(&S.bar_rows[g][ip], lane);
-      if (!wait_bar_warp(&S.bar_rows[g][ip], (rph >> ip) & 1u, abort_flag, args.err, args.wait_limit_ns)) {
+      if (prev_atom >= 0 && !flags(ip ^ 1, is == 0 ? 2 : is - 1, prev_atom)) {
         ok = false;
         break;
       }
-      rph ^= 1u << ip;
-      const AtomInfo inf = S.info_st[ip][g][lane];
-      float rv[kRowsPerAtom];
-#pragma unroll
-      for (int k = 0; k < kRowsPerAtom; ++k) rv[k] = fmaxf(S.rowval[ip][local][k][0], S.rowval[ip][local][k][1]);
-      const float best = fmaxf(fmaxf(fmaxf(rv[0] + inf.off[0], rv[1] + inf.off[1]),
-                                     fmaxf(rv[3] + inf.shi - inf.l2s, inf.t1)),
-                               inf.t2lb);
-      const float thr = best - inf.two_e;
-      const float add = r < 2 ? inf.off[r] : (r == 2 ? fmaxf(inf.u0, inf.u1) : inf.shi);
-      // A chunk is flagged when (its fp16 maximum) + add >= thr in fp32.  In
-      // fp16: maximum >= th with th <= thr - add, lowered by 2^-18 (|thr| +
-      // |add|) against the fp32 roundings and rounded down to fp16, so every
-      // chunk flagged in fp32 is flagged here (a few more may be).  th stays
-      // finite so that chunks without columns (maximum -inf) stay unflagged.
-      const float theta = (thr - add) - (fabsf(thr) + fabsf(add)) * 3.814697265625e-6f;
-      const __half2 th2 = __half2half2(__float2half_rd(fmaxf(theta, -65504.f)));
-      // Mask word h: logical tiles 2 i + h (i = 0..15), all of them tiles of
-      // stage h or their complements, whose maxima this warp wrote.
-      uint32_t wh = 0;
-#pragma unroll
-      for (int i = kGolayTiles / 2 - 1; i >= 0; --i)
-        wh = (wh << 1) | (__hge2_mask(S.cmax[2 * i + h][slot], th2) & 0x00010001u);
-      if (!(inf.two_e >= 0.f)) wh = 0;
-      if (atom < args.n) {
-        reinterpret_cast<uint32_t *>(args.masks)[(atom * kRowsPerAtom + r) * 2 + h] = wh;
-        if (r == 0 && h == 0) args.info[atom].thr = thr;
-      }
+      // Row maxima of the atom's four rows (both stages), exchanged through
+      // shared memory; every lane has read item j - 1's values before lane 0
+      // arrives.
+      S.rowval[ip][local][r][h] = rowmax;
+      __syncwarp();
+      mbar_arrive_lane0(&S.bar_rows[g][ip], lane);
+      prev_atom = atom;
       ip ^= 1;
+      is = is == 2 ? 0 : is + 1;
     }
+    if (ok && prev_atom >= 0) flags(ip ^ 1, is == 0 ? 2 : is - 1, prev_atom);
   }
 
   tc_fence_before();
