@@ -30,11 +30,12 @@
 //                       operand, and the per-atom constants (AtomInfo).
 //   2. screen_kernel    persistent tcgen05 kernel, one CTA per SM, 64 atoms
 //                       (two M=128 tiles of 32 atoms x 4 rows) per work item;
-//                       the 2048 representative Golay columns stream through a
-//                       shared-memory ring in 16 tiles of 128; M128 N128 K32
-//                       MMAs into two TMEM accumulator stages per M-tile, so
-//                       that the MMAs of one Golay tile run while the epilogue
-//                       reads the previous one.  8 epilogue warps keep, per
+//                       the 2048 representative Golay columns, 16 tiles of
+//                       128, are loaded into shared memory once per CTA and
+//                       stay there; M128 N128 K32 MMAs into two TMEM
+//                       accumulator stages per M-tile, so that the MMAs of one
+//                       Golay tile run while the epilogue reads the previous
+//                       one.  16 epilogue warps keep, per
 //                       row, the maximum of each 64-column chunk and, as minus
 //                       the minimum, that of its complement chunk; at the end of a work
 //                       item they form the atom's best achievable screening
@@ -82,7 +83,6 @@ constexpr int kMTiles = kWorkAtoms * kRowsPerAtom / 128;  // 2
 constexpr int kATileBytes = 128 * kRowBytes;       // 8192
 constexpr int kAItemBytes = kMTiles * kATileBytes; // 16384
 constexpr int kBTileBytes = kGolayTileN * kRowBytes;  // 8192
-constexpr int kStages = 8;                         // Golay tile ring depth
 constexpr int kChunkCols = 64;                     // candidate chunk: half a Golay tile
 constexpr int kScreenTiles = kGolayHalf / kGolayTileN;  // 16 Golay tiles multiplied per work item
 constexpr int kOctTiles = (kOctads + 1 + kGolayTileN - 1) / kGolayTileN;  // 6: tiles holding octad columns
@@ -100,7 +100,6 @@ constexpr int64_t kBatchAtoms = int64_t(1) << 20;  // atoms per pipeline batch
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s (default)
 static_assert(kOctTiles == 6 && kOctTailCol == 120, "octad columns 1-759 fill tiles 0-5 up to column 120 of tile 5");
 static_assert(kScreenTiles % (2 * kAccStages) == 0, "each stage is used an even number of times per item");
-static_assert(kScreenTiles % kStages == 0, "a work item's Golay tiles fill the ring a whole number of times");
 
 // Row type held by TMEM lane quarter q of M-tile g, and its inverse.  The two
 // |x| rows (loaded only for the 6 of the 16 multiplied tiles that hold octad
@@ -150,20 +149,17 @@ static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 
 struct __align__(1024) ScreenSmem {
   uint8_t a[2][kAItemBytes];          // A operand of two work items
-  uint8_t b[kStages][kBTileBytes];    // Golay tile ring
-  // By work-item parity, per logical Golay tile (all 32: the 16 multiplied
-  // ones and their complements) and epilogue thread slot (M-tile, lane
-  // quarter, lane): the maxima of the tile's two 64-column chunks, rounded up
-  // to fp16 (so the flags stay conservative).  Each slot is written and read
-  // by one thread; the flags of a work item are made while the next one is
-  // screened, hence two items.
-  __half2 cmax[2][kGolayTiles][kWorkAtoms * kRowsPerAtom];
+  uint8_t b[kScreenTiles][kBTileBytes];  // the 16 multiplied Golay tiles, loaded once per CTA
+  // Per logical Golay tile (all 32: the 16 multiplied ones and their
+  // complements) and epilogue thread slot (M-tile, lane quarter, lane): the
+  // maxima of the tile's two 64-column chunks, rounded up to fp16 (so the
+  // flags stay conservative).  Each slot is written and read by one thread.
+  __half2 cmax[kGolayTiles][kWorkAtoms * kRowsPerAtom];
   float rowval[2][kWorkAtoms][kRowsPerAtom][kAccStages];  // row maxima, by work-item parity and stage
-  AtomInfo info_st[3][kMTiles][32];   // per-atom constants, by work item modulo 3
+  AtomInfo info_st[2][kMTiles][32];   // per-atom constants of the work item, by work-item parity
   uint64_t bar_a_full[2];
   uint64_t bar_a_empty[2];          // one commit per issuer
-  uint64_t bar_b_full[kStages];
-  uint64_t bar_b_empty[kStages];    // one arrival per epilogue warp of the tile's stage
+  uint64_t bar_b_full;              // the Golay tiles have landed
   uint64_t bar_acc_full[kMTiles][kAccStages];
   uint64_t bar_acc_empty[kMTiles][kAccStages];
   uint64_t bar_rows[kMTiles][2];    // the eight warps of an M-tile, by work-item parity
@@ -171,6 +167,7 @@ struct __align__(1024) ScreenSmem {
   uint32_t tmem_base;
   int abort_flag;
 };
+static_assert(sizeof(ScreenSmem) + 1024 <= 227 * 1024, "screen shared memory (plus alignment) fits one CTA");
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -648,10 +645,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       mbar_init(&S.bar_a_empty[i], kMTiles);
       for (int g = 0; g < kMTiles; ++g) mbar_init(&S.bar_rows[g][i], 4 * kAccStages);
     }
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&S.bar_b_full[s], 1);
-      mbar_init(&S.bar_b_empty[s], kEpiPerStage);
-    }
+    mbar_init(&S.bar_b_full, 1);
     for (int g = 0; g < kMTiles; ++g) {
       for (int s = 0; s < kAccStages; ++s) {
         mbar_init(&S.bar_acc_full[g][s], 1);
@@ -680,10 +674,15 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
       const uint64_t once = policy_evict_first();
-      int bs = 0, ab = 0;
-      uint32_t bph = 0, aph = 0;
-      int last_b[kStages], last_a[2] = {-1, -1};
-      for (int s = 0; s < kStages; ++s) last_b[s] = -1;
+      // The Golay tiles are the same for every work item: all 16 are loaded
+      // once and stay resident, so the MMAs of the two M-tiles never wait on
+      // each other's use of a tile ring.
+      mbar_arrive_expect_tx(&S.bar_b_full, kScreenTiles * kBTileBytes);
+      for (int t = 0; t < kScreenTiles; ++t)
+        bulk_g2s(S.b[t], args.golay + t * kBTileBytes, kBTileBytes, &S.bar_b_full, keep);
+      int ab = 0;
+      uint32_t aph = 0;
+      int last_a[2] = {-1, -1};
       bool ok = true;
       for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
         if (!wait_bar(&S.bar_a_empty[ab], aph ^ 1, abort_flag, args.err, args.wait_limit_ns)) { ok = false; break; }
@@ -691,22 +690,13 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
         bulk_g2s(S.a[ab], args.a_tiles + it * kAItemBytes, kAItemBytes, &S.bar_a_full[ab], once);
         last_a[ab] = static_cast<int>(aph);
         if (++ab == 2) { ab = 0; aph ^= 1; }
-        for (int t = 0; t < kScreenTiles; ++t) {
-          if (!wait_bar(&S.bar_b_empty[bs], bph ^ 1, abort_flag, args.err, args.wait_limit_ns)) { ok = false; break; }
-          mbar_arrive_expect_tx(&S.bar_b_full[bs], kBTileBytes);
-          bulk_g2s(S.b[bs], args.golay + t * kBTileBytes, kBTileBytes, &S.bar_b_full[bs], keep);
-          last_b[bs] = static_cast<int>(bph);
-          if (++bs == kStages) { bs = 0; bph ^= 1; }
-        }
+      }
+      // Let every copy issued land before the CTA leaves (the Golay tiles
+      // too, for a CTA without work items).
+      const unsigned long long t0 = global_ns();
+      while (!mbar_try_wait(&S.bar_b_full, 0) && global_ns() - t0 < args.wait_limit_ns) {
       }
       if (!ok) {
-        // Let every copy already issued land before the CTA leaves.
-        const unsigned long long t0 = global_ns();
-        for (int s = 0; s < kStages; ++s)
-          if (last_b[s] >= 0)
-            while (!mbar_try_wait(&S.bar_b_full[s], static_cast<uint32_t>(last_b[s])) &&
-                   global_ns() - t0 < args.wait_limit_ns) {
-            }
         for (int i = 0; i < 2; ++i)
           if (last_a[i] >= 0)
             while (!mbar_try_wait(&S.bar_a_full[i], static_cast<uint32_t>(last_a[i])) &&
@@ -719,35 +709,34 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     // Golay tile t goes into accumulator stage s = t % 2 of M-tile g (TMEM
     // columns 128 (2 g + s)): one M128 N128 K32 product, two K=16 MMAs.  Stage
     // s is used 16 times per work item, so the release awaited before use
-    // u = t / 2 has parity (u & 1) ^ 1.  The Golay ring slot goes back to the
-    // producer through the epilogue warps, which see the MMAs complete.
+    // u = t / 2 has parity (u & 1) ^ 1.
     const int g = warp - kIssuerWarp;
     // The whole warp runs the loop (converged, uniform values); barrier waits
     // are polled by every lane and the MMAs are issued by the elected lane.
     const uint32_t a0 = smem_u32(S.a[0]), b0 = smem_u32(S.b[0]);
     constexpr uint64_t kKStep = 256 >> 4;  // next 16 K: two 16-byte chunks, descriptor units
-    int bs = 0, ab = 0;
-    uint32_t bph = 0, aph = 0;
-    bool ok = true, issued = false;
+    int ab = 0;
+    uint32_t aph = 0;
+    bool ok = blockIdx.x >= args.items ||
+              wait_bar_warp(&S.bar_b_full, 0, abort_flag, args.err, args.wait_limit_ns);
+    bool issued = false;
     for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
       if (!wait_bar_warp(&S.bar_a_full[ab], aph, abort_flag, args.err, args.wait_limit_ns)) { ok = false; break; }
       tc_fence_after();
       const uint64_t ad = smem_desc(a0 + static_cast<uint32_t>(ab * kAItemBytes + g * kATileBytes));
       for (int t = 0; t < kScreenTiles; ++t) {
         const int s = t & 1;
-        if (!wait_bar_warp(&S.bar_b_full[bs], bph, abort_flag, args.err, args.wait_limit_ns) ||
-            !wait_bar_warp(&S.bar_acc_empty[g][s], ((t >> 1) & 1) ^ 1, abort_flag, args.err, args.wait_limit_ns)) {
+        if (!wait_bar_warp(&S.bar_acc_empty[g][s], ((t >> 1) & 1) ^ 1, abort_flag, args.err, args.wait_limit_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t bd = smem_desc(b0 + static_cast<uint32_t>(bs) * kBTileBytes);
+        const uint64_t bd = smem_desc(b0 + static_cast<uint32_t>(t) * kBTileBytes);
         const uint32_t d = tmem_base + static_cast<uint32_t>((g * kAccStages + s) * kGolayTileN);
         mma_bf16_ss(d, ad, bd, 0);
         mma_bf16_ss(d, ad + kKStep, bd + kKStep, 1);
         mma_commit(&S.bar_acc_full[g][s]);
         issued = true;
-        if (++bs == kStages) { bs = 0; bph ^= 1; }
       }
       if (!ok) break;
       mma_commit(&S.bar_a_empty[ab]);
@@ -778,62 +767,18 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                            static_cast<uint32_t>((g * kAccStages + h) * kGolayTileN);
     bool ok = true;
-    int ip = 0;        // work-item parity: cmax, rowval and bar_rows
-    int is = 0;        // work item modulo 3: info_st
+    int ip = 0;
     uint32_t rph = 0;  // bit i: parity of the next phase of bar_rows[g][i]
-    // The flags of work item j are made after the tile loop of item j + 1, so
-    // the wait for the M-tile's other warps at item j's barrier has a whole
-    // item of slack.  Order per item j: tile loop (cmax[j % 2]); flags of item
-    // j - 1 (wait for its barrier, read rowval, cmax and constants of j - 1);
-    // rowval[j % 2] written and item j's barrier arrived on.  A warp thus
-    // writes rowval[j % 2] only after every warp of the M-tile has arrived on
-    // item j - 1's barrier, i.e. has read item j - 2's row maxima; and the
-    // stager overwrites the constants of item j - 3 only after every warp has
-    // arrived on item j - 2's barrier, having read them.
-    auto flags = [&](int pp, int ps, int64_t patom) -> bool {
-      if (!wait_bar_warp(&S.bar_rows[g][pp], (rph >> pp) & 1u, abort_flag, args.err, args.wait_limit_ns))
-        return false;
-      rph ^= 1u << pp;
-      const AtomInfo inf = S.info_st[ps][g][lane];
-      float rv[kRowsPerAtom];
-#pragma unroll
-      for (int k = 0; k < kRowsPerAtom; ++k) rv[k] = fmaxf(S.rowval[pp][local][k][0], S.rowval[pp][local][k][1]);
-      const float best = fmaxf(fmaxf(fmaxf(rv[0] + inf.off[0], rv[1] + inf.off[1]),
-                                     fmaxf(rv[3] + inf.shi - inf.l2s, inf.t1)),
-                               inf.t2lb);
-      const float thr = best - inf.two_e;
-      const float add = r < 2 ? inf.off[r] : (r == 2 ? fmaxf(inf.u0, inf.u1) : inf.shi);
-      // A chunk is flagged when (its fp16 maximum) + add >= thr in fp32.  In
-      // fp16: maximum >= th with th <= thr - add, lowered by 2^-18 (|thr| +
-      // |add|) against the fp32 roundings and rounded down to fp16, so every
-      // chunk flagged in fp32 is flagged here (a few more may be).  th stays
-      // finite so that chunks without columns (maximum -inf) stay unflagged.
-      const float theta = (thr - add) - (fabsf(thr) + fabsf(add)) * 3.814697265625e-6f;
-      const __half2 th2 = __half2half2(__float2half_rd(fmaxf(theta, -65504.f)));
-      // Mask word h: logical tiles 2 i + h (i = 0..15), all of them tiles of
-      // stage h or their complements, whose maxima this warp wrote.
-      uint32_t wh = 0;
-#pragma unroll
-      for (int i = kGolayTiles / 2 - 1; i >= 0; --i)
-        wh = (wh << 1) | (__hge2_mask(S.cmax[pp][2 * i + h][slot], th2) & 0x00010001u);
-      if (!(inf.two_e >= 0.f)) wh = 0;
-      if (patom < args.n) {
-        reinterpret_cast<uint32_t *>(args.masks)[(patom * kRowsPerAtom + r) * 2 + h] = wh;
-        if (r == 0 && h == 0) args.info[patom].thr = thr;
-      }
-      return true;
-    };
-    int64_t prev_atom = -1;  // this thread's atom in the previous work item
     for (int64_t it = blockIdx.x; ok && it < args.items; it += gridDim.x) {
       const int64_t atom = it * kWorkAtoms + local;
       // One warp per M-tile copies its 32 atoms' constants into shared memory
-      // now; they are read after the item's barrier, so no register holds
-      // them across the tile loop and the copy has the whole item to land.
+      // now; every warp reads them after the item's barrier, so no register
+      // holds them across the tile loop and the copy has the whole item to land.
       const bool stager = q == 0 && h == 0;
       if (stager) {
 #pragma unroll
         for (int k = 0; k < 3; ++k)
-          cp_async16(reinterpret_cast<uint4 *>(&S.info_st[is][g][lane]) + k,
+          cp_async16(reinterpret_cast<uint4 *>(&S.info_st[ip][g][lane]) + k,
                      reinterpret_cast<const uint4 *>(args.info + atom) + k);
         cp_async_commit();
       }
@@ -847,8 +792,6 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
           break;
         }
         tc_fence_after();
-        // The MMAs of tile t are complete: its Golay ring slot may be refilled.
-        mbar_arrive_lane0(&S.bar_b_empty[t % kStages], lane);
         float m0 = -INFINITY, m1 = -INFINITY, n0 = INFINITY, n1 = INFINITY;
         if (r != 3 || t < kOctTiles) {
           // The tile's two 64-column chunks, one TMEM load each.
@@ -881,27 +824,51 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
           __syncwarp();
           mbar_arrive_lane0(&S.bar_acc_empty[g][h], lane);
         }
-        S.cmax[ip][t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
-        S.cmax[ip][t + kScreenTiles][slot] = __halves2half2(__float2half_ru(-n0), __float2half_ru(-n1));
+        S.cmax[t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
+        S.cmax[t + kScreenTiles][slot] = __halves2half2(__float2half_ru(-n0), __float2half_ru(-n1));
         rowmax = fmaxf(fmaxf(rowmax, fmaxf(m0, m1)), fmaxf(-n0, -n1));
       }
       if (stager) cp_async_wait_all();  // the constants are in shared memory before the barrier
       if (!ok) break;
-      if (prev_atom >= 0 && !flags(ip ^ 1, is == 0 ? 2 : is - 1, prev_atom)) {
-        ok = false;
-        break;
-      }
       // Row maxima of the atom's four rows (both stages), exchanged through
-      // shared memory; every lane has read item j - 1's values before lane 0
-      // arrives.
+      // shared memory.
       S.rowval[ip][local][r][h] = rowmax;
       __syncwarp();
       mbar_arrive_lane0(&S.bar_rows[g][ip], lane);
-      prev_atom = atom;
+      if (!wait_bar_warp(&S.bar_rows[g][ip], (rph >> ip) & 1u, abort_flag, args.err, args.wait_limit_ns)) {
+        ok = false;
+        break;
+      }
+      rph ^= 1u << ip;
+      const AtomInfo inf = S.info_st[ip][g][lane];
+      float rv[kRowsPerAtom];
+#pragma unroll
+      for (int k = 0; k < kRowsPerAtom; ++k) rv[k] = fmaxf(S.rowval[ip][local][k][0], S.rowval[ip][local][k][1]);
+      const float best = fmaxf(fmaxf(fmaxf(rv[0] + inf.off[0], rv[1] + inf.off[1]),
+                                     fmaxf(rv[3] + inf.shi - inf.l2s, inf.t1)),
+                               inf.t2lb);
+      const float thr = best - inf.two_e;
+      const float add = r < 2 ? inf.off[r] : (r == 2 ? fmaxf(inf.u0, inf.u1) : inf.shi);
+      // A chunk is flagged when (its fp16 maximum) + add >= thr in fp32.  In
+      // fp16: maximum >= th with th <= thr - add, lowered by 2^-18 (|thr| +
+      // |add|) against the fp32 roundings and rounded down to fp16, so every
+      // chunk flagged in fp32 is flagged here (a few more may be).  th stays
+      // finite so that chunks without columns (maximum -inf) stay unflagged.
+      const float theta = (thr - add) - (fabsf(thr) + fabsf(add)) * 3.814697265625e-6f;
+      const __half2 th2 = __half2half2(__float2half_rd(fmaxf(theta, -65504.f)));
+      // Mask word h: logical tiles 2 i + h (i = 0..15), all of them tiles of
+      // stage h or their complements, whose maxima this warp wrote.
+      uint32_t wh = 0;
+#pragma unroll
+      for (int i = kGolayTiles / 2 - 1; i >= 0; --i)
+        wh = (wh << 1) | (__hge2_mask(S.cmax[2 * i + h][slot], th2) & 0x00010001u);
+      if (!(inf.two_e >= 0.f)) wh = 0;
+      if (atom < args.n) {
+        reinterpret_cast<uint32_t *>(args.masks)[(atom * kRowsPerAtom + r) * 2 + h] = wh;
+        if (r == 0 && h == 0) args.info[atom].thr = thr;
+      }
       ip ^= 1;
-      is = is == 2 ? 0 : is + 1;
     }
-    if (ok && prev_atom >= 0) flags(ip ^ 1, is == 0 ? 2 : is - 1, prev_atom);
   }
 
   tc_fence_before();
