@@ -143,7 +143,7 @@ struct __align__(16) AtomInfo {
   uint8_t p[3];  // p1, p2, p3
   uint8_t pad0;
   float thr;     // best - 2E, written by the screen
-  uint8_t pad[4];
+  int32_t triv;  // index of an atom that needs no search (trivial_index), else -1
 };
 static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 
@@ -411,6 +411,24 @@ __device__ __forceinline__ float max32(float m, const uint32_t *r) {
 // ---------------------------------------------------------------------------
 // 1. prep
 // ---------------------------------------------------------------------------
+// Index for atoms that need no search: non-finite input (training rule: the
+// origin, as the Triton kernel's never-improving running max snaps; pack rule:
+// row 1, torch.max's first NaN), or the pack rule's ||x|| < 1e-8.
+// Returns -1 when a search is needed.
+__device__ __forceinline__ int trivial_index(const float (&v)[kDim], int rule) {
+  bool finite = true;
+#pragma unroll
+  for (int i = 0; i < kDim; ++i) finite = finite && isfinite(v[i]);
+  if (!finite) return rule == H24_RULE_TRAIN ? 0 : 1;
+  if (rule == H24_RULE_PACK) {
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < kDim; ++i) ss = __fma_rn(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
+    if (sqrt(ss) < 1e-8) return 0;
+  }
+  return -1;
+}
+
 // Input atoms of one pipeline batch: segment i holds atoms [start[i],
 // start[i+1]) of the batch, stored contiguously at x[i] (24 elements per
 // atom, all of the batch's element type: fp32, or bf16 widened exactly to
@@ -474,7 +492,7 @@ __device__ __forceinline__ uint32_t a_offset(int L, int q) {
 // 2 plain, 3 |x|).
 template <typename T>
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
-                                                   int64_t n_pad,
+                                                   int64_t n_pad, int rule,
                                                    const uint2 *__restrict__ oct_by_triple,
                                                    uint8_t *__restrict__ a_tiles,
                                                    AtomInfo *__restrict__ info) {
@@ -586,8 +604,10 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   inf.p[2] = static_cast<uint8_t>(q2);
   inf.pad0 = 0;
   inf.thr = -INFINITY;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) inf.pad[k] = 0;
+  // Atoms that need no search: non-finite, or (pack rule) an exact norm below
+  // 1e-8, which needs every |x_i| < 2e-8 first (||x|| >= max |x_i|).
+  inf.triv = !finite ? (rule == H24_RULE_TRAIN ? 0 : 1)
+                     : (rule == H24_RULE_PACK && top[0] < 2e-8f ? trivial_index(v, rule) : -1);
   info[a] = inf;
 
   uint8_t *item = a_tiles + (a / kWorkAtoms) * kAItemBytes;
@@ -909,24 +929,6 @@ __device__ __forceinline__ void better(double &bs, int &bj, double s, int j) {
   }
 }
 
-// Index for atoms that need no search: non-finite input (training rule: the
-// origin, as the Triton kernel's never-improving running max snaps; pack rule:
-// row 1, torch.max's first NaN), or the pack rule's ||x|| < 1e-8.
-// Returns -1 when a search is needed.
-__device__ __forceinline__ int trivial_index(const float (&v)[kDim], int rule) {
-  bool finite = true;
-#pragma unroll
-  for (int i = 0; i < kDim; ++i) finite = finite && isfinite(v[i]);
-  if (!finite) return rule == H24_RULE_TRAIN ? 0 : 1;
-  if (rule == H24_RULE_PACK) {
-    double ss = 0.0;
-#pragma unroll
-    for (int i = 0; i < kDim; ++i) ss = __fma_rn(static_cast<double>(v[i]), static_cast<double>(v[i]), ss);
-    if (sqrt(ss) < 1e-8) return 0;
-  }
-  return -1;
-}
-
 __device__ __forceinline__ int32_t apply_rule(double best, int bj, int rule) {
   if (rule == H24_RULE_TRAIN && 2.0 * best < kCSqNorm) return 0;
   return bj + 1;
@@ -946,9 +948,6 @@ struct RescoreArgs {
   int rule;
 };
 
-// trivial_index for a warp whose lane i < 24 holds x_i in xl (all lanes hold
-// the atom in v): the exact fp64 norm only when the fp32 one is within a
-// factor 4 of the pack rule's 1e-8 (its rounding error is far smaller).
 __device__ __forceinline__ float warp_max(float v) {
   float m;
   asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
@@ -965,21 +964,6 @@ __device__ __forceinline__ uint32_t warp_or(uint32_t v) {
   uint32_t m;
   asm("redux.sync.or.b32 %0, %1, 0xffffffff;" : "=r"(m) : "r"(v));
   return m;
-}
-
-__device__ __forceinline__ float warp_max_abs(float v) {
-  float m;
-  asm("redux.sync.max.abs.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
-  return m;
-}
-
-__device__ __forceinline__ int trivial_index_warp(const float (&v)[kDim], float xl, int lane, int rule) {
-  const bool finite = __all_sync(0xffffffffu, lane >= kDim || isfinite(xl));
-  if (!finite) return rule == H24_RULE_TRAIN ? 0 : 1;
-  // ||x|| >= max |x_i|: only an atom whose |x_i| are all below 2e-8 can have
-  // ||x|| < 1e-8, and only such an atom needs the exact fp64 norm.
-  if (rule == H24_RULE_PACK && warp_max_abs(xl) < 2e-8f) return trivial_index(v, rule);
-  return -1;
 }
 
 // What the rescore reads of one atom, staged in shared memory by cp.async one
@@ -1042,7 +1026,7 @@ __device__ __noinline__ void exact_now(const float (&x)[kDim], const int8_t *__r
 template <typename In>
 __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     rescore_kernel(const __grid_constant__ Segs sg, const RescoreArgs r) {
-  __shared__ float tab[kRescoreWarps][3][256];
+  __shared__ __align__(16) float tab[kRescoreWarps][3][256];
   __shared__ float cand_s[kRescoreWarps][kCandCap];
   __shared__ uint32_t cand_c[kRescoreWarps][kCandCap];
   __shared__ int cand_n[kRescoreWarps];
@@ -1092,7 +1076,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     const AtomStage &A = stage[w][sb];
     const float(&v)[kDim] = A.x;  // the atom, read from the stage when needed
     const float xl = lane < kDim ? A.x[lane] : 0.f;  // lane i: x_i
-    const int triv = trivial_index_warp(v, xl, lane, r.rule);
+    const int triv = A.info.triv;
     // Row r's 64-bit chunk mask, read from the stage when its row is processed.
     const uint64_t *mrow = reinterpret_cast<const uint64_t *>(A.masks);
     const int nch = __popcll(mrow[0]) + __popcll(mrow[1]) + __popcll(mrow[2]) + __popcll(mrow[3]);
@@ -1112,23 +1096,22 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       lb.j = 0x7FFFFFFF;
       lb.n = 0;
       // Partial-sum tables: T[k][s] = sum of x_{8k+i} over the bits i of s.
+      // Lane l writes entries 8 l .. 8 l + 7 (two 16-byte stores): bits 3-7
+      // of s are the bits of l, bits 0-2 run over the eight entries.
 #pragma unroll
       for (int k = 0; k < 3; ++k) {
         const float4 f0 = reinterpret_cast<const float4 *>(A.x)[2 * k];
         const float4 f1 = reinterpret_cast<const float4 *>(A.x)[2 * k + 1];
-        const float v8[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-        float lo5 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 5; ++i)
-          if (lane >> i & 1) lo5 += v8[i];
-#pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          float hi3 = lo5;
-          if (m & 1) hi3 += v8[5];
-          if (m & 2) hi3 += v8[6];
-          if (m & 4) hi3 += v8[7];
-          T[k][lane + 32 * m] = hi3;
-        }
+        float h5 = 0.f;
+        if (lane & 1) h5 += f0.w;
+        if (lane & 2) h5 += f1.x;
+        if (lane & 4) h5 += f1.y;
+        if (lane & 8) h5 += f1.z;
+        if (lane & 16) h5 += f1.w;
+        const float s01 = f0.x + f0.y, s02 = f0.x + f0.z, s12 = f0.y + f0.z, s012 = s01 + f0.z;
+        float4 *dst = reinterpret_cast<float4 *>(&T[k][8 * lane]);
+        dst[0] = make_float4(h5, h5 + f0.x, h5 + f0.y, h5 + s01);
+        dst[1] = make_float4(h5 + f0.z, h5 + s02, h5 + s12, h5 + s012);
       }
       __syncwarp();
       // Sums over the coordinates, lane i holding x_i.
@@ -1276,13 +1259,25 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         }
       }
       __syncwarp();
+      const float two_ep = 3.0517578125e-5f * sumabs;  // 2 e'
+      if (cand_n[w] == 1) {
+        // One listed codeword (the usual case): the unique winner, unless the
+        // training rule's origin test is too close to call in fp32 (below).
+        const float og = cand_s[w][0] * 0.70710678f - static_cast<float>(kCSqNorm);
+        if (r.rule != H24_RULE_TRAIN || fabsf(og) > two_ep) {
+          if (lane == 0)
+            r.out[a] = (r.rule == H24_RULE_TRAIN && og < 0.f)
+                           ? 0
+                           : static_cast<int32_t>(kPendingIndex | cand_c[w][0]);
+          continue;
+        }
+      }
       const int nc = min(cand_n[w], kCandCap);
       heavy = cand_n[w] == 0;  // cannot happen while the bound holds
       if (!heavy) {
         float smax = -INFINITY;
         for (int k = lane; k < nc; k += 32) smax = fmaxf(smax, cand_s[w][k]);
         smax = warp_max(smax);
-        const float two_ep = 3.0517578125e-5f * sumabs;  // 2 e'
         const float cut = smax - two_ep;
         int nin = 0, jin = 0;
         for (int k = lane; k < nc; k += 32) {
@@ -1447,7 +1442,7 @@ int launch_batch_t(const Tables *t, const Segs &sg, int64_t nbatch, int rule, in
     for (auto &e : ev) cudaEventCreate(&e);
   if (timed) cudaEventRecord(ev[0], s);
   prep_kernel<T><<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(
-      sg, nbatch, npad, t->oct_by_triple, sc.a_tiles, sc.info);
+      sg, nbatch, npad, rule, t->oct_by_triple, sc.a_tiles, sc.info);
   if (timed) cudaEventRecord(ev[1], s);
   ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
                 nbatch, items, t->err, kWaitLimitNs};
