@@ -35,12 +35,14 @@
 //                       stay there; M128 N128 K32 MMAs into two TMEM
 //                       accumulator stages per M-tile, so that the MMAs of one
 //                       Golay tile run while the epilogue reads the previous
-//                       one.  16 epilogue warps keep, per
-//                       row, the maximum of each 64-column chunk and, as minus
-//                       the minimum, that of its complement chunk; at the end of a work
-//                       item they form the atom's best achievable screening
-//                       score and flag every chunk that may hold a codeword
-//                       within 2E of it (one 64-bit mask per row).
+//                       one.  16 epilogue warps keep, per row and 64-column
+//                       chunk, the maximum of |S| (rows 0-2: the chunk and its
+//                       complement chunk, whose scores are negated, at once)
+//                       or, for the |x| row, minus the minimum (the maximum of
+//                       the complement chunk); at the end of a work item they
+//                       form the atom's best achievable screening score and
+//                       flag every chunk (pair) that may hold a codeword within
+//                       2E of it (one 64-bit mask per row).
 //   3. rescore_kernel   one warp per atom: fp32 scores (from per-atom
 //                       partial-sum tables) of the codewords behind the
 //                       flagged chunks; a unique best within the fp32 error
@@ -119,8 +121,11 @@ static_assert(row_of_quarter(0, quarter_of_row(0, 1)) == 1 && row_of_quarter(0, 
               "quarter <-> row type maps are inverse, |x| rows in quarters 1 and 2");
 
 // Chunk of bit b of a row's 64-bit flag mask: bits 32 s + i and 32 s + 16 + i
-// hold the chunks 2 t and 2 t + 1 of Golay tile t = 2 i + s (the tiles of
-// accumulator stage s fill one 32-bit half of the mask).
+// hold the chunks 2 t and 2 t + 1 of logical Golay tile t = 2 i + s (the
+// tiles of accumulator stage s fill one 32-bit half of the mask); chunks 32-63
+// are the complements of chunks 0-31.  Rows 0-2 set only bits of chunks 0-31,
+// each flagging the chunk together with its complement; the |x| row sets only
+// bits of complement chunks (the weight-16 words).
 __host__ __device__ constexpr int chunk_of_bit(int b) {
   return 4 * (b & 15) + 2 * (b >> 5) + ((b >> 4) & 1);
 }
@@ -150,11 +155,13 @@ static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 struct __align__(1024) ScreenSmem {
   uint8_t a[2][kAItemBytes];          // A operand of two work items
   uint8_t b[kScreenTiles][kBTileBytes];  // the 16 multiplied Golay tiles, loaded once per CTA
-  // Per logical Golay tile (all 32: the 16 multiplied ones and their
-  // complements) and epilogue thread slot (M-tile, lane quarter, lane): the
-  // maxima of the tile's two 64-column chunks, rounded up to fp16 (so the
-  // flags stay conservative).  Each slot is written and read by one thread.
-  __half2 cmax[kGolayTiles][kWorkAtoms * kRowsPerAtom];
+  // Per multiplied Golay tile and epilogue thread slot (M-tile, lane
+  // quarter, lane), for each of the tile's two 64-column chunks, rounded up
+  // to fp16 (so the flags stay conservative): rows 0-2, the maximum of |S|,
+  // i.e. the larger of the chunk's maximum and its complement chunk's; the
+  // |x| row, the maximum over the complement chunk (minus the minimum).
+  // Each slot is written and read by one thread.
+  __half2 cmax[kScreenTiles][kWorkAtoms * kRowsPerAtom];
   float rowval[2][kWorkAtoms][kRowsPerAtom][kAccStages];  // row maxima, by work-item parity and stage
   AtomInfo info_st[2][kMTiles][32];   // per-atom constants of the work item, by work-item parity
   uint64_t bar_a_full[2];
@@ -395,14 +402,15 @@ __device__ __forceinline__ float min32(float m, const uint32_t *r) {
   return fmin3(fmin3(u0, u1, u2), t[9], t[10]);
 }
 
-// max(m, the 32 fp32 values held as raw bits): a tree of 3-input max.
-__device__ __forceinline__ float max32(float m, const uint32_t *r) {
+// max(m, |the 32 fp32 values held as raw bits|): a tree of 3-input max (the
+// absolute values are operand modifiers of the max, not extra instructions).
+__device__ __forceinline__ float max32abs(float m, const uint32_t *r) {
   float t[11];
 #pragma unroll
   for (int k = 0; k < 10; ++k)
-    t[k] = fmax3(__uint_as_float(r[3 * k]), __uint_as_float(r[3 * k + 1]),
-                 __uint_as_float(r[3 * k + 2]));
-  t[10] = fmax3(__uint_as_float(r[30]), __uint_as_float(r[31]), m);
+    t[k] = fmax3(fabsf(__uint_as_float(r[3 * k])), fabsf(__uint_as_float(r[3 * k + 1])),
+                 fabsf(__uint_as_float(r[3 * k + 2])));
+  t[10] = fmax3(fabsf(__uint_as_float(r[30])), fabsf(__uint_as_float(r[31])), m);
   const float u0 = fmax3(t[0], t[1], t[2]), u1 = fmax3(t[3], t[4], t[5]);
   const float u2 = fmax3(t[6], t[7], t[8]);
   return fmax3(fmax3(u0, u1, u2), t[9], t[10]);
@@ -804,7 +812,9 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       }
       float rowmax = -INFINITY;
       // Tile t holds columns 128 t .. 128 t + 127; the complements of its two
-      // chunks form logical tile t + 16, whose maxima are minus the minima.
+      // chunks form logical tile t + 16, where every score is negated.  Rows
+      // 0-2 keep max |S| per chunk: one flag for a chunk and its complement.
+      // The |x| row keeps minus the minimum (its complement chunk's maximum).
 #pragma unroll 1
       for (int t = h; t < kScreenTiles; t += kAccStages) {
         if (!wait_bar_warp(&S.bar_acc_full[g][h], (t >> 1) & 1, abort_flag, args.err, args.wait_limit_ns)) {
@@ -812,7 +822,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
           break;
         }
         tc_fence_after();
-        float m0 = -INFINITY, m1 = -INFINITY, n0 = INFINITY, n1 = INFINITY;
+        float m0 = -INFINITY, m1 = -INFINITY;
         if (r != 3 || t < kOctTiles) {
           // The tile's two 64-column chunks, one TMEM load each.
           uint32_t x[64];
@@ -821,10 +831,10 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
             // The |x| row counts only at the weight-16 words, the complements
             // of the octad columns 1-759: minima over those alone.
             if (t == 0) x[0] = 0x7F800000u;  // zero word (its complement: all ones)
+            m0 = -min32(min32(INFINITY, x), x + 32);
           } else {
-            m0 = max32(max32(-INFINITY, x), x + 32);
+            m0 = max32abs(max32abs(0.f, x), x + 32);
           }
-          n0 = min32(min32(INFINITY, x), x + 32);
           tmem_ld64_wait(t_row + 64u, x);
           // Loaded: hand the stage back to the MMA issuer.
           tc_fence_before();
@@ -835,18 +845,17 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
 #pragma unroll
               for (int j2 = kOctTailCol - 64; j2 < 64; ++j2) x[j2] = 0x7F800000u;  // dodecads
             }
+            m1 = -min32(min32(INFINITY, x), x + 32);
           } else {
-            m1 = max32(max32(-INFINITY, x), x + 32);
+            m1 = max32abs(max32abs(0.f, x), x + 32);
           }
-          n1 = min32(min32(INFINITY, x), x + 32);
         } else {
           tc_fence_before();
           __syncwarp();
           mbar_arrive_lane0(&S.bar_acc_empty[g][h], lane);
         }
         S.cmax[t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
-        S.cmax[t + kScreenTiles][slot] = __halves2half2(__float2half_ru(-n0), __float2half_ru(-n1));
-        rowmax = fmaxf(fmaxf(rowmax, fmaxf(m0, m1)), fmaxf(-n0, -n1));
+        rowmax = fmaxf(rowmax, fmaxf(m0, m1));
       }
       if (stager) cp_async_wait_all();  // the constants are in shared memory before the barrier
       if (!ok) break;
@@ -876,12 +885,16 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       // finite so that chunks without columns (maximum -inf) stay unflagged.
       const float theta = (thr - add) - (fabsf(thr) + fabsf(add)) * 3.814697265625e-6f;
       const __half2 th2 = __half2half2(__float2half_rd(fmaxf(theta, -65504.f)));
-      // Mask word h: logical tiles 2 i + h (i = 0..15), all of them tiles of
-      // stage h or their complements, whose maxima this warp wrote.
+      // Mask word h: bits i and 16 + i hold chunks 0 and 1 of logical tile
+      // 2 i + h (i = 0..15).  This warp wrote the maxima of tiles 2 i + h,
+      // i < 8: for rows 0-2 their bits (flagging each chunk together with its
+      // complement), for the |x| row the bits of their complements, logical
+      // tiles 2 (i + 8) + h.
       uint32_t wh = 0;
 #pragma unroll
-      for (int i = kGolayTiles / 2 - 1; i >= 0; --i)
+      for (int i = kScreenTiles / 2 - 1; i >= 0; --i)
         wh = (wh << 1) | (__hge2_mask(S.cmax[2 * i + h][slot], th2) & 0x00010001u);
+      if (r == 3) wh <<= kScreenTiles / 2;
       if (!(inf.two_e >= 0.f)) wh = 0;
       if (atom < args.n) {
         reinterpret_cast<uint32_t *>(args.masks)[(atom * kRowsPerAtom + r) * 2 + h] = wh;
@@ -1045,9 +1058,14 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   // fills only the first three chunks of the coordinates, as bit patterns,
   // and is widened in place once it has landed).
   constexpr int kXChunks = atom_chunks<In>();
+  // The atoms a warp visits only increase, so its segment is found by
+  // advancing a cursor rather than by a search per atom.
+  int seg = 0;
   const auto prefetch = [&](int64_t a, int s) {
     if (a < r.n) {
-      const uint4 *xa = reinterpret_cast<const uint4 *>(atom_ptr<In>(sg, a));
+      while (seg + 1 < sg.count && sg.start[seg + 1] <= a) ++seg;
+      const uint4 *xa = reinterpret_cast<const uint4 *>(static_cast<const In *>(sg.x[seg]) +
+                                                        (a - sg.start[seg]) * kDim);
       const uint4 *src = lane < 6 ? xa + lane
                                   : (lane < 8 ? r.masks + 2 * a + (lane - 6)
                                               : reinterpret_cast<const uint4 *>(r.info + a) + (lane - 8));
@@ -1078,8 +1096,9 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     const float xl = lane < kDim ? A.x[lane] : 0.f;  // lane i: x_i
     const int triv = A.info.triv;
     // Row r's 64-bit chunk mask, read from the stage when its row is processed.
+    // A flag of rows 0-2 stands for a chunk and its complement: two chunks.
     const uint64_t *mrow = reinterpret_cast<const uint64_t *>(A.masks);
-    const int nch = __popcll(mrow[0]) + __popcll(mrow[1]) + __popcll(mrow[2]) + __popcll(mrow[3]);
+    const int nch = 2 * (__popcll(mrow[0]) + __popcll(mrow[1]) + __popcll(mrow[2])) + __popcll(mrow[3]);
     if (triv >= 0) {
       if (lane == 0) r.out[a] = triv;
       continue;
@@ -1130,7 +1149,10 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         }
       };
       const int p1 = inf.p[0], p2 = inf.p[1], p3 = inf.p[2];
-      // Type 3 at the slice positions p1, p2.
+      // Type 3 at the slice positions p1, p2.  A flagged chunk of rows 0-2
+      // stands for its columns c < 2048 and their complements c + 2048, whose
+      // sums over the coordinates are sum(x) minus theirs: S(c + 2048) =
+      // -S(c) for the plain scores.
 #pragma unroll 1
       for (int s = 0; s < 2; ++s) {
         uint64_t m = s ? mrow[1] : mrow[0];
@@ -1143,8 +1165,12 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
           for (int k = 0; k < 2; ++k) {
             const int c = b * kChunkCols + 32 * k + lane;
             const uint32_t gm = gmask_s[c];
-            const float sc = sumx - 2.f * tsum(gm) - xp * ((gm >> p & 1u) ? 2.f : 4.f);
+            const float base = sumx - 2.f * tsum(gm);
+            const bool in = (gm >> p & 1u) != 0;
+            const float sc = base - xp * (in ? 2.f : 4.f);
             if (sc >= thr) push(sc, kCandType3 | static_cast<uint32_t>(c * kDim + p));
+            const float scc = -base - xp * (in ? 4.f : 2.f);
+            if (scc >= thr) push(scc, kCandType3 | static_cast<uint32_t>((c + kGolayHalf) * kDim + p));
           }
         }
       }
@@ -1161,15 +1187,24 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
             const int c = b * kChunkCols + 32 * k + lane;
             const uint32_t gm = gmask_s[c];
             const float bc = sumx - 2.f * tsum(gm);
-            uint32_t bal = __ballot_sync(0xffffffffu, bc + ((gm >> p3 & 1u) ? inf.u1 : inf.u0) >= thr);
+            const bool in3 = (gm >> p3 & 1u) != 0;
+            // Bit j < 32: column c of lane j; bit 32 + j: its complement.
+            uint64_t bal = __ballot_sync(0xffffffffu, bc + (in3 ? inf.u1 : inf.u0) >= thr) |
+                           static_cast<uint64_t>(__ballot_sync(0xffffffffu, -bc + (in3 ? inf.u0 : inf.u1) >= thr))
+                               << 32;
             while (bal) {
-              const int src = __ffs(bal) - 1;
+              const int bit = __ffsll(bal) - 1;
               bal &= bal - 1;
-              const uint32_t gmc = __shfl_sync(0xffffffffu, gm, src);
-              const float bcc = __shfl_sync(0xffffffffu, bc, src);
+              const int src = bit & 31;
+              const bool comp = bit >= 32;
+              const uint32_t gsrc = __shfl_sync(0xffffffffu, gm, src);
+              const float bsrc = __shfl_sync(0xffffffffu, bc, src);
+              const uint32_t gmc = comp ? ~gsrc & 0xFFFFFFu : gsrc;
+              const float bcc = comp ? -bsrc : bsrc;
               const float sc = bcc - xl * ((gmc >> lane & 1u) ? 2.f : 4.f);
+              const int col = b * kChunkCols + 32 * k + src + (comp ? kGolayHalf : 0);
               if (lane < kDim && lane != p1 && lane != p2 && sc >= thr)
-                push(sc, kCandType3 | static_cast<uint32_t>((b * kChunkCols + 32 * k + src) * kDim + lane));
+                push(sc, kCandType3 | static_cast<uint32_t>(col * kDim + lane));
             }
           }
         }
