@@ -466,7 +466,7 @@ def run_ours(args) -> None:
             "gpu_launches": launches,
             "clocks": clk,
             "search_stats": {"exhaustive_atoms": exhaustive, "exact_scores": exact_scores,
-                             "flagged_chunks": chunks, "atoms": atoms_timed,
+                             "flagged_32col_units": chunks, "atoms": atoms_timed,
                              "exhaustive_scan_equivalent_tflops":
                                  value * 1e9 * EXHAUSTIVE_FLOP_PER_ATOM / 1e12},
             "allgather": gather,
@@ -576,7 +576,7 @@ def run_stress(args, dev):
     rep = {"atoms": n, "rule": "training (castor_quantize_leech)", "ms": ms,
            "G_atoms_per_s": n / (ms / 1e3) / 1e9,
            "exhaustive_atoms_per_call": exh / reps, "exact_fp64_scores_per_atom": exact_scores / (reps * n),
-           "flagged_chunks_per_atom": chunks / (reps * n)}
+           "flagged_32col_units_per_atom": chunks / (reps * n)}
     # Against the reference's fixtures: fp64 squared distances on the GPU.
     g = np.load(os.path.join(HERE, "tests", "golden", "stress.npz"))
     xg = torch.from_numpy(g["atoms"]).to(dev)
@@ -663,7 +663,7 @@ def run_search_only(args) -> None:
                       "rescore_ms_per_call": kt["rescore_kernel"][0] / args.steps,
                       "prep_ms_per_call": kt["prep_kernel"][0] / args.steps,
                       "exhaustive_per_atom": exhaustive / n, "exact_scores_per_atom": exact_scores / n,
-                      "flagged_chunks_per_atom": chunks / n}), flush=True)
+                      "flagged_32col_units_per_atom": chunks / n}), flush=True)
 
 
 def run_components(args) -> dict:

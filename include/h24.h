@@ -295,8 +295,9 @@ int h24_timing_read_kernel(int kernel, double *ms, int64_t *launches);
 /* Counters accumulated by the quantize calls on the current device since the
  * previous read (reading resets them; synchronises `stream`): atoms resolved
  * by the exhaustive fp64 scan, codewords scored exactly in fp64 by the
- * rescore, and 128-codeword candidate chunks flagged by the screen. */
-int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *exact_scores, int64_t *flagged_chunks,
+ * rescore, and the 32-column units behind the screen's flags (a flag of the
+ * rows that also stand for the complements counts two). */
+int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *exact_scores, int64_t *flagged_units,
                        void *stream);
 
 /* Number of CUDA kernels this library has launched in this process. */

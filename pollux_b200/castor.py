@@ -340,7 +340,7 @@ def device_check(device=None) -> None:
 
 def quantize_stats(device=None) -> tuple[int, int, int]:
     """(atoms resolved by the exhaustive scan, codewords scored exactly in
-    fp64, candidate chunks flagged by the screen) since the last read."""
+    fp64, 32-column units behind the screen's flags) since the last read."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     a, b, c = ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int64(0)
     _call(dev, "h24_quantize_stats", ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), _stream(dev))

@@ -865,7 +865,7 @@ int h24_timing_read(double *ms, int64_t *launches) {
   return h24_timing_read_kernel(H24_KERNEL_SCREEN, ms, launches);
 }
 
-int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *exact_scores, int64_t *flagged_chunks,
+int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *exact_scores, int64_t *flagged_units,
                        void *stream) {
   H24_TABLES_OR_FAIL(T);
   int64_t h[3] = {0, 0, 0};
@@ -875,7 +875,7 @@ int h24_quantize_stats(int64_t *exhaustive_atoms, int64_t *exact_scores, int64_t
   H24_CUDA_TRY(cudaMemsetAsync(T->stats, 0, sizeof(h), s));
   if (exhaustive_atoms) *exhaustive_atoms = h[0];
   if (exact_scores) *exact_scores = h[1];
-  if (flagged_chunks) *flagged_chunks = h[2];
+  if (flagged_units) *flagged_units = h[2];
   return H24_OK;
 }
 

@@ -35,23 +35,23 @@
 //                       stay there; M128 N128 K32 MMAs into two TMEM
 //                       accumulator stages per M-tile, so that the MMAs of one
 //                       Golay tile run while the epilogue reads the previous
-//                       one.  16 epilogue warps keep, per row and 64-column
-//                       chunk, the maximum of |S| (rows 0-2: the chunk and its
-//                       complement chunk, whose scores are negated, at once)
-//                       or, for the |x| row, minus the minimum (the maximum of
-//                       the complement chunk); at the end of a work item they
-//                       form the atom's best achievable screening score and
-//                       flag every chunk (pair) that may hold a codeword within
-//                       2E of it (one 64-bit mask per row).
+//                       one.  16 epilogue warps keep, per row and 32-column
+//                       sub-chunk, the maximum of |S| (rows 0-2: the columns
+//                       and their complements, whose scores are negated, at
+//                       once) or, for the |x| row, minus the minimum (the
+//                       maximum over the complements); at the end of a work
+//                       item they form the atom's best achievable screening
+//                       score and flag every sub-chunk that may hold a
+//                       codeword within 2E of it (one 64-bit mask per row).
 //   3. rescore_kernel   one warp per atom: fp32 scores (from per-atom
 //                       partial-sum tables) of the codewords behind the
-//                       flagged chunks; a unique best within the fp32 error
+//                       flagged sub-chunks; a unique best within the fp32 error
 //                       bound is the winner, otherwise fp64 scores in the
 //                       reference's order for those within the bound, lowest
 //                       index on ties; then the origin rule.
 //   4. exhaustive_kernel  fp64 scan of all codewords for atoms with more than
-//                       kHeavyChunks flagged chunks (exact ties over many
-//                       codewords).
+//                       kHeavySubs flagged 32-column units (exact ties over
+//                       many codewords).
 //   5. decode_kernel    kissing-point index of each rescore winner, looked up
 //                       in bulk from its candidate code.
 //
@@ -85,7 +85,7 @@ constexpr int kMTiles = kWorkAtoms * kRowsPerAtom / 128;  // 2
 constexpr int kATileBytes = 128 * kRowBytes;       // 8192
 constexpr int kAItemBytes = kMTiles * kATileBytes; // 16384
 constexpr int kBTileBytes = kGolayTileN * kRowBytes;  // 8192
-constexpr int kChunkCols = 64;                     // candidate chunk: half a Golay tile
+constexpr int kSubCols = 32;                       // flagged sub-chunk: a quarter of a Golay tile
 constexpr int kScreenTiles = kGolayHalf / kGolayTileN;  // 16 Golay tiles multiplied per work item
 constexpr int kOctTiles = (kOctads + 1 + kGolayTileN - 1) / kGolayTileN;  // 6: tiles holding octad columns
 constexpr int kOctTailCol = kOctads + 1 - (kOctTiles - 1) * kGolayTileN;  // 120: dodecads from here in tile 5
@@ -96,7 +96,7 @@ constexpr int kProducerWarp = kEpiWarps;           // warp 16: TMA producer
 constexpr int kIssuerWarp = kEpiWarps + 1;         // warps 17-18: MMA issuer of M-tile 0, 1
 constexpr int kScreenThreads = 32 * (kEpiWarps + 1 + kMTiles);  // 608
 constexpr uint32_t kTmemCols = kMTiles * kAccStages * kGolayTileN;  // 512
-constexpr int kHeavyChunks = 192;                  // flagged chunks (of 204) beyond which the exhaustive scan runs
+constexpr int kHeavySubs = 384;                    // flagged 32-column units (of 408) beyond which the exhaustive scan runs
 constexpr int kMaxSegs = 64;                       // input segments per pipeline batch
 constexpr int64_t kBatchAtoms = int64_t(1) << 20;  // atoms per pipeline batch
 constexpr unsigned long long kWaitLimitNs = 4000000000ull;  // bounded waits: 4 s (default)
@@ -120,17 +120,17 @@ static_assert(row_of_quarter(0, quarter_of_row(0, 1)) == 1 && row_of_quarter(0, 
                   quarter_of_row(1, 3) == 2,
               "quarter <-> row type maps are inverse, |x| rows in quarters 1 and 2");
 
-// Chunk of bit b of a row's 64-bit flag mask: bits 32 s + i and 32 s + 16 + i
-// hold the chunks 2 t and 2 t + 1 of logical Golay tile t = 2 i + s (the
-// tiles of accumulator stage s fill one 32-bit half of the mask); chunks 32-63
-// are the complements of chunks 0-31.  Rows 0-2 set only bits of chunks 0-31,
-// each flagging the chunk together with its complement; the |x| row sets only
-// bits of complement chunks (the weight-16 words).
-__host__ __device__ constexpr int chunk_of_bit(int b) {
-  return 4 * (b & 15) + 2 * (b >> 5) + ((b >> 4) & 1);
+// Sub-chunk of bit b of a row's 64-bit flag mask: bit 32 s + 4 i + j holds
+// sub-chunk j (columns 32 j .. 32 j + 31) of Golay tile t = 2 i + s, i.e.
+// columns 32 u .. 32 u + 31 for u = 4 t + j (the tiles of accumulator stage s
+// fill one 32-bit half of the mask).  For rows 0-2 a bit flags those columns
+// together with their complements (columns + 2048); for the |x| row it flags
+// only the complements (the weight-16 words).
+__host__ __device__ constexpr int sub_of_bit(int b) {
+  return 8 * ((b & 31) >> 2) + 4 * (b >> 5) + (b & 3);
 }
-static_assert(chunk_of_bit(0) == 0 && chunk_of_bit(16) == 1 && chunk_of_bit(32) == 2 &&
-                  chunk_of_bit(48) == 3 && chunk_of_bit(1) == 4 && chunk_of_bit(63) == 63,
+static_assert(sub_of_bit(0) == 0 && sub_of_bit(3) == 3 && sub_of_bit(32) == 4 && sub_of_bit(4) == 8 &&
+                  sub_of_bit(63) == 63,
               "mask bit order");
 
 // Per-atom constants of the search (prep_kernel -> screen and rescore).
@@ -155,13 +155,13 @@ static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 struct __align__(1024) ScreenSmem {
   uint8_t a[2][kAItemBytes];          // A operand of two work items
   uint8_t b[kScreenTiles][kBTileBytes];  // the 16 multiplied Golay tiles, loaded once per CTA
-  // Per multiplied Golay tile and epilogue thread slot (M-tile, lane
-  // quarter, lane), for each of the tile's two 64-column chunks, rounded up
-  // to fp16 (so the flags stay conservative): rows 0-2, the maximum of |S|,
-  // i.e. the larger of the chunk's maximum and its complement chunk's; the
-  // |x| row, the maximum over the complement chunk (minus the minimum).
-  // Each slot is written and read by one thread.
-  __half2 cmax[kScreenTiles][kWorkAtoms * kRowsPerAtom];
+  // Per multiplied Golay tile, pair of 32-column sub-chunks (0-1, 2-3) and
+  // epilogue thread slot (M-tile, lane quarter, lane), rounded up to fp16 (so
+  // the flags stay conservative): rows 0-2, the maximum of |S| over the
+  // sub-chunk, i.e. the larger of its maximum and its complement's; the |x|
+  // row, the maximum over the complement sub-chunk (minus the minimum).
+  // Each entry is written and read by one thread.
+  __half2 cmax[kScreenTiles][2][kWorkAtoms * kRowsPerAtom];
   float rowval[2][kWorkAtoms][kRowsPerAtom][kAccStages];  // row maxima, by work-item parity and stage
   AtomInfo info_st[2][kMTiles][32];   // per-atom constants of the work item, by work-item parity
   uint64_t bar_a_full[2];
@@ -652,7 +652,7 @@ struct ScreenArgs {
   const uint8_t *a_tiles;   // [items][kAItemBytes]
   AtomInfo *info;           // [n_pad]; the screen fills in thr
   const uint8_t *golay;     // [kGolayTiles][kBTileBytes]
-  uint2 *masks;             // [n][4] flagged 64-column chunks per row type
+  uint2 *masks;             // [n][4] flagged 32-column sub-chunks per row type
   int64_t n;
   int64_t items;
   int *err;
@@ -822,18 +822,20 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
           break;
         }
         tc_fence_after();
-        float m0 = -INFINITY, m1 = -INFINITY;
+        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
         if (r != 3 || t < kOctTiles) {
-          // The tile's two 64-column chunks, one TMEM load each.
+          // The tile's two 64-column halves, one TMEM load each.
           uint32_t x[64];
           tmem_ld64_wait(t_row, x);
           if (r == 3) {
             // The |x| row counts only at the weight-16 words, the complements
             // of the octad columns 1-759: minima over those alone.
             if (t == 0) x[0] = 0x7F800000u;  // zero word (its complement: all ones)
-            m0 = -min32(min32(INFINITY, x), x + 32);
+            m0 = -min32(INFINITY, x);
+            m1 = -min32(INFINITY, x + 32);
           } else {
-            m0 = max32abs(max32abs(0.f, x), x + 32);
+            m0 = max32abs(0.f, x);
+            m1 = max32abs(0.f, x + 32);
           }
           tmem_ld64_wait(t_row + 64u, x);
           // Loaded: hand the stage back to the MMA issuer.
@@ -845,17 +847,20 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
 #pragma unroll
               for (int j2 = kOctTailCol - 64; j2 < 64; ++j2) x[j2] = 0x7F800000u;  // dodecads
             }
-            m1 = -min32(min32(INFINITY, x), x + 32);
+            m2 = -min32(INFINITY, x);
+            m3 = -min32(INFINITY, x + 32);
           } else {
-            m1 = max32abs(max32abs(0.f, x), x + 32);
+            m2 = max32abs(0.f, x);
+            m3 = max32abs(0.f, x + 32);
           }
         } else {
           tc_fence_before();
           __syncwarp();
           mbar_arrive_lane0(&S.bar_acc_empty[g][h], lane);
         }
-        S.cmax[t][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
-        rowmax = fmaxf(rowmax, fmaxf(m0, m1));
+        S.cmax[t][0][slot] = __halves2half2(__float2half_ru(m0), __float2half_ru(m1));
+        S.cmax[t][1][slot] = __halves2half2(__float2half_ru(m2), __float2half_ru(m3));
+        rowmax = fmaxf(rowmax, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
       }
       if (stager) cp_async_wait_all();  // the constants are in shared memory before the barrier
       if (!ok) break;
@@ -885,16 +890,15 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
       // finite so that chunks without columns (maximum -inf) stay unflagged.
       const float theta = (thr - add) - (fabsf(thr) + fabsf(add)) * 3.814697265625e-6f;
       const __half2 th2 = __half2half2(__float2half_rd(fmaxf(theta, -65504.f)));
-      // Mask word h: bits i and 16 + i hold chunks 0 and 1 of logical tile
-      // 2 i + h (i = 0..15).  This warp wrote the maxima of tiles 2 i + h,
-      // i < 8: for rows 0-2 their bits (flagging each chunk together with its
-      // complement), for the |x| row the bits of their complements, logical
-      // tiles 2 (i + 8) + h.
+      // Mask word h: bit 4 i + j holds sub-chunk j of tile 2 i + h (i = 0..7),
+      // whose maxima this warp wrote.
       uint32_t wh = 0;
 #pragma unroll
-      for (int i = kScreenTiles / 2 - 1; i >= 0; --i)
-        wh = (wh << 1) | (__hge2_mask(S.cmax[2 * i + h][slot], th2) & 0x00010001u);
-      if (r == 3) wh <<= kScreenTiles / 2;
+      for (int i = kScreenTiles / 2 - 1; i >= 0; --i) {
+        const uint32_t f0 = __hge2_mask(S.cmax[2 * i + h][0][slot], th2);
+        const uint32_t f1 = __hge2_mask(S.cmax[2 * i + h][1][slot], th2);
+        wh = (wh << 4) | (f0 & 1u) | ((f0 >> 15) & 2u) | ((f1 << 2) & 4u) | ((f1 >> 13) & 8u);
+      }
       if (!(inf.two_e >= 0.f)) wh = 0;
       if (atom < args.n) {
         reinterpret_cast<uint32_t *>(args.masks)[(atom * kRowsPerAtom + r) * 2 + h] = wh;
@@ -956,7 +960,7 @@ struct RescoreArgs {
   int32_t *out;
   int32_t *ovf_list;
   int32_t *ovf_count;
-  int64_t *stats;            // [0] exhaustive atoms, [1] exact scores, [2] flagged chunks
+  int64_t *stats;            // [0] exhaustive atoms, [1] exact scores, [2] flagged 32-column units
   int64_t n;
   int rule;
 };
@@ -1030,7 +1034,7 @@ __device__ __noinline__ void exact_now(const float (&x)[kDim], const int8_t *__r
 // barrier inside the loop, so a slow atom holds up only its own warp.
 //
 // Pass 1 recomputes the screening score S' of every codeword behind the
-// flagged chunks in fp32 from the exact coordinates (sum_{i in c} x_i is
+// flagged sub-chunks in fp32 from the exact coordinates (sum_{i in c} x_i is
 // three lookups in per-atom tables of the partial sums over each byte of the
 // position mask) and lists those with S' >= thr = best - 2E.  Pass 2 scores
 // in fp64, in the reference's order, the listed codewords within 2 e' of the
@@ -1095,8 +1099,9 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     const float(&v)[kDim] = A.x;  // the atom, read from the stage when needed
     const float xl = lane < kDim ? A.x[lane] : 0.f;  // lane i: x_i
     const int triv = A.info.triv;
-    // Row r's 64-bit chunk mask, read from the stage when its row is processed.
-    // A flag of rows 0-2 stands for a chunk and its complement: two chunks.
+    // Row r's 64-bit sub-chunk mask, read from the stage when its row is
+    // processed.  A flag of rows 0-2 stands for 32 columns and their
+    // complements: two 32-column units.
     const uint64_t *mrow = reinterpret_cast<const uint64_t *>(A.masks);
     const int nch = 2 * (__popcll(mrow[0]) + __popcll(mrow[1]) + __popcll(mrow[2])) + __popcll(mrow[3]);
     if (triv >= 0) {
@@ -1104,7 +1109,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       continue;
     }
     st_chunks += nch;
-    bool heavy = nch > kHeavyChunks;
+    bool heavy = nch > kHeavySubs;
     if (!heavy) {
       const float thr = A.info.thr;
       const AtomInfo inf = A.info;
@@ -1149,42 +1154,37 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         }
       };
       const int p1 = inf.p[0], p2 = inf.p[1], p3 = inf.p[2];
-      // Type 3 at the slice positions p1, p2.  A flagged chunk of rows 0-2
-      // stands for its columns c < 2048 and their complements c + 2048, whose
-      // sums over the coordinates are sum(x) minus theirs: S(c + 2048) =
-      // -S(c) for the plain scores.
+      // Type 3 at the slice positions p1, p2.  A flagged sub-chunk of rows
+      // 0-2 stands for its columns c < 2048 and their complements c + 2048,
+      // whose sums over the coordinates are sum(x) minus theirs: S(c + 2048)
+      // = -S(c) for the plain scores.  Lane i takes column 32 u + i.
 #pragma unroll 1
       for (int s = 0; s < 2; ++s) {
         uint64_t m = s ? mrow[1] : mrow[0];
         const int p = s ? p2 : p1;
         const float xp = __shfl_sync(0xffffffffu, xl, p);
         while (m) {
-          const int b = chunk_of_bit(__ffsll(m) - 1);
+          const int c = sub_of_bit(__ffsll(m) - 1) * kSubCols + lane;
           m &= m - 1;
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int c = b * kChunkCols + 32 * k + lane;
-            const uint32_t gm = gmask_s[c];
-            const float base = sumx - 2.f * tsum(gm);
-            const bool in = (gm >> p & 1u) != 0;
-            const float sc = base - xp * (in ? 2.f : 4.f);
-            if (sc >= thr) push(sc, kCandType3 | static_cast<uint32_t>(c * kDim + p));
-            const float scc = -base - xp * (in ? 4.f : 2.f);
-            if (scc >= thr) push(scc, kCandType3 | static_cast<uint32_t>((c + kGolayHalf) * kDim + p));
-          }
+          const uint32_t gm = gmask_s[c];
+          const float base = sumx - 2.f * tsum(gm);
+          const bool in = (gm >> p & 1u) != 0;
+          const float sc = base - xp * (in ? 2.f : 4.f);
+          if (sc >= thr) push(sc, kCandType3 | static_cast<uint32_t>(c * kDim + p));
+          const float scc = -base - xp * (in ? 4.f : 2.f);
+          if (scc >= thr) push(scc, kCandType3 | static_cast<uint32_t>((c + kGolayHalf) * kDim + p));
         }
       }
-      // Type 3 at the other positions, behind flagged chunks of the plain row:
+      // Type 3 at the other positions, behind flagged sub-chunks of the plain row:
       // each column whose bound reaches thr is broadcast, and lane i < 24
       // scores position i.
       {
         uint64_t m = mrow[2];
         while (m) {
-          const int b = chunk_of_bit(__ffsll(m) - 1);
+          const int c0 = sub_of_bit(__ffsll(m) - 1) * kSubCols;
           m &= m - 1;
-#pragma unroll 1
-          for (int k = 0; k < 2; ++k) {
-            const int c = b * kChunkCols + 32 * k + lane;
+          {
+            const int c = c0 + lane;
             const uint32_t gm = gmask_s[c];
             const float bc = sumx - 2.f * tsum(gm);
             const bool in3 = (gm >> p3 & 1u) != 0;
@@ -1202,14 +1202,14 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
               const uint32_t gmc = comp ? ~gsrc & 0xFFFFFFu : gsrc;
               const float bcc = comp ? -bsrc : bsrc;
               const float sc = bcc - xl * ((gmc >> lane & 1u) ? 2.f : 4.f);
-              const int col = b * kChunkCols + 32 * k + src + (comp ? kGolayHalf : 0);
+              const int col = c0 + src + (comp ? kGolayHalf : 0);
               if (lane < kDim && lane != p1 && lane != p2 && sc >= thr)
                 push(sc, kCandType3 | static_cast<uint32_t>(col * kDim + lane));
             }
           }
         }
       }
-      // Type 2, behind flagged chunks of the |x| row.  For an octad O with
+      // Type 2, behind flagged sub-chunks of the |x| row.  For an octad O with
       // 2 T(O) >= thr, the lanes holding its coordinates give, by warp
       // reductions, the parity of its negative coordinates, its smallest and
       // second smallest |x_i| (m1, m2) and the signs of its best even-parity
@@ -1221,11 +1221,10 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
         const float tie_gap = 9.094947e-13f * sumabs;  // 2^-40 sum|x|
         uint64_t m = mrow[3];
         while (m) {
-          const int b = chunk_of_bit(__ffsll(m) - 1);
+          // Lane i: the complement (a weight-16 word) of column 32 u + i.
+          const int c = kGolayHalf + sub_of_bit(__ffsll(m) - 1) * kSubCols + lane;
           m &= m - 1;
-#pragma unroll 1
-          for (int k = 0; k < 2; ++k) {
-            const int c = b * kChunkCols + 32 * k + lane;
+          {
             const int o = c - kW16First;
             uint32_t om = 0;
             float t2 = -INFINITY;

@@ -139,10 +139,10 @@ def test_config4_scale_sample(C, oracle):
     ours = C.quantize_indices(x, 1)
     C.device_check()
     stats = C.quantize_stats()
-    exhaustive, exact_scores, chunks = stats
+    exhaustive, exact_scores, units = stats  # units: 32 Golay columns behind a flag
     assert exhaustive < 0.01 * (1 << 20), stats
     assert exact_scores < 64 * (1 << 20), stats
-    assert chunks < 24 * (1 << 20), stats
+    assert units < 48 * (1 << 20), stats
     sel = torch.randperm(1 << 20, generator=torch.Generator().manual_seed(0))[:3000]
     xs = x[sel.cuda()].cpu().numpy()
     assert np.array_equal(ours[sel.cuda()].cpu().numpy(), oracle.nearest_exact(xs, 1))
