@@ -312,6 +312,7 @@ int build_device_tables(int dev, Tables *T) {
   uint64_t keep = ~uint64_t(0);
   H24_CUDA_TRY(cudaMemPoolSetAttribute(T->pool, cudaMemPoolAttrReleaseThreshold, &keep));
   H24_CUDA_TRY(cudaStreamCreateWithFlags(&T->copy_stream, cudaStreamNonBlocking));
+  H24_CUDA_TRY(cudaStreamCreateWithFlags(&T->d2h_stream, cudaStreamNonBlocking));
   std::memcpy(T->fingerprint, H.fingerprint, sizeof(T->fingerprint));
   T->device = dev;
   return H24_OK;
@@ -652,10 +653,12 @@ int h24_quantize_layer(const float *w, int64_t rows, int64_t in_features, uint16
 // device slots on the copy stream while the caller's stream quantises batch
 // k-1 (row scales of each piece with its whole matrix's plan, one search over
 // all the batch's pieces, 18-bit pack into each range's device output), so
-// the transfer hides behind the search.  All outputs come back to the host at
-// the end; the call returns once they are written.
+// the transfer hides behind the search.  The bytes and scales of a batch's
+// pieces go back to the host on a third stream as soon as the batch is
+// packed; the call returns once they are all written.
 static constexpr int kHostSlots = 3;
 static constexpr int64_t kHostBatchAtoms = int64_t(1) << 20;  // atoms per batch (one search call)
+static constexpr int64_t kHostFirstBatch = int64_t(1) << 17;   // the first batch; each next one doubles
 static constexpr int kHostPieces = 64;                         // row ranges per batch
 
 int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dtype, void *stream) {
@@ -675,6 +678,9 @@ int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dt
   // li, at byte offset `off` of the batch's slot), at most kHostPieces per
   // batch.  A batch is one search over all its pieces, so the device works on
   // batches as large as the device-resident path's whatever the matrix sizes.
+  // The first batch holds kHostFirstBatch atoms and each next one twice as
+  // many up to that size: the search starts after a short copy, and even a
+  // single matrix's copy overlaps its search.
   struct Piece { int li; int64_t c0, c1; size_t off; };
   struct Batch { size_t first, count; int64_t atoms; size_t bytes; };
   std::vector<Piece> pieces;
@@ -683,6 +689,7 @@ int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dt
   size_t out_bytes = 0;
   {
     Batch cur{0, 0, 0, 0};
+    int64_t cap = kHostFirstBatch;
     for (int i = 0; i < count; ++i) {
       const RowRange &r = R[i];
       out_pk[i] = out_bytes;
@@ -694,11 +701,12 @@ int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dt
       while (h) { const int64_t t2 = g % h; g = h; h = t2; }
       const int64_t rg = 96 / g;  // rows per whole number of 4-atom groups
       for (int64_t c0 = r.r0; c0 < r.r1;) {
-        int64_t fit = (kHostBatchAtoms - cur.atoms) * kDim / r.in / rg * rg;
+        int64_t fit = (cap - cur.atoms) * kDim / r.in / rg * rg;
         if (cur.count == 0 && fit < rg) fit = rg;  // a row group wider than a batch goes alone
         if (fit <= 0 || cur.count == static_cast<size_t>(kHostPieces)) {
           batches.push_back(cur);
           cur = Batch{pieces.size(), 0, 0, 0};
+          cap = cap * 2 < kHostBatchAtoms ? cap * 2 : kHostBatchAtoms;
           continue;
         }
         const int64_t c1 = c0 + fit < r.r1 ? c0 + fit : r.r1;
@@ -735,6 +743,9 @@ int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dt
   };
   cudaEvent_t ready = nullptr, copied[kHostSlots] = {}, freed[kHostSlots] = {};
   rc = event(&ready);
+  // The outputs of batch k are copied out after its pack (event done[k]).
+  std::vector<cudaEvent_t> done(batches.size(), nullptr);
+  for (size_t k = 0; k < batches.size() && rc == H24_OK; ++k) rc = event(&done[k]);
   for (int k = 0; k < kHostSlots && rc == H24_OK; ++k) {
     rc = event(&copied[k]);
     if (rc == H24_OK) rc = event(&freed[k]);
@@ -788,25 +799,35 @@ int h24_quantize_layer_rows_host(const h24_layer_rows *layers, int count, int dt
     }
     if (rc == H24_OK) {
       ce = cudaEventRecord(freed[sl], s);
+      if (ce == cudaSuccess) ce = cudaEventRecord(done[k], s);
       if (ce != cudaSuccess) rc = cuda_fail(ce, "slot release");
     }
+    // The batch's pieces of every range's bytes and scales back to the host.
+    // A piece starts on a whole 4-atom group, so its bytes are whole 9-byte
+    // groups; the last piece of a range ends with the range's last group.
+    if (rc == H24_OK) ce = cudaStreamWaitEvent(T->d2h_stream, done[k], 0);
+    for (size_t q = b.first; q < b.first + b.count && rc == H24_OK && ce == cudaSuccess; ++q) {
+      const Piece &pc = pieces[q];
+      const RowRange &r = R[pc.li];
+      const size_t p0 = static_cast<size_t>((pc.c0 - r.r0) * r.in / kDim / 4) * 9;
+      const size_t p1 = pc.c1 == r.r1 ? static_cast<size_t>((r.atoms() + 3) / 4) * 9
+                                      : static_cast<size_t>((pc.c1 - r.r0) * r.in / kDim / 4) * 9;
+      ce = cudaMemcpyAsync(r.sigma16 + (pc.c0 - r.r0), buf + out_sig[pc.li] + (pc.c0 - r.r0) * 2,
+                           static_cast<size_t>(pc.c1 - pc.c0) * 2, cudaMemcpyDeviceToHost, T->d2h_stream);
+      if (ce == cudaSuccess)
+        ce = cudaMemcpyAsync(r.packed + p0, buf + out_pk[pc.li] + p0, p1 - p0, cudaMemcpyDeviceToHost,
+                             T->d2h_stream);
+    }
+    if (rc == H24_OK && ce != cudaSuccess) rc = cuda_fail(ce, "output copy");
   }
-  for (int i = 0; i < count && rc == H24_OK; ++i) {
-    const RowRange &r = R[i];
-    if (r.r1 == r.r0) continue;
-    cudaError_t ce = cudaMemcpyAsync(r.sigma16, buf + out_sig[i], static_cast<size_t>(r.r1 - r.r0) * 2,
-                                     cudaMemcpyDeviceToHost, s);
-    if (ce == cudaSuccess)
-      ce = cudaMemcpyAsync(r.packed, buf + out_pk[i], static_cast<size_t>((r.atoms() + 3) / 4) * 9,
-                           cudaMemcpyDeviceToHost, s);
-    if (ce != cudaSuccess) rc = cuda_fail(ce, "output copy");
-  }
-  // Every copy-stream operation is ordered before the free (also after an
-  // error part way through the chunks).
-  cudaEvent_t drained = nullptr;
-  if (cudaEventCreateWithFlags(&drained, cudaEventDisableTiming) == cudaSuccess) {
-    evs.push_back(drained);
-    if (cudaEventRecord(drained, T->copy_stream) == cudaSuccess) cudaStreamWaitEvent(s, drained, 0);
+  // Every copy-stream and result-stream operation is ordered before the free
+  // (also after an error part way through the batches).
+  for (cudaStream_t cs : {T->copy_stream, T->d2h_stream}) {
+    cudaEvent_t drained = nullptr;
+    if (cudaEventCreateWithFlags(&drained, cudaEventDisableTiming) == cudaSuccess) {
+      evs.push_back(drained);
+      if (cudaEventRecord(drained, cs) == cudaSuccess) cudaStreamWaitEvent(s, drained, 0);
+    }
   }
   const cudaError_t fe = cudaFreeAsync(buf, s);
   const cudaError_t se = cudaStreamSynchronize(s);

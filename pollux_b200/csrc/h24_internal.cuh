@@ -94,14 +94,17 @@ struct Tables {
   float fingerprint[16];
   // Device counters: [0] atoms sent to the exhaustive scan, [1] exact fp64
   // codeword scores of the rescore, [2] candidate chunks flagged by the
-  // screen; and the error word set by a timed-out wait.
+  // screen (32-column units); and the error word set by a timed-out wait.
   int64_t *stats = nullptr;
   int *err = nullptr;
   // Stream-ordered pool for per-call scratch (kept warm between calls).
   cudaMemPool_t pool = nullptr;
-  // Non-blocking stream for the host-to-device copies of host-pointer entry
-  // points, so that the copy of one chunk overlaps the search of the previous.
+  // Non-blocking streams for the host-to-device copies of host-pointer entry
+  // points (so that the copy of one batch overlaps the search of the
+  // previous) and for their device-to-host result copies (a separate copy
+  // engine, so that results return while later batches are copied in).
   cudaStream_t copy_stream = nullptr;
+  cudaStream_t d2h_stream = nullptr;
 };
 
 // Returns the tables of the current device, building them on first use.

@@ -503,11 +503,15 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
                                                    int64_t n_pad, int rule,
                                                    const uint2 *__restrict__ oct_by_triple,
                                                    uint8_t *__restrict__ a_tiles,
-                                                   AtomInfo *__restrict__ info) {
+                                                   AtomInfo *__restrict__ info,
+                                                   int32_t *__restrict__ ovf_count) {
   // |x_i| of each thread's atom, [position][thread]: a warp's accesses hit 32
   // distinct banks whatever the positions.
   __shared__ float absx[kDim][256];
   const int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  // The batch's exhaustive-scan list starts empty (the previous batch on
+  // this stream has finished with it; the rescore of this one fills it).
+  if (a == 0) *ovf_count = 0;
   if (a >= n_pad) return;
   float v[kDim];
   if (a < n) {
@@ -1463,7 +1467,7 @@ Scratch carve(uint8_t *base, int64_t pad) {
   return sc;
 }
 
-// The five kernels of one batch (the overflow counter must be zero).
+// The five kernels of one batch (prep also empties the exhaustive-scan list).
 template <typename T>
 int launch_batch_t(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int32_t *ob,
                    const Scratch &sc, int sms, cudaStream_t s) {
@@ -1476,7 +1480,7 @@ int launch_batch_t(const Tables *t, const Segs &sg, int64_t nbatch, int rule, in
     for (auto &e : ev) cudaEventCreate(&e);
   if (timed) cudaEventRecord(ev[0], s);
   prep_kernel<T><<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(
-      sg, nbatch, npad, rule, t->oct_by_triple, sc.a_tiles, sc.info);
+      sg, nbatch, npad, rule, t->oct_by_triple, sc.a_tiles, sc.info, sc.ovf_count);
   if (timed) cudaEventRecord(ev[1], s);
   ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
                 nbatch, items, t->err, kWaitLimitNs};
@@ -1594,8 +1598,6 @@ int quantize_segments(const Tables *t, const void *const *xs, const int64_t *cou
       seg_off += take;
       if (seg_off == counts[seg]) { ++seg; seg_off = 0; }
     }
-    cudaError_t e = cudaMemsetAsync(sc.ovf_count, 0, sizeof(int32_t), s);
-    if (e != cudaSuccess) { rc = cuda_fail(e, "memset"); break; }
     rc = launch_batch(t, sg, nbatch, dtype, rule, out_idx + done, sc, sms, s);
     done += nbatch;
   }
@@ -1677,8 +1679,8 @@ int quantize_noalloc(const Tables *t, const float *x, int64_t n, int rule, int32
   sg.start[0] = 0;
   sg.start[1] = n;
   const Scratch sc = carve(scratch, kNoAllocMaxAtoms);
-  // The array keeps the previous call's contents: clear the overflow counter.
-  H24_CUDA_TRY(cudaMemsetAsync(sc.ovf_count, 0, sizeof(int32_t), s));
+  // The array keeps the previous call's contents; prep clears the overflow
+  // counter.
   return launch_batch(t, sg, n, H24_DTYPE_F32, rule, out_idx, sc, sms, s);
 }
 
