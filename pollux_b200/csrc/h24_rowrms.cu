@@ -122,7 +122,22 @@ __global__ void __launch_bounds__(512) row_rms_kernel(const T *__restrict__ w, i
         end = n - base;
       }
       float a1 = 0.f, a2 = 0.f, a3 = 0.f;
-      for (int64_t i = idx0; i * 4 + 3 < end; i += step) {
+      // Four vectors in flight per lane, added in the same order as one at a
+      // time.
+      int64_t i = idx0;
+      for (; (i + 3 * step) * 4 + 3 < end; i += 4 * step) {
+        float4 q[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = sq_vec4(data, base + (i + k * step) * 4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          a0 = __fadd_rn(a0, q[k].x);
+          a1 = __fadd_rn(a1, q[k].y);
+          a2 = __fadd_rn(a2, q[k].z);
+          a3 = __fadd_rn(a3, q[k].w);
+        }
+      }
+      for (; i * 4 + 3 < end; i += step) {
         const float4 q = sq_vec4(data, base + i * 4);
         a0 = __fadd_rn(a0, q.x);
         a1 = __fadd_rn(a1, q.y);
