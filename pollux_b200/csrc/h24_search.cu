@@ -146,9 +146,9 @@ struct __align__(16) AtomInfo {
   float two_e;   // 2E, or -1 for an atom with a non-finite coordinate
   float t2lb;    // best type-2 score over the 21 octads through the three largest |x_i|
   uint8_t p[3];  // p1, p2, p3
-  uint8_t pad0;
+  int8_t triv;   // index of an atom that needs no search (trivial_index: 0 or 1), else -1
   float thr;     // best - 2E, written by the screen
-  int32_t triv;  // index of an atom that needs no search (trivial_index), else -1
+  float add2;    // the plain row's offset: with x_p3 moved by d in its A row, max(u0 - d, u1 + d)
 };
 static_assert(sizeof(AtomInfo) == 48, "AtomInfo is three 16-byte loads");
 
@@ -499,7 +499,7 @@ __device__ __forceinline__ uint32_t a_offset(int L, int q) {
 // 32 * quarter_of_row(g, r) + a % 32 for row type r (0 slice p1, 1 slice p2,
 // 2 plain, 3 |x|).
 template <typename T>
-__global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
+__global__ void __launch_bounds__(256, 4) prep_kernel(const __grid_constant__ Segs sg, int64_t n,
                                                    int64_t n_pad, int rule,
                                                    const uint2 *__restrict__ oct_by_triple,
                                                    uint8_t *__restrict__ a_tiles,
@@ -614,8 +614,22 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
   inf.p[0] = static_cast<uint8_t>(q0);
   inf.p[1] = static_cast<uint8_t>(q1);
   inf.p[2] = static_cast<uint8_t>(q2);
-  inf.pad0 = 0;
   inf.thr = -INFINITY;
+  // The plain row bounds S(c, p) over the positions p outside {p1, p2} by
+  // B(c) + u1 for Golay words holding p3 and B(c) + u0 for the others.  Its A
+  // row carries x_p3 + d (rounded to bf16), which adds +d to B(c) for words
+  // without p3 and -d for words with it (and the opposite for the complement
+  // columns, whose scores are negated); then one offset max(u0 - d, u1 + d)
+  // bounds both, where max(u0, u1) did before.  d ~ (u0 - u1) / 2.
+  uint16_t hb3 = 0;
+#pragma unroll
+  for (int i = 0; i < kDim; ++i)
+    if (i == q2) hb3 = hb[i];
+  const float hf3 = __uint_as_float(static_cast<uint32_t>(hb3) << 16);
+  const __nv_bfloat16 v3 = __float2bfloat16_rn(hf3 + 0.5f * (inf.u0 - inf.u1));
+  const float d3 = __bfloat162float(v3) - hf3;  // exact: both are bf16 values
+  inf.add2 = fmaxf(inf.u0 - d3, inf.u1 + d3);
+  hb3 = __bfloat16_as_ushort(v3);
   // Atoms that need no search: non-finite, or (pack rule) an exact norm below
   // 1e-8, which needs every |x_i| < 2e-8 first (||x|| >= max |x_i|).
   inf.triv = !finite ? (rule == H24_RULE_TRAIN ? 0 : 1)
@@ -635,6 +649,10 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ Segs 
         const int p = r == 0 ? q0 : q1;
         if (p == 2 * k) lo = 0;
         if (p == 2 * k + 1) hi = 0;
+      }
+      if (r == 2) {
+        if (q2 == 2 * k) lo = hb3;
+        if (q2 == 2 * k + 1) hi = hb3;
       }
       w[k] = lo | (hi << 16);
     }
@@ -886,7 +904,7 @@ __global__ void __launch_bounds__(kScreenThreads, 1) screen_kernel(const ScreenA
                                      fmaxf(rv[3] + inf.shi - inf.l2s, inf.t1)),
                                inf.t2lb);
       const float thr = best - inf.two_e;
-      const float add = r < 2 ? inf.off[r] : (r == 2 ? fmaxf(inf.u0, inf.u1) : inf.shi);
+      const float add = r < 2 ? inf.off[r] : (r == 2 ? inf.add2 : inf.shi);
       // A chunk is flagged when (its fp16 maximum) + add >= thr in fp32.  In
       // fp16: maximum >= th with th <= thr - add, lowered by 2^-18 (|thr| +
       // |add|) against the fp32 roundings and rounded down to fp16, so every
