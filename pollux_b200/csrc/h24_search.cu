@@ -1057,15 +1057,15 @@ __device__ __noinline__ void exact_now(const float (&x)[kDim], const int8_t *__r
 //
 // Pass 1 recomputes the screening score S' of every codeword behind the
 // flagged sub-chunks in fp32 from the exact coordinates (sum_{i in c} x_i is
-// three lookups in per-atom tables of the partial sums over each byte of the
-// position mask) and lists those with S' >= thr = best - 2E.  Pass 2 scores
+// four lookups in per-atom tables of the partial sums over each 6-bit group
+// of the position mask) and lists those with S' >= thr = best - 2E.  Pass 2 scores
 // in fp64, in the reference's order, the listed codewords within 2 e' of the
 // largest S', e' = 2^-16 sum|x|, which bounds |S' - sqrt(8) R| with a wide
 // margin; the winner and every codeword tied with it are among them.
 template <typename In>
 __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     rescore_kernel(const __grid_constant__ Segs sg, const RescoreArgs r) {
-  __shared__ __align__(16) float tab[kRescoreWarps][3][256];
+  __shared__ __align__(16) float tab[kRescoreWarps][4][64];
   __shared__ float cand_s[kRescoreWarps][kCandCap];
   __shared__ uint32_t cand_c[kRescoreWarps][kCandCap];
   __shared__ int cand_n[kRescoreWarps];
@@ -1077,7 +1077,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   for (int i = threadIdx.x; i < kGolay / 4; i += blockDim.x)
     reinterpret_cast<uint4 *>(gmask_s)[i] = __ldg(reinterpret_cast<const uint4 *>(r.gmask) + i);
   __syncthreads();
-  float(*T)[256] = tab[w];
+  float(*T)[64] = tab[w];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
   uint32_t st_exh = 0, st_exact = 0, st_chunks = 0;
   // Lanes 0-10 copy one 16-byte chunk each of atom a's stage (a bf16 atom
@@ -1141,28 +1141,30 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       lb.s = -INFINITY;
       lb.j = 0x7FFFFFFF;
       lb.n = 0;
-      // Partial-sum tables: T[k][s] = sum of x_{8k+i} over the bits i of s.
-      // Lane l writes entries 8 l .. 8 l + 7 (two 16-byte stores): bits 3-7
-      // of s are the bits of l, bits 0-2 run over the eight entries.
-#pragma unroll
-      for (int k = 0; k < 3; ++k) {
-        const float4 f0 = reinterpret_cast<const float4 *>(A.x)[2 * k];
-        const float4 f1 = reinterpret_cast<const float4 *>(A.x)[2 * k + 1];
-        float h5 = 0.f;
-        if (lane & 1) h5 += f0.w;
-        if (lane & 2) h5 += f1.x;
-        if (lane & 4) h5 += f1.y;
-        if (lane & 8) h5 += f1.z;
-        if (lane & 16) h5 += f1.w;
-        const float s01 = f0.x + f0.y, s02 = f0.x + f0.z, s12 = f0.y + f0.z, s012 = s01 + f0.z;
-        float4 *dst = reinterpret_cast<float4 *>(&T[k][8 * lane]);
-        dst[0] = make_float4(h5, h5 + f0.x, h5 + f0.y, h5 + s01);
-        dst[1] = make_float4(h5 + f0.z, h5 + s02, h5 + s12, h5 + s012);
+      // Partial-sum tables: T[k][s] = sum of x_{6k+i} over the bits i of s
+      // (four tables of 64).  Lanes 8k .. 8k + 7 write table k, lane 8k + m
+      // entries 8 m .. 8 m + 7 (two 16-byte stores): bits 3-5 of s are the
+      // bits of m, bits 0-2 run over the eight entries.
+      {
+        const int k = lane >> 3, m = lane & 7;
+        const float2 c01 = reinterpret_cast<const float2 *>(A.x)[3 * k];      // x_6k, x_6k+1
+        const float2 c23 = reinterpret_cast<const float2 *>(A.x)[3 * k + 1];  // x_6k+2, x_6k+3
+        const float2 c45 = reinterpret_cast<const float2 *>(A.x)[3 * k + 2];  // x_6k+4, x_6k+5
+        float h3 = 0.f;
+        if (m & 1) h3 += c23.y;
+        if (m & 2) h3 += c45.x;
+        if (m & 4) h3 += c45.y;
+        const float s01 = c01.x + c01.y, s02 = c01.x + c23.x, s12 = c01.y + c23.x, s012 = s01 + c23.x;
+        float4 *dst = reinterpret_cast<float4 *>(&T[k][8 * m]);
+        dst[0] = make_float4(h3, h3 + c01.x, h3 + c01.y, h3 + s01);
+        dst[1] = make_float4(h3 + c23.x, h3 + s02, h3 + s12, h3 + s012);
       }
       __syncwarp();
       // Sums over the coordinates, lane i holding x_i.
       const uint32_t negm = __ballot_sync(0xffffffffu, xl < 0.f);
-      const auto tsum = [&](uint32_t m) { return T[0][m & 255] + T[1][(m >> 8) & 255] + T[2][m >> 16]; };
+      const auto tsum = [&](uint32_t m) {
+        return T[0][m & 63] + T[1][(m >> 6) & 63] + T[2][(m >> 12) & 63] + T[3][m >> 18];
+      };
       // Sum of x and of |x|, read from the tables.
       const float sumx = tsum(0xFFFFFFu);
       const float sumabs = sumx - 2.f * tsum(negm);
