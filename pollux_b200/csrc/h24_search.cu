@@ -1036,17 +1036,26 @@ __device__ __forceinline__ int32_t cand_index(const int32_t *__restrict__ idx3,
 }
 
 // Running fp64 best of one lane over the candidates beyond the list's
-// capacity (exact ties over many codewords), kept in shared memory.
+// capacity (exact ties over many codewords), kept in shared memory; it holds
+// atom `atom`'s values (it starts afresh on that atom's first overflow).
 struct LaneBest {
   double s;
   int j;
   int n;  // fp64 scores taken
+  int64_t atom;
 };
 
 // fp64 score of a listed candidate beyond the list's capacity: out of line.
 __device__ __noinline__ void exact_now(const float (&x)[kDim], const int8_t *__restrict__ cb_raw,
                                        const int32_t *__restrict__ idx3, const int32_t *__restrict__ idx2,
-                                       const int32_t *__restrict__ idx1, uint32_t code, LaneBest &lb) {
+                                       const int32_t *__restrict__ idx1, uint32_t code, LaneBest &lb,
+                                       int64_t atom) {
+  if (lb.atom != atom) {
+    lb.atom = atom;
+    lb.s = -INFINITY;
+    lb.j = 0x7FFFFFFF;
+    lb.n = 0;
+  }
   const int32_t j = cand_index(idx3, idx2, idx1, code);
   better(lb.s, lb.j, score64(x, cb_raw + static_cast<int64_t>(j) * kDim), j);
   ++lb.n;
@@ -1076,6 +1085,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   const int w = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < kGolay / 4; i += blockDim.x)
     reinterpret_cast<uint4 *>(gmask_s)[i] = __ldg(reinterpret_cast<const uint4 *>(r.gmask) + i);
+  lbest[w][lane].atom = -1;
   __syncthreads();
   float(*T)[64] = tab[w];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kRescoreWarps;
@@ -1087,14 +1097,19 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
   // The atoms a warp visits only increase, so its segment is found by
   // advancing a cursor rather than by a search per atom.
   int seg = 0;
+  // Lanes 6-7 copy chunk lane - 6 of the atom's masks (32 B per atom), lanes
+  // 8-10 chunk lane - 8 of its constants (48 B per atom): address base +
+  // a * stride.
+  const uintptr_t pf_base = lane < 8 ? reinterpret_cast<uintptr_t>(r.masks) + 16 * (lane - 6)
+                                     : reinterpret_cast<uintptr_t>(r.info) + 16 * (lane - 8);
+  const uintptr_t pf_stride = lane < 8 ? 32 : sizeof(AtomInfo);
   const auto prefetch = [&](int64_t a, int s) {
     if (a < r.n) {
       while (seg + 1 < sg.count && sg.start[seg + 1] <= a) ++seg;
-      const uint4 *xa = reinterpret_cast<const uint4 *>(static_cast<const In *>(sg.x[seg]) +
-                                                        (a - sg.start[seg]) * kDim);
-      const uint4 *src = lane < 6 ? xa + lane
-                                  : (lane < 8 ? r.masks + 2 * a + (lane - 6)
-                                              : reinterpret_cast<const uint4 *>(r.info + a) + (lane - 8));
+      const uint4 *src =
+          lane < 6 ? reinterpret_cast<const uint4 *>(static_cast<const In *>(sg.x[seg]) + (a - sg.start[seg]) * kDim) +
+                         lane
+                   : reinterpret_cast<const uint4 *>(pf_base + static_cast<uintptr_t>(a) * pf_stride);
       if (lane < 11 && (lane < kXChunks || lane >= 6))
         cp_async16(reinterpret_cast<uint4 *>(&stage[w][s]) + lane, src);
     }
@@ -1138,9 +1153,6 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
       __syncwarp();  // the previous atom's table and list reads are done
       if (lane == 0) cand_n[w] = 0;
       LaneBest &lb = lbest[w][lane];
-      lb.s = -INFINITY;
-      lb.j = 0x7FFFFFFF;
-      lb.n = 0;
       // Partial-sum tables: T[k][s] = sum of x_{6k+i} over the bits i of s
       // (four tables of 64).  Lanes 8k .. 8k + 7 write table k, lane 8k + m
       // entries 8 m .. 8 m + 7 (two 16-byte stores): bits 3-5 of s are the
@@ -1174,7 +1186,7 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
           cand_s[w][k] = sc;
           cand_c[w][k] = code;
         } else {
-          exact_now(v, r.cb_raw, r.idx3, r.idx2, r.idx1, code, lb);
+          exact_now(v, r.cb_raw, r.idx3, r.idx2, r.idx1, code, lb, a);
         }
       };
       const int p1 = inf.p[0], p2 = inf.p[1], p3 = inf.p[2];
@@ -1362,8 +1374,9 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
                            ? 0
                            : static_cast<int32_t>(kPendingIndex | static_cast<uint32_t>(jsrc));
         } else {
-          double bs = lb.s;
-          int bj = lb.j, nex = lb.n;
+          const bool own = lb.atom == a;  // this lane's list overflowed for this atom
+          double bs = own ? lb.s : -INFINITY;
+          int bj = own ? lb.j : 0x7FFFFFFF, nex = own ? lb.n : 0;
           for (int k = lane; k < nc; k += 32) {
             if (cand_s[w][k] >= cut) {
               const int j = cand_index(r.idx3, r.idx2, r.idx1, cand_c[w][k]);
