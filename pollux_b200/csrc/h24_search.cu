@@ -1124,17 +1124,20 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
     prefetch(a + nwarps, sb ^ 1);
     cp_async_wait1();
     __syncwarp();
+    const AtomStage &A = stage[w][sb];
+    const float(&v)[kDim] = A.x;  // the atom, read from the stage when needed
+    float xl;                     // lane i < 24: x_i; +0 on lanes 24-31
     if constexpr (sizeof(In) == 2) {
       // Widen the 24 bf16 patterns at the start of the coordinates in place.
       float *xs = stage[w][sb].x;
       const uint32_t h = lane < kDim ? reinterpret_cast<const uint16_t *>(xs)[lane] : 0u;
       __syncwarp();
-      if (lane < kDim) xs[lane] = bf16_bits_to_float(h);
+      xl = bf16_bits_to_float(h);
+      if (lane < kDim) xs[lane] = xl;
       __syncwarp();
+    } else {
+      xl = lane < kDim ? A.x[lane] : 0.f;
     }
-    const AtomStage &A = stage[w][sb];
-    const float(&v)[kDim] = A.x;  // the atom, read from the stage when needed
-    const float xl = lane < kDim ? A.x[lane] : 0.f;  // lane i: x_i
     const int triv = A.info.triv;
     // Row r's 64-bit sub-chunk mask, read from the stage when its row is
     // processed.  A flag of rows 0-2 stands for 32 columns and their
@@ -1206,9 +1209,11 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
           const float base = sumx - 2.f * tsum(gm);
           const bool in = (gm >> p & 1u) != 0;
           const float sc = base - xp * (in ? 2.f : 4.f);
-          if (sc >= thr) push(sc, kCandType3 | static_cast<uint32_t>(c * kDim + p));
           const float scc = -base - xp * (in ? 4.f : 2.f);
-          if (scc >= thr) push(scc, kCandType3 | static_cast<uint32_t>((c + kGolayHalf) * kDim + p));
+          if (sc >= thr || scc >= thr) {
+            if (sc >= thr) push(sc, kCandType3 | static_cast<uint32_t>(c * kDim + p));
+            if (scc >= thr) push(scc, kCandType3 | static_cast<uint32_t>((c + kGolayHalf) * kDim + p));
+          }
         }
       }
       // Type 3 at the other positions, behind flagged sub-chunks of the plain row:
@@ -1264,29 +1269,39 @@ __global__ void __launch_bounds__(32 * kRescoreWarps, kRescoreBlocksPerSm)
             const int o = c - kW16First;
             uint32_t om = 0;
             float t2 = -INFINITY;
+            bool oddl = false;  // odd number of negative coordinates in lane's octad
             if (o >= 0 && o < kOctads) {
               const uint32_t gm = gmask_s[c];
               om = ~gm & 0xFFFFFFu;
               t2 = 2.f * (sumabs - (tsum(gm & ~negm) - tsum(gm & negm)));  // 2 T(O)
+              oddl = (__popc(om & negm) & 1u) != 0;
             }
             uint32_t bal = __ballot_sync(0xffffffffu, t2 >= thr);
             while (bal) {
               const int src = __ffs(bal) - 1;
               bal &= bal - 1;
-              const int oc = __shfl_sync(0xffffffffu, o, src);
+              const int oc = c - lane + src - kW16First;  // the octad of lane src's column
               const uint32_t omc = __shfl_sync(0xffffffffu, om, src);
               const float t2c = __shfl_sync(0xffffffffu, t2, src);
+              const bool odd = __shfl_sync(0xffffffffu, oddl ? 1 : 0, src) != 0;
               // Lane i < 24 holds x_i; omc has 24 bits, so in_o is false on
               // lanes 24-31.
               const bool in_o = (omc >> lane & 1u) != 0;
-              const bool odd = __popc(__ballot_sync(0xffffffffu, in_o && xl < 0.f)) & 1;
               const float ax = in_o ? fabsf(xl) : INFINITY;
               const float m1 = warp_min(ax);
               const float t2x = odd ? t2c - 4.f * m1 : t2c;
               if (t2x < thr) continue;
-              const int kmin = __ffs(__ballot_sync(0xffffffffu, ax == m1)) - 1;  // lowest on ties
-              const float m2 = warp_min(lane == kmin ? INFINITY : ax);
-              if ((odd ? 4.f * (m2 - m1) : 4.f * (m1 + m2)) > tie_gap) {
+              // Even parity: the other patterns score at least 4 (m1 + m2) >=
+              // 8 m1 less, so the second smallest |x_i| is needed only when
+              // 8 m1 does not clear the gap.
+              int kmin = 0;
+              bool clear = true;
+              if (odd || !(8.f * m1 > tie_gap)) {
+                kmin = __ffs(__ballot_sync(0xffffffffu, ax == m1)) - 1;  // lowest on ties
+                const float m2 = warp_min(lane == kmin ? INFINITY : ax);
+                clear = (odd ? 4.f * (m2 - m1) : 4.f * (m1 + m2)) > tie_gap;
+              }
+              if (clear) {
                 // Pattern bit k (k < 7): the coordinate of rank k in O (rank
                 // 0 = lowest position) is negative; rank 7 follows from parity.
                 const uint32_t rank = __popc(omc & ((1u << lane) - 1u));
