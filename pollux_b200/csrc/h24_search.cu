@@ -142,7 +142,7 @@ struct __align__(16) AtomInfo {
   float u1;      // Golay word with p3: max(2 y3, 4 y4, 2 y4)
   float shi;     // sum |hi_i|: added to the |x| row at weight-16 columns
   float t1;      // 4 (|x|_(1) + |x|_(2)): best type-1 score
-  float l2s;     // 4 |x|_(8): type-2 parity allowance
+  float l2s;     // 4 |x|_(3): type-2 parity allowance (>= 4 |x|_(8))
   float two_e;   // 2E, or -1 for an atom with a non-finite coordinate
   float t2lb;    // best type-2 score over the 21 octads through the three largest |x_i|
   uint8_t p[3];  // p1, p2, p3
@@ -523,13 +523,13 @@ __global__ void __launch_bounds__(256, 4) prep_kernel(const __grid_constant__ Se
   float sum_d = 0.f, sum_d2 = 0.f, sum_x = 0.f, shi = 0.f;
   bool finite = true;
   uint16_t hb[kDim];
-  // Three smallest coordinates (lowest position first on ties) and the two
-  // largest and eighth largest |x_i|.
+  // Three smallest coordinates (lowest position first on ties) and the three
+  // largest |x_i|.
   float s0 = INFINITY, s1 = INFINITY, s2 = INFINITY, s3 = INFINITY;
   int q0 = 0, q1 = 1, q2 = 2;
-  float top[8];
+  float top[3];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) top[k] = 0.f;
+  for (int k = 0; k < 3; ++k) top[k] = 0.f;
   int a0 = 0, a1 = 1, a2 = 2;  // positions of the three largest |x_i|
   uint32_t negm = 0;
 #pragma unroll
@@ -563,7 +563,7 @@ __global__ void __launch_bounds__(256, 4) prep_kernel(const __grid_constant__ Se
     }
     float t = fabsf(x);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < 3; ++k) {
       const float hi_k = fmaxf(top[k], t);
       t = fminf(top[k], t);
       top[k] = hi_k;
@@ -584,7 +584,11 @@ __global__ void __launch_bounds__(256, 4) prep_kernel(const __grid_constant__ Se
   inf.u1 = fmaxf(2.f * y3, fmaxf(4.f * y4, 2.f * y4));
   inf.shi = shi;
   inf.t1 = 4.f * (top[0] + top[1]);
-  inf.l2s = 4.f * top[7];
+  // The parity allowance of the |x|-row bound: 4 min_O |x_i| <= 4 |x|_(8) <=
+  // 4 |x|_(3) for every octad O (the larger value only lowers the bound; the
+  // prep's type-2 bound over the octads through the three largest |x_i| is
+  // the tighter one in practice, and the flags of N(0,1) atoms are the same).
+  inf.l2s = 4.f * top[2];
   inf.two_e = finite ? 2.f * e : -1.f;
   // Achievable type-2 score: the best even-parity pattern, 2 T(O) - 4 [odd]
   // min_O |x|, over the 21 octads that contain the three largest |x_i|.
