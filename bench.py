@@ -74,16 +74,59 @@ def _peaks() -> dict:
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock, power and clock-event reasons of one GPU during the timed
+    region, read-only: NVML polled every 5 ms from a thread (so that even a
+    timed region of a few tens of ms has samples), else `nvidia-smi -lms 200`.
+    The GPU is found by the UUID torch reports for the CUDA device."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.nvml = None
+        self.samples = []  # (sm MHz, power W, reason bits)
+        self.max_mhz = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.gpu).uuid)
+        for cand in (uuid, "GPU-" + uuid):
+            try:
+                return pynvml, pynvml.nvmlDeviceGetHandleByUUID(cand)
+            except pynvml.NVMLError:
+                continue
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def start(self):
+        try:
+            nv, h = self._nvml_handle()
+            self.nvml = (nv, h)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            self.stop_flag = threading.Event()
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    try:
+                        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                             nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except nv.NVMLError:
+                        pass
+                    time.sleep(0.005)
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:  # no NVML bindings or device: nvidia-smi instead
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
@@ -99,6 +142,20 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            nv, _ = self.nvml
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
+            reasons = set()
+            for _, _, bits in self.samples:
+                for name, const in self.REASONS:
+                    if bits & getattr(nv, const, 0):
+                        reasons.add(name)
+            sm = [m for m, _, _ in self.samples]
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(reasons), "samples": len(sm),
+                    "power_w_max": max(p for _, p, _ in self.samples) if self.samples else None,
+                    "source": "NVML every 5 ms"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -124,7 +181,7 @@ class ClockSampler:
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm),
-                "power_w_max": max(power) if power else None}
+                "power_w_max": max(power) if power else None, "source": "nvidia-smi -lms 200"}
 
 
 # ---------------------------------------------------------------------------
