@@ -46,6 +46,19 @@ EXHAUSTIVE_FLOP_PER_ATOM = 2 * 24 * 196_560
 # Bytes the rescore must read per atom: its 24 coordinates (bf16), four 64-bit
 # chunk masks, the 48-byte per-atom constants; and write: one int32 index.
 RESCORE_BYTES_PER_ATOM_BF16 = 48 + 32 + 48 + 4
+# The rescore is bound by instruction issue (ncu: 72 % issue active, warps
+# mostly ready, DRAM at its floor), so its roofline is the SM issue rate:
+# 4 warp instructions per cycle per SM.  Its count per atom is ncu's
+# smsp__inst_executed.sum over one launch of 262,144 bf16 atoms (149.6 M,
+# profiles/rescore_kernel_262k.md).
+RESCORE_WARP_INST_PER_ATOM = 149.6e6 / 262_144
+ISSUE_SLOTS_PER_SM = 4
+# DRAM traffic per atom (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# captured launch of each kernel on 262,144 bf16 atoms, scaled to a launch of
+# the bench's size by its atom count (the traffic of both kernels grows in
+# proportion to the atoms): screen 79.9 + 3.2 MB, rescore 33.9 + 3.8 MB.
+SCREEN_TRAFFIC_PER_ATOM = (79.9e6 + 3.2e6) / 262_144
+RESCORE_TRAFFIC_PER_ATOM = (33.9e6 + 3.8e6) / 262_144
 CONFIG = 3
 METRIC = ("G atoms/s quantized (config-3 bf16 Pollux-1920 backbone: whole-backbone sigma16 + "
           "nearest codeword + 18-bit pack)")
@@ -424,15 +437,30 @@ def run_ours(args) -> None:
                    "peak": peak_t, "unit": "TFLOP/s", "frac": screen_tflops / peak_t,
                    "peak_source": peak_t_src, "flop_per_atom": SCREEN_FLOP_PER_ATOM,
                    "launch_ms_mean": scr["ms_per_launch"], "launches": scr["launches"],
-                   "traffic": None}
+                   "traffic": SCREEN_TRAFFIC_PER_ATOM * scr["atoms_per_launch"],
+                   "traffic_source": "ncu dram bytes of one 262,144-atom launch, scaled to this "
+                                     "launch's atoms (profiles/screen_kernel_262k.md)"}
     res_ = kern["rescore_kernel"]
-    rescore_gbs = RESCORE_BYTES_PER_ATOM_BF16 * res_["atoms_per_launch"] / (res_["ms_per_launch"] / 1e3) / 1e9
-    rescore_roof = {"bound": "hbm", "kernel": "rescore_kernel", "achieved": rescore_gbs, "peak": peak_b,
-                    "unit": "GB/s", "frac": rescore_gbs / peak_b, "peak_source": peak_b_src,
-                    "bytes_per_atom": RESCORE_BYTES_PER_ATOM_BF16,
+    res_s = res_["ms_per_launch"] / 1e3
+    rescore_gbs = RESCORE_BYTES_PER_ATOM_BF16 * res_["atoms_per_launch"] / res_s / 1e9
+    sm_mhz = (clk or {}).get("sm_mhz") or (clk or {}).get("sm_max_mhz") or 1965.0
+    issue_peak = torch.cuda.get_device_properties(dev).multi_processor_count * ISSUE_SLOTS_PER_SM \
+        * sm_mhz * 1e6 / 1e9
+    issue_rate = RESCORE_WARP_INST_PER_ATOM * res_["atoms_per_launch"] / res_s / 1e9
+    rescore_roof = {"bound": "issue", "kernel": "rescore_kernel", "achieved": issue_rate,
+                    "peak": issue_peak, "unit": "G warp-instructions/s", "frac": issue_rate / issue_peak,
+                    "peak_source": f"SMs x {ISSUE_SLOTS_PER_SM} warp instructions per cycle x the "
+                                   f"median SM clock sampled in the timed region ({sm_mhz:.0f} MHz)",
+                    "warp_instructions_per_atom": RESCORE_WARP_INST_PER_ATOM,
+                    "instructions_source": "ncu smsp__inst_executed.sum of one 262,144-atom launch "
+                                           "(profiles/rescore_kernel_262k.md)",
                     "launch_ms_mean": res_["ms_per_launch"], "launches": res_["launches"],
-                    "traffic": None,
-                    "note": "the rescore's memory floor; it runs issue-bound far above it"}
+                    "traffic": RESCORE_TRAFFIC_PER_ATOM * res_["atoms_per_launch"],
+                    "traffic_source": "ncu dram bytes of one 262,144-atom launch, scaled to this "
+                                      "launch's atoms (profiles/rescore_kernel_262k.md)",
+                    "memory_floor": {"bound": "hbm", "bytes_per_atom": RESCORE_BYTES_PER_ATOM_BF16,
+                                     "achieved": rescore_gbs, "peak": peak_b, "unit": "GB/s",
+                                     "frac": rescore_gbs / peak_b, "peak_source": peak_b_src}}
     dominant = max(("screen_kernel", "rescore_kernel"), key=lambda k: kern[k]["ms_total"])
     roofline = screen_roof if dominant == "screen_kernel" else rescore_roof
 

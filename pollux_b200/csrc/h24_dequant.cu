@@ -13,11 +13,15 @@
 // at most four distinct coordinates, fixed by its type, so the codebook is
 // stored as 2-bit positions in a per-type value list (16 bytes per codeword,
 // one 32-byte sector, 3.1 MB, L2-resident) and two output values come from
-// one byte permute (prmt) of the row's values for that list: per 8 elements,
-// one 4-byte gather, six prmt and one 16-byte store.  Each warp owns an equal
-// contiguous range of atoms (one resident wave, no block barriers) and walks
-// it in sub-tiles of up to 128 atoms; the per-row value lists live in an
-// 8-row shared-memory ring.
+// one byte permute (prmt) of the row's values for that list: per atom one
+// 16-byte gather of its code entry (staged in shared memory), per 8 elements
+// six prmt and one 16-byte store.  Each warp owns an equal contiguous range
+// of atoms (one resident wave, no block barriers) and walks it in sub-tiles
+// of up to 128 atoms, loading the next sub-tile's packed bytes while it
+// expands the current one; output unit u (8 elements) of a sub-tile goes to
+// lane u mod 32, so every store instruction writes 512 contiguous bytes (four
+// whole 128-byte lines when the output is 128-byte aligned).  The per-row
+// value lists live in an 8-row shared-memory ring.
 #include <cstddef>
 
 #include "h24_internal.cuh"
@@ -37,15 +41,18 @@ struct DequantBatch {
   int count;
 };
 
-// Per-warp shared memory: the sub-tile's packed bytes, the decoded
-// (index, ring slot) of its atoms and the value lists of up to 8 rows.
+// Per-warp shared memory: the sub-tile's packed bytes, the code words and
+// value-list offsets of its atoms and the value lists of up to 8 rows.
+constexpr int kPackedChunks = 20;  // 16-byte chunks: <= 297 bytes from a 16-byte-aligned start
 struct WarpSmem {
   alignas(16) uint32_t lists[kSlots][8];  // [slot][2*list .. 2*list+1] = a prmt source pair
-  uint32_t info[kSub];
-  uint8_t packed[9 * 33 + 3];
+  alignas(16) uint8_t packed[16 * kPackedChunks];
+  uint32_t code[3 * kSub];                // code words of atom a at 3a .. 3a+2
+  uint8_t lofs[kSub];                     // list_offset() of atom a
 };
-static_assert(offsetof(WarpSmem, lists) % 8 == 0 && sizeof(WarpSmem) % 16 == 0,
-              "value lists are read as 8-byte pairs");
+static_assert(offsetof(WarpSmem, lists) % 8 == 0 && offsetof(WarpSmem, packed) % 16 == 0 &&
+                  sizeof(WarpSmem) % 16 == 0,
+              "value lists are read as 8-byte pairs, packed bytes stored as 16-byte chunks");
 
 // Value lists of rows r_lo..r_hi (at most kSlots) into their ring slots, the
 // code orders of h24_capi.cu's table:
@@ -68,13 +75,19 @@ __device__ __forceinline__ void build_lists(uint32_t (*lists)[8], const uint16_t
   }
 }
 
-// 8 fp16 outputs from one code word: nibble e -> element e.
-__device__ __forceinline__ uint4 expand8(uint32_t w, const uint32_t *lists) {
+// Byte offset in a warp's value-list ring of the prmt source pair that the
+// code words of a codeword use: its row's ring slot and its list (bit 2 of
+// nibbles 0 and 1 of every word of its entry).
+__device__ __forceinline__ uint32_t list_offset(uint32_t slot, uint32_t w) {
+  return 32u * slot + 8u * (((w >> 2) & 1u) | ((w >> 5) & 2u));
+}
+
+// 8 fp16 outputs from one code word (nibble e -> element e) and the row's
+// value list for the word's codeword type.
+__device__ __forceinline__ uint4 expand8(uint32_t w, uint2 src) {
   // Code c -> the prmt selector pair (2c, 2c+1) of fp16 value c; the list bit
   // (bit 2) only selects the identical upper copy of the table.
   constexpr uint32_t kSel = 0x76543210u;
-  const uint32_t list = ((w >> 2) & 1u) | ((w >> 5) & 2u);
-  const uint2 src = reinterpret_cast<const uint2 *>(lists)[list];
   const uint32_t s_lo = __byte_perm(kSel, kSel, w);
   const uint32_t s_hi = __byte_perm(kSel, kSel, w >> 16);
   uint4 o;
@@ -85,8 +98,42 @@ __device__ __forceinline__ uint4 expand8(uint32_t w, const uint32_t *lists) {
   return o;
 }
 
+// Where a sub-tile's packed bytes lie: `chunks` 16-byte chunks from the
+// aligned address `base`, the first byte of group la0/4 at offset `shift`.
+// Every chunk read holds at least one byte of the stream, so it lies in
+// mapped memory even where the stream is an unaligned view.
+struct PackedSpan {
+  const uint4 *base;
+  int shift, chunks;
+};
+
+__device__ __forceinline__ PackedSpan packed_span(const uint8_t *packed, int64_t la0, int na) {
+  const int nbytes = 9 * ((static_cast<int>(la0 & 3) + na - 1) / 4 + 1);
+  const uint8_t *src = packed + 9 * (la0 >> 2);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(src) & ~static_cast<uintptr_t>(15);
+  PackedSpan p;
+  p.base = reinterpret_cast<const uint4 *>(a);
+  p.shift = static_cast<int>(reinterpret_cast<uintptr_t>(src) - a);
+  p.chunks = (p.shift + nbytes + 15) / 16;
+  return p;
+}
+
+// Atoms of the sub-tile that starts at global atom g inside layer li: at most
+// kSub, within the layer and the warp's range, and over at most 8 rows (so the
+// value lists fit the ring); a row-limited length is a multiple of 8 atoms so
+// that the output stays 128-byte aligned.
+__device__ __forceinline__ int sub_atoms(const DequantBatch &b, int li, int64_t g, int64_t g_end,
+                                         int32_t apr) {
+  int64_t lim = b.atom_start[li + 1] - g;
+  if (g_end - g < lim) lim = g_end - g;
+  int64_t rows7 = 7 * static_cast<int64_t>(apr);
+  if (rows7 >= 8) rows7 &= ~static_cast<int64_t>(7);
+  if (rows7 < lim) lim = rows7;
+  return static_cast<int>(lim < kSub ? lim : kSub);
+}
+
 __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_constant__ DequantBatch b,
-                                                           const uint32_t *__restrict__ codes,
+                                                           const uint4 *__restrict__ codes,
                                                            int32_t *__restrict__ bad) {
   __shared__ WarpSmem smem[kWarpsPerBlock];
   const int lane = threadIdx.x & 31;
@@ -94,93 +141,63 @@ __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_const
   const int64_t total = b.atom_start[b.count];
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarpsPerBlock;
   const int64_t wid = blockIdx.x * static_cast<int64_t>(kWarpsPerBlock) + (threadIdx.x >> 5);
-  const int64_t per = (total + nwarps - 1) / nwarps;
-  const int64_t g_end = (wid + 1) * per < total ? (wid + 1) * per : total;
-  // Output mapping: 10 atoms x 3 parts per round, lanes 30-31 idle, so the
-  // three gathers of one atom share one request.
-  const int my_atom = lane / 3, my_part = lane - 3 * (lane / 3);
-  int li = -1;
-  int64_t row = 0;     // row of the next atom
-  int32_t off = 0;     // its position in the row
-  int32_t apr = 1;     // atoms per row of layer li
-  int64_t built_hi = -1;
+  // Warp ranges are multiples of 32 atoms (1536 output bytes), so sub-tiles
+  // start 128-byte aligned in every layer whose atom count is a multiple of 8.
+  const int64_t per = ((total + nwarps - 1) / nwarps + 31) & ~static_cast<int64_t>(31);
+  const int64_t g_begin = wid * per < total ? wid * per : total;
+  const int64_t g_end = g_begin + per < total ? g_begin + per : total;
+  if (g_begin >= g_end) return;
+
+  int li = 0;
+  while (b.atom_start[li + 1] <= g_begin) ++li;
+  int32_t apr = static_cast<int32_t>(b.layer[li].in_features / kDim);
+  int64_t row = (g_begin - b.atom_start[li]) / apr;  // row of the sub-tile's first atom
+  int32_t off = static_cast<int32_t>(g_begin - b.atom_start[li] - row * apr);  // its position in the row
+  int64_t built_hi = row - 1;
+  int na = sub_atoms(b, li, g_begin, g_end, apr);
+  PackedSpan span = packed_span(b.layer[li].packed, g_begin - b.atom_start[li], na);
+  uint4 pk = make_uint4(0, 0, 0, 0);
+  if (lane < span.chunks) pk = __ldcs(span.base + lane);
   unsigned nbad = 0;
-  for (int64_t g = wid * per; g < g_end;) {
-    if (li < 0 || b.atom_start[li + 1] <= g) {  // entering a layer
-      while (b.atom_start[li + 1] <= g) ++li;
-      apr = static_cast<int32_t>(b.layer[li].in_features / kDim);
-      const int64_t la = g - b.atom_start[li];
-      row = la / apr;
-      off = static_cast<int32_t>(la - row * apr);
-      built_hi = row - 1;
-    }
+
+  for (int64_t g = g_begin; g < g_end;) {
     const h24_dequant_layer &L = b.layer[li];
     const int64_t la0 = g - b.atom_start[li];
-    int64_t lim = b.atom_start[li + 1] - g;
-    if (g_end - g < lim) lim = g_end - g;
-    if (7 * static_cast<int64_t>(apr) < lim) lim = 7 * static_cast<int64_t>(apr);  // <= kSlots rows
-    const int na = static_cast<int>(lim < kSub ? lim : kSub);
     const int64_t r1 = row + static_cast<uint32_t>(off + na - 1) / static_cast<uint32_t>(apr);
-
-    // 1. Packed bytes of the groups the sub-tile touches.
-    const int q0 = static_cast<int>(la0 & 3);
-    const int nbytes = 9 * ((q0 + na - 1) / 4 + 1);
-    const uint8_t *src = L.packed + 9 * (la0 >> 2);
-    {
-      constexpr int kLoads = (sizeof(W.packed) + 31) / 32;
-      uint8_t v[kLoads];
-#pragma unroll
-      for (int i = 0; i < kLoads; ++i)
-        if (lane + 32 * i < nbytes) v[i] = __ldcs(src + lane + 32 * i);
-#pragma unroll
-      for (int i = 0; i < kLoads; ++i)
-        if (lane + 32 * i < nbytes) W.packed[lane + 32 * i] = v[i];
-    }
+    // 1. This sub-tile's packed bytes (loaded during the previous sub-tile).
+    if (lane < kPackedChunks) reinterpret_cast<uint4 *>(W.packed)[lane] = pk;
     // 2. Value lists of rows not yet in the ring.
     if (r1 > built_hi) {
       build_lists(W.lists, L.sigma16, built_hi + 1 > row ? built_hi + 1 : row, r1, lane);
       built_hi = r1;
     }
     __syncwarp();
-    // 3. 18-bit index and ring slot of each atom.
+    // 3. 18-bit index, code words and value-list offset of each atom: one
+    //    16-byte gather (one 32-byte sector) per atom.
+    const int q0 = static_cast<int>(la0 & 3);
 #pragma unroll
     for (int k = 0; k < kSub / 32; ++k) {
       const int a = lane + 32 * k;
       if (a < na) {
         const int sa = q0 + a, q = sa & 3;
-        const uint8_t *p = W.packed + 9 * (sa >> 2) + 2 * q;
+        const uint8_t *p = W.packed + span.shift + 9 * (sa >> 2) + 2 * q;
         const uint32_t v24 = (static_cast<uint32_t>(p[0]) << 16) | (static_cast<uint32_t>(p[1]) << 8) | p[2];
         uint32_t idx = (v24 >> (6 - 2 * q)) & 0x3FFFFu;
         if (idx > static_cast<uint32_t>(kKissing)) {
           ++nbad;
           idx = 0;
         }
+        const uint4 c = __ldg(codes + idx);
+        W.code[3 * a] = c.x;
+        W.code[3 * a + 1] = c.y;
+        W.code[3 * a + 2] = c.z;
         const uint32_t rl = static_cast<uint32_t>(off + a) / static_cast<uint32_t>(apr);
-        W.info[a] = idx | (static_cast<uint32_t>((row + rl) & (kSlots - 1)) << 18);
-      }
-    }
-    __syncwarp();
-    // 4. Gather all code words of the sub-tile, then expand and store.
-    constexpr int kRounds = (kSub + 9) / 10;
-    uint32_t word[kRounds], slot[kRounds];
-#pragma unroll
-    for (int m = 0; m < kRounds; ++m) {
-      const int a = 10 * m + my_atom;
-      word[m] = 0;
-      slot[m] = 0;
-      if (lane < 30 && a < na) {
-        const uint32_t inf = W.info[a];
-        slot[m] = inf >> 18;
-        word[m] = __ldg(codes + 4 * (inf & 0x3FFFFu) + my_part);
+        W.lofs[a] = static_cast<uint8_t>(list_offset(static_cast<uint32_t>((row + rl) & (kSlots - 1)), c.x));
       }
     }
     uint4 *dst = reinterpret_cast<uint4 *>(L.out16 + la0 * kDim);
-#pragma unroll
-    for (int m = 0; m < kRounds; ++m) {
-      const int a = 10 * m + my_atom;
-      if (lane < 30 && a < na) __stcs(dst + 3 * a + my_part, expand8(word[m], W.lists[slot[m]]));
-    }
-    __syncwarp();
+    const int units = 3 * na;
+    // Advance to the next sub-tile and start loading its packed bytes.
     g += na;
     off += na;
     if (off >= apr) {
@@ -188,6 +205,29 @@ __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_const
       row += dr;
       off -= dr * apr;
     }
+    if (g < g_end) {
+      if (b.atom_start[li + 1] <= g) {  // entering a layer (its first atom)
+        while (b.atom_start[li + 1] <= g) ++li;
+        apr = static_cast<int32_t>(b.layer[li].in_features / kDim);
+        row = 0;
+        off = 0;
+        built_hi = -1;
+      }
+      na = sub_atoms(b, li, g, g_end, apr);
+      span = packed_span(b.layer[li].packed, g - b.atom_start[li], na);
+      if (lane < span.chunks) pk = __ldcs(span.base + lane);
+    }
+    __syncwarp();
+    // 4. Output unit u (8 elements, 16 bytes) of the sub-tile goes to lane
+    //    u mod 32: every store instruction writes 512 contiguous bytes.
+#pragma unroll
+    for (int m = 0; m < 3 * kSub / 32; ++m) {
+      const int u = 32 * m + lane;
+      if (u < units)
+        __stcs(dst + u, expand8(W.code[u], *reinterpret_cast<const uint2 *>(
+                                               reinterpret_cast<const uint8_t *>(W.lists) + W.lofs[u / 3])));
+    }
+    __syncwarp();
   }
   const unsigned total_bad = __reduce_add_sync(0xffffffffu, nbad);
   if (lane == 0 && total_bad && bad) atomicAdd(bad, static_cast<int32_t>(total_bad));
@@ -279,7 +319,7 @@ int launch_dequant(const Tables *t, const h24_dequant_layer * /*layers_dev*/,
     const int64_t want = (atoms + kSub * kWarpsPerBlock - 1) / (kSub * kWarpsPerBlock);
     const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks();
     const int grid = static_cast<int>(want < cap ? want : cap);
-    dequant_kernel<<<grid, kThreads, 0, s>>>(b, t->cb_nib, bad);
+    dequant_kernel<<<grid, kThreads, 0, s>>>(b, reinterpret_cast<const uint4 *>(t->cb_nib), bad);
     H24_CUDA_TRY(cudaGetLastError());
     count_launches(1);
   }

@@ -86,3 +86,20 @@ def test_rows_per_tile_regimes(PL, oracle, in_f):
     w = PL.dequant(packed, sig, rows, in_f)
     ref = oracle.dequant(packed.cpu().numpy(), sig.cpu().numpy(), rows, in_f)
     assert np.array_equal(w.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("shift", [1, 7, 9, 15])
+def test_unaligned_packed_view(PL, oracle, shift):
+    # A packed stream that starts at any byte offset (e.g. inside a .plx
+    # buffer) dequantises to the same weights as an aligned copy.
+    from pollux_b200 import castor
+    rows, in_f = 333, 288
+    gen = torch.Generator(device="cuda").manual_seed(100 + shift)
+    idx = torch.randint(0, 196561, (rows * in_f // 24,), generator=gen, device="cuda")
+    sig = (torch.rand(rows, generator=gen, device="cuda") * 0.2 + 1e-4).half()
+    packed = castor.pack_indices(idx)
+    buf = torch.zeros(packed.numel() + 64, dtype=torch.uint8, device="cuda")
+    buf[shift:shift + packed.numel()] = packed
+    w = PL.dequant(buf[shift:shift + packed.numel()], sig, rows, in_f)
+    ref = oracle.dequant(packed.cpu().numpy(), sig.cpu().numpy(), rows, in_f)
+    assert np.array_equal(w.cpu().numpy().view(np.uint16), ref.view(np.uint16))
