@@ -118,6 +118,19 @@ __device__ __forceinline__ PackedSpan packed_span(const uint8_t *packed, int64_t
   return p;
 }
 
+// x / d for the in-row positions x < d + kSub of a sub-tile, by one
+// multiply-high: with m = ceil(2^32 / d) and e = m d - 2^32 < d,
+// floor(x m / 2^32) = floor(x / d) whenever x e < 2^32, which holds for
+// d <= 65,000 ((d + 127)(d - 1) < 2^32); longer rows divide.
+struct RowDiv {
+  uint64_t m;
+  uint32_t d;
+  __device__ __forceinline__ explicit RowDiv(uint32_t d_) : m(((1ull << 32) + d_ - 1) / d_), d(d_) {}
+  __device__ __forceinline__ uint32_t operator()(uint32_t x) const {
+    return d <= 65000u ? static_cast<uint32_t>((x * m) >> 32) : x / d;
+  }
+};
+
 // Atoms of the sub-tile that starts at global atom g inside layer li: at most
 // kSub, within the layer and the warp's range, and over at most 8 rows (so the
 // value lists fit the ring); a row-limited length is a multiple of 8 atoms so
@@ -154,6 +167,7 @@ __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_const
   int64_t row = (g_begin - b.atom_start[li]) / apr;  // row of the sub-tile's first atom
   int32_t off = static_cast<int32_t>(g_begin - b.atom_start[li] - row * apr);  // its position in the row
   int64_t built_hi = row - 1;
+  RowDiv rdiv(static_cast<uint32_t>(apr));
   int na = sub_atoms(b, li, g_begin, g_end, apr);
   PackedSpan span = packed_span(b.layer[li].packed, g_begin - b.atom_start[li], na);
   uint4 pk = make_uint4(0, 0, 0, 0);
@@ -163,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_const
   for (int64_t g = g_begin; g < g_end;) {
     const h24_dequant_layer &L = b.layer[li];
     const int64_t la0 = g - b.atom_start[li];
-    const int64_t r1 = row + static_cast<uint32_t>(off + na - 1) / static_cast<uint32_t>(apr);
+    const int64_t r1 = row + rdiv(static_cast<uint32_t>(off + na - 1));
     // 1. This sub-tile's packed bytes (loaded during the previous sub-tile).
     if (lane < kPackedChunks) reinterpret_cast<uint4 *>(W.packed)[lane] = pk;
     // 2. Value lists of rows not yet in the ring.
@@ -191,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_const
         W.code[3 * a] = c.x;
         W.code[3 * a + 1] = c.y;
         W.code[3 * a + 2] = c.z;
-        const uint32_t rl = static_cast<uint32_t>(off + a) / static_cast<uint32_t>(apr);
+        const uint32_t rl = rdiv(static_cast<uint32_t>(off + a));
         W.lofs[a] = static_cast<uint8_t>(list_offset(static_cast<uint32_t>((row + rl) & (kSlots - 1)), c.x));
       }
     }
@@ -201,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_const
     g += na;
     off += na;
     if (off >= apr) {
-      const int32_t dr = static_cast<int32_t>(static_cast<uint32_t>(off) / static_cast<uint32_t>(apr));
+      const int32_t dr = static_cast<int32_t>(rdiv(static_cast<uint32_t>(off)));
       row += dr;
       off -= dr * apr;
     }
@@ -209,6 +223,7 @@ __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_const
       if (b.atom_start[li + 1] <= g) {  // entering a layer (its first atom)
         while (b.atom_start[li + 1] <= g) ++li;
         apr = static_cast<int32_t>(b.layer[li].in_features / kDim);
+        rdiv = RowDiv(static_cast<uint32_t>(apr));
         row = 0;
         off = 0;
         built_hi = -1;
