@@ -115,17 +115,6 @@ __device__ __forceinline__ int4 load_vec<int64_t>(const int64_t *p) {
                    static_cast<int32_t>(b.y));
 }
 
-// This warp's share [*t0, *t1) of `tiles` warp tiles: contiguous ranges whose
-// lengths differ by at most one tile.  Each warp loads its next tile while it
-// converts the current one, so two tiles per warp are in flight.
-__device__ __forceinline__ void warp_tiles(int64_t tiles, int64_t *t0, int64_t *t1) {
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
-  const int64_t w = blockIdx.x * static_cast<int64_t>(kWarps) + (threadIdx.x >> 5);
-  const int64_t q = tiles / nwarps, r = tiles - q * nwarps;
-  *t0 = w * q + (w < r ? w : r);
-  *t1 = *t0 + q + (w < r ? 1 : 0);
-}
-
 // `fast` = both pointers 16-byte aligned: whole warp tiles take the vector
 // path, the remaining groups (or all of them) one thread per group.
 template <typename T>
@@ -136,28 +125,20 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(const T *__restrict__ id
   int4 *S = slice[threadIdx.x >> 5];
   const int64_t groups = (n + 3) / 4;
   const int64_t full = fast ? n / kWarpIndices : 0;
-  int64_t wt, wt_end;
-  warp_tiles(full, &wt, &wt_end);
-  int4 v[4];
-  if (wt < wt_end) {
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t wt = blockIdx.x * static_cast<int64_t>(kWarps) + (threadIdx.x >> 5); wt < full;
+       wt += nwarps) {
+    const T *src = idx + wt * kWarpIndices;
+    int4 v[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = load_vec<T>(idx + wt * kWarpIndices + 4 * (lane + 32 * j));
-  }
-  for (; wt < wt_end; ++wt) {
+    for (int j = 0; j < 4; ++j) v[j] = load_vec<T>(src + 4 * (lane + 32 * j));
 #pragma unroll
     for (int j = 0; j < 4; ++j) S[swz(lane + 32 * j)] = v[j];
-    // The next tile's indices are in flight while this one is packed.
-    if (wt + 1 < wt_end) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        v[j] = load_vec<T>(idx + (wt + 1) * kWarpIndices + 4 * (lane + 32 * j));
-    }
     __syncwarp();
-    int4 u[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) u[i] = S[swz(4 * lane + i)];
+    for (int i = 0; i < 4; ++i) v[i] = S[swz(4 * lane + i)];
     uint32_t w[9];
-    pack_quad(u, w);
+    pack_quad(v, w);
     __syncwarp();
     uint32_t *W = reinterpret_cast<uint32_t *>(S);
 #pragma unroll
@@ -238,31 +219,20 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const uint8_t *__restr
     const int64_t by_n = n / kWarpIndices, by_groups = groups / kWarpGroups;
     full = by_n < by_groups ? by_n : by_groups;
   }
-  int64_t wt, wt_end;
-  warp_tiles(full, &wt, &wt_end);
-  int4 p[3];
-  if (wt < wt_end) {
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kWarps;
+  for (int64_t wt = blockIdx.x * static_cast<int64_t>(kWarps) + (threadIdx.x >> 5); wt < full;
+       wt += nwarps) {
     const int4 *src = reinterpret_cast<const int4 *>(packed + wt * kWarpBytes);
+    int4 p[3];
 #pragma unroll
     for (int m = 0; m < 3; ++m) {
       const int c = lane + 32 * m;
       if (c < kWarpBytes / 16) p[m] = __ldcs(src + c);
     }
-  }
-  for (; wt < wt_end; ++wt) {
 #pragma unroll
     for (int m = 0; m < 3; ++m) {
       const int c = lane + 32 * m;
       if (c < kWarpBytes / 16) S[c] = p[m];
-    }
-    // The next tile's bytes are in flight while this one is unpacked.
-    if (wt + 1 < wt_end) {
-      const int4 *src = reinterpret_cast<const int4 *>(packed + (wt + 1) * kWarpBytes);
-#pragma unroll
-      for (int m = 0; m < 3; ++m) {
-        const int c = lane + 32 * m;
-        if (c < kWarpBytes / 16) p[m] = __ldcs(src + c);
-      }
     }
     __syncwarp();
     const uint32_t *W = reinterpret_cast<const uint32_t *>(S);
