@@ -4,6 +4,12 @@
 // are the big-endian 72-bit integer i0<<54 | i1<<36 | i2<<18 | i3, each index
 // first truncated to 32 bits and then masked to 18 bits by the byte formulas.
 //
+// Both kernels are launched with programmatic stream serialization: a kernel
+// lets the next one in the stream launch as soon as it starts, and waits
+// (griddepcontrol.wait) for the previous one to complete before reading its
+// input, so the launch and ramp of one call overlap the tail of the previous
+// kernel.  Without such a launch the two instructions do nothing.
+//
 // Both kernels run independent warps (no block-wide barriers), each moving
 // 128 groups (512 indices, 1152 packed bytes) per iteration through its own
 // shared-memory slice, so that global traffic on both sides is fully
@@ -27,6 +33,29 @@ constexpr int kWarpBytes = 9 * kWarpGroups;       // 1152 = 72 x 16
 // patterns conflict-free for 128-bit accesses (8 distinct slots mod 8 in
 // every quarter warp).
 __device__ __forceinline__ int swz(int c) { return c ^ ((c >> 3) & 7); }
+
+// Waits for the previous kernel of the stream (its writes visible), then
+// allows the next one to launch.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch with programmatic stream serialization (see pdl_enter).
+template <typename K, typename... Args>
+cudaError_t launch_pdl(K kernel, int grid, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 __device__ __forceinline__ void pack_group(int32_t i0, int32_t i1, int32_t i2, int32_t i3,
                                            uint8_t *o) {
@@ -121,6 +150,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads) pack_kernel(const T *__restrict__ idx, int64_t n,
                                                         uint8_t *__restrict__ out, bool fast) {
   __shared__ int4 slice[kWarps][kWarpGroups];  // 2 KB per warp
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   int4 *S = slice[threadIdx.x >> 5];
   const int64_t groups = (n + 3) / 4;
@@ -211,6 +241,7 @@ __global__ void __launch_bounds__(kThreads) unpack_kernel(const uint8_t *__restr
                                                           int64_t groups, int64_t n,
                                                           T *__restrict__ out, bool fast) {
   __shared__ int4 slice[kWarps][kWarpGroups];
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   int4 *S = slice[threadIdx.x >> 5];
   const int64_t used_groups = (n + 3) / 4 < groups ? (n + 3) / 4 : groups;
@@ -276,8 +307,7 @@ int launch_pack(const T *idx, int64_t n, uint8_t *out, cudaStream_t s) {
   const bool fast = aligned16(idx) && aligned16(out);
   const int64_t tiles = fast ? n / kWarpIndices : 0;
   const int64_t rest = (n + 3) / 4 - tiles * kWarpGroups;
-  pack_kernel<T><<<grid_for(pack_kernel<T>, tiles, rest), kThreads, 0, s>>>(idx, n, out, fast);
-  H24_CUDA_TRY(cudaGetLastError());
+  H24_CUDA_TRY(launch_pdl(pack_kernel<T>, grid_for(pack_kernel<T>, tiles, rest), s, idx, n, out, fast));
   count_launches(1);
   return H24_OK;
 }
@@ -289,9 +319,8 @@ int launch_unpack(const uint8_t *p, int64_t groups, int64_t n, T *out, cudaStrea
   const int64_t used = (n + 3) / 4 < groups ? (n + 3) / 4 : groups;
   int64_t tiles = 0;
   if (fast) tiles = n / kWarpIndices < groups / kWarpGroups ? n / kWarpIndices : groups / kWarpGroups;
-  unpack_kernel<T><<<grid_for(unpack_kernel<T>, tiles, used - tiles * kWarpGroups), kThreads, 0, s>>>(
-      p, groups, n, out, fast);
-  H24_CUDA_TRY(cudaGetLastError());
+  H24_CUDA_TRY(launch_pdl(unpack_kernel<T>, grid_for(unpack_kernel<T>, tiles, used - tiles * kWarpGroups), s,
+                          p, groups, n, out, fast));
   count_launches(1);
   return H24_OK;
 }
