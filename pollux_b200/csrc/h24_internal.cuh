@@ -127,6 +127,32 @@ int cuda_fail(cudaError_t e, const char *what);
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Programmatic dependent launch.  A kernel launched by launch_pdl calls
+// pdl_enter() before touching memory: it waits until the previous kernel of
+// the stream has completed with its writes visible (griddepcontrol.wait),
+// then lets the next kernel launch (griddepcontrol.launch_dependents), so
+// that a launch and its ramp overlap the tail of the kernel before it.  In a
+// kernel launched without the attribute both instructions do nothing.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename K, typename... Args>
+cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Blocks of `kernel` that one SM holds at once (at least 1).
 template <typename K>
 int blocks_per_sm(K kernel, int threads, size_t dyn_smem) {

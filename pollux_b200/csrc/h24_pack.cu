@@ -34,28 +34,6 @@ constexpr int kWarpBytes = 9 * kWarpGroups;       // 1152 = 72 x 16
 // every quarter warp).
 __device__ __forceinline__ int swz(int c) { return c ^ ((c >> 3) & 7); }
 
-// Waits for the previous kernel of the stream (its writes visible), then
-// allows the next one to launch.
-__device__ __forceinline__ void pdl_enter() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// Launch with programmatic stream serialization (see pdl_enter).
-template <typename K, typename... Args>
-cudaError_t launch_pdl(K kernel, int grid, cudaStream_t s, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, args...);
-}
 
 __device__ __forceinline__ void pack_group(int32_t i0, int32_t i1, int32_t i2, int32_t i3,
                                            uint8_t *o) {
@@ -307,7 +285,8 @@ int launch_pack(const T *idx, int64_t n, uint8_t *out, cudaStream_t s) {
   const bool fast = aligned16(idx) && aligned16(out);
   const int64_t tiles = fast ? n / kWarpIndices : 0;
   const int64_t rest = (n + 3) / 4 - tiles * kWarpGroups;
-  H24_CUDA_TRY(launch_pdl(pack_kernel<T>, grid_for(pack_kernel<T>, tiles, rest), s, idx, n, out, fast));
+  H24_CUDA_TRY(launch_pdl(pack_kernel<T>, dim3(grid_for(pack_kernel<T>, tiles, rest)), dim3(kThreads), s, idx,
+                          n, out, fast));
   count_launches(1);
   return H24_OK;
 }
@@ -319,8 +298,8 @@ int launch_unpack(const uint8_t *p, int64_t groups, int64_t n, T *out, cudaStrea
   const int64_t used = (n + 3) / 4 < groups ? (n + 3) / 4 : groups;
   int64_t tiles = 0;
   if (fast) tiles = n / kWarpIndices < groups / kWarpGroups ? n / kWarpIndices : groups / kWarpGroups;
-  H24_CUDA_TRY(launch_pdl(unpack_kernel<T>, grid_for(unpack_kernel<T>, tiles, used - tiles * kWarpGroups), s,
-                          p, groups, n, out, fast));
+  H24_CUDA_TRY(launch_pdl(unpack_kernel<T>, dim3(grid_for(unpack_kernel<T>, tiles, used - tiles * kWarpGroups)),
+                          dim3(kThreads), s, p, groups, n, out, fast));
   count_launches(1);
   return H24_OK;
 }

@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(512) row_rms_kernel(const T *__restrict__ w, i
                                                       float *__restrict__ sigma32,
                                                       uint16_t *__restrict__ sigma16) {
   __shared__ float red[512];
+  pdl_enter();
   const int x = threadIdx.x, y = threadIdx.y;
   const int64_t row = p.split ? static_cast<int64_t>(blockIdx.x) : static_cast<int64_t>(blockIdx.x) * p.bh + y;
   const bool tail_owner = !p.split || y == 0;
@@ -225,15 +226,17 @@ int launch_row_rms(const void *w, int dtype, int64_t rows, int64_t n, int64_t ma
   const MeanPlan p = mean_plan(matrix_rows, n);
   const int64_t blocks = p.split ? rows : (rows + p.bh - 1) / p.bh;
   const dim3 block(p.bw, p.bh);
+  // Launched with programmatic stream serialization (pdl_enter): the row
+  // scales of consecutive matrices launch while the previous ones finish.
+  const dim3 grid(static_cast<unsigned>(blocks));
   if (dtype == H24_DTYPE_BF16)
-    row_rms_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), block, 0, s>>>(
-        static_cast<const __nv_bfloat16 *>(w), rows, n, first_row, p, sigma32, sigma16);
+    H24_CUDA_TRY(launch_pdl(row_rms_kernel<__nv_bfloat16>, grid, block, s, static_cast<const __nv_bfloat16 *>(w),
+                            rows, n, first_row, p, sigma32, sigma16));
   else if (dtype == H24_DTYPE_F32)
-    row_rms_kernel<float><<<static_cast<unsigned>(blocks), block, 0, s>>>(
-        static_cast<const float *>(w), rows, n, first_row, p, sigma32, sigma16);
+    H24_CUDA_TRY(launch_pdl(row_rms_kernel<float>, grid, block, s, static_cast<const float *>(w), rows, n,
+                            first_row, p, sigma32, sigma16));
   else
     return fail(H24_ERR_INVALID, "row_rms: weights must be fp32 or bf16");
-  H24_CUDA_TRY(cudaGetLastError());
   count_launches(1);
   return H24_OK;
 }
