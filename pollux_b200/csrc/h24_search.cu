@@ -511,6 +511,7 @@ __global__ void __launch_bounds__(256, 4) prep_kernel(const __grid_constant__ Se
   // |x_i| of each thread's atom, [position][thread]: a warp's accesses hit 32
   // distinct banks whatever the positions.
   __shared__ float absx[kDim][256];
+  pdl_enter();
   const int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   // The batch's exhaustive-scan list starts empty (the previous batch on
   // this stream has finished with it; the rescore of this one fills it).
@@ -1448,6 +1449,7 @@ __global__ void __launch_bounds__(256) exhaustive_kernel(const __grid_constant__
                                                          int32_t *__restrict__ out) {
   __shared__ double ws[8];
   __shared__ int wj[8];
+  pdl_enter();
   const int count = *ovf_count;
   for (int e = blockIdx.x; e < count; e += gridDim.x) {
     const int64_t a = ovf_list[e];
@@ -1482,6 +1484,7 @@ __global__ void __launch_bounds__(256) decode_kernel(int32_t *__restrict__ out, 
                                                      const int32_t *__restrict__ idx3,
                                                      const int32_t *__restrict__ idx2,
                                                      const int32_t *__restrict__ idx1) {
+  pdl_enter();
   for (int64_t a = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; a < n;
        a += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const uint32_t v = static_cast<uint32_t>(out[a]);
@@ -1523,6 +1526,8 @@ Scratch carve(uint8_t *base, int64_t pad) {
 }
 
 // The five kernels of one batch (prep also empties the exhaustive-scan list).
+// Prep, the exhaustive scan and decode use programmatic dependent launch
+// (pdl_enter): each waits for its predecessor before touching memory.
 template <typename T>
 int launch_batch_t(const Tables *t, const Segs &sg, int64_t nbatch, int rule, int32_t *ob,
                    const Scratch &sc, int sms, cudaStream_t s) {
@@ -1534,8 +1539,8 @@ int launch_batch_t(const Tables *t, const Segs &sg, int64_t nbatch, int rule, in
   if (timed)
     for (auto &e : ev) cudaEventCreate(&e);
   if (timed) cudaEventRecord(ev[0], s);
-  prep_kernel<T><<<static_cast<unsigned>((npad + 255) / 256), 256, 0, s>>>(
-      sg, nbatch, npad, rule, t->oct_by_triple, sc.a_tiles, sc.info, sc.ovf_count);
+  H24_CUDA_TRY(launch_pdl(prep_kernel<T>, dim3(static_cast<unsigned>((npad + 255) / 256)), dim3(256), s, sg,
+                          nbatch, npad, rule, t->oct_by_triple, sc.a_tiles, sc.info, sc.ovf_count));
   if (timed) cudaEventRecord(ev[1], s);
   ScreenArgs sa{sc.a_tiles, sc.info, reinterpret_cast<const uint8_t *>(t->golay_tiled), sc.masks,
                 nbatch, items, t->err, kWaitLimitNs};
@@ -1557,10 +1562,12 @@ int launch_batch_t(const Tables *t, const Segs &sg, int64_t nbatch, int rule, in
     timing_record(H24_KERNEL_SCREEN, ev[2], ev[3]);
     timing_record(H24_KERNEL_RESCORE, ev[4], ev[5]);
   }
-  exhaustive_kernel<T><<<2 * sms, 256, 0, s>>>(sg, rule, sc.ovf_list, sc.ovf_count, t->cb_raw, ob);
+  H24_CUDA_TRY(launch_pdl(exhaustive_kernel<T>, dim3(2 * sms), dim3(256), s, sg, rule,
+                          static_cast<const int32_t *>(sc.ovf_list), static_cast<const int32_t *>(sc.ovf_count),
+                          static_cast<const int8_t *>(t->cb_raw), ob));
   const int64_t dblocks = (nbatch + 255) / 256;
-  decode_kernel<<<static_cast<unsigned>(dblocks < 8 * sms ? dblocks : 8 * sms), 256, 0, s>>>(
-      ob, nbatch, t->idx3, t->idx2, t->idx1);
+  H24_CUDA_TRY(launch_pdl(decode_kernel, dim3(static_cast<unsigned>(dblocks < 8 * sms ? dblocks : 8 * sms)),
+                          dim3(256), s, ob, nbatch, t->idx3, t->idx2, t->idx1));
   count_launches(5);
   H24_CUDA_TRY(cudaGetLastError());
   return H24_OK;
