@@ -426,6 +426,7 @@ __global__ void __launch_bounds__(kFmaThreads, 4) lut_fma_kernel(const uint8_t *
                                                                  float *__restrict__ y,
                                                                  const uint32_t *__restrict__ codes,
                                                                  int32_t *__restrict__ bad) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const int sl = lane & 15;        // lane within the row's half warp
   const int hb = lane & 16;        // first lane of the half
@@ -588,13 +589,13 @@ int launch_lut_gemv(const Tables *t, const uint8_t *packed, const uint16_t *sigm
       const int grid = wave_grid((rows + per_block - 1) / per_block,
                                  nb == 1 ? blocks_per_sm(lut_fma_kernel<1>, kFmaThreads, 0)
                                          : blocks_per_sm(lut_fma_kernel<2>, kFmaThreads, 0));
-      if (nb == 1)
-        lut_fma_kernel<1><<<grid, kFmaThreads, 0, s>>>(packed, sigma16, rows, apr, x + b0 * in_f, in_f,
-                                                       y + b0 * rows, t->cb_nib, bad);
-      else
-        lut_fma_kernel<2><<<grid, kFmaThreads, 0, s>>>(packed, sigma16, rows, apr, x + b0 * in_f, in_f,
-                                                       y + b0 * rows, t->cb_nib, bad);
-      const cudaError_t e = cudaGetLastError();
+      // Programmatic dependent launch (pdl_enter): consecutive layers' GEMVs
+      // launch while the previous one finishes.
+      const cudaError_t e =
+          nb == 1 ? launch_pdl(lut_fma_kernel<1>, dim3(grid), dim3(kFmaThreads), s, packed, sigma16, rows, apr,
+                               x + b0 * in_f, in_f, y + b0 * rows, t->cb_nib, bad)
+                  : launch_pdl(lut_fma_kernel<2>, dim3(grid), dim3(kFmaThreads), s, packed, sigma16, rows, apr,
+                               x + b0 * in_f, in_f, y + b0 * rows, t->cb_nib, bad);
       count_launches(1);
       if (e != cudaSuccess) rc = cuda_fail(e, "lut_gemv launch");
       continue;
