@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 4) dequant_kernel(const __grid_const
                                                            const uint4 *__restrict__ codes,
                                                            int32_t *__restrict__ bad) {
   __shared__ WarpSmem smem[kWarpsPerBlock];
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   WarpSmem &W = smem[threadIdx.x >> 5];
   const int64_t total = b.atom_start[b.count];
@@ -334,8 +335,10 @@ int launch_dequant(const Tables *t, const h24_dequant_layer * /*layers_dev*/,
     const int64_t want = (atoms + kSub * kWarpsPerBlock - 1) / (kSub * kWarpsPerBlock);
     const int64_t cap = static_cast<int64_t>(sm_count()) * resident_blocks();
     const int grid = static_cast<int>(want < cap ? want : cap);
-    dequant_kernel<<<grid, kThreads, 0, s>>>(b, reinterpret_cast<const uint4 *>(t->cb_nib), bad);
-    H24_CUDA_TRY(cudaGetLastError());
+    // Programmatic dependent launch (pdl_enter): the launch overlaps the
+    // tail of the kernel before it.
+    H24_CUDA_TRY(launch_pdl(dequant_kernel, dim3(grid), dim3(kThreads), s, b,
+                            reinterpret_cast<const uint4 *>(t->cb_nib), bad));
     count_launches(1);
   }
   return H24_OK;

@@ -205,6 +205,7 @@ __global__ void __launch_bounds__(kThreads) int8_dequant_kernel(const int8_t *__
                                                                 const uint16_t *__restrict__ mu16,
                                                                 int64_t rows, int64_t cols,
                                                                 uint16_t *__restrict__ out, bool vec) {
+  pdl_enter();
   if (vec) {
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (kThreads / 32);
@@ -279,8 +280,9 @@ int launch_int8_dequant(const int8_t *q, const uint16_t *mu16, int64_t rows, int
   const bool vec = cols % 16 == 0 && aligned16(q) && aligned16(out);
   const int grid = vec ? grid_for(int8_dequant_kernel, rows, kThreads / 32)
                        : grid_for(int8_dequant_kernel, rows * cols, kThreads);
-  int8_dequant_kernel<<<grid, kThreads, 0, s>>>(q, mu16, rows, cols, out, vec);
-  H24_CUDA_TRY(cudaGetLastError());
+  // Programmatic dependent launch (pdl_enter): the launch overlaps the tail
+  // of the kernel before it.
+  H24_CUDA_TRY(launch_pdl(int8_dequant_kernel, dim3(grid), dim3(kThreads), s, q, mu16, rows, cols, out, vec));
   count_launches(1);
   return H24_OK;
 }
