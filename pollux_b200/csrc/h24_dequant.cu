@@ -9,7 +9,9 @@
 // reproduced, so the result is bit-identical given the same indices and
 // scales.
 //
-// The kernel is bound by the 48-byte fp16 output per atom.  A codeword holds
+// The 48-byte fp16 output of an atom (1.5 sectors) and its one code-entry
+// gather (one sector) pass each SM's L1-to-crossbar interface, which moves a
+// sector per cycle and bounds the kernel (80 % busy).  A codeword holds
 // at most four distinct coordinates, fixed by its type, so the codebook is
 // stored as 2-bit positions in a per-type value list (16 bytes per codeword,
 // one 32-byte sector, 3.1 MB, L2-resident) and two output values come from
