@@ -112,3 +112,16 @@ def test_packed_linear_buffers_match_reference_layout():
     assert m.packed_weights.dtype == torch.uint8 and m.packed_weights.numel() == 614400 // 4 * 9
     assert m.sigma_rows.dtype == torch.float16 and m.sigma_rows.numel() == 7680
     assert set(dict(m.named_buffers())) == {"packed_weights", "sigma_rows"}
+
+
+def test_row_division_by_multiply_high_is_exact():
+    # The dequant kernel divides in-row positions x < d + 128 by the row
+    # length d (atoms per row) as floor(x * ceil(2^32 / d) / 2^32) for
+    # d <= 65,000 (h24_dequant.cu, RowDiv).  Exhaustive for short rows, and at
+    # the largest d the kernel uses it for, where the error term is largest.
+    rng = np.random.default_rng(0)
+    ds = list(range(1, 1025)) + [int(v) for v in rng.integers(1025, 65001, 200)] + list(range(64900, 65001))
+    for d in ds:
+        m = np.uint64(((1 << 32) + d - 1) // d)
+        x = np.arange(0, d + 128, dtype=np.uint64)
+        assert np.array_equal((x * m) >> np.uint64(32), x // np.uint64(d)), d
